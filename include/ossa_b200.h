@@ -1,0 +1,136 @@
+/*
+ * ossa_b200.h — C ABI of the Blackwell (sm_100a) routed sparse-attention hot path.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA stream
+ * (passed as an opaque pointer, binary-compatible with cudaStream_t / CUstream).
+ * Nothing here allocates device memory: the caller owns every buffer, including
+ * outputs and the workspace whose size ossa_router_workspace_size() reports.
+ * Work is enqueued on `stream` and returns without a host synchronisation.
+ *
+ * Tensors are contiguous row-major:
+ *   q          (B, H,   N, D)
+ *   k, v       (B, Hkv, N, D)   Hkv divides H; query head h reads kv head h / (H / Hkv),
+ *                               the mapping repeat_interleave gives in
+ *                               ossa/bench/sparse_forward.py:175-178. Hkv == H is the
+ *                               already-repeated layout the reference passes around.
+ *   indices    (B, H,   N, K)   int32 or int64
+ *   out        (B, H,   N, D)   same dtype as q
+ *
+ * Status: every function returns OSSA_OK (0) or an error code; the message of the
+ * last error on the calling thread is available from ossa_last_error_string().
+ * No entry point calls exit/abort or traps on the device.
+ */
+#ifndef OSSA_B200_H
+#define OSSA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define OSSA_API __attribute__((visibility("default")))
+#else
+#define OSSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* ossa_stream_t; /* a cudaStream_t; NULL is the legacy default stream */
+
+enum ossa_status {
+    OSSA_OK = 0,
+    OSSA_ERR_INVALID = 1,     /* bad shape, dtype, pointer or alignment */
+    OSSA_ERR_CUDA = 2,        /* a CUDA launch or runtime call failed */
+    OSSA_ERR_WORKSPACE = 3,   /* workspace missing or smaller than required */
+    OSSA_ERR_UNSUPPORTED = 4  /* valid request outside what the kernels implement */
+};
+
+enum ossa_dtype {
+    OSSA_F32 = 0,
+    OSSA_BF16 = 1
+};
+
+/* Library version string, e.g. "0.1.0". */
+OSSA_API const char* ossa_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+OSSA_API const char* ossa_last_error_string(void);
+
+/*
+ * Number of kernels this library has launched in the process so far (all
+ * threads).  Diagnostic only, no counterpart in the reference: lets a caller
+ * count the device launches a region of its own code issued.
+ */
+OSSA_API uint64_t ossa_launch_count(void);
+
+/*
+ * Gathered top-K attention forward, O(N*K*D).
+ * Replaces topk_attention (ossa/triton_kernel.py:41-70) and the kernel it
+ * launches (ossa/triton_kernel.py:80-167, 170-218); computes the same result as
+ * sparse_attention_forward_chunked (ossa/sparse_attention.py:87-137):
+ *   s_j   = (q_i . k_{idx_j}) * scale, masked to -inf when idx_j is outside [0, N)
+ *           or (causal) idx_j > i;
+ *   out_i = softmax(s) . V[idx], and 0 for a row whose every entry is masked.
+ * dtype: OSSA_F32 or OSSA_BF16 for q, k, v and out (fp32 accumulation).
+ * idx_is_64: 0 for int32 indices, 1 for int64.  D in {16, 32, 64, 128, 256}.
+ */
+OSSA_API int ossa_topk_attention_fwd(const void* q, const void* k, const void* v,
+                            const void* indices, int idx_is_64, int dtype,
+                            int B, int H, int Hkv, int N, int D, int K,
+                            float scale, int causal, void* out,
+                            ossa_stream_t stream);
+
+/*
+ * Bytes of workspace ossa_router_topk / ossa_router_score need for this shape.
+ * Replaces nothing in the reference (its router materialises (B,H,N,N) logits,
+ * ossa/router.py:182-189); the workspace holds the projected q'/k' rows.
+ */
+OSSA_API size_t ossa_router_workspace_size(int B, int H, int Hkv, int N, int r, int K);
+
+/*
+ * ContentRouter causal (or full) top-K key selection.
+ * Replaces ContentRouter.score + masked_fill + torch.topk as the patched forward
+ * runs them (ossa/router.py:171-190, ossa/bench/sparse_forward.py:185-202) and
+ * ContentRouter.topk (ossa/router.py:202-203) when causal == 0.
+ *   q', k'      = q Wq^T, k Wk^T  (wq, wk: (r, D) fp32, the nn.Linear weights)
+ *   score(i,j)  = (q'_i . k'_j) * (1/sqrt(r)) + pos_bias[clamp(i - j + seq_len_cfg, 0, 2*seq_len_cfg - 1)]
+ * Selection is in fp32: the K best keys by (score desc, key index asc) among
+ * j <= i (causal) or all j.  Output row i lists the chosen key indices in
+ * ascending order, padded with -1 when fewer than K keys are eligible.
+ * q, k dtype: OSSA_F32 or OSSA_BF16 (converted exactly to fp32).
+ */
+OSSA_API int ossa_router_topk(const void* q, const void* k, int dtype,
+                     const float* wq, const float* wk, const float* pos_bias,
+                     int B, int H, int Hkv, int N, int D, int r, int seq_len_cfg,
+                     int K, int causal, int32_t* idx_out,
+                     void* workspace, size_t workspace_bytes,
+                     ossa_stream_t stream);
+
+/*
+ * Materialised router logits, (B, H, N, N) fp32, no causal mask.
+ * Replaces ContentRouter.score / ContentRouter.forward (ossa/router.py:171-200)
+ * with the same fp32 score definition ossa_router_topk selects on.
+ */
+OSSA_API int ossa_router_score(const void* q, const void* k, int dtype,
+                      const float* wq, const float* wk, const float* pos_bias,
+                      int B, int H, int Hkv, int N, int D, int r, int seq_len_cfg,
+                      float* scores_out, void* workspace, size_t workspace_bytes,
+                      ossa_stream_t stream);
+
+/*
+ * Oracle (exact dot-product) top-K selection, no router.
+ * Replaces the oracle selector of the patched forward
+ * (ossa/bench/sparse_forward.py:194-202): score(i,j) = (q_i . k_j) * scale in fp32,
+ * then the same causal top-K rule and output layout as ossa_router_topk.
+ */
+OSSA_API int ossa_oracle_topk(const void* q, const void* k, int dtype,
+                     int B, int H, int Hkv, int N, int D, float scale,
+                     int K, int causal, int32_t* idx_out,
+                     ossa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OSSA_B200_H */

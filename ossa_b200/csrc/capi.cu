@@ -1,0 +1,207 @@
+// C ABI entry points (declared in include/ossa_b200.h): argument validation,
+// workspace carving and kernel dispatch.  Validation happens before any CUDA
+// call, so a rejected request never touches the device.
+#include "../../include/ossa_b200.h"
+#include "kernels.h"
+
+#include <atomic>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string>
+
+namespace ossa {
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}
+void note_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+}  // namespace ossa
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return OSSA_OK;
+    return fail(OSSA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+bool valid_dtype(int d) { return d == OSSA_F32 || d == OSSA_BF16; }
+
+int check_heads(int B, int H, int Hkv, int N) {
+    if (B < 0 || H <= 0 || Hkv <= 0 || N < 0)
+        return fail(OSSA_ERR_INVALID, "bad shape B=%d H=%d Hkv=%d N=%d", B, H, Hkv, N);
+    if (H % Hkv != 0)
+        return fail(OSSA_ERR_INVALID, "H=%d is not a multiple of Hkv=%d", H, Hkv);
+    if ((long long)B * H > (1ll << 30) || N > (1 << 30))
+        return fail(OSSA_ERR_UNSUPPORTED, "shape too large B=%d H=%d N=%d", B, H, N);
+    return OSSA_OK;
+}
+
+struct RouterLayout {
+    size_t qp_off, kp_off, total;
+};
+
+RouterLayout router_layout(int B, int H, int Hkv, int N, int r) {
+    RouterLayout l;
+    const size_t qp = (size_t)B * H * N * r * sizeof(float);
+    const size_t kp = (size_t)B * Hkv * N * r * sizeof(float);
+    l.qp_off = 0;
+    l.kp_off = align_up(qp);
+    l.total = l.kp_off + align_up(kp);
+    return l;
+}
+
+bool supported_r(int r) { return r == 16 || r == 32 || r == 64 || r == 128; }
+
+int check_router(const void* q, const void* k, int dtype, const float* wq, const float* wk,
+                 const float* pos_bias, int B, int H, int Hkv, int N, int D, int r,
+                 int seq_len_cfg, const void* out, void* ws, size_t ws_bytes) {
+    int st = check_heads(B, H, Hkv, N);
+    if (st) return st;
+    if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);
+    if (D <= 0) return fail(OSSA_ERR_INVALID, "bad head_dim D=%d", D);
+    if (!supported_r(r)) return fail(OSSA_ERR_UNSUPPORTED, "proj_dim r=%d not in {16,32,64,128}", r);
+    if (seq_len_cfg <= 0 || seq_len_cfg > (1 << 28))
+        return fail(OSSA_ERR_INVALID, "bad seq_len_cfg %d", seq_len_cfg);
+    if ((long long)B * H * N == 0) return OSSA_OK;
+    if (!q || !k || !wq || !wk || !pos_bias || !out)
+        return fail(OSSA_ERR_INVALID, "null pointer argument");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(out))
+        return fail(OSSA_ERR_INVALID, "q, k and the output must be 16-byte aligned");
+    const RouterLayout l = router_layout(B, H, Hkv, N, r);
+    if (!ws || ws_bytes < l.total || !aligned16(ws))
+        return fail(OSSA_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required, got %zu",
+                    l.total, ws ? ws_bytes : (size_t)0);
+    return OSSA_OK;
+}
+
+int project_both(const void* q, const void* k, int dtype, const float* wq, const float* wk,
+                 int B, int H, int Hkv, int N, int D, int r, void* ws, cudaStream_t stream,
+                 float** qp_out, float** kp_out) {
+    const RouterLayout l = router_layout(B, H, Hkv, N, r);
+    char* base = static_cast<char*>(ws);
+    float* qp = reinterpret_cast<float*>(base + l.qp_off);
+    float* kp = reinterpret_cast<float*>(base + l.kp_off);
+    ossa::ProjectArgs pa{q, wq, qp, (long long)B * H * N, D, r, dtype};
+    int st = cuda_status(ossa::launch_project(pa, stream), "q projection launch");
+    if (st) return st;
+    ossa::ProjectArgs pk{k, wk, kp, (long long)B * Hkv * N, D, r, dtype};
+    st = cuda_status(ossa::launch_project(pk, stream), "k projection launch");
+    if (st) return st;
+    *qp_out = qp;
+    *kp_out = kp;
+    return OSSA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ossa_version(void) { return "0.1.0"; }
+
+const char* ossa_last_error_string(void) { return g_last_error.c_str(); }
+
+uint64_t ossa_launch_count(void) { return (uint64_t)ossa::g_launches.load(std::memory_order_relaxed); }
+
+int ossa_topk_attention_fwd(const void* q, const void* k, const void* v, const void* indices,
+                            int idx_is_64, int dtype, int B, int H, int Hkv, int N, int D, int K,
+                            float scale, int causal, void* out, ossa_stream_t stream) {
+    int st = check_heads(B, H, Hkv, N);
+    if (st) return st;
+    if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);
+    if (D != 16 && D != 32 && D != 64 && D != 128 && D != 256)
+        return fail(OSSA_ERR_UNSUPPORTED, "head_dim D=%d not in {16,32,64,128,256}", D);
+    if (K < 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
+    if (idx_is_64 != 0 && idx_is_64 != 1) return fail(OSSA_ERR_INVALID, "idx_is_64 must be 0 or 1");
+    if (!isfinite(scale)) return fail(OSSA_ERR_INVALID, "scale must be finite");
+    if ((long long)B * H * N == 0) return OSSA_OK;
+    if (!q || !k || !v || !out || (K > 0 && !indices))
+        return fail(OSSA_ERR_INVALID, "null pointer argument");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return fail(OSSA_ERR_INVALID, "q, k, v and out must be 16-byte aligned");
+    if (K > 0 && !aligned16(indices)) return fail(OSSA_ERR_INVALID, "indices must be 16-byte aligned");
+    ossa::GatherArgs a{q, k, v, indices, out, idx_is_64, dtype, B, H, Hkv, N, D, K, scale, causal ? 1 : 0};
+    return cuda_status(ossa::launch_gather_attn(a, static_cast<cudaStream_t>(stream)),
+                       "topk attention launch");
+}
+
+size_t ossa_router_workspace_size(int B, int H, int Hkv, int N, int r, int K) {
+    (void)K;
+    if (B < 0 || H <= 0 || Hkv <= 0 || N < 0 || r <= 0) return 0;
+    return router_layout(B, H, Hkv, N, r).total;
+}
+
+int ossa_router_topk(const void* q, const void* k, int dtype, const float* wq, const float* wk,
+                     const float* pos_bias, int B, int H, int Hkv, int N, int D, int r,
+                     int seq_len_cfg, int K, int causal, int32_t* idx_out, void* workspace,
+                     size_t workspace_bytes, ossa_stream_t stream) {
+    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, D, r, seq_len_cfg, idx_out,
+                          workspace, workspace_bytes);
+    if (st) return st;
+    if (K <= 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
+    if (!ossa::score_topk_supported(r, K))
+        return fail(OSSA_ERR_UNSUPPORTED, "top-K selection supports K <= 160 (got K=%d)", K);
+    if ((long long)B * H * N == 0) return OSSA_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float *qp = nullptr, *kp = nullptr;
+    st = project_both(q, k, dtype, wq, wk, B, H, Hkv, N, D, r, workspace, s, &qp, &kp);
+    if (st) return st;
+    ossa::ScoreTopkArgs a{qp, kp, ossa::kF32, pos_bias, seq_len_cfg, B, H, Hkv, N, r, K,
+                          (float)(1.0 / sqrt((double)r)), causal ? 1 : 0, idx_out};
+    return cuda_status(ossa::launch_score_topk(a, s), "router top-K launch");
+}
+
+int ossa_router_score(const void* q, const void* k, int dtype, const float* wq, const float* wk,
+                      const float* pos_bias, int B, int H, int Hkv, int N, int D, int r,
+                      int seq_len_cfg, float* scores_out, void* workspace, size_t workspace_bytes,
+                      ossa_stream_t stream) {
+    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, D, r, seq_len_cfg,
+                          scores_out, workspace, workspace_bytes);
+    if (st) return st;
+    if ((long long)B * H * N == 0) return OSSA_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float *qp = nullptr, *kp = nullptr;
+    st = project_both(q, k, dtype, wq, wk, B, H, Hkv, N, D, r, workspace, s, &qp, &kp);
+    if (st) return st;
+    ossa::ScoreDenseArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, N, r,
+                           (float)(1.0 / sqrt((double)r)), scores_out};
+    return cuda_status(ossa::launch_score_dense(a, s), "router score launch");
+}
+
+int ossa_oracle_topk(const void* q, const void* k, int dtype, int B, int H, int Hkv, int N, int D,
+                     float scale, int K, int causal, int32_t* idx_out, ossa_stream_t stream) {
+    int st = check_heads(B, H, Hkv, N);
+    if (st) return st;
+    if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);
+    if (!supported_r(D))
+        return fail(OSSA_ERR_UNSUPPORTED, "oracle selection supports head_dim in {16,32,64,128}, got %d", D);
+    if (K <= 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
+    if (!ossa::score_topk_supported(D, K))
+        return fail(OSSA_ERR_UNSUPPORTED, "top-K selection supports K <= 160 (got K=%d)", K);
+    if (!isfinite(scale)) return fail(OSSA_ERR_INVALID, "scale must be finite");
+    if ((long long)B * H * N == 0) return OSSA_OK;
+    if (!q || !k || !idx_out) return fail(OSSA_ERR_INVALID, "null pointer argument");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(idx_out))
+        return fail(OSSA_ERR_INVALID, "q, k and the output must be 16-byte aligned");
+    ossa::ScoreTopkArgs a{q, k, dtype, nullptr, 1, B, H, Hkv, N, D, K, scale, causal ? 1 : 0, idx_out};
+    return cuda_status(ossa::launch_score_topk(a, static_cast<cudaStream_t>(stream)),
+                       "oracle top-K launch");
+}
+
+}  // extern "C"

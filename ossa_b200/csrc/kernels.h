@@ -1,0 +1,68 @@
+// Internal launcher interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ossa {
+
+enum DType { kF32 = 0, kBF16 = 1 };
+
+// Counts successful kernel launches (ossa_launch_count); every launcher calls it.
+void note_launch(int n = 1);
+
+struct GatherArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    const void* idx;
+    void* out;
+    int idx_is_64;
+    int dtype;
+    int B, H, Hkv, N, D, K;
+    float scale;
+    int causal;
+};
+cudaError_t launch_gather_attn(const GatherArgs& a, cudaStream_t stream);
+
+// out[row][c] = fmaf-chain over d = 0..D-1 of x[row][d] * w[c][d], for c < R.
+struct ProjectArgs {
+    const void* x;   // (rows, D), dtype
+    const float* w;  // (R, D) fp32
+    float* out;      // (rows, R) fp32
+    long long rows;
+    int D, R, dtype;
+};
+cudaError_t launch_project(const ProjectArgs& a, cudaStream_t stream);
+
+// Exact fp32 causal/full top-K over score(i,j) = dot(qrows_i, krows_j) * scale
+// (+ pos_bias[clamp(i - j + L, 0, 2L - 1)] when bias != nullptr).
+// qrows: (B*H*N, R), krows: (B*Hkv*N, R), both `dtype`.
+struct ScoreTopkArgs {
+    const void* qrows;
+    const void* krows;
+    int dtype;
+    const float* bias;
+    int L;
+    int B, H, Hkv, N, R, K;
+    float scale;
+    int causal;
+    int32_t* out;  // (B*H*N, K)
+};
+cudaError_t launch_score_topk(const ScoreTopkArgs& a, cudaStream_t stream);
+bool score_topk_supported(int R, int K);
+
+// Dense fp32 scores (B, H, N, N) with the same score definition, no mask.
+struct ScoreDenseArgs {
+    const float* qrows;
+    const float* krows;
+    const float* bias;
+    int L;
+    int B, H, Hkv, N, R;
+    float scale;
+    float* out;
+};
+cudaError_t launch_score_dense(const ScoreDenseArgs& a, cudaStream_t stream);
+
+}  // namespace ossa

@@ -1,0 +1,115 @@
+// ContentRouter projections q' = q Wq^T and k' = k Wk^T (ossa/router.py:179-180).
+//
+// Each output is one fp32 fused-multiply-add chain over d = 0..D-1 starting from
+// 0.0f: acc = fmaf(x[d], w[c][d], acc).  That fixed order makes q'/k' bit-exact
+// against the CPU oracle (which evaluates the same chain with C fmaf) and is the
+// "fp32 projection" every selection decision downstream is defined on.
+//
+// Tiling: a CTA computes ROWS x R outputs with 256 threads; each thread owns a
+// 4 x 4 register tile.  D is consumed in chunks of 64: the x chunk is staged
+// transposed in shared memory (float4 broadcast reads of 4 rows) and W^T in
+// shared memory (float4 reads of 4 output columns), i.e. two LDS.128 per 16 FFMA.
+// The kprojection is GQA-aware by construction: the caller runs it on the Hkv key
+// heads only, never on repeated copies.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ossa {
+
+namespace {
+
+constexpr int kProjThreads = 256;
+constexpr int kDChunk = 64;
+
+template <typename T, int R>
+__global__ void __launch_bounds__(kProjThreads)
+project_kernel(const T* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
+               long long rows, int D) {
+    constexpr int CG = R / 4;                    // column groups
+    constexpr int RG = kProjThreads / CG;        // row groups
+    constexpr int ROWS = RG * 4;                 // rows per CTA
+    constexpr int XS = ROWS + 4;                 // padded stride (keeps float4 alignment)
+    extern __shared__ float4 smem4[];
+    float* Xs = reinterpret_cast<float*>(smem4);  // [kDChunk][XS]
+    float* Ws = Xs + kDChunk * XS;                // [kDChunk][R]
+
+    const int tid = threadIdx.x;
+    const int cg = tid % CG;
+    const int rg = tid / CG;
+    const long long row0 = (long long)blockIdx.x * ROWS;
+
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+
+    for (int dc = 0; dc < D; dc += kDChunk) {
+        const int dn = min(kDChunk, D - dc);
+        __syncthreads();
+        for (int e = tid; e < ROWS * kDChunk; e += kProjThreads) {
+            const int r = e / kDChunk, d = e - r * kDChunk;
+            const long long gr = row0 + r;
+            float val = 0.f;
+            if (gr < rows && d < dn) val = to_f32(x[gr * D + dc + d]);
+            Xs[d * XS + r] = val;
+        }
+        for (int e = tid; e < R * kDChunk; e += kProjThreads) {
+            const int d = e / R, c = e - d * R;
+            Ws[d * R + c] = d < dn ? __ldg(w + (size_t)c * D + dc + d) : 0.f;
+        }
+        __syncthreads();
+        for (int d = 0; d < dn; ++d) {
+            const float4 xv = *reinterpret_cast<const float4*>(Xs + d * XS + rg * 4);
+            const float4 wv = *reinterpret_cast<const float4*>(Ws + d * R + cg * 4);
+            const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+            const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[a][c] = fmaf(xa[a], wa[c], acc[a][c]);
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const long long gr = row0 + rg * 4 + a;
+        if (gr < rows) {
+            *reinterpret_cast<float4*>(out + gr * R + cg * 4) =
+                make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+        }
+    }
+}
+
+template <typename T, int R>
+cudaError_t launch_r(const ProjectArgs& a, cudaStream_t stream) {
+    constexpr int ROWS = (kProjThreads / (R / 4)) * 4;
+    const size_t smem = (size_t)kDChunk * (ROWS + 4) * sizeof(float) + (size_t)kDChunk * R * sizeof(float);
+    auto kern = project_kernel<T, R>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const long long nblk = (a.rows + ROWS - 1) / ROWS;
+    if (nblk == 0) return cudaSuccess;
+    kern<<<(unsigned)nblk, kProjThreads, smem, stream>>>(static_cast<const T*>(a.x), a.w, a.out, a.rows, a.D);
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) note_launch();
+    return err;
+}
+
+template <typename T>
+cudaError_t launch_t(const ProjectArgs& a, cudaStream_t stream) {
+    switch (a.R) {
+        case 16: return launch_r<T, 16>(a, stream);
+        case 32: return launch_r<T, 32>(a, stream);
+        case 64: return launch_r<T, 64>(a, stream);
+        case 128: return launch_r<T, 128>(a, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_project(const ProjectArgs& a, cudaStream_t stream) {
+    return a.dtype == kF32 ? launch_t<float>(a, stream) : launch_t<__nv_bfloat16>(a, stream);
+}
+
+}  // namespace ossa

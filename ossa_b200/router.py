@@ -1,0 +1,74 @@
+"""ContentRouter with fused sm_100a scoring and selection (ossa/router.py:136-203).
+
+Same configuration dataclass, parameter names and shapes as the reference, so
+``load_state_dict`` accepts the reference's checkpoints unchanged
+(``q_proj.0.weight`` (r, D), ``k_proj.0.weight`` (r, D), ``pos_bias.weight``
+(2*seq_len, 1)).  ``score``/``forward`` materialise the (B, H, N, N) fp32 logits
+with a CUDA kernel; ``topk`` never materialises them.
+
+Additive differences:
+* ``k`` may carry Hkv < H heads (GQA); the reference needs repeated heads.
+* ``topk(..., causal=True)`` masks keys j > i before selecting (the patched
+  forward's behaviour, sparse_forward.py:200-202); the default ``causal=False``
+  is the reference's unmasked ``topk`` (router.py:202-203).
+* ``topk`` returns each row's index set in ascending key order (torch.topk
+  orders by score), padded with -1 where fewer than ``top_k`` keys are
+  eligible under the causal mask.  ``index_dtype`` defaults to int64 like
+  torch.topk; int32 avoids a conversion.
+* Scores are defined by a fixed fp32 evaluation order (fmaf chains) so the
+  selected sets are reproducible bit for bit.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import select
+
+
+@dataclass
+class ContentRouterConfig:
+    head_dim: int
+    n_heads: int
+    seq_len: int
+    proj_dim: int = 64        # router-internal projection size
+    layers: int = 1           # unused, kept for config compatibility
+
+
+class ContentRouter(nn.Module):
+    """Content-based router: score(i, j) = (q_i Wq^T) . (k_j Wk^T) / sqrt(r)
+    + pos_bias[clamp(i - j + seq_len, 0, 2*seq_len - 1)]."""
+
+    def __init__(self, cfg: ContentRouterConfig) -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.q_proj = nn.Sequential(nn.Linear(cfg.head_dim, cfg.proj_dim, bias=False))
+        self.k_proj = nn.Sequential(nn.Linear(cfg.head_dim, cfg.proj_dim, bias=False))
+        self.pos_bias = nn.Embedding(2 * cfg.seq_len, 1)
+
+    def _params(self):
+        return self.q_proj[0].weight, self.k_proj[0].weight, self.pos_bias.weight
+
+    def score(self, q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+        """q: (B, H, N, D), k: (B, H or Hkv, N, D) -> (B, H, N, N) fp32 logits."""
+        wq, wk, pb = self._params()
+        return select.router_scores(q, k, wq, wk, pb, self.cfg.seq_len)
+
+    def forward(self, q: torch.Tensor, k: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if k is None:
+            raise TypeError("ContentRouter needs both q and k tensors; call .score(q, k).")
+        return self.score(q, k)
+
+    def topk(self, q: torch.Tensor, k: torch.Tensor, top_k: int, *, causal: bool = False,
+             index_dtype: torch.dtype = torch.int64) -> torch.Tensor:
+        """Indices (B, H, N, top_k) of the top_k keys per query (see module doc)."""
+        N = q.shape[2]
+        if not causal and top_k > N:
+            raise RuntimeError(f"selected index k out of range: top_k={top_k} > N={N}")
+        wq, wk, pb = self._params()
+        idx = select.router_topk(q, k, wq, wk, pb, self.cfg.seq_len, top_k, causal=causal)
+        return idx if index_dtype == torch.int32 else idx.to(index_dtype)

@@ -1,0 +1,147 @@
+"""Fused causal top-K key selection (router and exact-dot oracle selectors).
+
+Functional entry points behind ``ContentRouter.topk`` and the patched
+attention forward.  The reference materialises the full (B, H, N, N) selector
+and calls ``torch.topk`` (ossa/router.py:171-203,
+ossa/bench/sparse_forward.py:180-202); here one sm_100a kernel scores and
+selects per query block, so the N x N matrix never reaches HBM.
+
+Index convention (shared by every ossa_b200 selector and consumed by
+``topk_attention``): int32, shape (B, H, N, K), each row's chosen keys in
+ascending key order, padded with -1 when fewer than K keys are eligible
+(rows i < K-1 under the causal mask).  The set is exactly the set torch.topk
+returns on fp32 scores with ties broken toward the lower key index.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+
+def _check_qk(q: torch.Tensor, k: torch.Tensor):
+    if q.dim() != 4 or k.dim() != 4:
+        raise ValueError(f"q and k must be (B, H, N, D); got {tuple(q.shape)} and {tuple(k.shape)}")
+    B, H, N, D = q.shape
+    Bk, Hkv, Nk, Dk = k.shape
+    if (B, N, D) != (Bk, Nk, Dk):
+        raise ValueError(f"q {tuple(q.shape)} and k {tuple(k.shape)} disagree on B, N or D")
+    if Hkv <= 0 or H % Hkv != 0:
+        raise ValueError(f"query heads {H} must be a multiple of key heads {Hkv}")
+    return B, H, Hkv, N, D
+
+
+def _as_kernel_input(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    if t.dtype not in (torch.float32, torch.bfloat16):
+        t = t.float()  # float16 and friends convert exactly to fp32
+    return t.to(dtype).contiguous()
+
+
+def _common_dtype(q: torch.Tensor, k: torch.Tensor) -> torch.dtype:
+    return torch.bfloat16 if (q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16) else torch.float32
+
+
+def router_topk(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,
+                pos_bias: torch.Tensor, seq_len: int, top_k: int, *,
+                causal: bool = True) -> torch.Tensor:
+    """ContentRouter top-K (router.py:171-190 scores) -> int32 (B, H, N, top_k).
+
+    q: (B, H, N, D); k: (B, Hkv, N, D) with Hkv dividing H (or the repeated H
+    heads).  wq, wk: (r, D) projection weights; pos_bias: (2*seq_len, 1) or
+    (2*seq_len,).  Scores and selection are fp32.
+    """
+    B, H, Hkv, N, D = _check_qk(q, k)
+    dev = _lib.require_cuda(q, k, wq, wk, pos_bias)
+    r = wq.shape[0]
+    if wq.shape != (r, D) or wk.shape != (r, D):
+        raise ValueError(f"projection weights must be ({r}, {D}); got {tuple(wq.shape)}, {tuple(wk.shape)}")
+    if pos_bias.numel() != 2 * seq_len:
+        raise ValueError(f"pos_bias has {pos_bias.numel()} entries, expected 2*seq_len = {2 * seq_len}")
+    if top_k < 0:
+        raise ValueError(f"top_k must be >= 0, got {top_k}")
+    out = torch.empty((B, H, N, top_k), dtype=torch.int32, device=dev)
+    if out.numel() == 0:
+        return out
+    dt = _common_dtype(q, k)
+    qc = _as_kernel_input(q, dt)
+    kc = _as_kernel_input(k, dt)
+    wqc = wq.detach().float().contiguous()
+    wkc = wk.detach().float().contiguous()
+    pbc = pos_bias.detach().float().contiguous()
+    L = _lib.lib()
+    ws_bytes = L.ossa_router_workspace_size(B, H, Hkv, N, r, top_k)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = L.ossa_router_topk(qc.data_ptr(), kc.data_ptr(), _lib.dtype_code(qc), wqc.data_ptr(),
+                                wkc.data_ptr(), pbc.data_ptr(), B, H, Hkv, N, D, r, int(seq_len),
+                                int(top_k), 1 if causal else 0, out.data_ptr(), ws.data_ptr(),
+                                ws_bytes, _lib.stream_ptr(dev))
+    _lib.check(st)
+    return out
+
+
+def router_scores(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,
+                  pos_bias: torch.Tensor, seq_len: int) -> torch.Tensor:
+    """Materialised router logits (B, H, N, N) fp32 (ContentRouter.score)."""
+    B, H, Hkv, N, D = _check_qk(q, k)
+    dev = _lib.require_cuda(q, k, wq, wk, pos_bias)
+    r = wq.shape[0]
+    if wq.shape != (r, D) or wk.shape != (r, D):
+        raise ValueError(f"projection weights must be ({r}, {D}); got {tuple(wq.shape)}, {tuple(wk.shape)}")
+    if pos_bias.numel() != 2 * seq_len:
+        raise ValueError(f"pos_bias has {pos_bias.numel()} entries, expected 2*seq_len = {2 * seq_len}")
+    out = torch.empty((B, H, N, N), dtype=torch.float32, device=dev)
+    if out.numel() == 0:
+        return out
+    dt = _common_dtype(q, k)
+    qc = _as_kernel_input(q, dt)
+    kc = _as_kernel_input(k, dt)
+    wqc = wq.detach().float().contiguous()
+    wkc = wk.detach().float().contiguous()
+    pbc = pos_bias.detach().float().contiguous()
+    L = _lib.lib()
+    ws_bytes = L.ossa_router_workspace_size(B, H, Hkv, N, r, 0)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = L.ossa_router_score(qc.data_ptr(), kc.data_ptr(), _lib.dtype_code(qc), wqc.data_ptr(),
+                                 wkc.data_ptr(), pbc.data_ptr(), B, H, Hkv, N, D, r, int(seq_len),
+                                 out.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_ptr(dev))
+    _lib.check(st)
+    return out
+
+
+def oracle_topk(q: torch.Tensor, k: torch.Tensor, top_k: int, *, scale: float | None = None,
+                causal: bool = True) -> torch.Tensor:
+    """Exact-dot selector (sparse_forward.py:194-202): top-K of (q . k) * scale,
+    fp32, no router.  Returns int32 (B, H, N, top_k)."""
+    B, H, Hkv, N, D = _check_qk(q, k)
+    dev = _lib.require_cuda(q, k)
+    if top_k < 0:
+        raise ValueError(f"top_k must be >= 0, got {top_k}")
+    out = torch.empty((B, H, N, top_k), dtype=torch.int32, device=dev)
+    if out.numel() == 0:
+        return out
+    s = float(1.0 / math.sqrt(D)) if scale is None else float(scale)
+    dt = _common_dtype(q, k)
+    qc = _as_kernel_input(q, dt)
+    kc = _as_kernel_input(k, dt)
+    with torch.cuda.device(dev):
+        st = _lib.lib().ossa_oracle_topk(qc.data_ptr(), kc.data_ptr(), _lib.dtype_code(qc), B, H, Hkv,
+                                         N, D, s, int(top_k), 1 if causal else 0, out.data_ptr(),
+                                         _lib.stream_ptr(dev))
+    _lib.check(st)
+    return out
+
+
+def with_diagonal(idx: torch.Tensor) -> torch.Tensor:
+    """Appends the query's own position to every row that does not already list
+    it (-1 where it does): the forced diagonal of the reference's "mask" path
+    (ossa/bench/sparse_forward.py:216-218), expressed as an index set."""
+    N = idx.shape[2]
+    pos = torch.arange(N, device=idx.device, dtype=idx.dtype).view(1, 1, N, 1)
+    has = (idx == pos).any(dim=-1, keepdim=True)
+    diag = torch.where(has, torch.full_like(pos.expand_as(has), -1), pos.expand_as(has))
+    return torch.cat([idx, diag], dim=-1).contiguous()

@@ -1,0 +1,101 @@
+"""Host-side behaviour of the Python API that needs no GPU: the drop-in
+surface, checkpoint compatibility, argument checking, the loud refusal of CPU
+tensors, and the model patch/restore mechanics."""
+
+import inspect
+
+import numpy as np
+import pytest
+import torch
+
+import ossa_b200
+from ossa_b200 import ContentRouter, ContentRouterConfig, topk_attention
+from ossa_b200.bench.sparse_forward import PatchPlan, _patch_layer, select_indices
+
+
+def test_public_surface_matches_reference_names():
+    for name in ("dense_attention_reference", "sparse_attention_forward", "sparse_attention_forward_chunked",
+                 "topk_attention", "HAS_TRITON"):
+        assert hasattr(ossa_b200, name)
+    from ossa_b200.triton_kernel import topk_attention as t2
+    assert t2 is topk_attention
+    sig = inspect.signature(topk_attention)
+    assert list(sig.parameters) == ["q", "k", "v", "topk_indices", "causal", "block_m", "use_triton"]
+    assert sig.parameters["causal"].default is True and sig.parameters["block_m"].default == 32
+
+
+def test_router_loads_reference_checkpoint_state_dict(golden_dir):
+    z = np.load(golden_dir / "router_ckpt_c1.npz")
+    r = ContentRouter(ContentRouterConfig(head_dim=128, n_heads=12, seq_len=512, proj_dim=64))
+    sd = {"q_proj.0.weight": torch.from_numpy(z["wq"]), "k_proj.0.weight": torch.from_numpy(z["wk"]),
+          "pos_bias.weight": torch.from_numpy(z["pos_bias"])}
+    assert set(r.state_dict()) == set(sd)
+    r.load_state_dict(sd)
+    assert sum(p.numel() for p in r.parameters()) == 17408  # the reference's parameter count
+    with pytest.raises(TypeError):
+        r(torch.zeros(1, 1, 4, 128))
+
+
+def test_cpu_tensors_are_rejected_loudly():
+    q = torch.randn(1, 2, 8, 16)
+    idx = torch.zeros(1, 2, 8, 4, dtype=torch.int64)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        topk_attention(q, q, q, topk_indices=idx)
+    r = ContentRouter(ContentRouterConfig(head_dim=16, n_heads=2, seq_len=8, proj_dim=16))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        r.topk(q, q, 4, causal=True)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        r.score(q, q)
+
+
+@pytest.mark.parametrize("bad", [
+    dict(k=torch.randn(1, 3, 8, 16), v=torch.randn(1, 3, 8, 16)),
+    dict(idx=torch.zeros(1, 2, 7, 4, dtype=torch.int64)),
+    dict(idx=torch.zeros(1, 2, 8, 4, dtype=torch.float32)),
+    dict(v=torch.randn(1, 2, 8, 16).double()),
+])
+def test_topk_attention_argument_checks(bad):
+    q = torch.randn(1, 2, 8, 16)
+    a = dict(k=torch.randn(1, 2, 8, 16), v=torch.randn(1, 2, 8, 16), idx=torch.zeros(1, 2, 8, 4, dtype=torch.int64))
+    a.update(bad)
+    with pytest.raises((ValueError, TypeError)):
+        topk_attention(q, a["k"], a["v"], topk_indices=a["idx"])
+
+
+def test_router_topk_too_many_keys_unmasked():
+    r = ContentRouter(ContentRouterConfig(head_dim=16, n_heads=2, seq_len=8, proj_dim=16))
+    q = torch.randn(1, 2, 8, 16)
+    with pytest.raises(RuntimeError, match="out of range"):
+        r.topk(q, q, 9)
+
+
+def _tiny_qwen():
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    cfg = Qwen2Config(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, vocab_size=97, max_position_embeddings=64)
+    torch.manual_seed(0)
+    return Qwen2ForCausalLM(cfg).eval()
+
+
+def test_patch_and_restore_mechanics():
+    model = _tiny_qwen()
+    attn = [layer.self_attn for layer in model.model.layers]
+    before = [a.forward for a in attn]
+    restore = _patch_layer(model, PatchPlan(mode="oracle", k=4, layers=(0, 1), impl="gather"))
+    assert all(a.forward is not b for a, b in zip(attn, before))
+    ids = torch.randint(0, 97, (1, 12))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        model(input_ids=ids, use_cache=False)
+    restore()
+    # bound methods compare equal when they wrap the same function and instance
+    assert all(a.forward == b for a, b in zip(attn, before))
+    assert _patch_layer(model, PatchPlan(mode="dense", layers=(0,)))() is None
+
+
+def test_select_indices_rejects_unknown_modes():
+    q = torch.randn(1, 2, 8, 16)
+    with pytest.raises(ValueError):
+        select_indices(PatchPlan(mode="bogus", k=4, layers=(0,)), 0, q, q)
+    with pytest.raises(KeyError):
+        select_indices(PatchPlan(mode="router", k=4, layers=(0,), routers={}), 0, q, q)

@@ -1,0 +1,176 @@
+"""Bit-exact parity of the fused selection kernels against the CPU oracle.
+
+ossa_router_topk / ossa_oracle_topk must return exactly the oracle's index
+arrays (same sets, ascending order, -1 padding); ossa_router_score must return
+exactly the oracle's fp32 logits.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+from ossa_b200 import ContentRouter, ContentRouterConfig, oracle_topk, router_scores, router_topk
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _weights(D, r, L, seed, bias_scale=1.0):
+    wq, wk, pb = cases.router_weights(D, r, L, seed)
+    return wq, wk, pb * bias_scale
+
+
+def _assert_same(got: torch.Tensor, ref: np.ndarray):
+    g = got.cpu().numpy()
+    assert g.shape == ref.shape
+    bad = (g != ref).any(-1)
+    assert not bad.any(), f"{bad.sum()} rows differ; first at {np.argwhere(bad)[0]}"
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,H,Hkv,N,D,r,L,K", [
+    (1, 12, 2, 512, 128, 64, 512, 64),     # config 1 shape
+    (2, 6, 3, 200, 64, 32, 128, 16),       # ragged, clamped pos_bias
+    (1, 4, 1, 1, 128, 64, 16, 8),          # single row
+    (1, 2, 2, 65, 64, 16, 64, 64),         # K == N - 1
+    (1, 4, 2, 300, 128, 128, 300, 100),    # K not a multiple of 32
+    (1, 2, 1, 97, 32, 64, 40, 160),        # K > N: padded rows everywhere
+    (2, 12, 2, 1000, 128, 64, 1000, 128),  # config 5's K
+])
+@pytest.mark.parametrize("causal", [True, False])
+def test_router_topk_bit_exact(dtype, B, H, Hkv, N, D, r, L, K, causal):
+    seed = B + H + N + D + r + K
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=seed, scale=1.0 / math.sqrt(D))
+    q, k = q.to(dtype), k.to(dtype)
+    wq, wk, pb = _weights(D, r, L, seed)
+    got = router_topk(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K, causal=causal)
+    ref = oracle.router_topk(q, k, wq, wk, pb, L, K, causal=causal)
+    _assert_same(got, ref)
+
+
+@pytest.mark.parametrize("N,r", [(77, 64), (256, 32), (130, 128)])
+def test_router_scores_bit_exact(N, r):
+    B, H, Hkv, D, L = 2, 6, 2, 128, 96
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=N + r)
+    wq, wk, pb = _weights(D, r, L, seed=r)
+    got = router_scores(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L)
+    ref = oracle.router_scores(q, k, wq, wk, pb, L)
+    np.testing.assert_array_equal(got.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,H,Hkv,N,D,K", [
+    (1, 4, 2, 256, 128, 32),
+    (1, 12, 2, 700, 128, 128),
+    (2, 2, 1, 50, 64, 8),
+])
+def test_oracle_topk_bit_exact(dtype, B, H, Hkv, N, D, K):
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=N + K, scale=1.0 / math.sqrt(D))
+    q, k = q.to(dtype), k.to(dtype)
+    got = oracle_topk(q.to(DEV), k.to(DEV), K)
+    ref = oracle.oracle_topk(q, k, K)
+    _assert_same(got, ref)
+
+
+def test_checkpoint_router_matches_reference(golden_dir):
+    """Config 1 with the reference's trained router: the GPU selection equals the
+    reference's own causal top-64 sets on all 6144 rows."""
+    z = np.load(golden_dir / "router_ckpt_c1.npz")
+    q, k, _ = cases.c1_inputs()
+    router = ContentRouter(ContentRouterConfig(head_dim=128, n_heads=12, seq_len=512, proj_dim=64))
+    router.load_state_dict({"q_proj.0.weight": torch.from_numpy(z["wq"]),
+                            "k_proj.0.weight": torch.from_numpy(z["wk"]),
+                            "pos_bias.weight": torch.from_numpy(z["pos_bias"])})
+    router = router.to(DEV)
+    got = router.topk(q.to(DEV), k.to(DEV), 64, causal=True, index_dtype=torch.int32)
+    _assert_same(got, z["ref_sets"].astype(np.int32))
+    logits = router.score(q.to(DEV), k.to(DEV))
+    np.testing.assert_array_equal(logits[:, :, z["logit_rows"]].cpu().numpy(), z["ref_logits"])
+
+
+def test_random_router_matches_reference_unmasked(golden_dir):
+    """ContentRouter.topk without a causal mask (router.py:202-203) on the ragged
+    GQA golden case: same sets as the reference's torch.topk."""
+    z = np.load(golden_dir / "router_random_gqa.npz")
+    q, k, _ = cases.gqa_small_inputs()
+    D = q.shape[-1]
+    r, L, K = int(z["r"]), int(z["seq_len"]), int(z["K"])
+    wq, wk, pb = cases.router_weights(D, r, L, seed=int(z["weight_seed"]))
+    router = ContentRouter(ContentRouterConfig(head_dim=D, n_heads=6, seq_len=L, proj_dim=r))
+    with torch.no_grad():
+        router.q_proj[0].weight.copy_(wq)
+        router.k_proj[0].weight.copy_(wk)
+        router.pos_bias.weight.copy_(pb)
+    router = router.to(DEV)
+    full = router.topk(q.to(DEV), k.to(DEV), K)
+    assert full.dtype == torch.int64
+    _assert_same(full.int(), z["ref_full_sets"].astype(np.int32))
+    causal = router.topk(q.to(DEV), k.to(DEV), K, causal=True)
+    _assert_same(causal.int(), z["ref_sets"].astype(np.int32))
+
+
+def test_all_ties_pick_lowest_indices():
+    """Zero router weights and a constant bias: every score ties, so each row keeps
+    its K lowest eligible keys."""
+    B, H, Hkv, N, D, r, L, K = 1, 2, 1, 150, 64, 64, 150, 32
+    q = torch.randn(B, H, N, D)
+    k = torch.randn(B, Hkv, N, D)
+    wq = torch.zeros(r, D)
+    wk = torch.zeros(r, D)
+    pb = torch.full((2 * L, 1), 0.5)
+    got = router_topk(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K).cpu()
+    for i in (0, 1, 31, 32, 149):
+        m = min(K, i + 1)
+        assert got[0, 0, i].tolist() == list(range(m)) + [-1] * (K - m)
+    _assert_same(got, oracle.router_topk(q, k, wq, wk, pb, L, K))
+
+
+def test_bias_only_ties_many_duplicates():
+    """q = 0: scores are the pos_bias table, which repeats 4 values, so ties at
+    the K-th boundary are everywhere; the tie-break must follow key order."""
+    B, H, Hkv, N, D, r, L, K = 1, 3, 1, 400, 64, 32, 400, 64
+    q = torch.zeros(B, H, N, D)
+    k = torch.randn(B, Hkv, N, D)
+    wq, wk, _ = _weights(D, r, L, seed=9)
+    pb = (torch.arange(2 * L) % 4).float().view(-1, 1)
+    got = router_topk(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K)
+    _assert_same(got, oracle.router_topk(q, k, wq, wk, pb, L, K))
+
+
+def test_nan_scores_rank_first():
+    B, H, Hkv, N, D, K = 1, 1, 1, 64, 64, 4
+    q = torch.randn(B, H, N, D)
+    k = torch.randn(B, Hkv, N, D)
+    k[0, 0, 10, 3] = float("nan")
+    got = oracle_topk(q.to(DEV), k.to(DEV), K)
+    ref = oracle.oracle_topk(q, k, K)
+    _assert_same(got, ref)
+    assert (got[0, 0, 10:] == 10).any(-1).all()
+
+
+def test_full_size_config2_selection():
+    """Config 2 (B=8, 12/2 heads, D=128, N=4096, K=64, bf16, random router):
+    structural properties on every row and exact oracle agreement on a sample of
+    rows from every (b, h)."""
+    B, H, Hkv, N, D, r, K = 8, 12, 2, 4096, 128, 64, 64
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=4096, scale=1.0 / math.sqrt(D))
+    q, k = q.bfloat16(), k.bfloat16()
+    wq, wk, pb = _weights(D, r, N, seed=3)
+    got = router_topk(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
+    pos = torch.arange(N, device=DEV).view(1, 1, N, 1)
+    valid = got >= 0
+    assert torch.equal(valid.sum(-1), torch.clamp(torch.arange(N, device=DEV) + 1, max=K).expand(B, H, N))
+    assert bool((got <= pos).all())
+    big = torch.where(valid, got, torch.full_like(got, 1 << 30))
+    assert bool((big[..., 1:] > big[..., :-1]).all()), "indices must be strictly ascending"
+    gen = np.random.default_rng(0)
+    rows = []
+    for bh in range(B * H):
+        rows += list(bh * N + np.concatenate([[0, 62, 63, 64, N - 1], gen.integers(0, N, 3)]))
+    rows = np.array(rows, dtype=np.int64)
+    ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows)
+    _assert_same(got.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
