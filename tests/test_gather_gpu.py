@@ -1,9 +1,12 @@
 """Parity of the sm_100a gather forward (ossa_topk_attention_fwd via
 ossa_b200.topk_attention) against the oracle.
 
-Tolerances (stated by the task's north star): fp32 within 1e-5 abs/rel of the
-fp64 oracle; bf16 within 2e-3 abs/rel of the oracle evaluated on the same
-bf16 inputs cast up (the bf16 output rounding alone is 2^-9 relative).
+Tolerances: fp32 within 1e-5 abs/rel of the fp64 oracle; bf16 within 2e-3
+abs/rel of the oracle evaluated on the same bf16 inputs cast up.  bf16 cases
+draw q/k/v as N(0,1)/sqrt(D), the workload's distribution, so outputs stay
+below ~0.5 where one bf16 rounding of the output (<= 2^-9 relative) fits the
+2e-3 budget; unscaled N(0,1) values would put outputs near 2-4 where a single
+bf16 rounding step is already 0.0078.
 """
 
 import math
@@ -53,9 +56,10 @@ def _random_indices(B, H, N, K, gen, junk=True):
 @pytest.mark.parametrize("causal", [True, False])
 def test_gather_matches_oracle(dtype, B, H, Hkv, N, D, K, idx_dtype, causal):
     g = cases.gen(B * 1000 + H * 100 + N + D + K)
-    q = torch.randn(B, H, N, D, generator=g)
-    k = torch.randn(B, Hkv, N, D, generator=g)
-    v = torch.randn(B, Hkv, N, D, generator=g)
+    sc = 1.0 if dtype == torch.float32 else 1.0 / math.sqrt(D)
+    q = torch.randn(B, H, N, D, generator=g) * sc
+    k = torch.randn(B, Hkv, N, D, generator=g) * sc
+    v = torch.randn(B, Hkv, N, D, generator=g) * sc
     idx = _random_indices(B, H, N, K, g).to(idx_dtype)
     qd, kd, vd = (t.to(dtype) for t in (q, k, v))
     out = topk_attention(qd.to(DEV), kd.to(DEV), vd.to(DEV), topk_indices=idx.to(DEV), causal=causal)
