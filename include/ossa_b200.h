@@ -108,6 +108,15 @@ OSSA_API int ossa_router_topk(const void* q, const void* k, int dtype,
                      ossa_stream_t stream);
 
 /*
+ * Diagnostic, no counterpart in the reference: reads (synchronously) the
+ * counters block of a router workspace after ossa_router_topk has run on it:
+ * the number of rows the tensor-core selector handed to its exact fallback
+ * (near-ties or non-finite inputs) and the status word (0 = ok; nonzero = a
+ * bounded device-side wait expired and the output is not valid).
+ */
+OSSA_API int ossa_router_status(const void* workspace, int* fallback_rows, int* status);
+
+/*
  * Materialised router logits, (B, H, N, N) fp32, no causal mask.
  * Replaces ContentRouter.score / ContentRouter.forward (ossa/router.py:171-200)
  * with the same fp32 score definition ossa_router_topk selects on.

@@ -30,6 +30,7 @@ EXPORTED = (
     "ossa_topk_attention_fwd",
     "ossa_router_workspace_size",
     "ossa_router_topk",
+    "ossa_router_status",
     "ossa_router_score",
     "ossa_oracle_topk",
 )
@@ -60,6 +61,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ossa_router_workspace_size.restype = sz
     lib.ossa_router_topk.argtypes = [vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, ci, ci, vp, vp, sz, vp]
     lib.ossa_router_topk.restype = ci
+    lib.ossa_router_status.argtypes = [vp, ctypes.POINTER(ci), ctypes.POINTER(ci)]
+    lib.ossa_router_status.restype = ci
     lib.ossa_router_score.argtypes = [vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, vp, vp, sz, vp]
     lib.ossa_router_score.restype = ci
     lib.ossa_oracle_topk.argtypes = [vp, vp, ci, ci, ci, ci, ci, ci, cf, ci, ci, vp, vp]

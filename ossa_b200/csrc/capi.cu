@@ -8,6 +8,7 @@
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string>
 
 namespace ossa {
@@ -53,18 +54,33 @@ int check_heads(int B, int H, int Hkv, int N) {
     return OSSA_OK;
 }
 
+// Workspace: [counters 256 B][q' fp32][k' fp32][tensor-core selection scratch].
+// The counters block (fallback row count, status word) sits at offset 0 so
+// ossa_router_status can find it for any shape.
 struct RouterLayout {
-    size_t qp_off, kp_off, total;
+    size_t qp_off, kp_off, tc_off, total;
 };
+
+constexpr size_t kCountersBytes = 256;
 
 RouterLayout router_layout(int B, int H, int Hkv, int N, int r) {
     RouterLayout l;
     const size_t qp = (size_t)B * H * N * r * sizeof(float);
     const size_t kp = (size_t)B * Hkv * N * r * sizeof(float);
-    l.qp_off = 0;
-    l.kp_off = align_up(qp);
-    l.total = l.kp_off + align_up(kp);
+    l.qp_off = kCountersBytes;
+    l.kp_off = l.qp_off + align_up(qp);
+    l.tc_off = l.kp_off + align_up(kp);
+    l.total = l.tc_off + (r == 64 ? align_up(ossa::router_tc_workspace_bytes(B, H, Hkv, N)) : 0);
     return l;
+}
+
+// The tensor-core selector serves r = 64, K <= 96 and at least one full tile of
+// key rows; OSSA_ROUTER_SELECT=exact forces the CUDA-core exact selector (both
+// produce identical indices; the switch exists to cross-check them).
+bool use_tensor_core_select(int B, int Hkv, int N, int r, int K) {
+    const char* env = getenv("OSSA_ROUTER_SELECT");
+    if (env && env[0] == 'e') return false;
+    return ossa::router_tc_supported(r, K) && (long long)B * Hkv * N >= 128;
 }
 
 bool supported_r(int r) { return r == 16 || r == 32 || r == 64 || r == 128; }
@@ -141,6 +157,16 @@ int ossa_topk_attention_fwd(const void* q, const void* k, const void* v, const v
                        "topk attention launch");
 }
 
+int ossa_router_status(const void* workspace, int* fallback_rows, int* status) {
+    if (!workspace || !aligned16(workspace)) return fail(OSSA_ERR_INVALID, "bad workspace pointer");
+    int h[2] = {0, 0};
+    int st = cuda_status(cudaMemcpy(h, workspace, sizeof(h), cudaMemcpyDeviceToHost), "status read");
+    if (st) return st;
+    if (fallback_rows) *fallback_rows = h[0];
+    if (status) *status = h[1];
+    return OSSA_OK;
+}
+
 size_t ossa_router_workspace_size(int B, int H, int Hkv, int N, int r, int K) {
     (void)K;
     if (B < 0 || H <= 0 || Hkv <= 0 || N < 0 || r <= 0) return 0;
@@ -159,11 +185,21 @@ int ossa_router_topk(const void* q, const void* k, int dtype, const float* wq, c
         return fail(OSSA_ERR_UNSUPPORTED, "top-K selection supports K <= 160 (got K=%d)", K);
     if ((long long)B * H * N == 0) return OSSA_OK;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    st = cuda_status(cudaMemsetAsync(workspace, 0, kCountersBytes, s), "workspace counters reset");
+    if (st) return st;
     float *qp = nullptr, *kp = nullptr;
     st = project_both(q, k, dtype, wq, wk, B, H, Hkv, N, D, r, workspace, s, &qp, &kp);
     if (st) return st;
-    ossa::ScoreTopkArgs a{qp, kp, ossa::kF32, pos_bias, seq_len_cfg, B, H, Hkv, N, r, K,
-                          (float)(1.0 / sqrt((double)r)), causal ? 1 : 0, idx_out};
+    const float scale = (float)(1.0 / sqrt((double)r));
+    if (use_tensor_core_select(B, Hkv, N, r, K)) {
+        const RouterLayout l = router_layout(B, H, Hkv, N, r);
+        ossa::RouterTcArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, N, K, causal ? 1 : 0, scale,
+                             idx_out, static_cast<char*>(workspace) + l.tc_off,
+                             reinterpret_cast<int*>(workspace)};
+        return cuda_status(ossa::launch_router_tc(a, s), "tensor-core router top-K launch");
+    }
+    ossa::ScoreTopkArgs a{qp, kp, ossa::kF32, pos_bias, seq_len_cfg, B, H, Hkv, N, r, K, scale,
+                          causal ? 1 : 0, idx_out};
     return cuda_status(ossa::launch_score_topk(a, s), "router top-K launch");
 }
 

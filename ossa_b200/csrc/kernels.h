@@ -66,3 +66,26 @@ struct ScoreDenseArgs {
 cudaError_t launch_score_dense(const ScoreDenseArgs& a, cudaStream_t stream);
 
 }  // namespace ossa
+
+namespace ossa {
+
+// Tensor-core (tcgen05) router selection, r = 64.  qp32/kp32: canonical fp32
+// projections; ws: router_tc_workspace_bytes of scratch; counters: two ints
+// (rows sent to the exact fallback, status word: 0 = ok, nonzero = a bounded
+// wait expired), zeroed by the caller before the launch.
+struct RouterTcArgs {
+    const float* qp32;
+    const float* kp32;
+    const float* bias;
+    int L;
+    int B, H, Hkv, N, K, causal;
+    float scale;
+    int32_t* out;
+    void* ws;
+    int* counters;
+};
+bool router_tc_supported(int r, int K);
+size_t router_tc_workspace_bytes(int B, int H, int Hkv, int N);
+cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream);
+
+}  // namespace ossa

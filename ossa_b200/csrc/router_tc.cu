@@ -1,0 +1,780 @@
+// Router top-K selection on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces ContentRouter.score + causal mask + torch.topk (ossa/router.py:171-190,
+// ossa/bench/sparse_forward.py:180-202) for proj_dim r = 64 and K <= 64, with the
+// same result as the exact CUDA-core selector: the K best keys by canonical fp32
+// score (fmaf chains, see score_topk.cu), lowest key index first on ties, emitted
+// in ascending key order and -1 padded.
+//
+// Pipeline (one CTA = 128 query rows of one (b, h), one CTA per SM):
+//  1. prep kernels turn the canonical fp32 projections q', k' into fp16 copies
+//     scaled by powers of two (q' per row, k' per (b, kv head)) so every value
+//     sits in [2^12, 2^13) at most, plus per row the epilogue multiplier
+//     m_i = scale * 2^-(e_q + e_k) and an error bound delta_i with
+//     |approx score - canonical score| <= delta_i:
+//        delta_i = scale * 2^-8 * |q'_i| * max_j |k'_j| + 2^-22 * (max|bias| + scale * |q'_i| * max_j |k'_j|)
+//     (fp16 input rounding contributes <= 2^-10 |q'||k'|, fp32 accumulation in the
+//     tensor core and the canonical fmaf chain far less; 2^-8 leaves 4x margin).
+//  2. warp 0 (one thread) streams 128-key tiles of k'16 with TMA (128-byte
+//     swizzle) through a 2-stage ring; warp 1 (one thread) issues
+//     tcgen05.mma.kind::f16 128x128x64 into one of 4 TMEM accumulators;
+//     warps 2-5 (one TMEM lane quadrant each, one query row per thread) drain
+//     a finished accumulator with tcgen05.ld, release it, and score
+//        s = acc * m_i + pos_bias[clamp(i - j + L, 0, 2L - 1)]
+//     (pos_bias staged per warp and tile as four shifted copies so each thread
+//     reads 4 consecutive offsets with one aligned 16-byte load).
+//  3. Streaming selection per row: a candidate list in shared memory and a
+//     threshold theta.  A score enters if s >= theta.  Every 32 columns, rows
+//     whose list might overflow are compacted by their warp: radix-select the
+//     K-th best approximate score T, keep entries with s >= T - 2*delta_i and
+//     set theta to that bound.  Dropped entries have canonical score below
+//     T - delta_i, under the canonical score of K listed entries, so the list
+//     always contains the exact top K.
+//  4. End of row: with T the K-th best approximate score, entries above
+//     T + 2*delta_i are certainly selected, entries below T - 2*delta_i
+//     certainly not; the few in between are rescored with the canonical fp32
+//     formula and the remaining slots filled from them by (score desc, j asc).
+//  5. Rows whose list would overflow (massive near-ties) or whose inputs are
+//     not finite are appended to a list and recomputed afterwards by an exact
+//     warp-per-row selector (exact_rows_kernel).
+//
+// Every wait on an mbarrier is bounded (~1 s); on expiry the kernel records a
+// nonzero status word, lets the other roles finish their bounded waits, waits
+// for its own TMA loads and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "select_warp.cuh"
+#include "sm100.cuh"
+
+namespace ossa {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kR = 64;              // projection dim = MMA K
+constexpr int kTileM = 128;         // query rows per CTA
+constexpr int kTileN = 128;         // keys per MMA tile
+constexpr int kStages = 2;          // k' tile ring
+constexpr int kAccBufs = 4;         // TMEM accumulators (128 columns each)
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kEPL = 5;             // candidate entries per lane in a list
+constexpr int kCap = 32 * kEPL;     // candidate list capacity per row
+constexpr int kBufStride = kCap + 1;  // uint2 entries; odd stride spreads banks
+constexpr int kWinLen = 160;        // bias window entries per copy
+constexpr int kWinCopy = 168;       // copy stride (floats): copies 8 banks apart
+constexpr int kTileBytes = kTileM * kR * 2;
+constexpr uint32_t kTmemCols = kAccBufs * kTileN;
+constexpr int kMaxK = kCap - 64;    // K + 32 insertions + room for near-boundary entries
+
+constexpr size_t kOffA = 0;
+constexpr size_t kOffB = kOffA + kTileBytes;
+constexpr size_t kOffWin = kOffB + (size_t)kStages * kTileBytes;
+constexpr size_t kOffBuf = kOffWin + (size_t)kEpiWarps * 4 * kWinCopy * sizeof(float);
+constexpr size_t kOffBar = kOffBuf + (size_t)kTileM * kBufStride * sizeof(uint2);
+constexpr int kNumBars = 2 * kStages + 1 + 2 * kAccBufs + 1;
+constexpr size_t kOffSlot = kOffBar + kNumBars * sizeof(uint64_t);
+constexpr size_t kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kOffB % 1024 == 0 && kTileBytes % 1024 == 0, "swizzled tiles need 1 KB alignment");
+
+constexpr float kTwoPowM22 = 2.384185791015625e-07f;  // 2^-22
+
+// ---------------------------------------------------------------- prep kernels
+
+// stats[3*bg + 0] = max |k'| bits, [3*bg + 1] = max_j |k'_j|_2 bits, [3*bg + 2] = non-finite flag.
+__global__ void kstats_kernel(const float* __restrict__ kp, int N, uint32_t* __restrict__ stats) {
+    const int bg = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    float mabs = 0.f, ss = 0.f;
+    bool bad = false;
+    if (j < N) {
+        const float4* r = reinterpret_cast<const float4*>(kp + ((size_t)bg * N + j) * kR);
+#pragma unroll
+        for (int c = 0; c < kR / 4; ++c) {
+            const float4 x = __ldg(r + c);
+            mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+            ss = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, ss))));
+            bad |= !(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w));
+        }
+    }
+    const float nrm = sqrtf(ss) * 1.0001f;
+    uint32_t m1 = __reduce_max_sync(kFull, __float_as_uint(mabs));
+    uint32_t m2 = __reduce_max_sync(kFull, __float_as_uint(bad ? 0.f : nrm));
+    unsigned b = __reduce_or_sync(kFull, bad ? 1u : 0u);
+    if ((threadIdx.x & 31) == 0) {
+        atomicMax(stats + 3 * bg + 0, m1);
+        atomicMax(stats + 3 * bg + 1, m2);
+        if (b) atomicOr(stats + 3 * bg + 2, 1u);
+    }
+}
+
+// gstats[0] = max |bias| bits, gstats[1] = non-finite flag.
+__global__ void bias_stats_kernel(const float* __restrict__ bias, int n, uint32_t* __restrict__ gstats) {
+    float m = 0.f;
+    bool bad = false;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x) {
+        const float x = __ldg(bias + t);
+        bad |= !isfinite(x);
+        m = fmaxf(m, fabsf(x));
+    }
+    const uint32_t mm = __reduce_max_sync(kFull, __float_as_uint(m));
+    const unsigned b = __reduce_or_sync(kFull, bad ? 1u : 0u);
+    if ((threadIdx.x & 31) == 0) {
+        atomicMax(gstats + 0, mm);
+        if (b) atomicOr(gstats + 1, 1u);
+    }
+}
+
+// Power-of-two exponent e with max_abs * 2^e in [2^12, 2^13).
+__device__ __forceinline__ int scale_exponent(float max_abs) {
+    int ex = 0;
+    frexpf(max_abs, &ex);
+    return max_abs > 0.f ? 13 - ex : 0;
+}
+
+__global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict__ k16, int N,
+                                const uint32_t* __restrict__ stats) {
+    const int bg = blockIdx.y;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;  // one float4 per thread
+    if (t >= N * (kR / 4)) return;
+    const int e = scale_exponent(__uint_as_float(stats[3 * bg + 0]));
+    const size_t off = (size_t)bg * N * kR + (size_t)t * 4;
+    const float4 x = __ldg(reinterpret_cast<const float4*>(kp + off));
+    __half2 lo = __floats2half2_rn(ldexpf(x.x, e), ldexpf(x.y, e));
+    __half2 hi = __floats2half2_rn(ldexpf(x.z, e), ldexpf(x.w, e));
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(k16 + off) = pk;
+}
+
+// One thread per query row: scaled fp16 row, epilogue multiplier and error bound.
+__global__ void qprep_kernel(const float* __restrict__ qp, __half* __restrict__ q16, float2* __restrict__ rowinfo,
+                             long long rows, int H, int Hkv, int N, float scale,
+                             const uint32_t* __restrict__ stats, const uint32_t* __restrict__ gstats) {
+    const long long row = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= rows) return;
+    const long long bh = row / N;
+    const int b = (int)(bh / H);
+    const int h = (int)(bh - (long long)b * H);
+    const int bg = b * Hkv + h / (H / Hkv);
+    const float4* r = reinterpret_cast<const float4*>(qp + row * kR);
+    float4 x[kR / 4];
+    float mabs = 0.f, ss = 0.f;
+    bool bad = false;
+#pragma unroll
+    for (int c = 0; c < kR / 4; ++c) {
+        x[c] = __ldg(r + c);
+        mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(x[c].x), fabsf(x[c].y)), fmaxf(fabsf(x[c].z), fabsf(x[c].w))));
+        ss = fmaf(x[c].x, x[c].x, fmaf(x[c].y, x[c].y, fmaf(x[c].z, x[c].z, fmaf(x[c].w, x[c].w, ss))));
+        bad |= !(isfinite(x[c].x) && isfinite(x[c].y) && isfinite(x[c].z) && isfinite(x[c].w));
+    }
+    const int eq = scale_exponent(mabs);
+    const int ek = scale_exponent(__uint_as_float(stats[3 * bg + 0]));
+    const float kmax = __uint_as_float(stats[3 * bg + 1]);
+    const float bmax = __uint_as_float(gstats[0]);
+    bad |= stats[3 * bg + 2] != 0u || gstats[1] != 0u;
+    uint4* o = reinterpret_cast<uint4*>(q16 + row * kR);
+#pragma unroll
+    for (int c = 0; c < kR / 8; ++c) {
+        const float4 a = x[2 * c], bq = x[2 * c + 1];
+        __half2 h0 = __floats2half2_rn(ldexpf(a.x, eq), ldexpf(a.y, eq));
+        __half2 h1 = __floats2half2_rn(ldexpf(a.z, eq), ldexpf(a.w, eq));
+        __half2 h2 = __floats2half2_rn(ldexpf(bq.x, eq), ldexpf(bq.y, eq));
+        __half2 h3 = __floats2half2_rn(ldexpf(bq.z, eq), ldexpf(bq.w, eq));
+        uint4 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&h0);
+        pk.y = *reinterpret_cast<uint32_t*>(&h1);
+        pk.z = *reinterpret_cast<uint32_t*>(&h2);
+        pk.w = *reinterpret_cast<uint32_t*>(&h3);
+        o[c] = pk;
+    }
+    const float m = ldexpf(scale, -(eq + ek));
+    const float qn = sqrtf(ss) * 1.0001f;
+    const float cross = scale * qn * kmax;
+    const float delta = scale * 0.00390625f * qn * kmax + kTwoPowM22 * (bmax + cross) + 1e-30f;
+    if (bad || !isfinite(delta) || !(m >= 1.1754944e-38f) || !isfinite(m)) {
+        rowinfo[row] = make_float2(__int_as_float(0x7fc00000), 0.f);  // NaN multiplier: exact fallback
+    } else {
+        rowinfo[row] = make_float2(m, delta);
+    }
+}
+
+// ------------------------------------------------------------ selection kernel
+
+struct TcParams {
+    const float2* rowinfo;
+    const float* bias;
+    const float* qp32;
+    const float* kp32;
+    int32_t* out;
+    int* fb_count;
+    int32_t* fb_list;
+    int* status;
+    int L, H, Hkv, N, K, causal, nqb;
+    float scale;
+};
+
+// Canonical fp32 score of (query row qrow, key row krow) at offset i - j.
+__device__ __forceinline__ float canonical_score(const float* __restrict__ qrow, const float* __restrict__ krow,
+                                                 const float* __restrict__ bias, int L, int i, int j,
+                                                 float scale) {
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < kR; c += 4) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(qrow + c));
+        const float4 bk = __ldg(reinterpret_cast<const float4*>(krow + c));
+        acc = fmaf(a.x, bk.x, acc);
+        acc = fmaf(a.y, bk.y, acc);
+        acc = fmaf(a.z, bk.z, acc);
+        acc = fmaf(a.w, bk.w, acc);
+    }
+    int bi = i - j + L;
+    bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
+    return __fadd_rn(__fmul_rn(acc, scale), __ldg(bias + bi));
+}
+
+__device__ __forceinline__ void load_entries(const uint2* rb, int cnt, int lane, float (&s)[kEPL],
+                                             uint32_t (&j)[kEPL], bool (&val)[kEPL]) {
+#pragma unroll
+    for (int e = 0; e < kEPL; ++e) {
+        const int p = lane + 32 * e;
+        val[e] = p < cnt;
+        const uint2 t = val[e] ? rb[p] : make_uint2(0u, 0u);
+        s[e] = __uint_as_float(t.x);
+        j[e] = t.y;
+    }
+}
+
+// Rewrites the list with the kept entries, in order; returns their count.
+__device__ __forceinline__ int store_kept(uint2* rb, int lane, const float (&s)[kEPL], const uint32_t (&j)[kEPL],
+                                          const bool (&keep)[kEPL]) {
+    const unsigned lt = lanemask_lt();
+    int outpos = 0;
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < kEPL; ++e) {
+        const unsigned kb = __ballot_sync(kFull, keep[e]);
+        if (keep[e]) rb[outpos + __popc(kb & lt)] = make_uint2(__float_as_uint(s[e]), j[e]);
+        outpos += __popc(kb);
+    }
+    __syncwarp();
+    return outpos;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t* sA = smem + kOffA;
+    uint8_t* sB = smem + kOffB;
+    float* win = reinterpret_cast<float*>(smem + kOffWin);
+    uint2* buf = reinterpret_cast<uint2*>(smem + kOffBuf);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + kStages;
+    uint64_t* afull = bars + 2 * kStages;
+    uint64_t* tfull = afull + 1;
+    uint64_t* tempty = tfull + kAccBufs;
+    uint64_t* mdone = tempty + kAccBufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffSlot);
+
+    const int N = p.N, H = p.H, Hkv = p.Hkv;
+    const int BH = gridDim.x / p.nqb;
+    const int order = blockIdx.x / BH;
+    const int bh = blockIdx.x - order * BH;
+    const int qb = p.causal ? (p.nqb - 1 - order) : order;
+    const int b = bh / H;
+    const int h = bh - b * H;
+    const int g = h / (H / Hkv);
+    const int i0 = qb * kTileM;
+    const int jend = p.causal ? min(N, i0 + kTileM) : N;
+    const int T = (jend + kTileN - 1) / kTileN;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        mbar_init(afull, 1);
+        for (int s = 0; s < kAccBufs; ++s) {
+            mbar_init(tfull + s, 1);
+            mbar_init(tempty + s, kEpiWarps);
+        }
+        mbar_init(mdone, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            bool ok = true;
+            mbar_arrive_expect_tx(afull, kTileBytes);
+            tma_load_2d(sA, &tmA, afull, 0, bh * N + i0);
+            const int krow0 = (b * Hkv + g) * N;
+            int issued = 0;
+            for (int t = 0; t < T; ++t) {
+                const int s = t % kStages;
+                if (t >= kStages) ok = mbar_wait(empty + s, ((t / kStages) - 1) & 1);
+                if (!ok) break;
+                mbar_arrive_expect_tx(full + s, kTileBytes);
+                tma_load_2d(sB + (size_t)s * kTileBytes, &tmB, full + s, 0, krow0 + t * kTileN);
+                issued = t + 1;
+            }
+            // the loads of the last stages are never waited on by a refill: make
+            // sure they have landed before the CTA can retire
+            for (int t = max(0, issued - kStages); t < issued; ++t) mbar_wait(full + t % kStages, (t / kStages) & 1);
+            mbar_wait(afull, 0);
+            if (!ok) atomicOr(p.status, 1);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16(0u, kTileM, kTileN);
+            const uint64_t adesc = umma_desc_sw128(sA);
+            bool ok = mbar_wait(afull, 0);
+            for (int t = 0; t < T && ok; ++t) {
+                const int s = t % kStages;
+                const int ab = t % kAccBufs;
+                ok = mbar_wait(full + s, (t / kStages) & 1);
+                if (ok && t >= kAccBufs) ok = mbar_wait(tempty + ab, ((t / kAccBufs) - 1) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                const uint64_t bdesc = umma_desc_sw128(sB + (size_t)s * kTileBytes);
+                const uint32_t d = tmem + (uint32_t)(ab * kTileN);
+#pragma unroll
+                for (int k = 0; k < kR / 16; ++k)
+                    mma_f16(d, adesc + 2u * k, bdesc + 2u * k, idesc, k > 0 ? 1u : 0u);
+                mma_commit(empty + s);
+                mma_commit(tfull + ab);
+            }
+            mma_commit(mdone);  // completes once every MMA issued above has finished
+            mbar_wait(mdone, 0);
+            if (!ok) atomicOr(p.status, 2);
+        }
+    } else {
+        // ------------------------------------------------ epilogue: scoring + selection
+        const int ew = warp - 2;
+        const int qd = warp & 3;  // TMEM lane quadrant this warp may access
+        const int r0 = qd * 32;
+        const int row = r0 + lane;
+        const int i = i0 + row;
+        const int K = p.K;
+        const int L = p.L;
+        float m = 0.f, delta = 0.f;
+        bool fb = i >= N;  // inactive rows never insert and are skipped at the end
+        if (i < N) {
+            const float2 ri = p.rowinfo[(size_t)bh * N + i];
+            m = ri.x;
+            delta = ri.y;
+            if (!(m == m)) fb = true;
+        }
+        // a NaN threshold admits nothing (every comparison with NaN is false)
+        float theta = fb ? __int_as_float(0x7fc00000) : -INFINITY;
+        int cnt = 0;
+        uint2* rowbuf = buf + (size_t)row * kBufStride;
+        float* wcp = win + ew * 4 * kWinCopy;
+        const int s4 = lane & 3;
+        const float* mycopy = wcp + s4 * kWinCopy + (lane - s4) + 124;
+        bool ok = true;
+
+        for (int t = 0; t < T; ++t) {
+            const int j0 = t * kTileN;
+            // pos_bias window of this warp's rows x the tile's keys: copy s holds
+            // w[y + s], w[x] = bias[clamp(i0 + r0 - j0 - 127 + x + L)]
+            const int obase = i0 + r0 - j0 - (kTileN - 1) + L;
+            for (int y = lane; y < kWinLen; y += 32) {
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    int bi = obase + y + s;
+                    bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
+                    wcp[s * kWinCopy + y] = __ldg(p.bias + bi);
+                }
+            }
+            const int ab = t % kAccBufs;
+            const bool got = __all_sync(kFull, mbar_wait(tfull + ab, (t / kAccBufs) & 1));
+            if (!got) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t v[4][32];
+            const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN);
+            tmem_ld32(taddr + 0, v[0]);
+            tmem_ld32(taddr + 32, v[1]);
+            tmem_ld32(taddr + 64, v[2]);
+            tmem_ld32(taddr + 96, v[3]);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty + ab);
+
+            const bool full_tile = (j0 + kTileN <= N) && (!p.causal || j0 + kTileN - 1 <= i0 + r0);
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int c = ch * 32 + q * 4;  // column of v[ch][4q]
+                    const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
+                    const float sc[4] = {fmaf(__uint_as_float(v[ch][4 * q + 0]), m, bw.w),
+                                         fmaf(__uint_as_float(v[ch][4 * q + 1]), m, bw.z),
+                                         fmaf(__uint_as_float(v[ch][4 * q + 2]), m, bw.y),
+                                         fmaf(__uint_as_float(v[ch][4 * q + 3]), m, bw.x)};
+#pragma unroll
+                    for (int d = 0; d < 4; ++d) {
+                        const int jj = j0 + c + d;
+                        const bool valid = full_tile || (jj < N && (!p.causal || jj <= i));
+                        if (valid && sc[d] >= theta) {
+                            rowbuf[cnt] = make_uint2(__float_as_uint(sc[d]), (uint32_t)jj);
+                            ++cnt;
+                        }
+                    }
+                }
+                // lists that could overflow within the next 32 columns are compacted now
+                unsigned need = __ballot_sync(kFull, cnt > kCap - 32);
+                while (need) {
+                    const int src = __ffs(need) - 1;
+                    need &= need - 1;
+                    const int scnt = __shfl_sync(kFull, cnt, src);
+                    const float sdelta = __shfl_sync(kFull, delta, src);
+                    uint2* sb = buf + (size_t)(r0 + src) * kBufStride;
+                    float es[kEPL];
+                    uint32_t ej[kEPL], ek[kEPL];
+                    bool ev[kEPL], keep[kEPL];
+                    load_entries(sb, scnt, lane, es, ej, ev);
+#pragma unroll
+                    for (int e = 0; e < kEPL; ++e) ek[e] = order_key(es[e]);
+                    uint32_t Tk;
+                    int ties;
+                    warp_kth_key<kEPL>(ek, ev, K, Tk, ties);
+                    const float Tf = key_to_float(Tk);
+                    const float thr = Tf - (2.f * sdelta + fabsf(Tf) * kTwoPowM22);
+#pragma unroll
+                    for (int e = 0; e < kEPL; ++e) keep[e] = ev[e] && es[e] >= thr;
+                    const int nc = store_kept(sb, lane, es, ej, keep);
+                    if (lane == src) {
+                        if (nc > kCap - 32) {  // massive near-ties: exact fallback for this row
+                            fb = true;
+                            theta = __int_as_float(0x7fc00000);
+                            cnt = 0;
+                        } else {
+                            theta = thr;
+                            cnt = nc;
+                        }
+                    }
+                }
+            }
+            __syncwarp();  // window copies are rewritten for the next tile
+        }
+        if (!ok) atomicOr(p.status, 4);
+
+        // ---------------------------------------------- per-row final selection
+        const float scale = p.scale;
+        for (int src = 0; src < 32 && ok; ++src) {
+            const int ri = i0 + r0 + src;
+            if (ri >= N) break;
+            const bool sfb = __shfl_sync(kFull, fb ? 1 : 0, src) != 0;
+            const int scnt = __shfl_sync(kFull, cnt, src);
+            const float sdelta = __shfl_sync(kFull, delta, src);
+            const size_t orow_id = (size_t)bh * N + ri;
+            int32_t* orow = p.out + orow_id * K;
+            if (sfb) {
+                if (lane == 0) {
+                    const int pos = atomicAdd(p.fb_count, 1);
+                    p.fb_list[pos] = (int32_t)orow_id;
+                }
+                continue;
+            }
+            uint2* sb = buf + (size_t)(r0 + src) * kBufStride;
+            float es[kEPL];
+            uint32_t ej[kEPL];
+            bool ev[kEPL], keep[kEPL];
+            load_entries(sb, scnt, lane, es, ej, ev);
+            if (scnt <= K) {
+#pragma unroll
+                for (int e = 0; e < kEPL; ++e) keep[e] = ev[e];
+            } else {
+                uint32_t ek[kEPL];
+#pragma unroll
+                for (int e = 0; e < kEPL; ++e) ek[e] = order_key(es[e]);
+                uint32_t Tk;
+                int ties;
+                warp_kth_key<kEPL>(ek, ev, K, Tk, ties);
+                const float Tf = key_to_float(Tk);
+                const float m2 = 2.f * sdelta + fabsf(Tf) * kTwoPowM22;
+                bool in[kEPL], band[kEPL];
+                unsigned n_in = 0, n_band = 0;
+#pragma unroll
+                for (int e = 0; e < kEPL; ++e) {
+                    in[e] = ev[e] && es[e] > Tf + m2;
+                    band[e] = ev[e] && !in[e] && es[e] >= Tf - m2;
+                    n_in += in[e] ? 1u : 0u;
+                    n_band += band[e] ? 1u : 0u;
+                }
+                n_in = __reduce_add_sync(kFull, n_in);
+                n_band = __reduce_add_sync(kFull, n_band);
+                const int need = K - (int)n_in;
+                if ((int)n_band == need) {
+#pragma unroll
+                    for (int e = 0; e < kEPL; ++e) keep[e] = in[e] || band[e];
+                } else {
+                    // boundary candidates: canonical scores decide
+                    const float* qrow = p.qp32 + orow_id * kR;
+                    const float* kbase = p.kp32 + (size_t)(b * Hkv + g) * N * kR;
+                    uint32_t xk[kEPL];
+#pragma unroll
+                    for (int e = 0; e < kEPL; ++e) {
+                        xk[e] = 0u;
+                        if (band[e]) {
+                            const int jj = (int)ej[e];
+                            xk[e] = order_key(canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, ri, jj,
+                                                              scale));
+                        }
+                    }
+                    bool bk[kEPL];
+                    warp_topk_mask<kEPL>(xk, band, need, bk);
+#pragma unroll
+                    for (int e = 0; e < kEPL; ++e) keep[e] = in[e] || bk[e];
+                }
+            }
+            const unsigned lt = lanemask_lt();
+            int outpos = 0;
+#pragma unroll
+            for (int e = 0; e < kEPL; ++e) {
+                const unsigned kb = __ballot_sync(kFull, keep[e]);
+                if (keep[e]) orow[outpos + __popc(kb & lt)] = (int32_t)ej[e];
+                outpos += __popc(kb);
+            }
+            for (int q = outpos + lane; q < K; q += 32) orow[q] = -1;
+            __syncwarp();
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// --------------------------------------------------- exact fallback for listed rows
+
+// One warp per listed row: canonical scores on CUDA cores, streaming selection
+// with a per-warp candidate list (the same rule as the exact CTA selector).
+template <int EPL>
+__global__ void __launch_bounds__(256)
+exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, const float* __restrict__ bias,
+                  int L, int H, int Hkv, int N, int K, float scale, int causal, const int* __restrict__ fb_count,
+                  const int32_t* __restrict__ fb_list, int32_t* __restrict__ out) {
+    constexpr int CAP = 32 * EPL;
+    __shared__ uint2 sbuf[8][CAP];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = lanemask_lt();
+    const int total = *reinterpret_cast<const volatile int*>(fb_count);
+    uint2* wb = sbuf[warp];
+    for (int idx = blockIdx.x * 8 + warp; idx < total; idx += gridDim.x * 8) {
+        const long long row = fb_list[idx];
+        const long long bh = row / N;
+        const int i = (int)(row - bh * N);
+        const int b = (int)(bh / H);
+        const int h = (int)(bh - (long long)b * H);
+        const int g = h / (H / Hkv);
+        const float* qrow = qp + row * kR;
+        const float* kbase = kp + (size_t)(b * Hkv + g) * N * kR;
+        const int n = causal ? i + 1 : N;
+        uint32_t theta = 0u;
+        int cnt = 0;
+        for (int j0 = 0; j0 < n; j0 += 32) {
+            const int j = j0 + lane;
+            uint32_t key = 0u;
+            const bool valid = j < n;
+            if (valid) key = order_key(canonical_score(qrow, kbase + (size_t)j * kR, bias, L, i, j, scale));
+            const bool adm = valid && key > theta;
+            const unsigned bal = __ballot_sync(kFull, adm);
+            if (adm) wb[cnt + __popc(bal & lt)] = make_uint2(key, (uint32_t)j);
+            cnt += __popc(bal);
+            __syncwarp();
+            if (cnt > CAP - 32) {
+                uint32_t u[EPL], jv[EPL];
+                bool val[EPL], keep[EPL];
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) {
+                    const int q = lane + 32 * e;
+                    val[e] = q < cnt;
+                    const uint2 t = val[e] ? wb[q] : make_uint2(0u, 0u);
+                    u[e] = t.x;
+                    jv[e] = t.y;
+                }
+                uint32_t Tk;
+                warp_topk_mask<EPL>(u, val, K, keep, &Tk);
+                __syncwarp();
+                int outpos = 0;
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) {
+                    const unsigned kb = __ballot_sync(kFull, keep[e]);
+                    if (keep[e]) wb[outpos + __popc(kb & lt)] = make_uint2(u[e], jv[e]);
+                    outpos += __popc(kb);
+                }
+                __syncwarp();
+                cnt = outpos;
+                theta = Tk;
+            }
+        }
+        uint32_t u[EPL], jv[EPL];
+        bool val[EPL], keep[EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+            const int q = lane + 32 * e;
+            val[e] = q < cnt;
+            const uint2 t = val[e] ? wb[q] : make_uint2(0u, 0u);
+            u[e] = t.x;
+            jv[e] = t.y;
+        }
+        if (cnt > K) {
+            warp_topk_mask<EPL>(u, val, K, keep);
+        } else {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) keep[e] = val[e];
+        }
+        int32_t* orow = out + row * K;
+        int outpos = 0;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+            const unsigned kb = __ballot_sync(kFull, keep[e]);
+            if (keep[e]) orow[outpos + __popc(kb & lt)] = (int32_t)jv[e];
+            outpos += __popc(kb);
+        }
+        for (int q = outpos + lane; q < K; q += 32) orow[q] = -1;
+        __syncwarp();
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+// (rows x 64) fp16 row-major matrix -> 128 x 64 boxes with the 128-byte swizzle.
+bool make_row_map(CUtensorMap* map, const void* base, unsigned long long rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)kR, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kR * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kR, (cuuint32_t)kTileM};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t record(cudaError_t e) {
+    if (e == cudaSuccess) note_launch();
+    return e;
+}
+
+}  // namespace
+
+bool router_tc_supported(int r, int K) { return r == kR && K >= 1 && K <= kMaxK; }
+
+size_t router_tc_workspace_bytes(int B, int H, int Hkv, int N) {
+    auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+    const size_t rq = (size_t)B * H * N, rk = (size_t)B * Hkv * N;
+    return al(rq * kR * 2) + al(rk * kR * 2) + al(rq * sizeof(float2)) + al((3 * (size_t)B * Hkv + 2) * 4) +
+           al(rq * 4);
+}
+
+cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
+    auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+    const size_t rq = (size_t)a.B * a.H * a.N, rk = (size_t)a.B * a.Hkv * a.N;
+    char* w = static_cast<char*>(a.ws);
+    __half* q16 = reinterpret_cast<__half*>(w);
+    w += al(rq * kR * 2);
+    __half* k16 = reinterpret_cast<__half*>(w);
+    w += al(rk * kR * 2);
+    float2* rowinfo = reinterpret_cast<float2*>(w);
+    w += al(rq * sizeof(float2));
+    uint32_t* stats = reinterpret_cast<uint32_t*>(w);
+    uint32_t* gstats = stats + 3 * (size_t)a.B * a.Hkv;
+    w += al((3 * (size_t)a.B * a.Hkv + 2) * 4);
+    int32_t* fb_list = reinterpret_cast<int32_t*>(w);
+    int* counters = a.counters;  // [0] fallback rows, [1] status
+
+    cudaError_t e = cudaMemsetAsync(stats, 0, (3 * (size_t)a.B * a.Hkv + 2) * 4, stream);
+    if (e != cudaSuccess) return e;
+
+    const int BG = a.B * a.Hkv;
+    {
+        dim3 grid((a.N + 255) / 256, BG);
+        kstats_kernel<<<grid, 256, 0, stream>>>(a.kp32, a.N, stats);
+        if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        bias_stats_kernel<<<8, 256, 0, stream>>>(a.bias, 2 * a.L, gstats);
+        if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        dim3 g2((a.N * (kR / 4) + 255) / 256, BG);
+        kconvert_kernel<<<g2, 256, 0, stream>>>(a.kp32, k16, a.N, stats);
+        if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        qprep_kernel<<<(unsigned)((rq + 127) / 128), 128, 0, stream>>>(a.qp32, q16, rowinfo, (long long)rq, a.H,
+                                                                      a.Hkv, a.N, a.scale, stats, gstats);
+        if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+    }
+    CUtensorMap tmA, tmB;
+    if (!make_row_map(&tmA, q16, rq) || !make_row_map(&tmB, k16, rk)) return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    TcParams prm;
+    prm.rowinfo = rowinfo;
+    prm.bias = a.bias;
+    prm.qp32 = a.qp32;
+    prm.kp32 = a.kp32;
+    prm.out = a.out;
+    prm.fb_count = counters;
+    prm.fb_list = fb_list;
+    prm.status = counters + 1;
+    prm.L = a.L;
+    prm.H = a.H;
+    prm.Hkv = a.Hkv;
+    prm.N = a.N;
+    prm.K = a.K;
+    prm.causal = a.causal;
+    prm.nqb = (a.N + kTileM - 1) / kTileM;
+    prm.scale = a.scale;
+    const long long nblk = (long long)prm.nqb * a.B * a.H;
+    router_tc_kernel<<<(unsigned)nblk, kThreads, kSmemBytes, stream>>>(tmA, tmB, prm);
+    if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+    exact_rows_kernel<4><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, a.K, a.scale,
+                                                      a.causal, counters, fb_list, a.out);
+    return record(cudaGetLastError());
+}
+
+}  // namespace ossa

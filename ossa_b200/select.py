@@ -15,6 +15,7 @@ returns on fp32 scores with ties broken toward the lower key index.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -53,6 +54,17 @@ def router_topk(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Te
     heads).  wq, wk: (r, D) projection weights; pos_bias: (2*seq_len, 1) or
     (2*seq_len,).  Scores and selection are fp32.
     """
+    return _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, causal=causal)[0]
+
+
+def router_topk_with_status(q, k, wq, wk, pos_bias, seq_len: int, top_k: int, *, causal: bool = True):
+    """router_topk plus (rows sent to the exact fallback, device status word),
+    read back synchronously; a nonzero status means a bounded device wait
+    expired and the indices are not valid."""
+    return _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, causal=causal, with_status=True)
+
+
+def _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, *, causal=True, with_status=False):
     B, H, Hkv, N, D = _check_qk(q, k)
     dev = _lib.require_cuda(q, k, wq, wk, pos_bias)
     r = wq.shape[0]
@@ -64,7 +76,7 @@ def router_topk(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Te
         raise ValueError(f"top_k must be >= 0, got {top_k}")
     out = torch.empty((B, H, N, top_k), dtype=torch.int32, device=dev)
     if out.numel() == 0:
-        return out
+        return out, 0, 0
     dt = _common_dtype(q, k)
     qc = _as_kernel_input(q, dt)
     kc = _as_kernel_input(k, dt)
@@ -80,7 +92,13 @@ def router_topk(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Te
                                 int(top_k), 1 if causal else 0, out.data_ptr(), ws.data_ptr(),
                                 ws_bytes, _lib.stream_ptr(dev))
     _lib.check(st)
-    return out
+    if not with_status:
+        return out, None, None
+    fb = ctypes.c_int(0)
+    status = ctypes.c_int(0)
+    with torch.cuda.device(dev):
+        _lib.check(L.ossa_router_status(ws.data_ptr(), ctypes.byref(fb), ctypes.byref(status)))
+    return out, fb.value, status.value
 
 
 def router_scores(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,

@@ -14,6 +14,7 @@ import torch
 import cases
 import oracle
 from ossa_b200 import ContentRouter, ContentRouterConfig, oracle_topk, router_scores, router_topk
+from ossa_b200.select import router_topk_with_status
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -160,7 +161,8 @@ def test_full_size_config2_selection():
     q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=4096, scale=1.0 / math.sqrt(D))
     q, k = q.bfloat16(), k.bfloat16()
     wq, wk, pb = _weights(D, r, N, seed=3)
-    got = router_topk(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
+    got, fb, status = router_topk_with_status(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
+    assert status == 0
     pos = torch.arange(N, device=DEV).view(1, 1, N, 1)
     valid = got >= 0
     assert torch.equal(valid.sum(-1), torch.clamp(torch.arange(N, device=DEV) + 1, max=K).expand(B, H, N))
@@ -175,3 +177,71 @@ def test_full_size_config2_selection():
     rows = np.array(rows, dtype=np.int64)
     ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows)
     _assert_same(got.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
+
+
+def _run_both(q, k, wq, wk, pb, L, K, causal=True):
+    """Tensor-core selector (default for r = 64, K <= 96) and, forced through
+    OSSA_ROUTER_SELECT=exact, the CUDA-core exact selector on the same inputs."""
+    import os
+
+    args = (q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K)
+    tc, fb, status = router_topk_with_status(*args, causal=causal)
+    os.environ["OSSA_ROUTER_SELECT"] = "exact"
+    try:
+        ex = router_topk(*args, causal=causal)
+    finally:
+        del os.environ["OSSA_ROUTER_SELECT"]
+    return tc, ex, fb, status
+
+
+@pytest.mark.parametrize("N,K,causal", [(2048, 64, True), (777, 32, True), (640, 64, False), (300, 96, True)])
+def test_tensor_core_and_exact_selectors_agree(N, K, causal):
+    B, H, Hkv, D, r = 2, 12, 2, 128, 64
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=N + K, scale=1.0 / math.sqrt(D))
+    q, k = q.bfloat16(), k.bfloat16()
+    wq, wk, pb = _weights(D, r, N, seed=K)
+    tc, ex, fb, status = _run_both(q, k, wq, wk, pb, N, K, causal)
+    assert status == 0
+    assert torch.equal(tc, ex), f"{(tc != ex).any(-1).sum().item()} rows differ"
+    rows = np.arange(0, B * H * N, 97, dtype=np.int64)
+    ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows, causal=causal)
+    _assert_same(tc.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
+
+
+def test_tensor_core_selector_content_dominated_scores():
+    """Trained-router-like regime: content scores dominate the position bias, so
+    the boundary band is decided by the q'.k' products the tensor cores compute."""
+    B, H, Hkv, N, D, r, K = 1, 12, 2, 1024, 128, 64, 64
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=77)
+    wq, wk, pb = _weights(D, r, N, seed=8, bias_scale=0.01)
+    wq, wk = wq * 4, wk * 4
+    tc, fb, status = router_topk_with_status(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
+    assert status == 0
+    _assert_same(tc, oracle.router_topk(q, k, wq, wk, pb, N, K))
+
+
+def test_tensor_core_selector_ties_go_to_exact_fallback():
+    """All scores tie: every row's candidate list overflows and is recomputed by
+    the exact warp-per-row selector; the result is still the lowest indices."""
+    B, H, Hkv, N, D, r, L, K = 1, 4, 2, 256, 64, 64, 256, 64
+    q = torch.randn(B, H, N, D)
+    k = torch.randn(B, Hkv, N, D)
+    wq = torch.zeros(r, D)
+    wk = torch.zeros(r, D)
+    pb = torch.full((2 * L, 1), 0.25)
+    got, fb, status = router_topk_with_status(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K)
+    assert status == 0 and fb > 0
+    _assert_same(got, oracle.router_topk(q, k, wq, wk, pb, L, K))
+
+
+def test_tensor_core_selector_non_finite_rows():
+    """A key with an infinite component makes every score of that (b, kv head)
+    non-finite: those rows go to the exact selector, which ranks NaN first as
+    torch.topk does."""
+    B, H, Hkv, N, D, r, K = 1, 4, 2, 200, 64, 64, 16
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=5)
+    k[0, 1, 50, 7] = float("inf")
+    wq, wk, pb = _weights(D, r, N, seed=6)
+    got, fb, status = router_topk_with_status(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
+    assert status == 0 and fb >= 2 * N
+    _assert_same(got, oracle.router_topk(q, k, wq, wk, pb, N, K))
