@@ -69,7 +69,8 @@ constexpr int kWinLen = 160;        // bias window entries per copy
 constexpr int kWinCopy = 168;       // copy stride (floats): copies 8 banks apart
 constexpr int kTileBytes = kTileM * kR * 2;
 constexpr uint32_t kTmemCols = kAccBufs * kTileN;
-constexpr int kMaxK = kCap - 64;    // K + 32 insertions + room for near-boundary entries
+constexpr int kMaxK = 64;           // selection bound uses the K-th of 128 column-class maxima
+constexpr int kMaxBand = 16;        // boundary candidates rescored per row before falling back
 
 constexpr size_t kOffA = 0;
 constexpr size_t kOffB = kOffA + kTileBytes;
@@ -267,6 +268,50 @@ __device__ __forceinline__ int store_kept(uint2* rb, int lane, const float (&s)[
     return outpos;
 }
 
+// Count of x[q] >= v.
+template <int NX>
+__device__ __forceinline__ int count_ge(const float (&x)[NX], float v) {
+    int c = 0;
+#pragma unroll
+    for (int q = 0; q < NX; ++q) c += x[q] >= v ? 1 : 0;
+    return c;
+}
+
+// A lower bound on the K-th largest of x (padding entries are -inf): the result
+// v satisfies count(x >= v) >= K, found by bisection between the smallest and
+// largest finite values; -inf if fewer than K entries are finite.
+template <int NX>
+__device__ __forceinline__ float kth_lower_bound(const float (&x)[NX], int K, int iters) {
+    float lo = INFINITY, hi = -INFINITY;
+    int nfin = 0;
+#pragma unroll
+    for (int q = 0; q < NX; ++q) {
+        const bool f = x[q] > -INFINITY;
+        nfin += f ? 1 : 0;
+        lo = f ? fminf(lo, x[q]) : lo;
+        hi = fmaxf(hi, x[q]);
+    }
+    if (nfin < K) return -INFINITY;
+    for (int it = 0; it < iters; ++it) {
+        const float mid = lo + 0.5f * (hi - lo);
+        if (!(mid > lo && mid < hi)) break;
+        if (count_ge<NX>(x, mid) >= K) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+// Narrows [lo, hi] (count(x >= lo) >= K, count(x > hi) < K on entry) until
+// hi - lo <= width: afterwards the K-th largest of x lies in [lo, hi].
+template <int NX>
+__device__ __forceinline__ void bisect_kth(const float (&x)[NX], int K, float width, int iters, float& lo,
+                                           float& hi) {
+    for (int it = 0; it < iters && hi - lo > width; ++it) {
+        const float mid = lo + 0.5f * (hi - lo);
+        if (!(mid > lo && mid < hi)) break;
+        if (count_ge<NX>(x, mid) >= K) lo = mid; else hi = mid;
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
 router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const TcParams p) {
@@ -296,7 +341,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const int g = h / (H / Hkv);
     const int i0 = qb * kTileM;
     const int jend = p.causal ? min(N, i0 + kTileM) : N;
-    const int T = (jend + kTileN - 1) / kTileN;
+    const int T = (jend + kTileN - 1) / kTileN;  // key tiles per pass
+    const int T2 = 2 * T;                          // two passes over the same key tiles
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
@@ -330,12 +376,12 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             tma_load_2d(sA, &tmA, afull, 0, bh * N + i0);
             const int krow0 = (b * Hkv + g) * N;
             int issued = 0;
-            for (int t = 0; t < T; ++t) {
+            for (int t = 0; t < T2; ++t) {
                 const int s = t % kStages;
                 if (t >= kStages) ok = mbar_wait(empty + s, ((t / kStages) - 1) & 1);
                 if (!ok) break;
                 mbar_arrive_expect_tx(full + s, kTileBytes);
-                tma_load_2d(sB + (size_t)s * kTileBytes, &tmB, full + s, 0, krow0 + t * kTileN);
+                tma_load_2d(sB + (size_t)s * kTileBytes, &tmB, full + s, 0, krow0 + (t % T) * kTileN);
                 issued = t + 1;
             }
             // the loads of the last stages are never waited on by a refill: make
@@ -350,7 +396,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             constexpr uint32_t idesc = umma_idesc_f16(0u, kTileM, kTileN);
             const uint64_t adesc = umma_desc_sw128(sA);
             bool ok = mbar_wait(afull, 0);
-            for (int t = 0; t < T && ok; ++t) {
+            for (int t = 0; t < T2 && ok; ++t) {
                 const int s = t % kStages;
                 const int ab = t % kAccBufs;
                 ok = mbar_wait(full + s, (t / kStages) & 1);
@@ -386,17 +432,21 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             delta = ri.y;
             if (!(m == m)) fb = true;
         }
-        // a NaN threshold admits nothing (every comparison with NaN is false)
-        float theta = fb ? __int_as_float(0x7fc00000) : -INFINITY;
+        // pass-2 admission threshold; a NaN threshold admits nothing
+        float theta = __int_as_float(0x7fc00000);
         int cnt = 0;
         uint2* rowbuf = buf + (size_t)row * kBufStride;
         float* wcp = win + ew * 4 * kWinCopy;
         const int s4 = lane & 3;
         const float* mycopy = wcp + s4 * kWinCopy + (lane - s4) + 124;
+        float cm[kTileN];  // pass 1: maximum score per column class (key index mod 128)
+#pragma unroll
+        for (int c = 0; c < kTileN; ++c) cm[c] = -INFINITY;
         bool ok = true;
 
-        for (int t = 0; t < T; ++t) {
-            const int j0 = t * kTileN;
+        for (int t = 0; t < T2; ++t) {
+            const bool pass2 = t >= T;
+            const int j0 = (pass2 ? t - T : t) * kTileN;
             // pos_bias window of this warp's rows x the tile's keys: copy s holds
             // w[y + s], w[x] = bias[clamp(i0 + r0 - j0 - 127 + x + L)]
             const int obase = i0 + r0 - j0 - (kTileN - 1) + L;
@@ -409,161 +459,199 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 }
             }
             const int ab = t % kAccBufs;
-            const bool got = __all_sync(kFull, mbar_wait(tfull + ab, (t / kAccBufs) & 1));
-            if (!got) {
+            if (!__all_sync(kFull, mbar_wait(tfull + ab, (t / kAccBufs) & 1))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            uint32_t v[4][32];
             const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN);
-            tmem_ld32(taddr + 0, v[0]);
-            tmem_ld32(taddr + 32, v[1]);
-            tmem_ld32(taddr + 64, v[2]);
-            tmem_ld32(taddr + 96, v[3]);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty + ab);
-
             const bool full_tile = (j0 + kTileN <= N) && (!p.causal || j0 + kTileN - 1 <= i0 + r0);
+            uint32_t va[32], vb[32];
+            tmem_ld32(taddr, va);
+            tmem_wait_ld();
+            __syncwarp();  // window copies visible to the whole warp
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
+                uint32_t(&cur)[32] = (ch & 1) ? vb : va;
+                uint32_t(&nxt)[32] = (ch & 1) ? va : vb;
+                if (ch < 3) {
+                    tmem_ld32(taddr + 32u * (ch + 1), nxt);
+                } else {
+                    // every column of this accumulator is in registers: hand it back
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty + ab);
+                }
+                if (!pass2) {
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const int c = ch * 32 + q * 4;  // column of v[ch][4q]
-                    const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
-                    const float sc[4] = {fmaf(__uint_as_float(v[ch][4 * q + 0]), m, bw.w),
-                                         fmaf(__uint_as_float(v[ch][4 * q + 1]), m, bw.z),
-                                         fmaf(__uint_as_float(v[ch][4 * q + 2]), m, bw.y),
-                                         fmaf(__uint_as_float(v[ch][4 * q + 3]), m, bw.x)};
+                    for (int q = 0; q < 8; ++q) {
+                        const int c = ch * 32 + q * 4;
+                        const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
+                        const float sc[4] = {fmaf(__uint_as_float(cur[4 * q + 0]), m, bw.w),
+                                             fmaf(__uint_as_float(cur[4 * q + 1]), m, bw.z),
+                                             fmaf(__uint_as_float(cur[4 * q + 2]), m, bw.y),
+                                             fmaf(__uint_as_float(cur[4 * q + 3]), m, bw.x)};
 #pragma unroll
-                    for (int d = 0; d < 4; ++d) {
-                        const int jj = j0 + c + d;
-                        const bool valid = full_tile || (jj < N && (!p.causal || jj <= i));
-                        if (valid && sc[d] >= theta) {
-                            rowbuf[cnt] = make_uint2(__float_as_uint(sc[d]), (uint32_t)jj);
-                            ++cnt;
+                        for (int d = 0; d < 4; ++d) {
+                            const int jj = j0 + c + d;
+                            const bool valid = full_tile || (jj < N && (!p.causal || jj <= i));
+                            cm[c + d] = fmaxf(cm[c + d], valid ? sc[d] : -INFINITY);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const int c = ch * 32 + q * 4;
+                        const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
+                        const float sc[4] = {fmaf(__uint_as_float(cur[4 * q + 0]), m, bw.w),
+                                             fmaf(__uint_as_float(cur[4 * q + 1]), m, bw.z),
+                                             fmaf(__uint_as_float(cur[4 * q + 2]), m, bw.y),
+                                             fmaf(__uint_as_float(cur[4 * q + 3]), m, bw.x)};
+#pragma unroll
+                        for (int d = 0; d < 4; ++d) {
+                            const int jj = j0 + c + d;
+                            const bool valid = full_tile || (jj < N && (!p.causal || jj <= i));
+                            if (valid && sc[d] >= theta) {
+                                rowbuf[cnt] = make_uint2(__float_as_uint(sc[d]), (uint32_t)jj);
+                                ++cnt;
+                            }
+                        }
+                    }
+                    // rare: a list that could overflow within the next 32 columns is
+                    // compacted by its warp (keep everything within 2*delta of the
+                    // current K-th best)
+                    unsigned need = __ballot_sync(kFull, cnt > kCap - 32);
+                    while (need) {
+                        const int src = __ffs(need) - 1;
+                        need &= need - 1;
+                        const int scnt = __shfl_sync(kFull, cnt, src);
+                        const float sdelta = __shfl_sync(kFull, delta, src);
+                        uint2* sb = buf + (size_t)(r0 + src) * kBufStride;
+                        float es[kEPL];
+                        uint32_t ej[kEPL], ek[kEPL];
+                        bool ev[kEPL], keep[kEPL];
+                        load_entries(sb, scnt, lane, es, ej, ev);
+#pragma unroll
+                        for (int e = 0; e < kEPL; ++e) ek[e] = order_key(es[e]);
+                        uint32_t Tk;
+                        int ties;
+                        warp_kth_key<kEPL>(ek, ev, K, Tk, ties);
+                        const float Tf = key_to_float(Tk);
+                        const float thr = Tf - (2.f * sdelta + fabsf(Tf) * kTwoPowM22);
+#pragma unroll
+                        for (int e = 0; e < kEPL; ++e) keep[e] = ev[e] && es[e] >= thr;
+                        const int nc = store_kept(sb, lane, es, ej, keep);
+                        if (lane == src) {
+                            if (nc > kCap - 32) {  // massive near-ties: exact fallback for this row
+                                fb = true;
+                                theta = __int_as_float(0x7fc00000);
+                                cnt = 0;
+                            } else {
+                                theta = fmaxf(theta, thr);
+                                cnt = nc;
+                            }
                         }
                     }
                 }
-                // lists that could overflow within the next 32 columns are compacted now
-                unsigned need = __ballot_sync(kFull, cnt > kCap - 32);
-                while (need) {
-                    const int src = __ffs(need) - 1;
-                    need &= need - 1;
-                    const int scnt = __shfl_sync(kFull, cnt, src);
-                    const float sdelta = __shfl_sync(kFull, delta, src);
-                    uint2* sb = buf + (size_t)(r0 + src) * kBufStride;
-                    float es[kEPL];
-                    uint32_t ej[kEPL], ek[kEPL];
-                    bool ev[kEPL], keep[kEPL];
-                    load_entries(sb, scnt, lane, es, ej, ev);
-#pragma unroll
-                    for (int e = 0; e < kEPL; ++e) ek[e] = order_key(es[e]);
-                    uint32_t Tk;
-                    int ties;
-                    warp_kth_key<kEPL>(ek, ev, K, Tk, ties);
-                    const float Tf = key_to_float(Tk);
-                    const float thr = Tf - (2.f * sdelta + fabsf(Tf) * kTwoPowM22);
-#pragma unroll
-                    for (int e = 0; e < kEPL; ++e) keep[e] = ev[e] && es[e] >= thr;
-                    const int nc = store_kept(sb, lane, es, ej, keep);
-                    if (lane == src) {
-                        if (nc > kCap - 32) {  // massive near-ties: exact fallback for this row
-                            fb = true;
-                            theta = __int_as_float(0x7fc00000);
-                            cnt = 0;
-                        } else {
-                            theta = thr;
-                            cnt = nc;
-                        }
-                    }
-                }
+                if (ch < 3) tmem_wait_ld();  // the next chunk has landed in registers
+            }
+            if (t == T - 1 && !fb) {
+                // End of pass 1: the K-th largest class maximum is a valid lower
+                // bound on the row's K-th best approximate score (K distinct keys
+                // reach it), and every exact top-K key scores at least that minus
+                // 2*delta.  Bisection finds the bound to a small fraction of the
+                // value range; any lower value is equally safe.
+                const float lb = kth_lower_bound<kTileN>(cm, K, 12);
+                theta = lb == -INFINITY ? -INFINITY : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
             }
             __syncwarp();  // window copies are rewritten for the next tile
         }
         if (!ok) atomicOr(p.status, 4);
 
         // ---------------------------------------------- per-row final selection
-        const float scale = p.scale;
-        for (int src = 0; src < 32 && ok; ++src) {
-            const int ri = i0 + r0 + src;
-            if (ri >= N) break;
-            const bool sfb = __shfl_sync(kFull, fb ? 1 : 0, src) != 0;
-            const int scnt = __shfl_sync(kFull, cnt, src);
-            const float sdelta = __shfl_sync(kFull, delta, src);
-            const size_t orow_id = (size_t)bh * N + ri;
+        // One thread per row (the row's list is in shared memory).
+        if (ok && i < N) {
+            const size_t orow_id = (size_t)bh * N + i;
             int32_t* orow = p.out + orow_id * K;
-            if (sfb) {
-                if (lane == 0) {
-                    const int pos = atomicAdd(p.fb_count, 1);
-                    p.fb_list[pos] = (int32_t)orow_id;
-                }
-                continue;
-            }
-            uint2* sb = buf + (size_t)(r0 + src) * kBufStride;
-            float es[kEPL];
-            uint32_t ej[kEPL];
-            bool ev[kEPL], keep[kEPL];
-            load_entries(sb, scnt, lane, es, ej, ev);
-            if (scnt <= K) {
-#pragma unroll
-                for (int e = 0; e < kEPL; ++e) keep[e] = ev[e];
-            } else {
-                uint32_t ek[kEPL];
-#pragma unroll
-                for (int e = 0; e < kEPL; ++e) ek[e] = order_key(es[e]);
-                uint32_t Tk;
-                int ties;
-                warp_kth_key<kEPL>(ek, ev, K, Tk, ties);
-                const float Tf = key_to_float(Tk);
-                const float m2 = 2.f * sdelta + fabsf(Tf) * kTwoPowM22;
-                bool in[kEPL], band[kEPL];
-                unsigned n_in = 0, n_band = 0;
-#pragma unroll
-                for (int e = 0; e < kEPL; ++e) {
-                    in[e] = ev[e] && es[e] > Tf + m2;
-                    band[e] = ev[e] && !in[e] && es[e] >= Tf - m2;
-                    n_in += in[e] ? 1u : 0u;
-                    n_band += band[e] ? 1u : 0u;
-                }
-                n_in = __reduce_add_sync(kFull, n_in);
-                n_band = __reduce_add_sync(kFull, n_band);
-                const int need = K - (int)n_in;
-                if ((int)n_band == need) {
-#pragma unroll
-                    for (int e = 0; e < kEPL; ++e) keep[e] = in[e] || band[e];
+            bool to_fallback = fb || cnt > kTileN;
+            if (!to_fallback) {
+                if (cnt <= K) {
+                    for (int q = 0; q < cnt; ++q) orow[q] = (int32_t)rowbuf[q].y;
+                    for (int q = cnt; q < K; ++q) orow[q] = -1;
                 } else {
-                    // boundary candidates: canonical scores decide
-                    const float* qrow = p.qp32 + orow_id * kR;
-                    const float* kbase = p.kp32 + (size_t)(b * Hkv + g) * N * kR;
-                    uint32_t xk[kEPL];
+                    float x[kTileN];
 #pragma unroll
-                    for (int e = 0; e < kEPL; ++e) {
-                        xk[e] = 0u;
-                        if (band[e]) {
-                            const int jj = (int)ej[e];
-                            xk[e] = order_key(canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, ri, jj,
-                                                              scale));
+                    for (int q = 0; q < kTileN; ++q)
+                        x[q] = q < cnt ? __uint_as_float(rowbuf[q].x) : -INFINITY;
+                    // bracket [lo, hi] around the K-th best approximate score
+                    float lo = INFINITY, hi = -INFINITY;
+#pragma unroll
+                    for (int q = 0; q < kTileN; ++q) {
+                        if (q < cnt) {
+                            lo = fminf(lo, x[q]);
+                            hi = fmaxf(hi, x[q]);
                         }
                     }
-                    bool bk[kEPL];
-                    warp_topk_mask<kEPL>(xk, band, need, bk);
+                    bisect_kth<kTileN>(x, K, 0.25f * delta, 24, lo, hi);
+                    const float m2 = 2.f * delta + fmaxf(fabsf(lo), fabsf(hi)) * kTwoPowM22;
+                    const float top = hi + m2, bot = lo - m2;
+                    int n_in = 0, n_band = 0;
 #pragma unroll
-                    for (int e = 0; e < kEPL; ++e) keep[e] = in[e] || bk[e];
+                    for (int q = 0; q < kTileN; ++q) {
+                        n_in += x[q] > top ? 1 : 0;
+                        n_band += (x[q] >= bot && x[q] <= top) ? 1 : 0;
+                    }
+                    const int need = K - n_in;
+                    uint32_t sel = 0xffffffffu;
+                    if (n_band != need) {
+                        if (n_band > kMaxBand) {
+                            to_fallback = true;
+                        } else {
+                            // boundary candidates: canonical scores decide
+                            uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)row * kMaxBand;
+                            const float* qrow = p.qp32 + orow_id * kR;
+                            const float* kbase = p.kp32 + (size_t)(b * Hkv + g) * N * kR;
+                            int nb = 0;
+                            for (int q = 0; q < cnt; ++q) {
+                                const uint2 e = rowbuf[q];
+                                const float sq = __uint_as_float(e.x);
+                                if (sq >= bot && sq <= top) {
+                                    const int jj = (int)e.y;
+                                    const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, i, jj,
+                                                                     p.scale);
+                                    scratch[nb++] = make_uint2(order_key(ex), (uint32_t)q);
+                                }
+                            }
+                            sel = 0u;
+                            for (int a = 0; a < nb; ++a) {
+                                const uint32_t ka = scratch[a].x;
+                                int rank = 0;
+                                for (int c2 = 0; c2 < nb; ++c2) {
+                                    const uint32_t kc = scratch[c2].x;
+                                    rank += (kc > ka || (kc == ka && c2 < a)) ? 1 : 0;
+                                }
+                                if (rank < need) sel |= 1u << a;
+                            }
+                        }
+                    }
+                    if (!to_fallback) {
+                        int outpos = 0, bidx = 0;
+                        for (int q = 0; q < cnt; ++q) {
+                            const uint2 e = rowbuf[q];
+                            const float sq = __uint_as_float(e.x);
+                            const bool inb = sq >= bot && sq <= top;
+                            const bool keep = sq > top || (inb && ((sel >> bidx) & 1u));
+                            bidx += inb ? 1 : 0;
+                            if (keep) orow[outpos++] = (int32_t)e.y;
+                        }
+                        for (int q = outpos; q < K; ++q) orow[q] = -1;
+                    }
                 }
             }
-            const unsigned lt = lanemask_lt();
-            int outpos = 0;
-#pragma unroll
-            for (int e = 0; e < kEPL; ++e) {
-                const unsigned kb = __ballot_sync(kFull, keep[e]);
-                if (keep[e]) orow[outpos + __popc(kb & lt)] = (int32_t)ej[e];
-                outpos += __popc(kb);
+            if (to_fallback) {
+                const int pos = atomicAdd(p.fb_count, 1);
+                p.fb_list[pos] = (int32_t)orow_id;
             }
-            for (int q = outpos + lane; q < K; q += 32) orow[q] = -1;
-            __syncwarp();
         }
     }
 

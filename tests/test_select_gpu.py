@@ -194,7 +194,7 @@ def _run_both(q, k, wq, wk, pb, L, K, causal=True):
     return tc, ex, fb, status
 
 
-@pytest.mark.parametrize("N,K,causal", [(2048, 64, True), (777, 32, True), (640, 64, False), (300, 96, True)])
+@pytest.mark.parametrize("N,K,causal", [(2048, 64, True), (777, 32, True), (640, 64, False), (300, 48, True), (4096, 16, True)])
 def test_tensor_core_and_exact_selectors_agree(N, K, causal):
     B, H, Hkv, D, r = 2, 12, 2, 128, 64
     q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=N + K, scale=1.0 / math.sqrt(D))
