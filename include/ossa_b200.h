@@ -138,6 +138,25 @@ OSSA_API int ossa_oracle_topk(const void* q, const void* k, int dtype,
                      int K, int causal, int32_t* idx_out,
                      ossa_stream_t stream);
 
+/*
+ * ossa_router_topk without a caller-provided workspace.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory where
+ * they launch this work (a host framework that owns every byte of device
+ * memory and forbids allocation while enqueueing, or an FFI caller without a
+ * device allocator).  It allocates nothing: the workspace is a fixed 32 MiB
+ * array inside the library, held on every GPU that loads the library until the
+ * process exits.  Shapes whose ossa_router_workspace_size exceeds 32 MiB are
+ * rejected with OSSA_ERR_WORKSPACE.  The first call on each device looks up the
+ * array's device address (make it before any stream capture).  All calls share
+ * the array: calls whose work overlaps on the GPU race and must be serialised
+ * by the caller.  Same arguments and results as ossa_router_topk otherwise.
+ */
+OSSA_API int ossa_router_topk_noalloc(const void* q, const void* k, int dtype,
+                                      const float* wq, const float* wk, const float* pos_bias,
+                                      int B, int H, int Hkv, int N, int D, int r, int seq_len_cfg,
+                                      int K, int causal, int32_t* idx_out,
+                                      ossa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -33,6 +33,7 @@ EXPORTED = (
     "ossa_router_status",
     "ossa_router_score",
     "ossa_oracle_topk",
+    "ossa_router_topk_noalloc",
 )
 
 _lock = threading.Lock()
@@ -67,6 +68,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ossa_router_score.restype = ci
     lib.ossa_oracle_topk.argtypes = [vp, vp, ci, ci, ci, ci, ci, ci, cf, ci, ci, vp, vp]
     lib.ossa_oracle_topk.restype = ci
+    lib.ossa_router_topk_noalloc.argtypes = [vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, ci, ci, vp, vp]
+    lib.ossa_router_topk_noalloc.restype = ci
 
 
 def lib() -> ctypes.CDLL:

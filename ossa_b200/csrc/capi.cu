@@ -32,6 +32,16 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
+}  // namespace
+
+namespace ossa {
+// Lets other translation units of the library report a message through
+// ossa_last_error_string.
+void set_error_message(const char* msg) { g_last_error = msg; }
+}  // namespace ossa
+
+namespace {
+
 int cuda_status(cudaError_t e, const char* what) {
     if (e == cudaSuccess) return OSSA_OK;
     return fail(OSSA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));

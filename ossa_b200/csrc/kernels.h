@@ -12,6 +12,9 @@ enum DType { kF32 = 0, kBF16 = 1 };
 // Counts successful kernel launches (ossa_launch_count); every launcher calls it.
 void note_launch(int n = 1);
 
+// Sets the message ossa_last_error_string returns on this thread.
+void set_error_message(const char* msg);
+
 struct GatherArgs {
     const void* q;
     const void* k;
