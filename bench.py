@@ -161,6 +161,7 @@ def run_ours(args) -> None:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=dev)
     from ossa_b200 import _lib, router_topk, topk_attention
+    from ossa_b200.select import router_topk_with_status
 
     w = WORKLOAD
     B, H, Hkv, N, D, K, r, L = (w[x] for x in ("B", "H", "Hkv", "N", "D", "K", "r", "seq_len"))
@@ -196,6 +197,7 @@ def run_ours(args) -> None:
             e2.record(stream)
         barrier()
     launches = _lib.launch_count() - launches0
+    _, fb_rows, sel_status = router_topk_with_status(q, k, wq, wk, pb, L, K, causal=True)
     sel_ms = [a.elapsed_time(b) for a, b, _ in evs]
     gat_ms = [b.elapsed_time(c) for _, b, c in evs]
     step_ms = [s + g for s, g in zip(sel_ms, gat_ms)]
@@ -277,6 +279,7 @@ def run_ours(args) -> None:
             "e2e": {"value": world * args.steps * B * N / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
+            "select_exact_fallback_rows": fb_rows, "select_status": sel_status,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -268,6 +268,31 @@ __device__ __forceinline__ int store_kept(uint2* rb, int lane, const float (&s)[
     return outpos;
 }
 
+// Appends {s, j} at shared address `addr` (advancing it) when s >= theta.
+// Written with an explicit predicate so the per-score insert is branch-free.
+__device__ __forceinline__ void insert_if(uint32_t& addr, float s, float theta, uint32_t j) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ge.f32 p, %1, %2;\n\t"
+        "@p st.shared.v2.u32 [%0], {%3, %4};\n\t"
+        "@p add.u32 %0, %0, 8;\n\t}"
+        : "+r"(addr)
+        : "f"(s), "f"(theta), "r"(__float_as_uint(s)), "r"(j));
+}
+
+// insert_if restricted to eligible columns (col < climit).
+__device__ __forceinline__ void insert_if_col(uint32_t& addr, float s, float theta, uint32_t j, int col,
+                                              int climit) {
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.lt.s32 q, %5, %6;\n\t"
+        "setp.ge.and.f32 p, %1, %2, q;\n\t"
+        "@p st.shared.v2.u32 [%0], {%3, %4};\n\t"
+        "@p add.u32 %0, %0, 8;\n\t}"
+        : "+r"(addr)
+        : "f"(s), "f"(theta), "r"(__float_as_uint(s)), "r"(j), "r"(col), "r"(climit));
+}
+
 // Count of x[q] >= v.
 template <int NX>
 __device__ __forceinline__ int count_ge(const float (&x)[NX], float v) {
@@ -434,7 +459,6 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         // pass-2 admission threshold; a NaN threshold admits nothing
         float theta = __int_as_float(0x7fc00000);
-        int cnt = 0;
         uint2* rowbuf = buf + (size_t)row * kBufStride;
         float* wcp = win + ew * 4 * kWinCopy;
         const int s4 = lane & 3;
@@ -444,11 +468,16 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         for (int c = 0; c < kTileN; ++c) cm[c] = -INFINITY;
         bool ok = true;
 
-        for (int t = 0; t < T2; ++t) {
-            const bool pass2 = t >= T;
-            const int j0 = (pass2 ? t - T : t) * kTileN;
-            // pos_bias window of this warp's rows x the tile's keys: copy s holds
-            // w[y + s], w[x] = bias[clamp(i0 + r0 - j0 - 127 + x + L)]
+        const uint32_t list_base = smem_u32(rowbuf);
+        uint32_t laddr = list_base;  // shared address of the next free list entry
+        // keys j < lim are eligible for this row
+        const int lim = p.causal ? min(N, i + 1) : N;
+
+        // Tile prologue shared by both passes: stage the pos_bias window of this
+        // warp's rows x the tile's keys (copy s holds w[y + s], with
+        // w[x] = bias[clamp(i0 + r0 - j0 - 127 + x + L)]) and wait for the tile's
+        // accumulator.  Returns false if the bounded wait expired.
+        auto tile_prologue = [&](int t, int j0) -> bool {
             const int obase = i0 + r0 - j0 - (kTileN - 1) + L;
             for (int y = lane; y < kWinLen; y += 32) {
 #pragma unroll
@@ -458,73 +487,117 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     wcp[s * kWinCopy + y] = __ldg(p.bias + bi);
                 }
             }
+            if (!__all_sync(kFull, mbar_wait(tfull + t % kAccBufs, (t / kAccBufs) & 1))) return false;
+            tc_fence_after();
+            return true;
+        };
+
+        for (int t = 0; t < T && ok; ++t) {
+            const int j0 = t * kTileN;
             const int ab = t % kAccBufs;
-            if (!__all_sync(kFull, mbar_wait(tfull + ab, (t / kAccBufs) & 1))) {
+            if (!tile_prologue(t, j0)) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
             const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN);
-            const bool full_tile = (j0 + kTileN <= N) && (!p.causal || j0 + kTileN - 1 <= i0 + r0);
-            uint32_t va[32], vb[32];
-            tmem_ld32(taddr, va);
-            tmem_wait_ld();
-            __syncwarp();  // window copies visible to the whole warp
+            // every row of the warp sees all 128 keys of the tile as eligible
+            const bool full_tile = __all_sync(kFull, j0 + kTileN <= lim || fb);
+            const int climit = lim - j0;  // columns c < climit are eligible
+            {
+                // ---------------- pass 1: per column-class maxima
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t(&cur)[32] = (ch & 1) ? vb : va;
-                uint32_t(&nxt)[32] = (ch & 1) ? va : vb;
-                if (ch < 3) {
-                    tmem_ld32(taddr + 32u * (ch + 1), nxt);
-                } else {
-                    // every column of this accumulator is in registers: hand it back
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(tempty + ab);
-                }
-                if (!pass2) {
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint32_t v[64];
+                    tmem_ld32(taddr + 64u * hf, *reinterpret_cast<uint32_t(*)[32]>(v));
+                    tmem_ld32(taddr + 64u * hf + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+                    tmem_wait_ld();
+                    if (hf == 1) {
+                        // the whole accumulator is in registers: hand it back
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(tempty + ab);
+                    } else {
+                        __syncwarp();  // window copies visible to the whole warp
+                    }
+                    if (full_tile) {
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const int c = ch * 32 + q * 4;
-                        const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
-                        const float sc[4] = {fmaf(__uint_as_float(cur[4 * q + 0]), m, bw.w),
-                                             fmaf(__uint_as_float(cur[4 * q + 1]), m, bw.z),
-                                             fmaf(__uint_as_float(cur[4 * q + 2]), m, bw.y),
-                                             fmaf(__uint_as_float(cur[4 * q + 3]), m, bw.x)};
+                        for (int q = 0; q < 16; ++q) {
+                            const int c = hf * 64 + q * 4;
+                            const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
+                            cm[c + 0] = fmaxf(cm[c + 0], fmaf(__uint_as_float(v[4 * q + 0]), m, bw.w));
+                            cm[c + 1] = fmaxf(cm[c + 1], fmaf(__uint_as_float(v[4 * q + 1]), m, bw.z));
+                            cm[c + 2] = fmaxf(cm[c + 2], fmaf(__uint_as_float(v[4 * q + 2]), m, bw.y));
+                            cm[c + 3] = fmaxf(cm[c + 3], fmaf(__uint_as_float(v[4 * q + 3]), m, bw.x));
+                        }
+                    } else {
 #pragma unroll
-                        for (int d = 0; d < 4; ++d) {
-                            const int jj = j0 + c + d;
-                            const bool valid = full_tile || (jj < N && (!p.causal || jj <= i));
-                            cm[c + d] = fmaxf(cm[c + d], valid ? sc[d] : -INFINITY);
+                        for (int q = 0; q < 16; ++q) {
+                            const int c = hf * 64 + q * 4;
+                            const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
+                            const float b4[4] = {bw.w, bw.z, bw.y, bw.x};
+#pragma unroll
+                            for (int d = 0; d < 4; ++d) {
+                                const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
+                                cm[c + d] = fmaxf(cm[c + d], c + d < climit ? sc : -INFINITY);
+                            }
                         }
                     }
-                } else {
+                }
+            }
+            __syncwarp();  // window copies are rewritten for the next tile
+        }
+        if (ok && !fb) {
+            // End of pass 1: the K-th largest class maximum is a valid lower bound
+            // on the row's K-th best approximate score (K distinct keys reach it),
+            // and every exact top-K key scores at least that minus 2*delta.
+            // Bisection finds the bound to a small fraction of the value range;
+            // any lower value is equally safe.
+            const float lb = kth_lower_bound<kTileN>(cm, K, 12);
+            theta = lb == -INFINITY ? -INFINITY : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
+        }
+
+        for (int t = T; t < T2 && ok; ++t) {
+            const int j0 = (t - T) * kTileN;
+            const int ab = t % kAccBufs;
+            if (!tile_prologue(t, j0)) {
+                ok = false;
+                break;
+            }
+            const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN);
+            const bool full_tile = __all_sync(kFull, j0 + kTileN <= lim || fb);
+            const int climit = lim - j0;
+            {
+                // ---------------- pass 2: collect candidates s >= theta
+                uint32_t v[kTileN];
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch)
+                    tmem_ld32(taddr + 32u * ch, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * ch));
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty + ab);
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
                         const int c = ch * 32 + q * 4;
                         const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
-                        const float sc[4] = {fmaf(__uint_as_float(cur[4 * q + 0]), m, bw.w),
-                                             fmaf(__uint_as_float(cur[4 * q + 1]), m, bw.z),
-                                             fmaf(__uint_as_float(cur[4 * q + 2]), m, bw.y),
-                                             fmaf(__uint_as_float(cur[4 * q + 3]), m, bw.x)};
+                        const float b4[4] = {bw.w, bw.z, bw.y, bw.x};
 #pragma unroll
                         for (int d = 0; d < 4; ++d) {
-                            const int jj = j0 + c + d;
-                            const bool valid = full_tile || (jj < N && (!p.causal || jj <= i));
-                            if (valid && sc[d] >= theta) {
-                                rowbuf[cnt] = make_uint2(__float_as_uint(sc[d]), (uint32_t)jj);
-                                ++cnt;
-                            }
+                            const float sc = fmaf(__uint_as_float(v[c + d]), m, b4[d]);
+                            if (full_tile) insert_if(laddr, sc, theta, (uint32_t)(j0 + c + d));
+                            else insert_if_col(laddr, sc, theta, (uint32_t)(j0 + c + d), c + d, climit);
                         }
                     }
                     // rare: a list that could overflow within the next 32 columns is
                     // compacted by its warp (keep everything within 2*delta of the
                     // current K-th best)
-                    unsigned need = __ballot_sync(kFull, cnt > kCap - 32);
+                    unsigned need = __ballot_sync(kFull, laddr - list_base > 8u * (kCap - 32));
                     while (need) {
                         const int src = __ffs(need) - 1;
                         need &= need - 1;
-                        const int scnt = __shfl_sync(kFull, cnt, src);
+                        const int scnt = (int)((__shfl_sync(kFull, laddr - list_base, src)) >> 3);
                         const float sdelta = __shfl_sync(kFull, delta, src);
                         uint2* sb = buf + (size_t)(r0 + src) * kBufStride;
                         float es[kEPL];
@@ -545,27 +618,18 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                             if (nc > kCap - 32) {  // massive near-ties: exact fallback for this row
                                 fb = true;
                                 theta = __int_as_float(0x7fc00000);
-                                cnt = 0;
+                                laddr = list_base;
                             } else {
                                 theta = fmaxf(theta, thr);
-                                cnt = nc;
+                                laddr = list_base + 8u * nc;
                             }
                         }
                     }
                 }
-                if (ch < 3) tmem_wait_ld();  // the next chunk has landed in registers
-            }
-            if (t == T - 1 && !fb) {
-                // End of pass 1: the K-th largest class maximum is a valid lower
-                // bound on the row's K-th best approximate score (K distinct keys
-                // reach it), and every exact top-K key scores at least that minus
-                // 2*delta.  Bisection finds the bound to a small fraction of the
-                // value range; any lower value is equally safe.
-                const float lb = kth_lower_bound<kTileN>(cm, K, 12);
-                theta = lb == -INFINITY ? -INFINITY : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
             }
             __syncwarp();  // window copies are rewritten for the next tile
         }
+        const int cnt = (int)((laddr - list_base) >> 3);
         if (!ok) atomicOr(p.status, 4);
 
         // ---------------------------------------------- per-row final selection
@@ -592,7 +656,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                             hi = fmaxf(hi, x[q]);
                         }
                     }
-                    bisect_kth<kTileN>(x, K, 0.25f * delta, 24, lo, hi);
+                    bisect_kth<kTileN>(x, K, delta, 20, lo, hi);
                     const float m2 = 2.f * delta + fmaxf(fabsf(lo), fabsf(hi)) * kTwoPowM22;
                     const float top = hi + m2, bot = lo - m2;
                     int n_in = 0, n_band = 0;
