@@ -6,11 +6,12 @@
 // "fp32 projection" every selection decision downstream is defined on.
 //
 // Tiling: a CTA computes ROWS x R outputs with 256 threads; each thread owns a
-// 4 x 4 register tile.  D is consumed in chunks of 64: the x chunk is staged
-// transposed in shared memory (float4 broadcast reads of 4 rows) and W^T in
-// shared memory (float4 reads of 4 output columns), i.e. two LDS.128 per 16 FFMA.
-// The kprojection is GQA-aware by construction: the caller runs it on the Hkv key
-// heads only, never on repeated copies.
+// 4 x 4 register tile.  D is consumed in chunks of up to 128: the x chunk is
+// fetched with 16-byte loads (all issued before the first use) and stored
+// transposed in shared memory (float4 broadcast reads of 4 rows), W^T sits in
+// shared memory (float4 reads of 4 output columns): two LDS.128 per 16 FFMA.
+// The k projection is GQA-aware by construction: the caller runs it on the Hkv
+// key heads only, never on repeated copies.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -19,7 +20,13 @@ namespace ossa {
 namespace {
 
 constexpr int kProjThreads = 256;
-constexpr int kDChunk = 64;
+constexpr int kDChunk = 128;
+
+// Elements of x per 16-byte vector load.
+template <typename T>
+struct ChunkLoader {
+    static constexpr int VEC = 16 / sizeof(T);  // elements per 16-byte load
+};
 
 template <typename T, int R>
 __global__ void __launch_bounds__(kProjThreads)
@@ -29,6 +36,7 @@ project_kernel(const T* __restrict__ x, const float* __restrict__ w, float* __re
     constexpr int RG = kProjThreads / CG;        // row groups
     constexpr int ROWS = RG * 4;                 // rows per CTA
     constexpr int XS = ROWS + 4;                 // padded stride (keeps float4 alignment)
+    constexpr int VEC = ChunkLoader<T>::VEC;
     extern __shared__ float4 smem4[];
     float* Xs = reinterpret_cast<float*>(smem4);  // [kDChunk][XS]
     float* Ws = Xs + kDChunk * XS;                // [kDChunk][R]
@@ -37,6 +45,7 @@ project_kernel(const T* __restrict__ x, const float* __restrict__ w, float* __re
     const int cg = tid % CG;
     const int rg = tid / CG;
     const long long row0 = (long long)blockIdx.x * ROWS;
+    const bool vec_ok = (D % VEC) == 0;
 
     float acc[4][4];
 #pragma unroll
@@ -47,18 +56,58 @@ project_kernel(const T* __restrict__ x, const float* __restrict__ w, float* __re
     for (int dc = 0; dc < D; dc += kDChunk) {
         const int dn = min(kDChunk, D - dc);
         __syncthreads();
-        for (int e = tid; e < ROWS * kDChunk; e += kProjThreads) {
-            const int r = e / kDChunk, d = e - r * kDChunk;
-            const long long gr = row0 + r;
-            float val = 0.f;
-            if (gr < rows && d < dn) val = to_f32(x[gr * D + dc + d]);
-            Xs[d * XS + r] = val;
+        if (vec_ok) {
+            // ROWS rows x (dn / VEC) vectors; every load is issued before any store
+            constexpr int kPer = (ROWS * kDChunk / VEC + kProjThreads - 1) / kProjThreads;
+            const int nvec = dn / VEC;
+            uint4 buf[kPer];
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) {
+                // consecutive threads take consecutive rows, so the transposed
+                // shared-memory stores below hit consecutive banks
+                const int e = tid + u * kProjThreads;
+                const int vcol = e / ROWS, r = e - vcol * ROWS;
+                const long long gr = row0 + r;
+                buf[u] = make_uint4(0u, 0u, 0u, 0u);
+                if (vcol < kDChunk / VEC && vcol < nvec && gr < rows)
+                    buf[u] = __ldg(reinterpret_cast<const uint4*>(x + gr * D + dc) + vcol);
+            }
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) {
+                const int e = tid + u * kProjThreads;
+                const int vcol = e / ROWS, r = e - vcol * ROWS;
+                if (vcol < kDChunk / VEC) {
+                    float f[VEC];
+                    if constexpr (sizeof(T) == 2) {
+                        unpack_bf16x2(buf[u].x, f[0], f[1]);
+                        unpack_bf16x2(buf[u].y, f[2], f[3]);
+                        unpack_bf16x2(buf[u].z, f[4], f[5]);
+                        unpack_bf16x2(buf[u].w, f[6], f[7]);
+                    } else {
+                        f[0] = __uint_as_float(buf[u].x);
+                        f[1] = __uint_as_float(buf[u].y);
+                        f[2] = __uint_as_float(buf[u].z);
+                        f[3] = __uint_as_float(buf[u].w);
+                    }
+#pragma unroll
+                    for (int t = 0; t < VEC; ++t) Xs[(vcol * VEC + t) * XS + r] = f[t];
+                }
+            }
+        } else {
+            for (int e = tid; e < ROWS * kDChunk; e += kProjThreads) {
+                const int r = e / kDChunk, d = e - r * kDChunk;
+                const long long gr = row0 + r;
+                float val = 0.f;
+                if (gr < rows && d < dn) val = to_f32(x[gr * D + dc + d]);
+                Xs[d * XS + r] = val;
+            }
         }
         for (int e = tid; e < R * kDChunk; e += kProjThreads) {
             const int d = e / R, c = e - d * R;
             Ws[d * R + c] = d < dn ? __ldg(w + (size_t)c * D + dc + d) : 0.f;
         }
         __syncthreads();
+#pragma unroll 4
         for (int d = 0; d < dn; ++d) {
             const float4 xv = *reinterpret_cast<const float4*>(Xs + d * XS + rg * 4);
             const float4 wv = *reinterpret_cast<const float4*>(Ws + d * R + cg * 4);

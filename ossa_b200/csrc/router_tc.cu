@@ -293,13 +293,13 @@ __device__ __forceinline__ void insert_if_col(uint32_t& addr, float s, float the
         : "f"(s), "f"(theta), "r"(__float_as_uint(s)), "r"(j), "r"(col), "r"(climit));
 }
 
-// Count of x[q] >= v.
+// Count of x[q] >= v (eight independent partial counts: no long add chain).
 template <int NX>
 __device__ __forceinline__ int count_ge(const float (&x)[NX], float v) {
-    int c = 0;
+    int c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-    for (int q = 0; q < NX; ++q) c += x[q] >= v ? 1 : 0;
-    return c;
+    for (int q = 0; q < NX; ++q) c[q & 7] += x[q] >= v ? 1 : 0;
+    return ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
 }
 
 // A lower bound on the K-th largest of x (padding entries are -inf): the result
@@ -307,14 +307,28 @@ __device__ __forceinline__ int count_ge(const float (&x)[NX], float v) {
 // largest finite values; -inf if fewer than K entries are finite.
 template <int NX>
 __device__ __forceinline__ float kth_lower_bound(const float (&x)[NX], int K, int iters) {
-    float lo = INFINITY, hi = -INFINITY;
-    int nfin = 0;
+    float lo8[8], hi8[8];
+    int nf8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        lo8[u] = INFINITY;
+        hi8[u] = -INFINITY;
+        nf8[u] = 0;
+    }
 #pragma unroll
     for (int q = 0; q < NX; ++q) {
         const bool f = x[q] > -INFINITY;
-        nfin += f ? 1 : 0;
-        lo = f ? fminf(lo, x[q]) : lo;
-        hi = fmaxf(hi, x[q]);
+        nf8[q & 7] += f ? 1 : 0;
+        lo8[q & 7] = f ? fminf(lo8[q & 7], x[q]) : lo8[q & 7];
+        hi8[q & 7] = fmaxf(hi8[q & 7], x[q]);
+    }
+    float lo = lo8[0], hi = hi8[0];
+    int nfin = nf8[0];
+#pragma unroll
+    for (int u = 1; u < 8; ++u) {
+        lo = fminf(lo, lo8[u]);
+        hi = fmaxf(hi, hi8[u]);
+        nfin += nf8[u];
     }
     if (nfin < K) return -INFINITY;
     for (int it = 0; it < iters; ++it) {
@@ -478,13 +492,23 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // w[x] = bias[clamp(i0 + r0 - j0 - 127 + x + L)]) and wait for the tile's
         // accumulator.  Returns false if the bounded wait expired.
         auto tile_prologue = [&](int t, int j0) -> bool {
+            // each lane fetches w[x] for x = lane + 32u once and writes it to the
+            // four copies (copy s at y = x - s)
             const int obase = i0 + r0 - j0 - (kTileN - 1) + L;
-            for (int y = lane; y < kWinLen; y += 32) {
+            float wv[(kWinLen + 3 + 31) / 32];
+#pragma unroll
+            for (int u = 0; u < (kWinLen + 3 + 31) / 32; ++u) {
+                int bi = obase + lane + 32 * u;
+                bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
+                wv[u] = __ldg(p.bias + bi);
+            }
+#pragma unroll
+            for (int u = 0; u < (kWinLen + 3 + 31) / 32; ++u) {
+                const int x = lane + 32 * u;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    int bi = obase + y + s;
-                    bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
-                    wcp[s * kWinCopy + y] = __ldg(p.bias + bi);
+                    const int y = x - s;
+                    if (y >= 0 && y < kWinLen) wcp[s * kWinCopy + y] = wv[u];
                 }
             }
             if (!__all_sync(kFull, mbar_wait(tfull + t % kAccBufs, (t / kAccBufs) & 1))) return false;
@@ -648,22 +672,37 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     for (int q = 0; q < kTileN; ++q)
                         x[q] = q < cnt ? __uint_as_float(rowbuf[q].x) : -INFINITY;
                     // bracket [lo, hi] around the K-th best approximate score
-                    float lo = INFINITY, hi = -INFINITY;
+                    float lo8[8], hi8[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        lo8[u] = INFINITY;
+                        hi8[u] = -INFINITY;
+                    }
 #pragma unroll
                     for (int q = 0; q < kTileN; ++q) {
-                        if (q < cnt) {
-                            lo = fminf(lo, x[q]);
-                            hi = fmaxf(hi, x[q]);
-                        }
+                        lo8[q & 7] = q < cnt ? fminf(lo8[q & 7], x[q]) : lo8[q & 7];
+                        hi8[q & 7] = fmaxf(hi8[q & 7], x[q]);
+                    }
+                    float lo = lo8[0], hi = hi8[0];
+#pragma unroll
+                    for (int u = 1; u < 8; ++u) {
+                        lo = fminf(lo, lo8[u]);
+                        hi = fmaxf(hi, hi8[u]);
                     }
                     bisect_kth<kTileN>(x, K, delta, 20, lo, hi);
                     const float m2 = 2.f * delta + fmaxf(fabsf(lo), fabsf(hi)) * kTwoPowM22;
                     const float top = hi + m2, bot = lo - m2;
-                    int n_in = 0, n_band = 0;
+                    int ni8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, nb8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
                     for (int q = 0; q < kTileN; ++q) {
-                        n_in += x[q] > top ? 1 : 0;
-                        n_band += (x[q] >= bot && x[q] <= top) ? 1 : 0;
+                        ni8[q & 7] += x[q] > top ? 1 : 0;
+                        nb8[q & 7] += (x[q] >= bot && x[q] <= top) ? 1 : 0;
+                    }
+                    int n_in = 0, n_band = 0;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        n_in += ni8[u];
+                        n_band += nb8[u];
                     }
                     const int need = K - n_in;
                     uint32_t sel = 0xffffffffu;
