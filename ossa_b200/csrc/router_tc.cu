@@ -17,26 +17,29 @@
 //     tensor core and the canonical fmaf chain far less; 2^-8 leaves 4x margin).
 //  2. warp 0 (one thread) streams 128-key tiles of k'16 with TMA (128-byte
 //     swizzle) through a 2-stage ring; warp 1 (one thread) issues
-//     tcgen05.mma.kind::f16 128x128x64 into one of 4 TMEM accumulators;
-//     warps 2-5 (one TMEM lane quadrant each, one query row per thread) drain
-//     a finished accumulator with tcgen05.ld, release it, and score
+//     tcgen05.mma.kind::f16 128x128x64 into one of 4 TMEM accumulators; eight
+//     epilogue warps (two per TMEM lane quadrant, each owning 64 of the 128
+//     columns; one query row per thread) drain a finished accumulator with
+//     tcgen05.ld, release it, and score
 //        s = acc * m_i + pos_bias[clamp(i - j + L, 0, 2L - 1)]
 //     (pos_bias staged per warp and tile as four shifted copies so each thread
 //     reads 4 consecutive offsets with one aligned 16-byte load).
-//  3. Streaming selection per row: a candidate list in shared memory and a
-//     threshold theta.  A score enters if s >= theta.  Every 32 columns, rows
-//     whose list might overflow are compacted by their warp: radix-select the
-//     K-th best approximate score T, keep entries with s >= T - 2*delta_i and
-//     set theta to that bound.  Dropped entries have canonical score below
-//     T - delta_i, under the canonical score of K listed entries, so the list
-//     always contains the exact top K.
-//  4. End of row: with T the K-th best approximate score, entries above
-//     T + 2*delta_i are certainly selected, entries below T - 2*delta_i
-//     certainly not; the few in between are rescored with the canonical fp32
-//     formula and the remaining slots filled from them by (score desc, j asc).
-//  5. Rows whose list would overflow (massive near-ties) or whose inputs are
-//     not finite are appended to a list and recomputed afterwards by an exact
-//     warp-per-row selector (exact_rows_kernel).
+//  3. Two passes over the same key tiles (the MMA runs twice; the epilogue is
+//     the bottleneck, not the tensor core).  Pass 1 keeps, per row, the maximum
+//     score of each column class (key index mod 128).  The K-th largest of those
+//     128 maxima is a valid lower bound on the row's K-th best score (K distinct
+//     keys reach it), so theta = bound - 2*delta_i can only drop keys outside
+//     the exact top K.  Pass 2 appends every score >= theta to the thread's
+//     candidate sub-list (about 1.3 K entries per row on random data).
+//  4. End of row (one thread per row): bisection on the candidates' approximate
+//     scores brackets the K-th best T; entries above T + 2*delta_i are certainly
+//     selected, entries below T - 2*delta_i certainly not, and the few in between
+//     are rescored with the canonical fp32 formula; the remaining slots go to
+//     them by (score desc, j asc).  Output in ascending key order.
+//  5. Rows whose sub-list would overflow (massive near-ties), whose boundary
+//     band is too wide, or whose inputs are not finite are appended to a list
+//     and recomputed afterwards by an exact warp-per-row selector
+//     (exact_rows_kernel).
 //
 // Every wait on an mbarrier is bounded (~1 s); on expiry the kernel records a
 // nonzero status word, lets the other roles finish their bounded waits, waits
@@ -60,13 +63,14 @@ constexpr int kTileM = 128;         // query rows per CTA
 constexpr int kTileN = 128;         // keys per MMA tile
 constexpr int kStages = 2;          // k' tile ring
 constexpr int kAccBufs = 4;         // TMEM accumulators (128 columns each)
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;        // two per TMEM lane quadrant, 64 columns each
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kEPL = 5;             // candidate entries per lane in a list
-constexpr int kCap = 32 * kEPL;     // candidate list capacity per row
-constexpr int kBufStride = kCap + 1;  // uint2 entries; odd stride spreads banks
-constexpr int kWinLen = 160;        // bias window entries per copy
-constexpr int kWinCopy = 168;       // copy stride (floats): copies 8 banks apart
+constexpr int kHalfCols = kTileN / 2;
+constexpr int kSubCap = 80;         // candidate sub-list capacity (per row and column half)
+constexpr int kSubLimit = kSubCap - 16;  // past this after a 16-column step: exact fallback
+constexpr int kRowStride = 2 * kSubCap + 1;  // uint2 entries per row; odd stride spreads banks
+constexpr int kWinLen = 96;         // bias window entries per copy (32 rows x 64 columns)
+constexpr int kWinCopy = 104;       // copy stride (floats): copies 8 banks apart
 constexpr int kTileBytes = kTileM * kR * 2;
 constexpr uint32_t kTmemCols = kAccBufs * kTileN;
 constexpr int kMaxK = 64;           // selection bound uses the K-th of 128 column-class maxima
@@ -76,7 +80,8 @@ constexpr size_t kOffA = 0;
 constexpr size_t kOffB = kOffA + kTileBytes;
 constexpr size_t kOffWin = kOffB + (size_t)kStages * kTileBytes;
 constexpr size_t kOffBuf = kOffWin + (size_t)kEpiWarps * 4 * kWinCopy * sizeof(float);
-constexpr size_t kOffBar = kOffBuf + (size_t)kTileM * kBufStride * sizeof(uint2);
+constexpr size_t kOffBar = kOffBuf + (size_t)kTileM * kRowStride * sizeof(uint2);
+static_assert(4 * kWinCopy >= 2 * 32, "a quadrant's row metadata reuses one warp's window");
 constexpr int kNumBars = 2 * kStages + 1 + 2 * kAccBufs + 1;
 constexpr size_t kOffSlot = kOffBar + kNumBars * sizeof(uint64_t);
 constexpr size_t kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
@@ -240,57 +245,9 @@ __device__ __forceinline__ float canonical_score(const float* __restrict__ qrow,
     return __fadd_rn(__fmul_rn(acc, scale), __ldg(bias + bi));
 }
 
-__device__ __forceinline__ void load_entries(const uint2* rb, int cnt, int lane, float (&s)[kEPL],
-                                             uint32_t (&j)[kEPL], bool (&val)[kEPL]) {
-#pragma unroll
-    for (int e = 0; e < kEPL; ++e) {
-        const int p = lane + 32 * e;
-        val[e] = p < cnt;
-        const uint2 t = val[e] ? rb[p] : make_uint2(0u, 0u);
-        s[e] = __uint_as_float(t.x);
-        j[e] = t.y;
-    }
-}
-
-// Rewrites the list with the kept entries, in order; returns their count.
-__device__ __forceinline__ int store_kept(uint2* rb, int lane, const float (&s)[kEPL], const uint32_t (&j)[kEPL],
-                                          const bool (&keep)[kEPL]) {
-    const unsigned lt = lanemask_lt();
-    int outpos = 0;
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < kEPL; ++e) {
-        const unsigned kb = __ballot_sync(kFull, keep[e]);
-        if (keep[e]) rb[outpos + __popc(kb & lt)] = make_uint2(__float_as_uint(s[e]), j[e]);
-        outpos += __popc(kb);
-    }
-    __syncwarp();
-    return outpos;
-}
-
-// Appends {s, j} at shared address `addr` (advancing it) when s >= theta.
-// Written with an explicit predicate so the per-score insert is branch-free.
-__device__ __forceinline__ void insert_if(uint32_t& addr, float s, float theta, uint32_t j) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ge.f32 p, %1, %2;\n\t"
-        "@p st.shared.v2.u32 [%0], {%3, %4};\n\t"
-        "@p add.u32 %0, %0, 8;\n\t}"
-        : "+r"(addr)
-        : "f"(s), "f"(theta), "r"(__float_as_uint(s)), "r"(j));
-}
-
-// insert_if restricted to eligible columns (col < climit).
-__device__ __forceinline__ void insert_if_col(uint32_t& addr, float s, float theta, uint32_t j, int col,
-                                              int climit) {
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.lt.s32 q, %5, %6;\n\t"
-        "setp.ge.and.f32 p, %1, %2, q;\n\t"
-        "@p st.shared.v2.u32 [%0], {%3, %4};\n\t"
-        "@p add.u32 %0, %0, 8;\n\t}"
-        : "+r"(addr)
-        : "f"(s), "f"(theta), "r"(__float_as_uint(s)), "r"(j), "r"(col), "r"(climit));
+// Barrier over `count` threads (a multiple of 32) using hardware barrier `id`.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // Count of x[q] >= v (eight independent partial counts: no long add chain).
@@ -456,45 +413,41 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
     } else {
         // ------------------------------------------------ epilogue: scoring + selection
-        const int ew = warp - 2;
-        const int qd = warp & 3;  // TMEM lane quadrant this warp may access
+        // Eight warps: warp (quadrant qd, half hf) owns TMEM lanes 32*qd.. (query
+        // rows) and accumulator columns 64*hf.. of every tile; each row is served
+        // by two threads, one per column half, with one candidate sub-list each.
+        const int ew = warp - 2;             // 0..7
+        const int qd = warp & 3;             // TMEM lane quadrant this warp may access
+        const int hf = ew >> 2;              // column half
         const int r0 = qd * 32;
         const int row = r0 + lane;
         const int i = i0 + row;
         const int K = p.K;
         const int L = p.L;
+        const int cbase = hf * kHalfCols;    // first tile column of this thread
+        const uint32_t pair_bar = 1u + (uint32_t)qd;  // named barrier of the quadrant's two warps
         float m = 0.f, delta = 0.f;
-        bool fb = i >= N;  // inactive rows never insert and are skipped at the end
+        bool fb = i >= N;  // rows to skip (inactive) or to recompute exactly
         if (i < N) {
             const float2 ri = p.rowinfo[(size_t)bh * N + i];
             m = ri.x;
             delta = ri.y;
             if (!(m == m)) fb = true;
         }
-        // pass-2 admission threshold; a NaN threshold admits nothing
-        float theta = __int_as_float(0x7fc00000);
-        uint2* rowbuf = buf + (size_t)row * kBufStride;
+        uint2* rowbuf = buf + (size_t)row * kRowStride;
+        uint2* sub = rowbuf + hf * kSubCap;  // this thread's candidate sub-list
         float* wcp = win + ew * 4 * kWinCopy;
         const int s4 = lane & 3;
-        const float* mycopy = wcp + s4 * kWinCopy + (lane - s4) + 124;
-        float cm[kTileN];  // pass 1: maximum score per column class (key index mod 128)
-#pragma unroll
-        for (int c = 0; c < kTileN; ++c) cm[c] = -INFINITY;
+        const float* mycopy = wcp + s4 * kWinCopy + (lane - s4) + (kHalfCols - 4);
+        const int lim = p.causal ? min(N, i + 1) : N;  // keys j < lim are eligible
         bool ok = true;
 
-        const uint32_t list_base = smem_u32(rowbuf);
-        uint32_t laddr = list_base;  // shared address of the next free list entry
-        // keys j < lim are eligible for this row
-        const int lim = p.causal ? min(N, i + 1) : N;
-
-        // Tile prologue shared by both passes: stage the pos_bias window of this
-        // warp's rows x the tile's keys (copy s holds w[y + s], with
-        // w[x] = bias[clamp(i0 + r0 - j0 - 127 + x + L)]) and wait for the tile's
-        // accumulator.  Returns false if the bounded wait expired.
+        // Tile prologue shared by both passes: stage this warp's pos_bias window
+        // (copy s holds w[y + s], w[x] = bias[clamp(i0 + r0 - j0 - 63 - cbase + x + L)],
+        // so column c of row lane reads w[lane - (c - cbase) + 63]) and wait for the
+        // tile's accumulator.  Returns false if the bounded wait expired.
         auto tile_prologue = [&](int t, int j0) -> bool {
-            // each lane fetches w[x] for x = lane + 32u once and writes it to the
-            // four copies (copy s at y = x - s)
-            const int obase = i0 + r0 - j0 - (kTileN - 1) + L;
+            const int obase = i0 + r0 - j0 - (kHalfCols - 1) - cbase + L;
             float wv[(kWinLen + 3 + 31) / 32];
 #pragma unroll
             for (int u = 0; u < (kWinLen + 3 + 31) / 32; ++u) {
@@ -511,11 +464,16 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     if (y >= 0 && y < kWinLen) wcp[s * kWinCopy + y] = wv[u];
                 }
             }
+            __syncwarp();
             if (!__all_sync(kFull, mbar_wait(tfull + t % kAccBufs, (t / kAccBufs) & 1))) return false;
             tc_fence_after();
             return true;
         };
 
+        // ---------------- pass 1: maximum score per column class (key index mod 128)
+        float cm[kHalfCols];
+#pragma unroll
+        for (int c = 0; c < kHalfCols; ++c) cm[c] = -INFINITY;
         for (int t = 0; t < T && ok; ++t) {
             const int j0 = t * kTileN;
             const int ab = t % kAccBufs;
@@ -523,63 +481,69 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 ok = false;
                 break;
             }
-            const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN);
-            // every row of the warp sees all 128 keys of the tile as eligible
-            const bool full_tile = __all_sync(kFull, j0 + kTileN <= lim || fb);
-            const int climit = lim - j0;  // columns c < climit are eligible
-            {
-                // ---------------- pass 1: per column-class maxima
+            const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN + cbase);
+            const bool full_tile = __all_sync(kFull, j0 + cbase + kHalfCols <= lim || fb);
+            const int climit = lim - j0 - cbase;  // local columns c < climit are eligible
+            uint32_t v[kHalfCols];
+            tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
+            tmem_ld32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty + ab);
+            if (full_tile) {
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    uint32_t v[64];
-                    tmem_ld32(taddr + 64u * hf, *reinterpret_cast<uint32_t(*)[32]>(v));
-                    tmem_ld32(taddr + 64u * hf + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-                    tmem_wait_ld();
-                    if (hf == 1) {
-                        // the whole accumulator is in registers: hand it back
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(tempty + ab);
-                    } else {
-                        __syncwarp();  // window copies visible to the whole warp
-                    }
-                    if (full_tile) {
+                for (int q = 0; q < kHalfCols / 4; ++q) {
+                    const int c = q * 4;
+                    const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
+                    cm[c + 0] = fmaxf(cm[c + 0], fmaf(__uint_as_float(v[c + 0]), m, bw.w));
+                    cm[c + 1] = fmaxf(cm[c + 1], fmaf(__uint_as_float(v[c + 1]), m, bw.z));
+                    cm[c + 2] = fmaxf(cm[c + 2], fmaf(__uint_as_float(v[c + 2]), m, bw.y));
+                    cm[c + 3] = fmaxf(cm[c + 3], fmaf(__uint_as_float(v[c + 3]), m, bw.x));
+                }
+            } else {
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            const int c = hf * 64 + q * 4;
-                            const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
-                            cm[c + 0] = fmaxf(cm[c + 0], fmaf(__uint_as_float(v[4 * q + 0]), m, bw.w));
-                            cm[c + 1] = fmaxf(cm[c + 1], fmaf(__uint_as_float(v[4 * q + 1]), m, bw.z));
-                            cm[c + 2] = fmaxf(cm[c + 2], fmaf(__uint_as_float(v[4 * q + 2]), m, bw.y));
-                            cm[c + 3] = fmaxf(cm[c + 3], fmaf(__uint_as_float(v[4 * q + 3]), m, bw.x));
-                        }
-                    } else {
+                for (int q = 0; q < kHalfCols / 4; ++q) {
+                    const int c = q * 4;
+                    const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
+                    const float b4[4] = {bw.w, bw.z, bw.y, bw.x};
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            const int c = hf * 64 + q * 4;
-                            const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
-                            const float b4[4] = {bw.w, bw.z, bw.y, bw.x};
-#pragma unroll
-                            for (int d = 0; d < 4; ++d) {
-                                const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
-                                cm[c + d] = fmaxf(cm[c + d], c + d < climit ? sc : -INFINITY);
-                            }
-                        }
+                    for (int d = 0; d < 4; ++d) {
+                        const float sc = fmaf(__uint_as_float(v[c + d]), m, b4[d]);
+                        cm[c + d] = fmaxf(cm[c + d], c + d < climit ? sc : -INFINITY);
                     }
                 }
             }
             __syncwarp();  // window copies are rewritten for the next tile
         }
-        if (ok && !fb) {
-            // End of pass 1: the K-th largest class maximum is a valid lower bound
-            // on the row's K-th best approximate score (K distinct keys reach it),
-            // and every exact top-K key scores at least that minus 2*delta.
-            // Bisection finds the bound to a small fraction of the value range;
-            // any lower value is equally safe.
-            const float lb = kth_lower_bound<kTileN>(cm, K, 12);
-            theta = lb == -INFINITY ? -INFINITY : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
-        }
 
+        // End of pass 1: the two threads of a row exchange their 64 class maxima
+        // through the (still empty) candidate area; the K-th largest of the 128 is
+        // a valid lower bound on the row's K-th best approximate score (K distinct
+        // keys reach it), and every exact top-K key scores at least that minus
+        // 2*delta.  Both threads compute the same bound from the same 128 values.
+        float* xch = reinterpret_cast<float*>(sub);
+#pragma unroll
+        for (int c = 0; c < kHalfCols; ++c) xch[c] = cm[c];
+        named_bar_sync(pair_bar, 64);
+        float theta = __int_as_float(0x7fc00000);  // NaN admits nothing
+        {
+            const float* other = reinterpret_cast<const float*>(rowbuf + (1 - hf) * kSubCap);
+            float x[kTileN];
+#pragma unroll
+            for (int c = 0; c < kHalfCols; ++c) {
+                x[c] = cm[c];
+                x[kHalfCols + c] = other[c];
+            }
+            if (ok && !fb) {
+                const float lb = kth_lower_bound<kTileN>(x, K, 12);
+                theta = lb == -INFINITY ? -INFINITY : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
+            }
+        }
+        named_bar_sync(pair_bar, 64);  // both halves have read before sub-lists are written
+
+        // ---------------- pass 2: collect candidates s >= theta into the sub-list
+        int cnt = 0;
         for (int t = T; t < T2 && ok; ++t) {
             const int j0 = (t - T) * kTileN;
             const int ab = t % kAccBufs;
@@ -587,90 +551,85 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 ok = false;
                 break;
             }
-            const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN);
-            const bool full_tile = __all_sync(kFull, j0 + kTileN <= lim || fb);
-            const int climit = lim - j0;
-            {
-                // ---------------- pass 2: collect candidates s >= theta
-                uint32_t v[kTileN];
+            const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN + cbase);
+            const bool full_tile = __all_sync(kFull, j0 + cbase + kHalfCols <= lim || fb);
+            const int climit = lim - j0 - cbase;
+            const uint32_t jb = (uint32_t)(j0 + cbase);
+            uint32_t v[kHalfCols];
+            tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
+            tmem_ld32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty + ab);
+            uint2* wp = sub + cnt;
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch)
-                    tmem_ld32(taddr + 32u * ch, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * ch));
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(tempty + ab);
+            for (int q = 0; q < kHalfCols / 4; ++q) {
+                const int c = q * 4;
+                const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
+                const float b4[4] = {bw.w, bw.z, bw.y, bw.x};
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const int c = ch * 32 + q * 4;
-                        const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
-                        const float b4[4] = {bw.w, bw.z, bw.y, bw.x};
-#pragma unroll
-                        for (int d = 0; d < 4; ++d) {
-                            const float sc = fmaf(__uint_as_float(v[c + d]), m, b4[d]);
-                            if (full_tile) insert_if(laddr, sc, theta, (uint32_t)(j0 + c + d));
-                            else insert_if_col(laddr, sc, theta, (uint32_t)(j0 + c + d), c + d, climit);
-                        }
-                    }
-                    // rare: a list that could overflow within the next 32 columns is
-                    // compacted by its warp (keep everything within 2*delta of the
-                    // current K-th best)
-                    unsigned need = __ballot_sync(kFull, laddr - list_base > 8u * (kCap - 32));
-                    while (need) {
-                        const int src = __ffs(need) - 1;
-                        need &= need - 1;
-                        const int scnt = (int)((__shfl_sync(kFull, laddr - list_base, src)) >> 3);
-                        const float sdelta = __shfl_sync(kFull, delta, src);
-                        uint2* sb = buf + (size_t)(r0 + src) * kBufStride;
-                        float es[kEPL];
-                        uint32_t ej[kEPL], ek[kEPL];
-                        bool ev[kEPL], keep[kEPL];
-                        load_entries(sb, scnt, lane, es, ej, ev);
-#pragma unroll
-                        for (int e = 0; e < kEPL; ++e) ek[e] = order_key(es[e]);
-                        uint32_t Tk;
-                        int ties;
-                        warp_kth_key<kEPL>(ek, ev, K, Tk, ties);
-                        const float Tf = key_to_float(Tk);
-                        const float thr = Tf - (2.f * sdelta + fabsf(Tf) * kTwoPowM22);
-#pragma unroll
-                        for (int e = 0; e < kEPL; ++e) keep[e] = ev[e] && es[e] >= thr;
-                        const int nc = store_kept(sb, lane, es, ej, keep);
-                        if (lane == src) {
-                            if (nc > kCap - 32) {  // massive near-ties: exact fallback for this row
-                                fb = true;
-                                theta = __int_as_float(0x7fc00000);
-                                laddr = list_base;
-                            } else {
-                                theta = fmaxf(theta, thr);
-                                laddr = list_base + 8u * nc;
-                            }
-                        }
+                for (int d = 0; d < 4; ++d) {
+                    const float sc = fmaf(__uint_as_float(v[c + d]), m, b4[d]);
+                    const bool adm = (full_tile || c + d < climit) && sc >= theta;
+                    if (adm) *wp = make_uint2(__float_as_uint(sc), jb + (uint32_t)(c + d));
+                    wp += adm ? 1 : 0;
+                }
+                if ((q & 3) == 3) {
+                    // after every 16 columns: a sub-list that could overflow during
+                    // the next 16 sends its row to the exact fallback
+                    const int n = (int)(wp - sub);
+                    if (n > kSubLimit) {
+                        fb = true;
+                        theta = __int_as_float(0x7fc00000);
+                        wp = sub;
                     }
                 }
             }
+            cnt = (int)(wp - sub);
             __syncwarp();  // window copies are rewritten for the next tile
         }
-        const int cnt = (int)((laddr - list_base) >> 3);
         if (!ok) atomicOr(p.status, 4);
 
         // ---------------------------------------------- per-row final selection
-        // One thread per row (the row's list is in shared memory).
-        if (ok && i < N) {
-            const size_t orow_id = (size_t)bh * N + i;
+        // Publish (count, fallback) of both sub-lists, then one thread per row
+        // (lanes 16*hf .. 16*hf + 15 of the quadrant's two warps) finishes it.
+        // The quadrant's metadata lives in the window of its column-half-0 warp:
+        // only the two warps of this quadrant touch it, and both are past their
+        // last window read once the first barrier below completes.
+        int* qmeta = reinterpret_cast<int*>(win + (ew & 3) * 4 * kWinCopy);
+        named_bar_sync(pair_bar, 64);  // window reads of both warps are done
+        qmeta[2 * lane + hf] = fb ? -1 : cnt;
+        named_bar_sync(pair_bar, 64);
+        const int frow = r0 + (lane >> 4) * 16 + (lane & 15);
+        const bool mine = ((lane >> 4) == hf) && ok;
+        const int fi = i0 + frow;
+        if (mine && fi < N) {
+            const int* fm = qmeta + 2 * (frow - r0);
+            const int ca = fm[0], cb = fm[1];
+            const float fdelta = p.rowinfo[(size_t)bh * N + fi].y;
+            const uint2* la = buf + (size_t)frow * kRowStride;
+            const uint2* lb2 = la + kSubCap;
+            const size_t orow_id = (size_t)bh * N + fi;
             int32_t* orow = p.out + orow_id * K;
-            bool to_fallback = fb || cnt > kTileN;
+            bool to_fallback = ca < 0 || cb < 0 || ca + cb > kTileN;
             if (!to_fallback) {
-                if (cnt <= K) {
-                    for (int q = 0; q < cnt; ++q) orow[q] = (int32_t)rowbuf[q].y;
-                    for (int q = cnt; q < K; ++q) orow[q] = -1;
+                const int tot = ca + cb;
+                if (tot <= K) {
+                    int ia = 0, ib = 0, q = 0;
+                    while (ia < ca || ib < cb) {
+                        const bool ta = ib >= cb || (ia < ca && la[ia].y < lb2[ib].y);
+                        orow[q++] = (int32_t)(ta ? la[ia++].y : lb2[ib++].y);
+                    }
+                    for (; q < K; ++q) orow[q] = -1;
                 } else {
                     float x[kTileN];
 #pragma unroll
-                    for (int q = 0; q < kTileN; ++q)
-                        x[q] = q < cnt ? __uint_as_float(rowbuf[q].x) : -INFINITY;
+                    for (int q = 0; q < kTileN; ++q) {
+                        const int qb2 = q - ca;
+                        x[q] = q < ca ? __uint_as_float(la[q].x)
+                                      : (qb2 < cb ? __uint_as_float(lb2[qb2 < 0 ? 0 : qb2].x) : -INFINITY);
+                    }
                     // bracket [lo, hi] around the K-th best approximate score
                     float lo8[8], hi8[8];
 #pragma unroll
@@ -680,7 +639,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     }
 #pragma unroll
                     for (int q = 0; q < kTileN; ++q) {
-                        lo8[q & 7] = q < cnt ? fminf(lo8[q & 7], x[q]) : lo8[q & 7];
+                        lo8[q & 7] = q < tot ? fminf(lo8[q & 7], x[q]) : lo8[q & 7];
                         hi8[q & 7] = fmaxf(hi8[q & 7], x[q]);
                     }
                     float lo = lo8[0], hi = hi8[0];
@@ -689,8 +648,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         lo = fminf(lo, lo8[u]);
                         hi = fmaxf(hi, hi8[u]);
                     }
-                    bisect_kth<kTileN>(x, K, delta, 20, lo, hi);
-                    const float m2 = 2.f * delta + fmaxf(fabsf(lo), fabsf(hi)) * kTwoPowM22;
+                    bisect_kth<kTileN>(x, K, fdelta, 20, lo, hi);
+                    const float m2 = 2.f * fdelta + fmaxf(fabsf(lo), fabsf(hi)) * kTwoPowM22;
                     const float top = hi + m2, bot = lo - m2;
                     int ni8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, nb8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
@@ -710,19 +669,21 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         if (n_band > kMaxBand) {
                             to_fallback = true;
                         } else {
-                            // boundary candidates: canonical scores decide
-                            uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)row * kMaxBand;
+                            // boundary candidates, in ascending key order: canonical
+                            // scores decide, ties to the lower key index
+                            uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)frow * kMaxBand;
                             const float* qrow = p.qp32 + orow_id * kR;
                             const float* kbase = p.kp32 + (size_t)(b * Hkv + g) * N * kR;
-                            int nb = 0;
-                            for (int q = 0; q < cnt; ++q) {
-                                const uint2 e = rowbuf[q];
+                            int nb = 0, ia = 0, ib = 0;
+                            while (ia < ca || ib < cb) {
+                                const bool ta = ib >= cb || (ia < ca && la[ia].y < lb2[ib].y);
+                                const uint2 e = ta ? la[ia++] : lb2[ib++];
                                 const float sq = __uint_as_float(e.x);
                                 if (sq >= bot && sq <= top) {
                                     const int jj = (int)e.y;
-                                    const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, i, jj,
-                                                                     p.scale);
-                                    scratch[nb++] = make_uint2(order_key(ex), (uint32_t)q);
+                                    const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, fi,
+                                                                     jj, p.scale);
+                                    scratch[nb++] = make_uint2(order_key(ex), (uint32_t)jj);
                                 }
                             }
                             sel = 0u;
@@ -738,9 +699,10 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         }
                     }
                     if (!to_fallback) {
-                        int outpos = 0, bidx = 0;
-                        for (int q = 0; q < cnt; ++q) {
-                            const uint2 e = rowbuf[q];
+                        int outpos = 0, bidx = 0, ia = 0, ib = 0;
+                        while (ia < ca || ib < cb) {
+                            const bool ta = ib >= cb || (ia < ca && la[ia].y < lb2[ib].y);
+                            const uint2 e = ta ? la[ia++] : lb2[ib++];
                             const float sq = __uint_as_float(e.x);
                             const bool inb = sq >= bot && sq <= top;
                             const bool keep = sq > top || (inb && ((sel >> bidx) & 1u));
