@@ -47,6 +47,8 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <climits>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "select_warp.cuh"
@@ -232,13 +234,20 @@ __device__ __forceinline__ float canonical_score(const float* __restrict__ qrow,
                                                  float scale) {
     float acc = 0.f;
 #pragma unroll
-    for (int c = 0; c < kR; c += 4) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(qrow + c));
-        const float4 bk = __ldg(reinterpret_cast<const float4*>(krow + c));
-        acc = fmaf(a.x, bk.x, acc);
-        acc = fmaf(a.y, bk.y, acc);
-        acc = fmaf(a.z, bk.z, acc);
-        acc = fmaf(a.w, bk.w, acc);
+    for (int c0 = 0; c0 < kR; c0 += 16) {
+        float4 a[4], bk[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            a[u] = __ldg(reinterpret_cast<const float4*>(qrow + c0) + u);
+            bk[u] = __ldg(reinterpret_cast<const float4*>(krow + c0) + u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            acc = fmaf(a[u].x, bk[u].x, acc);
+            acc = fmaf(a[u].y, bk[u].y, acc);
+            acc = fmaf(a[u].z, bk[u].z, acc);
+            acc = fmaf(a[u].w, bk[u].w, acc);
+        }
     }
     int bi = i - j + L;
     bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
@@ -446,17 +455,22 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // (copy s holds w[y + s], w[x] = bias[clamp(i0 + r0 - j0 - 63 - cbase + x + L)],
         // so column c of row lane reads w[lane - (c - cbase) + 63]) and wait for the
         // tile's accumulator.  Returns false if the bounded wait expired.
-        auto tile_prologue = [&](int t, int j0) -> bool {
+        // The bias values of tile t + 1 are fetched from global memory while tile
+        // t is processed (wv), so staging never waits on that load.
+        constexpr int kWinVals = (kWinLen + 3 + 31) / 32;
+        float wv[kWinVals];
+        auto fetch_window = [&](int j0) {
             const int obase = i0 + r0 - j0 - (kHalfCols - 1) - cbase + L;
-            float wv[(kWinLen + 3 + 31) / 32];
 #pragma unroll
-            for (int u = 0; u < (kWinLen + 3 + 31) / 32; ++u) {
+            for (int u = 0; u < kWinVals; ++u) {
                 int bi = obase + lane + 32 * u;
                 bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
                 wv[u] = __ldg(p.bias + bi);
             }
+        };
+        auto tile_prologue = [&](int t) -> bool {
 #pragma unroll
-            for (int u = 0; u < (kWinLen + 3 + 31) / 32; ++u) {
+            for (int u = 0; u < kWinVals; ++u) {
                 const int x = lane + 32 * u;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
@@ -465,10 +479,12 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 }
             }
             __syncwarp();
+            if (t + 1 < T2) fetch_window(((t + 1) % T) * kTileN);
             if (!__all_sync(kFull, mbar_wait(tfull + t % kAccBufs, (t / kAccBufs) & 1))) return false;
             tc_fence_after();
             return true;
         };
+        fetch_window(0);
 
         // ---------------- pass 1: maximum score per column class (key index mod 128)
         float cm[kHalfCols];
@@ -477,77 +493,132 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         for (int t = 0; t < T && ok; ++t) {
             const int j0 = t * kTileN;
             const int ab = t % kAccBufs;
-            if (!tile_prologue(t, j0)) {
+            if (!tile_prologue(t)) {
                 ok = false;
                 break;
             }
             const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN + cbase);
             const bool full_tile = __all_sync(kFull, j0 + cbase + kHalfCols <= lim || fb);
             const int climit = lim - j0 - cbase;  // local columns c < climit are eligible
-            uint32_t v[kHalfCols];
-            tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
-            tmem_ld32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty + ab);
-            if (full_tile) {
+            // Two 32-column chunks: the chunk's accumulator columns and its bias
+            // values are loaded together, so the shared-memory latency is paid
+            // once per chunk rather than once per 4 columns.
 #pragma unroll
-                for (int q = 0; q < kHalfCols / 4; ++q) {
-                    const int c = q * 4;
-                    const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
-                    cm[c + 0] = fmaxf(cm[c + 0], fmaf(__uint_as_float(v[c + 0]), m, bw.w));
-                    cm[c + 1] = fmaxf(cm[c + 1], fmaf(__uint_as_float(v[c + 1]), m, bw.z));
-                    cm[c + 2] = fmaxf(cm[c + 2], fmaf(__uint_as_float(v[c + 2]), m, bw.y));
-                    cm[c + 3] = fmaxf(cm[c + 3], fmaf(__uint_as_float(v[c + 3]), m, bw.x));
+            for (int h2 = 0; h2 < 2; ++h2) {
+                uint32_t v[32];
+                float4 bw[8];
+                tmem_ld32(taddr + 32u * h2, v);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) bw[q] = *reinterpret_cast<const float4*>(mycopy - (32 * h2 + 4 * q));
+                tmem_wait_ld();
+                if (h2 == 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty + ab);
                 }
-            } else {
+                if (full_tile) {
 #pragma unroll
-                for (int q = 0; q < kHalfCols / 4; ++q) {
-                    const int c = q * 4;
-                    const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
-                    const float b4[4] = {bw.w, bw.z, bw.y, bw.x};
+                    for (int q = 0; q < 8; ++q) {
+                        const int c = 32 * h2 + 4 * q;
+                        cm[c + 0] = fmaxf(cm[c + 0], fmaf(__uint_as_float(v[4 * q + 0]), m, bw[q].w));
+                        cm[c + 1] = fmaxf(cm[c + 1], fmaf(__uint_as_float(v[4 * q + 1]), m, bw[q].z));
+                        cm[c + 2] = fmaxf(cm[c + 2], fmaf(__uint_as_float(v[4 * q + 2]), m, bw[q].y));
+                        cm[c + 3] = fmaxf(cm[c + 3], fmaf(__uint_as_float(v[4 * q + 3]), m, bw[q].x));
+                    }
+                } else {
 #pragma unroll
-                    for (int d = 0; d < 4; ++d) {
-                        const float sc = fmaf(__uint_as_float(v[c + d]), m, b4[d]);
-                        cm[c + d] = fmaxf(cm[c + d], c + d < climit ? sc : -INFINITY);
+                    for (int q = 0; q < 8; ++q) {
+                        const int c = 32 * h2 + 4 * q;
+                        const float b4[4] = {bw[q].w, bw[q].z, bw[q].y, bw[q].x};
+#pragma unroll
+                        for (int d = 0; d < 4; ++d) {
+                            const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
+                            cm[c + d] = fmaxf(cm[c + d], c + d < climit ? sc : -INFINITY);
+                        }
                     }
                 }
             }
             __syncwarp();  // window copies are rewritten for the next tile
         }
 
-        // End of pass 1: the two threads of a row exchange their 64 class maxima
-        // through the (still empty) candidate area; the K-th largest of the 128 is
-        // a valid lower bound on the row's K-th best approximate score (K distinct
-        // keys reach it), and every exact top-K key scores at least that minus
-        // 2*delta.  Both threads compute the same bound from the same 128 values.
+        // End of pass 1: the 128 class maxima of a row lie in two warps (64 each).
+        // They go through the (still empty) candidate area to a lane pair of one
+        // warp: lanes 2r and 2r+1 of warp hf take row r0 + 16*hf + r, one half
+        // each, and bisect on the value until exactly K maxima are >= lo (or the
+        // bracket cannot be split).  lo is then a lower bound on the row's K-th
+        // best approximate score (K distinct keys reach it), and every exact
+        // top-K key scores at least lo - 2*delta.  The bound goes back through
+        // the row's spare list entry.
         float* xch = reinterpret_cast<float*>(sub);
 #pragma unroll
         for (int c = 0; c < kHalfCols; ++c) xch[c] = cm[c];
         named_bar_sync(pair_bar, 64);
-        float theta = __int_as_float(0x7fc00000);  // NaN admits nothing
         {
-            const float* other = reinterpret_cast<const float*>(rowbuf + (1 - hf) * kSubCap);
-            float x[kTileN];
+            const int brow = r0 + 16 * hf + (lane >> 1);
+            const int bhalf = lane & 1;
+            const float* cls = reinterpret_cast<const float*>(buf + (size_t)brow * kRowStride + bhalf * kSubCap);
+            float y[kHalfCols];
+#pragma unroll
+            for (int c = 0; c < kHalfCols; ++c) y[c] = cls[c ^ bhalf];  // the pair reads different banks
+            float lo8[8], hi8[8];
+            int nf8[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                lo8[u] = INFINITY;
+                hi8[u] = -INFINITY;
+                nf8[u] = 0;
+            }
 #pragma unroll
             for (int c = 0; c < kHalfCols; ++c) {
-                x[c] = cm[c];
-                x[kHalfCols + c] = other[c];
+                const bool f = y[c] > -INFINITY;
+                nf8[c & 7] += f ? 1 : 0;
+                lo8[c & 7] = f ? fminf(lo8[c & 7], y[c]) : lo8[c & 7];
+                hi8[c & 7] = fmaxf(hi8[c & 7], y[c]);
             }
-            if (ok && !fb) {
-                const float lb = kth_lower_bound<kTileN>(x, K, 12);
-                theta = lb == -INFINITY ? -INFINITY : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
+            float lo = lo8[0], hi = hi8[0];
+            int nfin = nf8[0];
+#pragma unroll
+            for (int u = 1; u < 8; ++u) {
+                lo = fminf(lo, lo8[u]);
+                hi = fmaxf(hi, hi8[u]);
+                nfin += nf8[u];
             }
+            lo = fminf(lo, __shfl_xor_sync(kFull, lo, 1));
+            hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, 1));
+            nfin += __shfl_xor_sync(kFull, nfin, 1);
+            bool done = nfin <= K;
+            for (int it = 0; it < 32; ++it) {
+                if (__all_sync(kFull, done)) break;
+                const float mid = lo + 0.5f * (hi - lo);
+                int c = count_ge<kHalfCols>(y, mid);
+                c += __shfl_xor_sync(kFull, c, 1);
+                if (!done) {
+                    if (!(mid > lo && mid < hi)) {
+                        done = true;
+                    } else if (c >= K) {
+                        lo = mid;
+                        done = c == K;
+                    } else {
+                        hi = mid;
+                    }
+                }
+            }
+            const float lbv = nfin < K ? -INFINITY : lo;
+            if (bhalf == 0) buf[(size_t)brow * kRowStride + (kRowStride - 1)].x = __float_as_uint(lbv);
         }
-        named_bar_sync(pair_bar, 64);  // both halves have read before sub-lists are written
+        named_bar_sync(pair_bar, 64);  // bounds published; class maxima read before sub-lists are written
+        float theta = __int_as_float(0x7fc00000);  // NaN admits nothing
+        if (ok && !fb) {
+            const float lb = __uint_as_float(rowbuf[kRowStride - 1].x);
+            theta = lb == -INFINITY ? -INFINITY : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
+        }
 
         // ---------------- pass 2: collect candidates s >= theta into the sub-list
         int cnt = 0;
         for (int t = T; t < T2 && ok; ++t) {
             const int j0 = (t - T) * kTileN;
             const int ab = t % kAccBufs;
-            if (!tile_prologue(t, j0)) {
+            if (!tile_prologue(t)) {
                 ok = false;
                 break;
             }
@@ -555,34 +626,42 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const bool full_tile = __all_sync(kFull, j0 + cbase + kHalfCols <= lim || fb);
             const int climit = lim - j0 - cbase;
             const uint32_t jb = (uint32_t)(j0 + cbase);
-            uint32_t v[kHalfCols];
-            tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
-            tmem_ld32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty + ab);
             uint2* wp = sub + cnt;
+            // Two 32-column chunks, each loading its accumulator columns and bias
+            // values together (as in pass 1).
 #pragma unroll
-            for (int q = 0; q < kHalfCols / 4; ++q) {
-                const int c = q * 4;
-                const float4 bw = *reinterpret_cast<const float4*>(mycopy - c);
-                const float b4[4] = {bw.w, bw.z, bw.y, bw.x};
+            for (int h2 = 0; h2 < 2; ++h2) {
+                uint32_t v[32];
+                float4 bw[8];
+                tmem_ld32(taddr + 32u * h2, v);
 #pragma unroll
-                for (int d = 0; d < 4; ++d) {
-                    const float sc = fmaf(__uint_as_float(v[c + d]), m, b4[d]);
-                    const bool adm = (full_tile || c + d < climit) && sc >= theta;
-                    if (adm) *wp = make_uint2(__float_as_uint(sc), jb + (uint32_t)(c + d));
-                    wp += adm ? 1 : 0;
+                for (int q = 0; q < 8; ++q) bw[q] = *reinterpret_cast<const float4*>(mycopy - (32 * h2 + 4 * q));
+                tmem_wait_ld();
+                if (h2 == 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty + ab);
                 }
-                if ((q & 3) == 3) {
-                    // after every 16 columns: a sub-list that could overflow during
-                    // the next 16 sends its row to the exact fallback
-                    const int n = (int)(wp - sub);
-                    if (n > kSubLimit) {
-                        fb = true;
-                        theta = __int_as_float(0x7fc00000);
-                        wp = sub;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int c = 32 * h2 + 4 * q;
+                    const float b4[4] = {bw[q].w, bw[q].z, bw[q].y, bw[q].x};
+#pragma unroll
+                    for (int d = 0; d < 4; ++d) {
+                        const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
+                        const bool adm = (full_tile || c + d < climit) && sc >= theta;
+                        if (adm) *wp = make_uint2(__float_as_uint(sc), jb + (uint32_t)(c + d));
+                        wp += adm ? 1 : 0;
+                    }
+                    if ((q & 3) == 3) {
+                        // after every 16 columns: a sub-list that could overflow during
+                        // the next 16 sends its row to the exact fallback
+                        const int n = (int)(wp - sub);
+                        if (n > kSubLimit) {
+                            fb = true;
+                            theta = __int_as_float(0x7fc00000);
+                            wp = sub;
+                        }
                     }
                 }
             }
@@ -592,128 +671,237 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         if (!ok) atomicOr(p.status, 4);
 
         // ---------------------------------------------- per-row final selection
-        // Publish (count, fallback) of both sub-lists, then one thread per row
-        // (lanes 16*hf .. 16*hf + 15 of the quadrant's two warps) finishes it.
-        // The quadrant's metadata lives in the window of its column-half-0 warp:
-        // only the two warps of this quadrant touch it, and both are past their
-        // last window read once the first barrier below completes.
+        // Publish both sub-list counts (-1: exact fallback); then the lane pair
+        // (2r, 2r+1) of warp hf finishes row r0 + 16*hf + r, each lane owning one
+        // sub-list (both are in ascending key order).
+        //  1. bisection on the approximate scores from [lb, max] until exactly K
+        //     are >= lo; x_K = min{s >= lo}, x_K1 = max{s < lo}.  Entries above
+        //     U = x_K1 + 2*delta are certainly in the exact top K, entries below
+        //     W = x_K - 2*delta certainly not (with a bracket [lo, hi] instead
+        //     when the scores do not split: U = hi + 2*delta, W = lo - 2*delta).
+        //  2. entries in [W, U] (usually none) are rescored with the canonical
+        //     fp32 formula and the best K - #(s > U) of them by (score desc,
+        //     key asc) are kept.
+        //  3. each lane compacts its kept keys in place; lane 2r merges the two
+        //     lists from the front, lane 2r+1 from the back, into the output row.
+        // Quadrant metadata lives in the window of its column-half-0 warp: only
+        // the quadrant's two warps touch it, and both are past their last window
+        // read once the first barrier below completes.
         int* qmeta = reinterpret_cast<int*>(win + (ew & 3) * 4 * kWinCopy);
-        named_bar_sync(pair_bar, 64);  // window reads of both warps are done
+        named_bar_sync(pair_bar, 64);
         qmeta[2 * lane + hf] = fb ? -1 : cnt;
         named_bar_sync(pair_bar, 64);
-        const int frow = r0 + (lane >> 4) * 16 + (lane & 15);
-        const bool mine = ((lane >> 4) == hf) && ok;
-        const int fi = i0 + frow;
-        if (mine && fi < N) {
-            const int* fm = qmeta + 2 * (frow - r0);
-            const int ca = fm[0], cb = fm[1];
-            const float fdelta = p.rowinfo[(size_t)bh * N + fi].y;
-            const uint2* la = buf + (size_t)frow * kRowStride;
-            const uint2* lb2 = la + kSubCap;
-            const size_t orow_id = (size_t)bh * N + fi;
-            int32_t* orow = p.out + orow_id * K;
-            bool to_fallback = ca < 0 || cb < 0 || ca + cb > kTileN;
-            if (!to_fallback) {
-                const int tot = ca + cb;
-                if (tot <= K) {
-                    int ia = 0, ib = 0, q = 0;
-                    while (ia < ca || ib < cb) {
-                        const bool ta = ib >= cb || (ia < ca && la[ia].y < lb2[ib].y);
-                        orow[q++] = (int32_t)(ta ? la[ia++].y : lb2[ib++].y);
-                    }
-                    for (; q < K; ++q) orow[q] = -1;
-                } else {
-                    float x[kTileN];
+        {
+            const int frow = r0 + 16 * hf + (lane >> 1);
+            const int fh = lane & 1;
+            const int fi = i0 + frow;
+            const bool active = ok && fi < N;
+            const int ca = qmeta[2 * (frow - r0)], cb = qmeta[2 * (frow - r0) + 1];
+            uint2* frowbuf = buf + (size_t)frow * kRowStride;
+            uint2* own = frowbuf + fh * kSubCap;
+            const int nown = fh ? cb : ca;
+            bool to_fallback = active && (ca < 0 || cb < 0);
+            bool work = active && !to_fallback;
+            const int tot = ca + cb;
+            const bool all_in = tot <= K;
+            const size_t orow_id = (size_t)bh * N + (size_t)(fi < N ? fi : 0);
+            float fdelta = 0.f, lo = 0.f;
+            if (work) {
+                fdelta = p.rowinfo[orow_id].y;
+                lo = __uint_as_float(frowbuf[kRowStride - 1].x);
+            }
+            float x[kSubCap];
 #pragma unroll
-                    for (int q = 0; q < kTileN; ++q) {
-                        const int qb2 = q - ca;
-                        x[q] = q < ca ? __uint_as_float(la[q].x)
-                                      : (qb2 < cb ? __uint_as_float(lb2[qb2 < 0 ? 0 : qb2].x) : -INFINITY);
-                    }
-                    // bracket [lo, hi] around the K-th best approximate score
-                    float lo8[8], hi8[8];
+            for (int q = 0; q < kSubCap; ++q) x[q] = (work && q < nown) ? __uint_as_float(own[q].x) : -INFINITY;
+
+            // 1. split at the K-th best approximate score
+            float hi8[8];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        lo8[u] = INFINITY;
-                        hi8[u] = -INFINITY;
-                    }
+            for (int u = 0; u < 8; ++u) hi8[u] = -INFINITY;
 #pragma unroll
-                    for (int q = 0; q < kTileN; ++q) {
-                        lo8[q & 7] = q < tot ? fminf(lo8[q & 7], x[q]) : lo8[q & 7];
-                        hi8[q & 7] = fmaxf(hi8[q & 7], x[q]);
-                    }
-                    float lo = lo8[0], hi = hi8[0];
-#pragma unroll
-                    for (int u = 1; u < 8; ++u) {
-                        lo = fminf(lo, lo8[u]);
-                        hi = fmaxf(hi, hi8[u]);
-                    }
-                    bisect_kth<kTileN>(x, K, fdelta, 20, lo, hi);
-                    const float m2 = 2.f * fdelta + fmaxf(fabsf(lo), fabsf(hi)) * kTwoPowM22;
-                    const float top = hi + m2, bot = lo - m2;
-                    int ni8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, nb8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-                    for (int q = 0; q < kTileN; ++q) {
-                        ni8[q & 7] += x[q] > top ? 1 : 0;
-                        nb8[q & 7] += (x[q] >= bot && x[q] <= top) ? 1 : 0;
-                    }
-                    int n_in = 0, n_band = 0;
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        n_in += ni8[u];
-                        n_band += nb8[u];
-                    }
-                    const int need = K - n_in;
-                    uint32_t sel = 0xffffffffu;
-                    if (n_band != need) {
-                        if (n_band > kMaxBand) {
-                            to_fallback = true;
-                        } else {
-                            // boundary candidates, in ascending key order: canonical
-                            // scores decide, ties to the lower key index
-                            uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)frow * kMaxBand;
-                            const float* qrow = p.qp32 + orow_id * kR;
-                            const float* kbase = p.kp32 + (size_t)(b * Hkv + g) * N * kR;
-                            int nb = 0, ia = 0, ib = 0;
-                            while (ia < ca || ib < cb) {
-                                const bool ta = ib >= cb || (ia < ca && la[ia].y < lb2[ib].y);
-                                const uint2 e = ta ? la[ia++] : lb2[ib++];
-                                const float sq = __uint_as_float(e.x);
-                                if (sq >= bot && sq <= top) {
-                                    const int jj = (int)e.y;
-                                    const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, fi,
-                                                                     jj, p.scale);
-                                    scratch[nb++] = make_uint2(order_key(ex), (uint32_t)jj);
-                                }
-                            }
-                            sel = 0u;
-                            for (int a = 0; a < nb; ++a) {
-                                const uint32_t ka = scratch[a].x;
-                                int rank = 0;
-                                for (int c2 = 0; c2 < nb; ++c2) {
-                                    const uint32_t kc = scratch[c2].x;
-                                    rank += (kc > ka || (kc == ka && c2 < a)) ? 1 : 0;
-                                }
-                                if (rank < need) sel |= 1u << a;
-                            }
-                        }
-                    }
-                    if (!to_fallback) {
-                        int outpos = 0, bidx = 0, ia = 0, ib = 0;
-                        while (ia < ca || ib < cb) {
-                            const bool ta = ib >= cb || (ia < ca && la[ia].y < lb2[ib].y);
-                            const uint2 e = ta ? la[ia++] : lb2[ib++];
-                            const float sq = __uint_as_float(e.x);
-                            const bool inb = sq >= bot && sq <= top;
-                            const bool keep = sq > top || (inb && ((sel >> bidx) & 1u));
-                            bidx += inb ? 1 : 0;
-                            if (keep) orow[outpos++] = (int32_t)e.y;
-                        }
-                        for (int q = outpos; q < K; ++q) orow[q] = -1;
+            for (int q = 0; q < kSubCap; ++q) hi8[q & 7] = fmaxf(hi8[q & 7], x[q]);
+            float hi = fmaxf(fmaxf(fmaxf(hi8[0], hi8[1]), fmaxf(hi8[2], hi8[3])),
+                             fmaxf(fmaxf(hi8[4], hi8[5]), fmaxf(hi8[6], hi8[7])));
+            hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, 1));
+            int cnt_lo = count_ge<kSubCap>(x, lo);
+            cnt_lo += __shfl_xor_sync(kFull, cnt_lo, 1);
+            if (work && !all_in && cnt_lo < K) {
+                to_fallback = true;  // cannot happen: lb is reached by K candidates
+                work = false;
+            }
+            bool done = !work || all_in || cnt_lo == K;
+            for (int it = 0; it < 40; ++it) {
+                if (__all_sync(kFull, done)) break;
+                const float mid = lo + 0.5f * (hi - lo);
+                int c = count_ge<kSubCap>(x, mid);
+                c += __shfl_xor_sync(kFull, c, 1);
+                if (!done) {
+                    if (!(mid > lo && mid < hi)) {
+                        done = true;
+                    } else if (c >= K) {
+                        lo = mid;
+                        cnt_lo = c;
+                        done = c == K;
+                    } else {
+                        hi = mid;
                     }
                 }
             }
-            if (to_fallback) {
+            float kmin8[8], kmax8[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                kmin8[u] = INFINITY;
+                kmax8[u] = -INFINITY;
+            }
+#pragma unroll
+            for (int q = 0; q < kSubCap; ++q) {
+                const bool ge = x[q] >= lo;
+                kmin8[q & 7] = ge ? fminf(kmin8[q & 7], x[q]) : kmin8[q & 7];
+                kmax8[q & 7] = ge ? kmax8[q & 7] : fmaxf(kmax8[q & 7], x[q]);
+            }
+            float xk = kmin8[0], xk1 = kmax8[0];
+#pragma unroll
+            for (int u = 1; u < 8; ++u) {
+                xk = fminf(xk, kmin8[u]);
+                xk1 = fmaxf(xk1, kmax8[u]);
+            }
+            xk = fminf(xk, __shfl_xor_sync(kFull, xk, 1));
+            xk1 = fmaxf(xk1, __shfl_xor_sync(kFull, xk1, 1));
+            float U = -INFINITY, W = INFINITY;  // all_in: keep every entry, empty band
+            if (work && !all_in) {
+                const bool split = cnt_lo == K && xk1 > -INFINITY;
+                const float top = split ? xk1 : hi;
+                const float bot = split ? xk : lo;
+                const float sl = fmaxf(fabsf(top), fabsf(bot));
+                const float m2 = 2.f * fdelta + (sl + 2.f * fdelta) * kTwoPowM22;
+                U = top + m2;
+                W = bot - m2;
+            }
+            int n_in = 0, own_nb = 0;
+            {
+                int ni8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, nb8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+                for (int q = 0; q < kSubCap; ++q) {
+                    ni8[q & 7] += x[q] > U ? 1 : 0;
+                    nb8[q & 7] += (x[q] >= W && x[q] <= U) ? 1 : 0;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    n_in += ni8[u];
+                    own_nb += nb8[u];
+                }
+            }
+            n_in += __shfl_xor_sync(kFull, n_in, 1);
+            const int oth_nb = __shfl_xor_sync(kFull, own_nb, 1);
+            const int need = K - n_in;
+            bool rescore = work && !all_in && own_nb + oth_nb != need;
+            if (rescore && (own_nb > kMaxBand / 2 || oth_nb > kMaxBand / 2)) {
+                to_fallback = true;
+                work = false;
+                rescore = false;
+            }
+
+            // 2. canonical rescoring of the boundary band
+            uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)frow * kMaxBand;  // MMAs are done with sA
+            uint2* myslots = scratch + fh * (kMaxBand / 2);
+            if (rescore) {
+                uint2* wp = myslots;
+#pragma unroll
+                for (int q = 0; q < kSubCap; ++q) {
+                    const bool inb = x[q] >= W && x[q] <= U;
+                    if (inb) *wp = make_uint2((uint32_t)q, 0u);
+                    wp += inb ? 1 : 0;
+                }
+            }
+            const int nbmax = __reduce_max_sync(kFull, rescore ? (unsigned)own_nb : 0u);
+            if (nbmax > 0) {
+                __syncwarp();
+                const float* qrow = p.qp32 + orow_id * kR;
+                const float* kbase = p.kp32 + (size_t)(b * Hkv + g) * N * kR;
+                for (int u = 0; u < nbmax; ++u) {
+                    if (rescore && u < own_nb) {
+                        const int jj = (int)own[myslots[u].x].y;
+                        const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, fi, jj, p.scale);
+                        myslots[u] = make_uint2(order_key(ex), (uint32_t)jj);
+                    }
+                }
+                __syncwarp();
+            }
+            uint32_t selmask = 0u;
+            if (rescore) {
+                const uint2* oslots = scratch + (1 - fh) * (kMaxBand / 2);
+                for (int a2 = 0; a2 < own_nb; ++a2) {
+                    const uint2 ea = myslots[a2];
+                    int rank = 0;
+                    for (int c2 = 0; c2 < own_nb; ++c2) {
+                        const uint2 e = myslots[c2];
+                        rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
+                    }
+                    for (int c2 = 0; c2 < oth_nb; ++c2) {
+                        const uint2 e = oslots[c2];
+                        rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
+                    }
+                    if (rank < need) selmask |= 1u << a2;
+                }
+            }
+
+            // 3. compact kept keys in place, then merge the two lists
+            int nsel = 0;
+            if (work) {
+                uint2* wp = own;
+                int bidx = 0;
+#pragma unroll
+                for (int q = 0; q < kSubCap; ++q) {
+                    // scores re-read from the list: x[] is not kept live across the band work
+                    const uint2 e = own[q];
+                    const float sq = q < nown ? __uint_as_float(e.x) : -INFINITY;
+                    const bool inb = sq >= W && sq <= U;
+                    const bool keep = sq > U || (inb && (!rescore || ((selmask >> bidx) & 1u)));
+                    bidx += inb ? 1 : 0;
+                    if (keep) wp->y = e.y;
+                    wp += keep ? 1 : 0;
+                }
+                nsel = (int)(wp - own);
+            }
+            const int nsel_oth = __shfl_xor_sync(kFull, nsel, 1);
+            __syncwarp();
+            const int nA = fh ? nsel_oth : nsel;
+            const int nB = fh ? nsel : nsel_oth;
+            const int ntot = nA + nB;
+            const int mfront = (ntot + 1) >> 1;
+            const int mcount = fh ? ntot - mfront : mfront;
+            const int steps = (int)__reduce_max_sync(kFull, work ? (unsigned)mcount : 0u);
+            {
+                const uint2* LA = frowbuf;
+                const uint2* LB = frowbuf + kSubCap;
+                const int dir = fh ? -1 : 1;
+                int ia = fh ? nA - 1 : 0, ib = fh ? nB - 1 : 0;
+                // lane 2r takes the smaller key each step, lane 2r+1 the larger:
+                // compare on j for the front and on -j for the back
+                const int sgn = fh ? -1 : 1;
+                int ja = (work && ia >= 0 && ia < nA) ? (int)LA[ia].y : -1;
+                int jb = (work && ib >= 0 && ib < nB) ? (int)LB[ib].y : -1;
+                int32_t* orow = p.out + orow_id * K;
+                for (int st = 0; st < steps; ++st) {
+                    if (work && st < mcount) {
+                        const int ka = ja < 0 ? INT_MAX : sgn * ja;
+                        const int kb = jb < 0 ? INT_MAX : sgn * jb;
+                        const bool ta = ka < kb;
+                        orow[fh ? ntot - 1 - st : st] = ta ? ja : jb;
+                        if (ta) {
+                            ia += dir;
+                            ja = (ia >= 0 && ia < nA) ? (int)LA[ia].y : -1;
+                        } else {
+                            ib += dir;
+                            jb = (ib >= 0 && ib < nB) ? (int)LB[ib].y : -1;
+                        }
+                    }
+                }
+                if (work && fh) {
+                    for (int q = ntot; q < K; ++q) orow[q] = -1;
+                }
+            }
+            if (to_fallback && fh == 0) {
                 const int pos = atomicAdd(p.fb_count, 1);
                 p.fb_list[pos] = (int32_t)orow_id;
             }
