@@ -77,7 +77,9 @@ def select_flops(B, H, Hkv, N, D, r) -> int:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """nvidia-smi clocks/throttle sampling during the timed region: sampling starts
+    before the region (the first sample is awaited, so the region is covered from its
+    start) and only samples taken inside the region are summarised."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -88,28 +90,47 @@ class ClockSampler:
         vis = [x.strip() for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip()]
         self.gpu_index = vis[local_index] if local_index < len(vis) else str(local_index)
         self.proc = None
+        self.lines = []
+        self.samples = []
+
+    def _reader(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.monotonic(), line))
 
     def __enter__(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._reader, daemon=True)
+        self.thread.start()
+        t_wait = time.monotonic()
+        while not self.lines and time.monotonic() - t_wait < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
         self.samples = []
         if self.proc is None:
             return False
+        t1 = time.monotonic()
+        time.sleep(0.06)  # let the sample that covers the end of the region arrive
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=10)
+            self.proc.wait(timeout=10)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
-        for line in out.strip().splitlines():
+            self.proc.wait()
+        self.thread.join(timeout=5)
+        inside = [ln for t, ln in self.lines if self.t0 <= t <= t1 + 0.06]
+        for line in inside:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) == 9:
                 self.samples.append(parts)
@@ -161,6 +182,7 @@ def run_ours(args) -> None:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=dev)
     from ossa_b200 import _lib, router_topk, topk_attention
+    from ossa_b200.host_pipeline import routed_attention_from_host
     from ossa_b200.select import router_topk_with_status
 
     w = WORKLOAD
@@ -212,12 +234,8 @@ def run_ours(args) -> None:
     d2h = oh.numel() * 2
 
     def e2e_step():
-        qd = qh.to(dev, non_blocking=True)
-        kd = kh.to(dev, non_blocking=True)
-        vd = vh.to(dev, non_blocking=True)
-        idx = router_topk(qd, kd, wq, wk, pb, L, K, causal=True)
-        out = topk_attention(qd, kd, vd, topk_indices=idx, causal=True)
-        oh.copy_(out, non_blocking=True)
+        # public host-buffer entry point: chunked H2D / kernels / D2H on three streams
+        routed_attention_from_host(qh, kh, vh, wq, wk, pb, L, K, oh, causal=True, chunk=2)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -249,7 +267,7 @@ def run_ours(args) -> None:
                    "unit": "GB/s", "traffic": traffic.get("gather_attn_fwd")}
     gather_roof["frac"] = gather_roof["achieved"] / gather_roof["peak"]
     select_roof = {"bound": "tensor", "achieved": sflops / sel_avg_s / 1e12, "peak": peaks["bf16_tflops"],
-                   "unit": "TFLOP/s", "traffic": traffic.get("score_topk")}
+                   "unit": "TFLOP/s", "traffic": traffic.get("router_tc")}
     select_roof["frac"] = select_roof["achieved"] / select_roof["peak"]
     dominant = gather_roof if gat_tot >= sel_tot else select_roof
     roof = dict(dominant)
@@ -373,8 +391,8 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)

@@ -99,3 +99,20 @@ def test_select_indices_rejects_unknown_modes():
         select_indices(PatchPlan(mode="bogus", k=4, layers=(0,)), 0, q, q)
     with pytest.raises(KeyError):
         select_indices(PatchPlan(mode="router", k=4, layers=(0,), routers={}), 0, q, q)
+
+
+def test_host_pipeline_argument_checks():
+    from ossa_b200.host_pipeline import routed_attention_from_host
+
+    q = torch.zeros(2, 4, 8, 16, dtype=torch.bfloat16)
+    k = torch.zeros(2, 2, 8, 16, dtype=torch.bfloat16)
+    w = torch.zeros(8, 16)
+    pb = torch.zeros(16, 1)
+    with pytest.raises(ValueError, match="out_host"):
+        routed_attention_from_host(q, k, k, w, w, pb, 8, 4, torch.zeros(2, 4, 8, 16))
+    with pytest.raises(ValueError, match="batch"):
+        routed_attention_from_host(q, k[:1], k[:1], w, w, pb, 8, 4, torch.zeros_like(q))
+    with pytest.raises(ValueError, match="chunk"):
+        routed_attention_from_host(q, k, k, w, w, pb, 8, 4, torch.zeros_like(q), chunk=0)
+    with pytest.raises(ValueError, match="CUDA"):
+        routed_attention_from_host(q, k, k, w, w, pb, 8, 4, torch.zeros_like(q))

@@ -1,0 +1,32 @@
+"""Host-buffer entry point (ossa_b200.host_pipeline): the chunked three-stream
+pipeline returns exactly what the device-tensor API returns for the same
+inputs, for ragged chunking and GQA."""
+
+import pytest
+import torch
+
+from ossa_b200 import router_topk, topk_attention
+from ossa_b200.host_pipeline import routed_attention_from_host
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.mark.parametrize("B,chunk", [(3, 2), (4, 1), (2, 5)])
+def test_host_pipeline_matches_device_path(B, chunk):
+    H, Hkv, N, D, r, K, L = 4, 2, 384, 128, 64, 32, 512
+    g = torch.Generator().manual_seed(B * 10 + chunk)
+    s = D ** -0.5
+    q = (torch.randn(B, H, N, D, generator=g) * s).bfloat16().pin_memory()
+    k = (torch.randn(B, Hkv, N, D, generator=g) * s).bfloat16().pin_memory()
+    v = (torch.randn(B, Hkv, N, D, generator=g) * s).bfloat16().pin_memory()
+    wq = (torch.randn(r, D, generator=g) * 0.1).to(DEV)
+    wk = (torch.randn(r, D, generator=g) * 0.1).to(DEV)
+    pb = torch.randn(2 * L, 1, generator=g).to(DEV)
+    out_h = torch.empty_like(q).pin_memory()
+    routed_attention_from_host(q, k, v, wq, wk, pb, L, K, out_h, chunk=chunk)
+    torch.cuda.current_stream().synchronize()
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    idx = router_topk(qd, kd, wq, wk, pb, L, K)
+    ref = topk_attention(qd, kd, vd, topk_indices=idx, causal=True).cpu()
+    assert torch.equal(out_h, ref)
