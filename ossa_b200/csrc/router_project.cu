@@ -12,6 +12,9 @@
 // shared memory (float4 reads of 4 output columns): two LDS.128 per 16 FFMA.
 // The k projection is GQA-aware by construction: the caller runs it on the Hkv
 // key heads only, never on repeated copies.
+#include <algorithm>
+#include <cstdint>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -129,8 +132,150 @@ project_kernel(const T* __restrict__ x, const float* __restrict__ w, float* __re
     }
 }
 
+// 16-byte asynchronous global->shared copy; src_bytes = 0 zero-fills the slot.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, int src_bytes) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gsrc), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// Persistent variant for D <= 128 with D a multiple of the 16-byte vector: W^T
+// is staged in shared memory once per CTA, and the raw rows of the next tile
+// stream in with cp.async while the current tile is converted and multiplied.
+// Same per-output fmaf chain (d = 0..D-1 from 0.0f) as project_kernel.
+template <typename T, int R>
+__global__ void __launch_bounds__(kProjThreads)
+project_persistent_kernel(const T* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
+                          long long rows, int D, long long ntiles) {
+    constexpr int CG = R / 4;
+    constexpr int RG = kProjThreads / CG;
+    constexpr int ROWS = RG * 4;
+    constexpr int XS = ROWS + 4;
+    constexpr int VEC = ChunkLoader<T>::VEC;
+    constexpr int kStageVecs = ROWS * kDChunk / VEC;  // 16-byte vectors per stage (at D = 128)
+    extern __shared__ float4 smem4[];
+    float* Ws = reinterpret_cast<float*>(smem4);      // [kDChunk][R]
+    float* Xs = Ws + kDChunk * R;                      // [kDChunk][XS]
+    uint4* stage = reinterpret_cast<uint4*>(Xs + kDChunk * XS);  // 2 x [ROWS][D / VEC]
+
+    const int tid = threadIdx.x;
+    const int cg = tid % CG;
+    const int rg = tid / CG;
+    const int nvec = D / VEC;
+
+    auto issue = [&](long long tile, int buf) {
+        const long long row0 = tile * ROWS;
+        uint4* st = stage + (size_t)buf * kStageVecs;
+        for (int e = tid; e < ROWS * nvec; e += kProjThreads) {
+            const int r = e / nvec, v = e - r * nvec;
+            const long long gr = row0 + r;
+            const bool in = gr < rows;
+            const T* src = x + (in ? gr : 0) * (long long)D + v * VEC;
+            cp_async16(st + e, src, in ? 16 : 0);
+        }
+        cp_async_commit();
+    };
+
+    for (int e = tid; e < R * D; e += kProjThreads) {
+        const int d = e / R, c = e - d * R;
+        Ws[d * R + c] = __ldg(w + (size_t)c * D + d);
+    }
+    long long tile = blockIdx.x;
+    int buf = 0;
+    if (tile < ntiles) issue(tile, 0);
+    for (; tile < ntiles; tile += gridDim.x, buf ^= 1) {
+        cp_async_wait_all();
+        __syncthreads();  // stage[buf] landed for all threads; Xs is free again
+        if (tile + gridDim.x < ntiles) issue(tile + gridDim.x, buf ^ 1);
+        const uint4* st = stage + (size_t)buf * kStageVecs;
+        // consecutive threads take consecutive rows: conflict-free transposed stores
+        for (int e = tid; e < ROWS * nvec; e += kProjThreads) {
+            const int v = e / ROWS, r = e - v * ROWS;
+            const uint4 u = st[r * nvec + v];
+            float f[VEC];
+            if constexpr (sizeof(T) == 2) {
+                unpack_bf16x2(u.x, f[0], f[1]);
+                unpack_bf16x2(u.y, f[2], f[3]);
+                unpack_bf16x2(u.z, f[4], f[5]);
+                unpack_bf16x2(u.w, f[6], f[7]);
+            } else {
+                f[0] = __uint_as_float(u.x);
+                f[1] = __uint_as_float(u.y);
+                f[2] = __uint_as_float(u.z);
+                f[3] = __uint_as_float(u.w);
+            }
+#pragma unroll
+            for (int t = 0; t < VEC; ++t) Xs[(v * VEC + t) * XS + r] = f[t];
+        }
+        __syncthreads();
+        float acc[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < D; ++d) {
+            const float4 xv = *reinterpret_cast<const float4*>(Xs + d * XS + rg * 4);
+            const float4 wv = *reinterpret_cast<const float4*>(Ws + d * R + cg * 4);
+            const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+            const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[a][c] = fmaf(xa[a], wa[c], acc[a][c]);
+        }
+        const long long row0 = tile * ROWS;
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const long long gr = row0 + rg * 4 + a;
+            if (gr < rows) {
+                *reinterpret_cast<float4*>(out + gr * R + cg * 4) =
+                    make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+            }
+        }
+    }
+    cp_async_wait_all();
+}
+
+template <typename T, int R>
+constexpr size_t persistent_smem_bytes();
+
+template <typename T, int R>
+cudaError_t launch_persistent(const ProjectArgs& a, cudaStream_t stream) {
+    constexpr int ROWS = (kProjThreads / (R / 4)) * 4;
+    const size_t smem = persistent_smem_bytes<T, R>();
+    auto kern = project_persistent_kernel<T, R>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 0, per_sm = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kProjThreads, smem)) != cudaSuccess)
+        return e;
+    const long long ntiles = (a.rows + ROWS - 1) / ROWS;
+    if (ntiles == 0) return cudaSuccess;
+    const long long grid = std::min<long long>(ntiles, (long long)sms * std::max(1, per_sm));
+    kern<<<(unsigned)grid, kProjThreads, smem, stream>>>(static_cast<const T*>(a.x), a.w, a.out, a.rows, a.D,
+                                                          ntiles);
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) note_launch();
+    return err;
+}
+
+template <typename T, int R>
+constexpr size_t persistent_smem_bytes() {
+    constexpr int ROWS = (kProjThreads / (R / 4)) * 4;
+    return (size_t)kDChunk * R * sizeof(float) + (size_t)kDChunk * (ROWS + 4) * sizeof(float) +
+           2 * (size_t)ROWS * kDChunk / ChunkLoader<T>::VEC * 16;
+}
+
 template <typename T, int R>
 cudaError_t launch_r(const ProjectArgs& a, cudaStream_t stream) {
+    if constexpr (persistent_smem_bytes<T, R>() <= 200 * 1024) {
+        if (a.D <= kDChunk && a.D % ChunkLoader<T>::VEC == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0)
+            return launch_persistent<T, R>(a, stream);
+    }
     constexpr int ROWS = (kProjThreads / (R / 4)) * 4;
     const size_t smem = (size_t)kDChunk * (ROWS + 4) * sizeof(float) + (size_t)kDChunk * R * sizeof(float);
     auto kern = project_kernel<T, R>;

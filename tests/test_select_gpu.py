@@ -64,6 +64,20 @@ def test_router_scores_bit_exact(N, r):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D,r", [(20, 64), (40, 16), (256, 64), (136, 32)])
+def test_router_scores_head_dims(dtype, D, r):
+    """Projection paths: D a multiple of the 16-byte vector and <= 128 (persistent
+    kernel), and D that is not, or is > 128 (chunked kernel)."""
+    B, H, Hkv, N, L = 1, 4, 2, 150, 80
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=D + r)
+    q, k = q.to(dtype), k.to(dtype)
+    wq, wk, pb = _weights(D, r, L, seed=D)
+    got = router_scores(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L)
+    ref = oracle.router_scores(q, k, wq, wk, pb, L)
+    np.testing.assert_array_equal(got.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("B,H,Hkv,N,D,K", [
     (1, 4, 2, 256, 128, 32),
     (1, 12, 2, 700, 128, 128),
