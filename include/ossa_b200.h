@@ -157,6 +157,31 @@ OSSA_API int ossa_router_topk_noalloc(const void* q, const void* k, int dtype,
                                       int K, int causal, int32_t* idx_out,
                                       ossa_stream_t stream);
 
+/*
+ * Query-row ranges for sequence sharding.  No counterpart in the reference,
+ * which runs one process over the whole sequence
+ * (ossa/bench/sparse_forward.py:157-229); these serve a rank that holds a
+ * contiguous block of Nq query rows at positions q_start .. q_start+Nq-1
+ * against all Nk keys of the sequence (k, v gathered from every rank):
+ *   q, indices, out  (B, H, Nq, ...)      k, v  (B, Hkv, Nk, D)
+ * Row l is query position q_start + l in the causal mask (j <= q_start + l)
+ * and in the position bias (offset q_start + l - j).  With Nq == Nk and
+ * q_start == 0 they are ossa_topk_attention_fwd, ossa_router_workspace_size and
+ * ossa_router_topk exactly (those three call them).
+ */
+OSSA_API int ossa_topk_attention_fwd_rows(const void* q, const void* k, const void* v,
+                                          const void* indices, int idx_is_64, int dtype,
+                                          int B, int H, int Hkv, int Nq, int Nk, int D, int K,
+                                          float scale, int causal, int q_start, void* out,
+                                          ossa_stream_t stream);
+OSSA_API size_t ossa_router_workspace_size_rows(int B, int H, int Hkv, int Nq, int Nk, int r, int K);
+OSSA_API int ossa_router_topk_rows(const void* q, const void* k, int dtype,
+                                   const float* wq, const float* wk, const float* pos_bias,
+                                   int B, int H, int Hkv, int Nq, int Nk, int D, int r, int seq_len_cfg,
+                                   int K, int causal, int q_start, int32_t* idx_out,
+                                   void* workspace, size_t workspace_bytes,
+                                   ossa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

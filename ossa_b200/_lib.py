@@ -34,6 +34,9 @@ EXPORTED = (
     "ossa_router_score",
     "ossa_oracle_topk",
     "ossa_router_topk_noalloc",
+    "ossa_topk_attention_fwd_rows",
+    "ossa_router_workspace_size_rows",
+    "ossa_router_topk_rows",
 )
 
 _lock = threading.Lock()
@@ -70,6 +73,12 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ossa_oracle_topk.restype = ci
     lib.ossa_router_topk_noalloc.argtypes = [vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, ci, ci, vp, vp]
     lib.ossa_router_topk_noalloc.restype = ci
+    lib.ossa_topk_attention_fwd_rows.argtypes = [vp, vp, vp, vp] + [ci] * 9 + [cf, ci, ci, vp, vp]
+    lib.ossa_topk_attention_fwd_rows.restype = ci
+    lib.ossa_router_workspace_size_rows.argtypes = [ci] * 7
+    lib.ossa_router_workspace_size_rows.restype = sz
+    lib.ossa_router_topk_rows.argtypes = [vp, vp, ci, vp, vp, vp] + [ci] * 11 + [vp, vp, sz, vp]
+    lib.ossa_router_topk_rows.restype = ci
 
 
 def lib() -> ctypes.CDLL:

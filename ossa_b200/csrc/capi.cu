@@ -73,44 +73,53 @@ struct RouterLayout {
 
 constexpr size_t kCountersBytes = 256;
 
-RouterLayout router_layout(int B, int H, int Hkv, int N, int r) {
+// Nq query rows per (b, h) against Nk keys per (b, kv head).
+RouterLayout router_layout(int B, int H, int Hkv, int Nq, int Nk, int r) {
     RouterLayout l;
-    const size_t qp = (size_t)B * H * N * r * sizeof(float);
-    const size_t kp = (size_t)B * Hkv * N * r * sizeof(float);
+    const size_t qp = (size_t)B * H * Nq * r * sizeof(float);
+    const size_t kp = (size_t)B * Hkv * Nk * r * sizeof(float);
     l.qp_off = kCountersBytes;
     l.kp_off = l.qp_off + align_up(qp);
     l.tc_off = l.kp_off + align_up(kp);
-    l.total = l.tc_off + (r == 64 ? align_up(ossa::router_tc_workspace_bytes(B, H, Hkv, N)) : 0);
+    l.total = l.tc_off + (r == 64 ? align_up(ossa::router_tc_workspace_bytes(B, H, Hkv, Nq, Nk)) : 0);
     return l;
 }
 
-// The tensor-core selector serves r = 64, K <= 96 and at least one full tile of
-// key rows; OSSA_ROUTER_SELECT=exact forces the CUDA-core exact selector (both
-// produce identical indices; the switch exists to cross-check them).
-bool use_tensor_core_select(int B, int Hkv, int N, int r, int K) {
+// The tensor-core selector serves r = 64, K <= 64 and at least one full tile of
+// query and key rows; OSSA_ROUTER_SELECT=exact forces the CUDA-core exact selector
+// (both produce identical indices; the switch exists to cross-check them).
+bool use_tensor_core_select(int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
     const char* env = getenv("OSSA_ROUTER_SELECT");
     if (env && env[0] == 'e') return false;
-    return ossa::router_tc_supported(r, K) && (long long)B * Hkv * N >= 128;
+    return ossa::router_tc_supported(r, K) && (long long)B * Hkv * Nk >= 128 && (long long)B * H * Nq >= 128;
 }
 
 bool supported_r(int r) { return r == 16 || r == 32 || r == 64 || r == 128; }
 
+int check_rows(int Nq, int Nk, int q0) {
+    if (Nq < 0 || q0 < 0 || (long long)q0 + Nq > (1ll << 30))
+        return fail(OSSA_ERR_INVALID, "bad query rows Nq=%d q_start=%d (keys %d)", Nq, q0, Nk);
+    return OSSA_OK;
+}
+
 int check_router(const void* q, const void* k, int dtype, const float* wq, const float* wk,
-                 const float* pos_bias, int B, int H, int Hkv, int N, int D, int r,
+                 const float* pos_bias, int B, int H, int Hkv, int Nq, int Nk, int q0, int D, int r,
                  int seq_len_cfg, const void* out, void* ws, size_t ws_bytes) {
-    int st = check_heads(B, H, Hkv, N);
+    int st = check_heads(B, H, Hkv, Nk);
     if (st) return st;
+    if ((st = check_rows(Nq, Nk, q0))) return st;
     if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);
     if (D <= 0) return fail(OSSA_ERR_INVALID, "bad head_dim D=%d", D);
     if (!supported_r(r)) return fail(OSSA_ERR_UNSUPPORTED, "proj_dim r=%d not in {16,32,64,128}", r);
     if (seq_len_cfg <= 0 || seq_len_cfg > (1 << 28))
         return fail(OSSA_ERR_INVALID, "bad seq_len_cfg %d", seq_len_cfg);
-    if ((long long)B * H * N == 0) return OSSA_OK;
+    if ((long long)B * H * Nq == 0) return OSSA_OK;
+    if (Nk == 0) return fail(OSSA_ERR_INVALID, "query rows need at least one key (Nk=0)");
     if (!q || !k || !wq || !wk || !pos_bias || !out)
         return fail(OSSA_ERR_INVALID, "null pointer argument");
     if (!aligned16(q) || !aligned16(k) || !aligned16(out))
         return fail(OSSA_ERR_INVALID, "q, k and the output must be 16-byte aligned");
-    const RouterLayout l = router_layout(B, H, Hkv, N, r);
+    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r);
     if (!ws || ws_bytes < l.total || !aligned16(ws))
         return fail(OSSA_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required, got %zu",
                     l.total, ws ? ws_bytes : (size_t)0);
@@ -118,16 +127,16 @@ int check_router(const void* q, const void* k, int dtype, const float* wq, const
 }
 
 int project_both(const void* q, const void* k, int dtype, const float* wq, const float* wk,
-                 int B, int H, int Hkv, int N, int D, int r, void* ws, cudaStream_t stream,
+                 int B, int H, int Hkv, int Nq, int Nk, int D, int r, void* ws, cudaStream_t stream,
                  float** qp_out, float** kp_out) {
-    const RouterLayout l = router_layout(B, H, Hkv, N, r);
+    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r);
     char* base = static_cast<char*>(ws);
     float* qp = reinterpret_cast<float*>(base + l.qp_off);
     float* kp = reinterpret_cast<float*>(base + l.kp_off);
-    ossa::ProjectArgs pa{q, wq, qp, (long long)B * H * N, D, r, dtype};
+    ossa::ProjectArgs pa{q, wq, qp, (long long)B * H * Nq, D, r, dtype};
     int st = cuda_status(ossa::launch_project(pa, stream), "q projection launch");
     if (st) return st;
-    ossa::ProjectArgs pk{k, wk, kp, (long long)B * Hkv * N, D, r, dtype};
+    ossa::ProjectArgs pk{k, wk, kp, (long long)B * Hkv * Nk, D, r, dtype};
     st = cuda_status(ossa::launch_project(pk, stream), "k projection launch");
     if (st) return st;
     *qp_out = qp;
@@ -145,26 +154,37 @@ const char* ossa_last_error_string(void) { return g_last_error.c_str(); }
 
 uint64_t ossa_launch_count(void) { return (uint64_t)ossa::g_launches.load(std::memory_order_relaxed); }
 
-int ossa_topk_attention_fwd(const void* q, const void* k, const void* v, const void* indices,
-                            int idx_is_64, int dtype, int B, int H, int Hkv, int N, int D, int K,
-                            float scale, int causal, void* out, ossa_stream_t stream) {
-    int st = check_heads(B, H, Hkv, N);
+int ossa_topk_attention_fwd_rows(const void* q, const void* k, const void* v, const void* indices,
+                                 int idx_is_64, int dtype, int B, int H, int Hkv, int Nq, int Nk, int D, int K,
+                                 float scale, int causal, int q_start, void* out, ossa_stream_t stream) {
+    int st = check_heads(B, H, Hkv, Nk);
     if (st) return st;
+    if ((st = check_rows(Nq, Nk, q_start))) return st;
     if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);
     if (D != 16 && D != 32 && D != 64 && D != 128 && D != 256)
         return fail(OSSA_ERR_UNSUPPORTED, "head_dim D=%d not in {16,32,64,128,256}", D);
     if (K < 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
     if (idx_is_64 != 0 && idx_is_64 != 1) return fail(OSSA_ERR_INVALID, "idx_is_64 must be 0 or 1");
     if (!isfinite(scale)) return fail(OSSA_ERR_INVALID, "scale must be finite");
-    if ((long long)B * H * N == 0) return OSSA_OK;
+    if ((long long)B * H * Nq == 0) return OSSA_OK;
+    if (Nk == 0) return fail(OSSA_ERR_INVALID, "query rows need at least one key (Nk=0)");
     if (!q || !k || !v || !out || (K > 0 && !indices))
         return fail(OSSA_ERR_INVALID, "null pointer argument");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
         return fail(OSSA_ERR_INVALID, "q, k, v and out must be 16-byte aligned");
     if (K > 0 && !aligned16(indices)) return fail(OSSA_ERR_INVALID, "indices must be 16-byte aligned");
-    ossa::GatherArgs a{q, k, v, indices, out, idx_is_64, dtype, B, H, Hkv, N, D, K, scale, causal ? 1 : 0};
+    ossa::GatherArgs a{q, k, v, indices, out, idx_is_64, dtype, B, H, Hkv, Nk, D, K, scale, causal ? 1 : 0};
+    a.Nq = Nq;
+    a.q0 = q_start;
     return cuda_status(ossa::launch_gather_attn(a, static_cast<cudaStream_t>(stream)),
                        "topk attention launch");
+}
+
+int ossa_topk_attention_fwd(const void* q, const void* k, const void* v, const void* indices,
+                            int idx_is_64, int dtype, int B, int H, int Hkv, int N, int D, int K,
+                            float scale, int causal, void* out, ossa_stream_t stream) {
+    return ossa_topk_attention_fwd_rows(q, k, v, indices, idx_is_64, dtype, B, H, Hkv, N, N, D, K, scale, causal,
+                                        0, out, stream);
 }
 
 int ossa_router_status(const void* workspace, int* fallback_rows, int* status) {
@@ -177,53 +197,69 @@ int ossa_router_status(const void* workspace, int* fallback_rows, int* status) {
     return OSSA_OK;
 }
 
-size_t ossa_router_workspace_size(int B, int H, int Hkv, int N, int r, int K) {
+size_t ossa_router_workspace_size_rows(int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
     (void)K;
-    if (B < 0 || H <= 0 || Hkv <= 0 || N < 0 || r <= 0) return 0;
-    return router_layout(B, H, Hkv, N, r).total;
+    if (B < 0 || H <= 0 || Hkv <= 0 || Nq < 0 || Nk < 0 || r <= 0) return 0;
+    return router_layout(B, H, Hkv, Nq, Nk, r).total;
+}
+
+size_t ossa_router_workspace_size(int B, int H, int Hkv, int N, int r, int K) {
+    return ossa_router_workspace_size_rows(B, H, Hkv, N, N, r, K);
+}
+
+int ossa_router_topk_rows(const void* q, const void* k, int dtype, const float* wq, const float* wk,
+                          const float* pos_bias, int B, int H, int Hkv, int Nq, int Nk, int D, int r,
+                          int seq_len_cfg, int K, int causal, int q_start, int32_t* idx_out, void* workspace,
+                          size_t workspace_bytes, ossa_stream_t stream) {
+    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, Nq, Nk, q_start, D, r, seq_len_cfg, idx_out,
+                          workspace, workspace_bytes);
+    if (st) return st;
+    if (K <= 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
+    if (!ossa::score_topk_supported(r, K))
+        return fail(OSSA_ERR_UNSUPPORTED, "top-K selection supports K <= 160 (got K=%d)", K);
+    if ((long long)B * H * Nq == 0) return OSSA_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    st = cuda_status(cudaMemsetAsync(workspace, 0, kCountersBytes, s), "workspace counters reset");
+    if (st) return st;
+    float *qp = nullptr, *kp = nullptr;
+    st = project_both(q, k, dtype, wq, wk, B, H, Hkv, Nq, Nk, D, r, workspace, s, &qp, &kp);
+    if (st) return st;
+    const float scale = (float)(1.0 / sqrt((double)r));
+    if (use_tensor_core_select(B, H, Hkv, Nq, Nk, r, K)) {
+        const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r);
+        ossa::RouterTcArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, Nk, K, causal ? 1 : 0, scale,
+                             idx_out, static_cast<char*>(workspace) + l.tc_off,
+                             reinterpret_cast<int*>(workspace)};
+        a.Nq = Nq;
+        a.q0 = q_start;
+        return cuda_status(ossa::launch_router_tc(a, s), "tensor-core router top-K launch");
+    }
+    ossa::ScoreTopkArgs a{qp, kp, ossa::kF32, pos_bias, seq_len_cfg, B, H, Hkv, Nk, r, K, scale,
+                          causal ? 1 : 0, idx_out};
+    a.Nq = Nq;
+    a.q0 = q_start;
+    return cuda_status(ossa::launch_score_topk(a, s), "router top-K launch");
 }
 
 int ossa_router_topk(const void* q, const void* k, int dtype, const float* wq, const float* wk,
                      const float* pos_bias, int B, int H, int Hkv, int N, int D, int r,
                      int seq_len_cfg, int K, int causal, int32_t* idx_out, void* workspace,
                      size_t workspace_bytes, ossa_stream_t stream) {
-    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, D, r, seq_len_cfg, idx_out,
-                          workspace, workspace_bytes);
-    if (st) return st;
-    if (K <= 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
-    if (!ossa::score_topk_supported(r, K))
-        return fail(OSSA_ERR_UNSUPPORTED, "top-K selection supports K <= 160 (got K=%d)", K);
-    if ((long long)B * H * N == 0) return OSSA_OK;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    st = cuda_status(cudaMemsetAsync(workspace, 0, kCountersBytes, s), "workspace counters reset");
-    if (st) return st;
-    float *qp = nullptr, *kp = nullptr;
-    st = project_both(q, k, dtype, wq, wk, B, H, Hkv, N, D, r, workspace, s, &qp, &kp);
-    if (st) return st;
-    const float scale = (float)(1.0 / sqrt((double)r));
-    if (use_tensor_core_select(B, Hkv, N, r, K)) {
-        const RouterLayout l = router_layout(B, H, Hkv, N, r);
-        ossa::RouterTcArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, N, K, causal ? 1 : 0, scale,
-                             idx_out, static_cast<char*>(workspace) + l.tc_off,
-                             reinterpret_cast<int*>(workspace)};
-        return cuda_status(ossa::launch_router_tc(a, s), "tensor-core router top-K launch");
-    }
-    ossa::ScoreTopkArgs a{qp, kp, ossa::kF32, pos_bias, seq_len_cfg, B, H, Hkv, N, r, K, scale,
-                          causal ? 1 : 0, idx_out};
-    return cuda_status(ossa::launch_score_topk(a, s), "router top-K launch");
+    return ossa_router_topk_rows(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, N, D, r, seq_len_cfg, K, causal, 0,
+                                 idx_out, workspace, workspace_bytes, stream);
 }
 
 int ossa_router_score(const void* q, const void* k, int dtype, const float* wq, const float* wk,
                       const float* pos_bias, int B, int H, int Hkv, int N, int D, int r,
                       int seq_len_cfg, float* scores_out, void* workspace, size_t workspace_bytes,
                       ossa_stream_t stream) {
-    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, D, r, seq_len_cfg,
+    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, N, 0, D, r, seq_len_cfg,
                           scores_out, workspace, workspace_bytes);
     if (st) return st;
     if ((long long)B * H * N == 0) return OSSA_OK;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     float *qp = nullptr, *kp = nullptr;
-    st = project_both(q, k, dtype, wq, wk, B, H, Hkv, N, D, r, workspace, s, &qp, &kp);
+    st = project_both(q, k, dtype, wq, wk, B, H, Hkv, N, N, D, r, workspace, s, &qp, &kp);
     if (st) return st;
     ossa::ScoreDenseArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, N, r,
                            (float)(1.0 / sqrt((double)r)), scores_out};

@@ -52,7 +52,7 @@ template <typename T, int D, typename IdxT>
 __global__ void __launch_bounds__(kGatherThreads)
 gather_attn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k,
                        const T* __restrict__ v, const IdxT* __restrict__ idx,
-                       T* __restrict__ out, int H, int Hkv, int N, int K,
+                       T* __restrict__ out, int H, int Hkv, int N, int Nq, int q0, int K,
                        float scale_log2, int causal, int qtile) {
     constexpr int DPL = D >= 32 ? D / 32 : 1;  // dims owned by one lane
     constexpr int ACTIVE = D / DPL;            // lanes that own dims
@@ -63,7 +63,7 @@ gather_attn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k,
     const int b = bg / Hkv;
     const int g = bg - b * Hkv;
     const int i0 = blockIdx.x * qtile;
-    const int nq = min(qtile, N - i0);
+    const int nq = min(qtile, Nq - i0);
     const int items = nq * G;
     const bool dim_lane = lane < ACTIVE;
 
@@ -74,9 +74,10 @@ gather_attn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k,
     const T* vb = v + (size_t)bg * N * D + lane * DPL;
 
     for (int w = warp; w < items; w += kGatherWarps) {
-        const int i = i0 + w / G;
+        const int il = i0 + w / G;  // query row (local); its key-sequence position is q0 + il
+        const int i = q0 + il;
         const int h = g * G + (w - (w / G) * G);
-        const size_t row = ((size_t)b * H + h) * N + i;
+        const size_t row = ((size_t)b * H + h) * Nq + il;
 
         float qv[DPL];
         if (dim_lane) {
@@ -203,8 +204,8 @@ template <typename IdxT>
 __global__ void __launch_bounds__(kGatherThreads)
 gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                              const __nv_bfloat16* __restrict__ v, const IdxT* __restrict__ idx,
-                             __nv_bfloat16* __restrict__ out, int H, int Hkv, int N, int K,
-                             float scale_log2, int causal, int qtile) {
+                             __nv_bfloat16* __restrict__ out, int H, int Hkv, int N, int Nq, int q0,
+                             int K, float scale_log2, int causal, int qtile) {
     constexpr int D = 128;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -215,7 +216,7 @@ gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
     const int b = bg / Hkv;
     const int g = bg - b * Hkv;
     const int i0 = blockIdx.x * qtile;
-    const int nq = min(qtile, N - i0);
+    const int nq = min(qtile, Nq - i0);
     const int items = nq * G;
     const uint4* kb = reinterpret_cast<const uint4*>(k + (size_t)bg * N * D) + hl;
     const uint4* vb = reinterpret_cast<const uint4*>(v + (size_t)bg * N * D) + hl;
@@ -223,9 +224,10 @@ gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
     const int myslot = 2 * hl + half;
 
     for (int w = warp; w < items; w += kGatherWarps) {
-        const int i = i0 + w / G;
+        const int il = i0 + w / G;  // query row (local); its key-sequence position is q0 + il
+        const int i = q0 + il;
         const int h = g * G + (w - (w / G) * G);
-        const size_t row = ((size_t)b * H + h) * N + i;
+        const size_t row = ((size_t)b * H + h) * Nq + il;
         const uint4 qv = __ldg(reinterpret_cast<const uint4*>(q + row * D) + hl);
         const IdxT* irow = idx + row * K;
         float m_run = -INFINITY, l_run = 0.f;
@@ -302,7 +304,8 @@ gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
 template <typename T, typename IdxT>
 cudaError_t launch_typed(const GatherArgs& a, cudaStream_t stream) {
     const int qtile = 8;
-    dim3 grid((a.N + qtile - 1) / qtile, a.B * a.Hkv);
+    const int Nq = a.Nq > 0 ? a.Nq : a.N;
+    dim3 grid((Nq + qtile - 1) / qtile, a.B * a.Hkv);
     dim3 block(kGatherThreads);
     const float scale_log2 = a.scale * 1.4426950408889634f;
     const T* q = static_cast<const T*>(a.q);
@@ -312,8 +315,8 @@ cudaError_t launch_typed(const GatherArgs& a, cudaStream_t stream) {
     T* o = static_cast<T*>(a.out);
     if constexpr (sizeof(T) == 2) {
         if (a.D == 128) {
-            gather_attn_bf16_d128_kernel<IdxT><<<grid, block, 0, stream>>>(q, k, v, ix, o, a.H, a.Hkv, a.N, a.K,
-                                                                          scale_log2, a.causal, qtile);
+            gather_attn_bf16_d128_kernel<IdxT><<<grid, block, 0, stream>>>(q, k, v, ix, o, a.H, a.Hkv, a.N, Nq,
+                                                                          a.q0, a.K, scale_log2, a.causal, qtile);
             cudaError_t e = cudaGetLastError();
             if (e == cudaSuccess) note_launch();
             return e;
@@ -323,7 +326,7 @@ cudaError_t launch_typed(const GatherArgs& a, cudaStream_t stream) {
 #define OSSA_GATHER_CASE(DD)                                                              \
     case DD:                                                                              \
         gather_attn_fwd_kernel<T, DD, IdxT><<<grid, block, 0, stream>>>(                  \
-            q, k, v, ix, o, a.H, a.Hkv, a.N, a.K, scale_log2, a.causal, qtile);           \
+            q, k, v, ix, o, a.H, a.Hkv, a.N, Nq, a.q0, a.K, scale_log2, a.causal, qtile); \
         break;
         OSSA_GATHER_CASE(16)
         OSSA_GATHER_CASE(32)

@@ -26,6 +26,8 @@ struct GatherArgs {
     int B, H, Hkv, N, D, K;
     float scale;
     int causal;
+    int Nq = 0;  // query rows per (b, h); 0 means N (queries are the keys' positions)
+    int q0 = 0;  // position of query row 0 in the key sequence
 };
 cudaError_t launch_gather_attn(const GatherArgs& a, cudaStream_t stream);
 
@@ -51,7 +53,9 @@ struct ScoreTopkArgs {
     int B, H, Hkv, N, R, K;
     float scale;
     int causal;
-    int32_t* out;  // (B*H*N, K)
+    int32_t* out;  // (B*H*Nq, K)
+    int Nq = 0;    // query rows per (b, h); 0 means N (queries are the keys' positions)
+    int q0 = 0;    // position of query row 0 in the key sequence
 };
 cudaError_t launch_score_topk(const ScoreTopkArgs& a, cudaStream_t stream);
 bool score_topk_supported(int R, int K);
@@ -86,9 +90,11 @@ struct RouterTcArgs {
     int32_t* out;
     void* ws;
     int* counters;
+    int Nq = 0;  // query rows per (b, h); 0 means N (queries are the keys' positions)
+    int q0 = 0;  // position of query row 0 in the key sequence
 };
 bool router_tc_supported(int r, int K);
-size_t router_tc_workspace_bytes(int B, int H, int Hkv, int N);
+size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N);
 cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream);
 
 }  // namespace ossa

@@ -163,11 +163,11 @@ __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict
 
 // One thread per query row: scaled fp16 row, epilogue multiplier and error bound.
 __global__ void qprep_kernel(const float* __restrict__ qp, __half* __restrict__ q16, float2* __restrict__ rowinfo,
-                             long long rows, int H, int Hkv, int N, float scale,
+                             long long rows, int H, int Hkv, int Nq, float scale,
                              const uint32_t* __restrict__ stats, const uint32_t* __restrict__ gstats) {
     const long long row = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= rows) return;
-    const long long bh = row / N;
+    const long long bh = row / Nq;
     const int b = (int)(bh / H);
     const int h = (int)(bh - (long long)b * H);
     const int bg = b * Hkv + h / (H / Hkv);
@@ -225,6 +225,7 @@ struct TcParams {
     int32_t* fb_list;
     int* status;
     int L, H, Hkv, N, K, causal, nqb;
+    int Nq, q0;  // query rows per (b, h) and the key-sequence position of row 0
     float scale;
 };
 
@@ -336,7 +337,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint64_t* mdone = tempty + kAccBufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffSlot);
 
-    const int N = p.N, H = p.H, Hkv = p.Hkv;
+    const int N = p.N, H = p.H, Hkv = p.Hkv, Nq = p.Nq;
     const int BH = gridDim.x / p.nqb;
     const int order = blockIdx.x / BH;
     const int bh = blockIdx.x - order * BH;
@@ -344,8 +345,9 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const int b = bh / H;
     const int h = bh - b * H;
     const int g = h / (H / Hkv);
-    const int i0 = qb * kTileM;
-    const int jend = p.causal ? min(N, i0 + kTileM) : N;
+    const int i0 = qb * kTileM;     // first query row of the block (local index)
+    const int i0g = p.q0 + i0;      // its position in the key sequence
+    const int jend = p.causal ? min(N, i0g + kTileM) : N;
     const int T = (jend + kTileN - 1) / kTileN;  // key tiles per pass
     const int T2 = 2 * T;                          // two passes over the same key tiles
     const int warp = threadIdx.x >> 5;
@@ -378,7 +380,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         if (lane == 0) {
             bool ok = true;
             mbar_arrive_expect_tx(afull, kTileBytes);
-            tma_load_2d(sA, &tmA, afull, 0, bh * N + i0);
+            tma_load_2d(sA, &tmA, afull, 0, bh * Nq + i0);
             const int krow0 = (b * Hkv + g) * N;
             int issued = 0;
             for (int t = 0; t < T2; ++t) {
@@ -430,15 +432,15 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         const int hf = ew >> 2;              // column half
         const int r0 = qd * 32;
         const int row = r0 + lane;
-        const int i = i0 + row;
+        const int i = i0 + row;              // local query row
         const int K = p.K;
         const int L = p.L;
         const int cbase = hf * kHalfCols;    // first tile column of this thread
         const uint32_t pair_bar = 1u + (uint32_t)qd;  // named barrier of the quadrant's two warps
         float m = 0.f, delta = 0.f;
-        bool fb = i >= N;  // rows to skip (inactive) or to recompute exactly
-        if (i < N) {
-            const float2 ri = p.rowinfo[(size_t)bh * N + i];
+        bool fb = i >= Nq;  // rows to skip (inactive) or to recompute exactly
+        if (i < Nq) {
+            const float2 ri = p.rowinfo[(size_t)bh * Nq + i];
             m = ri.x;
             delta = ri.y;
             if (!(m == m)) fb = true;
@@ -448,11 +450,11 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         float* wcp = win + ew * 4 * kWinCopy;
         const int s4 = lane & 3;
         const float* mycopy = wcp + s4 * kWinCopy + (lane - s4) + (kHalfCols - 4);
-        const int lim = p.causal ? min(N, i + 1) : N;  // keys j < lim are eligible
+        const int lim = p.causal ? min(N, p.q0 + i + 1) : N;  // keys j < lim are eligible
         bool ok = true;
 
         // Tile prologue shared by both passes: stage this warp's pos_bias window
-        // (copy s holds w[y + s], w[x] = bias[clamp(i0 + r0 - j0 - 63 - cbase + x + L)],
+        // (copy s holds w[y + s], w[x] = bias[clamp(i0g + r0 - j0 - 63 - cbase + x + L)],
         // so column c of row lane reads w[lane - (c - cbase) + 63]) and wait for the
         // tile's accumulator.  Returns false if the bounded wait expired.
         // The bias values of tile t + 1 are fetched from global memory while tile
@@ -460,7 +462,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         constexpr int kWinVals = (kWinLen + 3 + 31) / 32;
         float wv[kWinVals];
         auto fetch_window = [&](int j0) {
-            const int obase = i0 + r0 - j0 - (kHalfCols - 1) - cbase + L;
+            const int obase = i0g + r0 - j0 - (kHalfCols - 1) - cbase + L;
 #pragma unroll
             for (int u = 0; u < kWinVals; ++u) {
                 int bi = obase + lane + 32 * u;
@@ -695,7 +697,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const int frow = r0 + 16 * hf + (lane >> 1);
             const int fh = lane & 1;
             const int fi = i0 + frow;
-            const bool active = ok && fi < N;
+            const bool active = ok && fi < Nq;
             const int ca = qmeta[2 * (frow - r0)], cb = qmeta[2 * (frow - r0) + 1];
             uint2* frowbuf = buf + (size_t)frow * kRowStride;
             uint2* own = frowbuf + fh * kSubCap;
@@ -704,7 +706,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             bool work = active && !to_fallback;
             const int tot = ca + cb;
             const bool all_in = tot <= K;
-            const size_t orow_id = (size_t)bh * N + (size_t)(fi < N ? fi : 0);
+            const size_t orow_id = (size_t)bh * Nq + (size_t)(fi < Nq ? fi : 0);
             float fdelta = 0.f, lo = 0.f;
             if (work) {
                 fdelta = p.rowinfo[orow_id].y;
@@ -821,7 +823,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 for (int u = 0; u < nbmax; ++u) {
                     if (rescore && u < own_nb) {
                         const int jj = (int)own[myslots[u].x].y;
-                        const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, fi, jj, p.scale);
+                        const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, p.q0 + fi, jj,
+                                                                     p.scale);
                         myslots[u] = make_uint2(order_key(ex), (uint32_t)jj);
                     }
                 }
@@ -923,7 +926,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 template <int EPL>
 __global__ void __launch_bounds__(256)
 exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, const float* __restrict__ bias,
-                  int L, int H, int Hkv, int N, int K, float scale, int causal, const int* __restrict__ fb_count,
+                  int L, int H, int Hkv, int N, int Nq, int q0, int K, float scale, int causal,
+                  const int* __restrict__ fb_count,
                   const int32_t* __restrict__ fb_list, int32_t* __restrict__ out) {
     constexpr int CAP = 32 * EPL;
     __shared__ uint2 sbuf[8][CAP];
@@ -934,14 +938,14 @@ exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, co
     uint2* wb = sbuf[warp];
     for (int idx = blockIdx.x * 8 + warp; idx < total; idx += gridDim.x * 8) {
         const long long row = fb_list[idx];
-        const long long bh = row / N;
-        const int i = (int)(row - bh * N);
+        const long long bh = row / Nq;
+        const int i = q0 + (int)(row - bh * Nq);  // position in the key sequence
         const int b = (int)(bh / H);
         const int h = (int)(bh - (long long)b * H);
         const int g = h / (H / Hkv);
         const float* qrow = qp + row * kR;
         const float* kbase = kp + (size_t)(b * Hkv + g) * N * kR;
-        const int n = causal ? i + 1 : N;
+        const int n = causal ? min(i + 1, N) : N;
         uint32_t theta = 0u;
         int cnt = 0;
         for (int j0 = 0; j0 < n; j0 += 32) {
@@ -1049,16 +1053,17 @@ cudaError_t record(cudaError_t e) {
 
 bool router_tc_supported(int r, int K) { return r == kR && K >= 1 && K <= kMaxK; }
 
-size_t router_tc_workspace_bytes(int B, int H, int Hkv, int N) {
+size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N) {
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
-    const size_t rq = (size_t)B * H * N, rk = (size_t)B * Hkv * N;
+    const size_t rq = (size_t)B * H * Nq, rk = (size_t)B * Hkv * N;
     return al(rq * kR * 2) + al(rk * kR * 2) + al(rq * sizeof(float2)) + al((3 * (size_t)B * Hkv + 2) * 4) +
            al(rq * 4);
 }
 
 cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
-    const size_t rq = (size_t)a.B * a.H * a.N, rk = (size_t)a.B * a.Hkv * a.N;
+    const int Nq = a.Nq > 0 ? a.Nq : a.N;
+    const size_t rq = (size_t)a.B * a.H * Nq, rk = (size_t)a.B * a.Hkv * a.N;
     char* w = static_cast<char*>(a.ws);
     __half* q16 = reinterpret_cast<__half*>(w);
     w += al(rq * kR * 2);
@@ -1086,7 +1091,7 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
         kconvert_kernel<<<g2, 256, 0, stream>>>(a.kp32, k16, a.N, stats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
         qprep_kernel<<<(unsigned)((rq + 127) / 128), 128, 0, stream>>>(a.qp32, q16, rowinfo, (long long)rq, a.H,
-                                                                      a.Hkv, a.N, a.scale, stats, gstats);
+                                                                      a.Hkv, Nq, a.scale, stats, gstats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     }
     CUtensorMap tmA, tmB;
@@ -1108,13 +1113,15 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.N = a.N;
     prm.K = a.K;
     prm.causal = a.causal;
-    prm.nqb = (a.N + kTileM - 1) / kTileM;
+    prm.Nq = Nq;
+    prm.q0 = a.q0;
+    prm.nqb = (Nq + kTileM - 1) / kTileM;
     prm.scale = a.scale;
     const long long nblk = (long long)prm.nqb * a.B * a.H;
     router_tc_kernel<<<(unsigned)nblk, kThreads, kSmemBytes, stream>>>(tmA, tmB, prm);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-    exact_rows_kernel<4><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, a.K, a.scale,
-                                                      a.causal, counters, fb_list, a.out);
+    exact_rows_kernel<4><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0, a.K,
+                                                      a.scale, a.causal, counters, fb_list, a.out);
     return record(cudaGetLastError());
 }
 

@@ -88,7 +88,7 @@ __device__ __forceinline__ void warp_compact_row(uint2* rowbuf, int rot, int cnt
 template <int R, typename KT, bool BIAS, int EPL>
 __global__ void __launch_bounds__(kRows, 1)
 score_topk_kernel(const KT* __restrict__ qrows, const KT* __restrict__ krows,
-                  const float* __restrict__ bias, int L, int H, int Hkv, int N, int K,
+                  const float* __restrict__ bias, int L, int H, int Hkv, int N, int Nq, int q0, int K,
                   float scale, int causal, int32_t* __restrict__ out, int nqb) {
     constexpr int CAP = 32 * EPL;
     constexpr int KS = R + 4;  // padded key-row stride in shared memory (float4 aligned)
@@ -105,13 +105,14 @@ score_topk_kernel(const KT* __restrict__ qrows, const KT* __restrict__ krows,
     const int g = h / (H / Hkv);
     const int tid = threadIdx.x;
     const int lane = tid & 31;
-    const int i0 = qb * kRows;
-    const int i = i0 + tid;
-    const bool active = i < N;
+    const int i0 = qb * kRows;          // first query row of the block (local)
+    const int il = i0 + tid;
+    const bool active = il < Nq;
+    const int i = q0 + il;              // its position in the key sequence
 
     float a[R];
     {
-        const KT* qp = qrows + ((size_t)bh * N + (active ? i : 0)) * R;
+        const KT* qp = qrows + ((size_t)bh * Nq + (active ? il : 0)) * R;
 #pragma unroll
         for (int c = 0; c < R; ++c) a[c] = active ? to_f32(qp[c]) : 0.f;
     }
@@ -121,7 +122,7 @@ score_topk_kernel(const KT* __restrict__ qrows, const KT* __restrict__ krows,
 
     uint32_t theta = 0u;  // order key threshold; 0 admits every real score
     int cnt = 0;
-    const int jend = causal ? min(N, i0 + kRows) : N;
+    const int jend = causal ? min(N, q0 + i0 + kRows) : N;
 
     for (int j0 = 0; j0 < jend; j0 += kKeyTile) {
         __syncthreads();
@@ -189,7 +190,7 @@ score_topk_kernel(const KT* __restrict__ qrows, const KT* __restrict__ krows,
     const int wbase = tid & ~31;
     for (int src = 0; src < 32; ++src) {
         const int row_i = i0 + wbase + src;
-        if (row_i >= N) break;  // warp-uniform
+        if (row_i >= Nq) break;  // warp-uniform
         int scnt = __shfl_sync(kFull, cnt, src);
         const int srot = __shfl_sync(kFull, rot, src);
         uint2* sbuf = buf + (size_t)(wbase + src) * CAP;
@@ -199,7 +200,7 @@ score_topk_kernel(const KT* __restrict__ qrows, const KT* __restrict__ krows,
             warp_compact_row<EPL>(sbuf, srot, scnt, K, lane, nt, nc);
             scnt = nc;
         }
-        int32_t* orow = out + ((size_t)bh * N + row_i) * K;
+        int32_t* orow = out + ((size_t)bh * Nq + row_i) * K;
         for (int p = lane; p < K; p += 32) {
             int32_t jv = -1;
             if (p < scnt) {
@@ -220,12 +221,13 @@ cudaError_t launch_cfg(const ScoreTopkArgs& a, cudaStream_t stream) {
     auto kern = score_topk_kernel<R, KT, BIAS, EPL>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const int nqb = (a.N + kRows - 1) / kRows;
+    const int Nq = a.Nq > 0 ? a.Nq : a.N;
+    const int nqb = (Nq + kRows - 1) / kRows;
     const long long nblk = (long long)nqb * a.B * a.H;
     if (nblk == 0) return cudaSuccess;
     kern<<<(unsigned)nblk, kRows, smem, stream>>>(
         static_cast<const KT*>(a.qrows), static_cast<const KT*>(a.krows), a.bias, a.L,
-        a.H, a.Hkv, a.N, a.K, a.scale, a.causal, a.out, nqb);
+        a.H, a.Hkv, a.N, Nq, a.q0, a.K, a.scale, a.causal, a.out, nqb);
     cudaError_t err = cudaGetLastError();
     if (err == cudaSuccess) note_launch();
     return err;

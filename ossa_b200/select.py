@@ -18,17 +18,19 @@ from __future__ import annotations
 import ctypes
 import math
 
+from typing import Optional
+
 import torch
 
 from . import _lib
 
 
-def _check_qk(q: torch.Tensor, k: torch.Tensor):
+def _check_qk(q: torch.Tensor, k: torch.Tensor, rows: bool = False):
     if q.dim() != 4 or k.dim() != 4:
         raise ValueError(f"q and k must be (B, H, N, D); got {tuple(q.shape)} and {tuple(k.shape)}")
     B, H, N, D = q.shape
     Bk, Hkv, Nk, Dk = k.shape
-    if (B, N, D) != (Bk, Nk, Dk):
+    if (B, D) != (Bk, Dk) or (not rows and N != Nk):
         raise ValueError(f"q {tuple(q.shape)} and k {tuple(k.shape)} disagree on B, N or D")
     if Hkv <= 0 or H % Hkv != 0:
         raise ValueError(f"query heads {H} must be a multiple of key heads {Hkv}")
@@ -47,14 +49,19 @@ def _common_dtype(q: torch.Tensor, k: torch.Tensor) -> torch.dtype:
 
 def router_topk(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,
                 pos_bias: torch.Tensor, seq_len: int, top_k: int, *,
-                causal: bool = True) -> torch.Tensor:
+                causal: bool = True, q_start: Optional[int] = None) -> torch.Tensor:
     """ContentRouter top-K (router.py:171-190 scores) -> int32 (B, H, N, top_k).
 
     q: (B, H, N, D); k: (B, Hkv, N, D) with Hkv dividing H (or the repeated H
     heads).  wq, wk: (r, D) projection weights; pos_bias: (2*seq_len, 1) or
     (2*seq_len,).  Scores and selection are fp32.
+
+    ``q_start`` (additive, for sequence sharding): q then holds Nq query rows at
+    positions q_start .. q_start + Nq - 1 against all Nk keys of k; positions
+    enter the causal mask and the position bias.  The result is (B, H, Nq, top_k)
+    and equals the matching rows of the unsharded call.
     """
-    return _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, causal=causal)[0]
+    return _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, causal=causal, q_start=q_start)[0]
 
 
 def router_topk_with_status(q, k, wq, wk, pos_bias, seq_len: int, top_k: int, *, causal: bool = True):
@@ -64,8 +71,12 @@ def router_topk_with_status(q, k, wq, wk, pos_bias, seq_len: int, top_k: int, *,
     return _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, causal=causal, with_status=True)
 
 
-def _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, *, causal=True, with_status=False):
-    B, H, Hkv, N, D = _check_qk(q, k)
+def _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, *, causal=True, with_status=False, q_start=None):
+    B, H, Hkv, N, D = _check_qk(q, k, rows=q_start is not None)
+    Nk = k.shape[2]
+    q0 = 0 if q_start is None else int(q_start)
+    if q0 < 0:
+        raise ValueError(f"q_start must be >= 0, got {q0}")
     dev = _lib.require_cuda(q, k, wq, wk, pos_bias)
     r = wq.shape[0]
     if wq.shape != (r, D) or wk.shape != (r, D):
@@ -84,13 +95,19 @@ def _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, *, causal=True, with_st
     wkc = wk.detach().float().contiguous()
     pbc = pos_bias.detach().float().contiguous()
     L = _lib.lib()
-    ws_bytes = L.ossa_router_workspace_size(B, H, Hkv, N, r, top_k)
+    ws_bytes = L.ossa_router_workspace_size_rows(B, H, Hkv, N, Nk, r, top_k)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        st = L.ossa_router_topk(qc.data_ptr(), kc.data_ptr(), _lib.dtype_code(qc), wqc.data_ptr(),
-                                wkc.data_ptr(), pbc.data_ptr(), B, H, Hkv, N, D, r, int(seq_len),
-                                int(top_k), 1 if causal else 0, out.data_ptr(), ws.data_ptr(),
-                                ws_bytes, _lib.stream_ptr(dev))
+        if q_start is None:
+            st = L.ossa_router_topk(qc.data_ptr(), kc.data_ptr(), _lib.dtype_code(qc), wqc.data_ptr(),
+                                    wkc.data_ptr(), pbc.data_ptr(), B, H, Hkv, N, D, r, int(seq_len),
+                                    int(top_k), 1 if causal else 0, out.data_ptr(), ws.data_ptr(),
+                                    ws_bytes, _lib.stream_ptr(dev))
+        else:
+            st = L.ossa_router_topk_rows(qc.data_ptr(), kc.data_ptr(), _lib.dtype_code(qc), wqc.data_ptr(),
+                                         wkc.data_ptr(), pbc.data_ptr(), B, H, Hkv, N, Nk, D, r, int(seq_len),
+                                         int(top_k), 1 if causal else 0, q0, out.data_ptr(), ws.data_ptr(),
+                                         ws_bytes, _lib.stream_ptr(dev))
     _lib.check(st)
     if not with_status:
         return out, None, None

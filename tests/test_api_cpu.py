@@ -20,7 +20,12 @@ def test_public_surface_matches_reference_names():
     from ossa_b200.triton_kernel import topk_attention as t2
     assert t2 is topk_attention
     sig = inspect.signature(topk_attention)
-    assert list(sig.parameters) == ["q", "k", "v", "topk_indices", "causal", "block_m", "use_triton"]
+    # the reference's parameters, in order, then only additive keyword-only ones with defaults
+    ref = ["q", "k", "v", "topk_indices", "causal", "block_m", "use_triton"]
+    assert list(sig.parameters)[:len(ref)] == ref
+    for extra in list(sig.parameters)[len(ref):]:
+        prm = sig.parameters[extra]
+        assert prm.kind is inspect.Parameter.KEYWORD_ONLY and prm.default is None
     assert sig.parameters["causal"].default is True and sig.parameters["block_m"].default == 32
 
 

@@ -1,0 +1,75 @@
+"""Query-row ranges (q_start): a block of query rows at positions
+q_start .. q_start + Nq - 1 against the full key sequence must give exactly the
+matching rows of the unsharded call, for the tensor-core selector, the exact
+selector and the gather; and the selection rows match the oracle."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+from ossa_b200 import router_topk, topk_attention
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _inputs(B, H, Hkv, N, D, r, L, seed):
+    q, k, v = cases.qkv(B, H, Hkv, N, D, seed=seed, scale=1.0 / math.sqrt(D))
+    wq, wk, pb = cases.router_weights(D, r, L, seed)
+    return q.bfloat16(), k.bfloat16(), v.bfloat16(), wq, wk, pb
+
+
+@pytest.mark.parametrize("r,K", [(64, 64), (64, 16), (32, 40), (64, 128)])
+@pytest.mark.parametrize("q0,nq", [(0, 300), (300, 257), (129, 128), (640, 1), (511, 130)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_router_rows_match_full(r, K, q0, nq, causal):
+    B, H, Hkv, N, D, L = 1, 4, 2, 768, 128, 768
+    q, k, _, wq, wk, pb = _inputs(B, H, Hkv, N, D, r, L, seed=r + K)
+    qd, kd = q.to(DEV), k.to(DEV)
+    args = (wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K)
+    full = router_topk(qd, kd, *args, causal=causal)
+    part = router_topk(qd[:, :, q0:q0 + nq].contiguous(), kd, *args, causal=causal, q_start=q0)
+    assert torch.equal(part, full[:, :, q0:q0 + nq])
+
+
+def test_router_rows_match_oracle():
+    B, H, Hkv, N, D, r, L, K = 2, 6, 2, 640, 128, 64, 512, 64
+    q, k, _, wq, wk, pb = _inputs(B, H, Hkv, N, D, r, L, seed=5)
+    q0, nq = 200, 333
+    part = router_topk(q[:, :, q0:q0 + nq].contiguous().to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV),
+                       pb.to(DEV), L, K, q_start=q0)
+    rows = np.array([(bh * N + i) for bh in range(B * H) for i in range(q0, q0 + nq)])
+    ref = oracle.router_topk_rows(q, k, wq, wk, pb, L, K, rows)
+    np.testing.assert_array_equal(part.cpu().numpy().reshape(-1, K), ref)
+
+
+@pytest.mark.parametrize("q0,nq", [(0, 100), (100, 155), (37, 1), (250, 5)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_gather_rows_match_full(q0, nq, causal):
+    B, H, Hkv, N, D, K = 2, 6, 2, 256, 128, 48
+    q, k, v, _, _, _ = _inputs(B, H, Hkv, N, D, 64, 256, seed=q0 + nq)
+    g = cases.gen(11)
+    idx = torch.randint(-1, N, (B, H, N, K), generator=g).int()
+    qd, kd, vd, idd = q.to(DEV), k.to(DEV), v.to(DEV), idx.to(DEV)
+    full = topk_attention(qd, kd, vd, topk_indices=idd, causal=causal)
+    part = topk_attention(qd[:, :, q0:q0 + nq].contiguous(), kd, vd,
+                          topk_indices=idd[:, :, q0:q0 + nq].contiguous(), causal=causal, q_start=q0)
+    assert torch.equal(part, full[:, :, q0:q0 + nq])
+
+
+def test_rows_argument_checks():
+    from ossa_b200._lib import OssaError
+
+    q = torch.zeros(1, 2, 8, 128, device=DEV, dtype=torch.bfloat16)
+    k = torch.zeros(1, 2, 16, 128, device=DEV, dtype=torch.bfloat16)
+    idx = torch.zeros(1, 2, 8, 4, device=DEV, dtype=torch.int32)
+    with pytest.raises(ValueError):
+        topk_attention(q, k, k, topk_indices=idx, q_start=-1)
+    with pytest.raises(ValueError):
+        topk_attention(q, k, k, topk_indices=idx)  # row counts differ without q_start
+    with pytest.raises(OssaError):
+        topk_attention(q, k[:, :, :0], k[:, :, :0], topk_indices=idx, q_start=0)
