@@ -450,6 +450,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         float* wcp = win + ew * 4 * kWinCopy;
         const int s4 = lane & 3;
         const float* mycopy = wcp + s4 * kWinCopy + (lane - s4) + (kHalfCols - 4);
+        const uint32_t mycopy_s = smem_u32(mycopy);  // its shared address
+        const uint32_t wcp_s = smem_u32(wcp);
         const int lim = p.causal ? min(N, p.q0 + i + 1) : N;  // keys j < lim are eligible
         bool ok = true;
 
@@ -477,7 +479,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
                     const int y = x - s;
-                    if (y >= 0 && y < kWinLen) wcp[s * kWinCopy + y] = wv[u];
+                    if (y >= 0 && y < kWinLen) sts_f32(wcp_s + 4u * (uint32_t)(s * kWinCopy + y), wv[u]);
                 }
             }
             __syncwarp();
@@ -511,7 +513,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 float4 bw[8];
                 tmem_ld32(taddr + 32u * h2, v);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) bw[q] = *reinterpret_cast<const float4*>(mycopy - (32 * h2 + 4 * q));
+                for (int q = 0; q < 8; ++q) bw[q] = lds_f4(mycopy_s - 4u * (uint32_t)(32 * h2 + 4 * q));
                 tmem_wait_ld();
                 if (h2 == 1) {
                     tc_fence_before();
@@ -628,7 +630,9 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const bool full_tile = __all_sync(kFull, j0 + cbase + kHalfCols <= lim || fb);
             const int climit = lim - j0 - cbase;
             const uint32_t jb = (uint32_t)(j0 + cbase);
-            uint2* wp = sub + cnt;
+            // 32-bit shared-memory write address and an explicitly predicated
+            // st.shared: the per-column append then costs one store and one add
+            uint32_t waddr = smem_u32(sub) + 8u * (uint32_t)cnt;
             // Two 32-column chunks, each loading its accumulator columns and bias
             // values together (as in pass 1).
 #pragma unroll
@@ -637,7 +641,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 float4 bw[8];
                 tmem_ld32(taddr + 32u * h2, v);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) bw[q] = *reinterpret_cast<const float4*>(mycopy - (32 * h2 + 4 * q));
+                for (int q = 0; q < 8; ++q) bw[q] = lds_f4(mycopy_s - 4u * (uint32_t)(32 * h2 + 4 * q));
                 tmem_wait_ld();
                 if (h2 == 1) {
                     tc_fence_before();
@@ -652,22 +656,23 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     for (int d = 0; d < 4; ++d) {
                         const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
                         const bool adm = (full_tile || c + d < climit) && sc >= theta;
-                        if (adm) *wp = make_uint2(__float_as_uint(sc), jb + (uint32_t)(c + d));
-                        wp += adm ? 1 : 0;
+                        asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %3, 0;\n @p st.shared.v2.u32 [%0], {%1, %2};\n}"
+                                     :: "r"(waddr), "r"(__float_as_uint(sc)), "r"(jb + (uint32_t)(c + d)), "r"(adm ? 1 : 0));
+                        waddr += adm ? 8u : 0u;
                     }
                     if ((q & 3) == 3) {
                         // after every 16 columns: a sub-list that could overflow during
                         // the next 16 sends its row to the exact fallback
-                        const int n = (int)(wp - sub);
+                        const int n = (int)((waddr - smem_u32(sub)) >> 3);
                         if (n > kSubLimit) {
                             fb = true;
                             theta = __int_as_float(0x7fc00000);
-                            wp = sub;
+                            waddr = smem_u32(sub);
                         }
                     }
                 }
             }
-            cnt = (int)(wp - sub);
+            cnt = (int)((waddr - smem_u32(sub)) >> 3);
             __syncwarp();  // window copies are rewritten for the next tile
         }
         if (!ok) atomicOr(p.status, 4);
