@@ -47,6 +47,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <cfloat>
 #include <climits>
 
 #include "common.cuh"
@@ -68,6 +69,7 @@ constexpr int kAccBufs = 4;         // TMEM accumulators (128 columns each)
 constexpr int kEpiWarps = 8;        // two per TMEM lane quadrant, 64 columns each
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kHalfCols = kTileN / 2;
+constexpr int kChunk = 32;          // accumulator columns per tcgen05.ld in the epilogue
 constexpr int kSubCap = 80;         // candidate sub-list capacity (per row and column half)
 constexpr int kSubLimit = kSubCap - 16;  // past this after a 16-column step: exact fallback
 constexpr int kRowStride = 2 * kSubCap + 1;  // uint2 entries per row; odd stride spreads banks
@@ -83,6 +85,7 @@ constexpr size_t kOffB = kOffA + kTileBytes;
 constexpr size_t kOffWin = kOffB + (size_t)kStages * kTileBytes;
 constexpr size_t kOffBuf = kOffWin + (size_t)kEpiWarps * 4 * kWinCopy * sizeof(float);
 constexpr size_t kOffBar = kOffBuf + (size_t)kTileM * kRowStride * sizeof(uint2);
+static_assert(kChunk % 16 == 0, "the overflow check runs every 16 columns");
 static_assert(4 * kWinCopy >= 2 * 32, "a quadrant's row metadata reuses one warp's window");
 constexpr int kNumBars = 2 * kStages + 1 + 2 * kAccBufs + 1;
 constexpr size_t kOffSlot = kOffBar + kNumBars * sizeof(uint64_t);
@@ -266,6 +269,20 @@ __device__ __forceinline__ int count_ge(const float (&x)[NX], float v) {
     int c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
     for (int q = 0; q < NX; ++q) c[q & 7] += x[q] >= v ? 1 : 0;
+    return ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
+}
+
+// count_ge over the first nch 8-entry chunks of x only (nch uniform across the warp).
+template <int NX>
+__device__ __forceinline__ int count_ge_chunks(const float (&x)[NX], float v, int nch) {
+    int c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int ch = 0; ch < NX / 8; ++ch) {
+        if (ch < nch) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) c[u] += x[8 * ch + u] >= v ? 1 : 0;
+        }
+    }
     return ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
 }
 
@@ -467,9 +484,11 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const int obase = i0g + r0 - j0 - (kHalfCols - 1) - cbase + L;
 #pragma unroll
             for (int u = 0; u < kWinVals; ++u) {
-                int bi = obase + lane + 32 * u;
-                bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
-                wv[u] = __ldg(p.bias + bi);
+                const int braw = obase + lane + 32 * u;  // i - j + L for this window slot
+                const int bi = braw < 0 ? 0 : (braw > 2 * L - 1 ? 2 * L - 1 : braw);
+                // causal: a key after the query (i - j < 0) gets -inf, so full tiles
+                // need no per-column mask
+                wv[u] = (p.causal && braw < L) ? -INFINITY : __ldg(p.bias + bi);
             }
         };
         auto tile_prologue = [&](int t) -> bool {
@@ -502,28 +521,30 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 break;
             }
             const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN + cbase);
-            const bool full_tile = __all_sync(kFull, j0 + cbase + kHalfCols <= lim || fb);
+            // columns past the last key need the explicit mask (the tile reads on
+            // into the next head's keys); causally masked keys score -inf anyway
+            const bool full_tile = j0 + cbase + kHalfCols <= N;
             const int climit = lim - j0 - cbase;  // local columns c < climit are eligible
-            // Two 32-column chunks: the chunk's accumulator columns and its bias
-            // values are loaded together, so the shared-memory latency is paid
-            // once per chunk rather than once per 4 columns.
+            // 32-column chunks: the chunk's accumulator columns and its bias values
+            // are loaded together, so the shared-memory latency is paid once per
+            // chunk rather than once per 4 columns.
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-                uint32_t v[32];
-                float4 bw[8];
-                tmem_ld32(taddr + 32u * h2, v);
+            for (int h2 = 0; h2 < kHalfCols / kChunk; ++h2) {
+                uint32_t v[kChunk];
+                float4 bw[kChunk / 4];
+                tmem_ld_chunk(taddr + (uint32_t)(kChunk * h2), v);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) bw[q] = lds_f4(mycopy_s - 4u * (uint32_t)(32 * h2 + 4 * q));
+                for (int q = 0; q < kChunk / 4; ++q) bw[q] = lds_f4(mycopy_s - 4u * (uint32_t)(kChunk * h2 + 4 * q));
                 tmem_wait_ld();
-                if (h2 == 1) {
+                if (h2 == kHalfCols / kChunk - 1) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(tempty + ab);
                 }
                 if (full_tile) {
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const int c = 32 * h2 + 4 * q;
+                    for (int q = 0; q < kChunk / 4; ++q) {
+                        const int c = kChunk * h2 + 4 * q;
                         cm[c + 0] = fmaxf(cm[c + 0], fmaf(__uint_as_float(v[4 * q + 0]), m, bw[q].w));
                         cm[c + 1] = fmaxf(cm[c + 1], fmaf(__uint_as_float(v[4 * q + 1]), m, bw[q].z));
                         cm[c + 2] = fmaxf(cm[c + 2], fmaf(__uint_as_float(v[4 * q + 2]), m, bw[q].y));
@@ -531,8 +552,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     }
                 } else {
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const int c = 32 * h2 + 4 * q;
+                    for (int q = 0; q < kChunk / 4; ++q) {
+                        const int c = kChunk * h2 + 4 * q;
                         const float b4[4] = {bw[q].w, bw[q].z, bw[q].y, bw[q].x};
 #pragma unroll
                         for (int d = 0; d < 4; ++d) {
@@ -614,7 +635,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         float theta = __int_as_float(0x7fc00000);  // NaN admits nothing
         if (ok && !fb) {
             const float lb = __uint_as_float(rowbuf[kRowStride - 1].x);
-            theta = lb == -INFINITY ? -INFINITY : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
+            // fewer than K eligible keys: admit every finite score (masked keys are -inf)
+            theta = lb == -INFINITY ? -FLT_MAX : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
         }
 
         // ---------------- pass 2: collect candidates s >= theta into the sub-list
@@ -627,52 +649,73 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 break;
             }
             const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN + cbase);
-            const bool full_tile = __all_sync(kFull, j0 + cbase + kHalfCols <= lim || fb);
+            const bool full_tile = j0 + cbase + kHalfCols <= N;
             const int climit = lim - j0 - cbase;
             const uint32_t jb = (uint32_t)(j0 + cbase);
             // 32-bit shared-memory write address and an explicitly predicated
             // st.shared: the per-column append then costs one store and one add
             uint32_t waddr = smem_u32(sub) + 8u * (uint32_t)cnt;
-            // Two 32-column chunks, each loading its accumulator columns and bias
-            // values together (as in pass 1).
+            // After every 16 columns: a sub-list that could overflow during the next
+            // 16 sends its row to the exact fallback (kSubLimit = kSubCap - 16).
+            const uint32_t sub_s = smem_u32(sub);
+            auto overflow_check = [&]() {
+                if ((int)((waddr - sub_s) >> 3) > kSubLimit) {
+                    fb = true;
+                    theta = __int_as_float(0x7fc00000);
+                    waddr = sub_s;
+                }
+            };
+            // 32-column chunks, each loading its accumulator columns and bias values
+            // together (as in pass 1).
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-                uint32_t v[32];
-                float4 bw[8];
-                tmem_ld32(taddr + 32u * h2, v);
+            for (int h2 = 0; h2 < kHalfCols / kChunk; ++h2) {
+                uint32_t v[kChunk];
+                float4 bw[kChunk / 4];
+                tmem_ld_chunk(taddr + (uint32_t)(kChunk * h2), v);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) bw[q] = lds_f4(mycopy_s - 4u * (uint32_t)(32 * h2 + 4 * q));
+                for (int q = 0; q < kChunk / 4; ++q) bw[q] = lds_f4(mycopy_s - 4u * (uint32_t)(kChunk * h2 + 4 * q));
                 tmem_wait_ld();
-                if (h2 == 1) {
+                if (h2 == kHalfCols / kChunk - 1) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(tempty + ab);
                 }
+                if (full_tile) {
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const int c = 32 * h2 + 4 * q;
-                    const float b4[4] = {bw[q].w, bw[q].z, bw[q].y, bw[q].x};
+                    for (int q = 0; q < kChunk / 4; ++q) {
+                        const int c = kChunk * h2 + 4 * q;
+                        const float b4[4] = {bw[q].w, bw[q].z, bw[q].y, bw[q].x};
 #pragma unroll
-                    for (int d = 0; d < 4; ++d) {
-                        const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
-                        const bool adm = (full_tile || c + d < climit) && sc >= theta;
-                        asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %3, 0;\n @p st.shared.v2.u32 [%0], {%1, %2};\n}"
-                                     :: "r"(waddr), "r"(__float_as_uint(sc)), "r"(jb + (uint32_t)(c + d)), "r"(adm ? 1 : 0));
-                        waddr += adm ? 8u : 0u;
-                    }
-                    if ((q & 3) == 3) {
-                        // after every 16 columns: a sub-list that could overflow during
-                        // the next 16 sends its row to the exact fallback
-                        const int n = (int)((waddr - smem_u32(sub)) >> 3);
-                        if (n > kSubLimit) {
-                            fb = true;
-                            theta = __int_as_float(0x7fc00000);
-                            waddr = smem_u32(sub);
+                        for (int d = 0; d < 4; ++d) {
+                            const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
+                            // append (score, key) when score >= theta; the address chain
+                            // only carries the add (the compare is repeated off it)
+                            asm volatile("{\n .reg .pred p;\n setp.ge.f32 p, %1, %2;\n"
+                                         " @p st.shared.v2.b32 [%0], {%1, %3};\n}"
+                                         :: "r"(waddr), "f"(sc), "f"(theta), "r"(jb + (uint32_t)(c + d)));
+                            waddr += sc >= theta ? 8u : 0u;
                         }
+                        if ((q & 3) == 3) overflow_check();
+                    }
+                } else {
+#pragma unroll
+                    for (int q = 0; q < kChunk / 4; ++q) {
+                        const int c = kChunk * h2 + 4 * q;
+                        const float b4[4] = {bw[q].w, bw[q].z, bw[q].y, bw[q].x};
+#pragma unroll
+                        for (int d = 0; d < 4; ++d) {
+                            const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
+                            asm volatile("{\n .reg .pred p, e;\n setp.ge.f32 p, %1, %2;\n setp.lt.s32 e, %4, %5;\n"
+                                         " and.pred p, p, e;\n @p st.shared.v2.b32 [%0], {%1, %3};\n}"
+                                         :: "r"(waddr), "f"(sc), "f"(theta), "r"(jb + (uint32_t)(c + d)), "r"(c + d),
+                                            "r"(climit));
+                            waddr += (sc >= theta && c + d < climit) ? 8u : 0u;
+                        }
+                        if ((q & 3) == 3) overflow_check();
                     }
                 }
             }
-            cnt = (int)((waddr - smem_u32(sub)) >> 3);
+            cnt = (int)((waddr - sub_s) >> 3);
             __syncwarp();  // window copies are rewritten for the next tile
         }
         if (!ok) atomicOr(p.status, 4);
@@ -717,20 +760,39 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 fdelta = p.rowinfo[orow_id].y;
                 lo = __uint_as_float(frowbuf[kRowStride - 1].x);
             }
+            const uint32_t own_s = smem_u32(own);
+            // Slots past the warp's longest sub-list hold -inf in every lane and
+            // change no count or extremum below: loops stop after nch 8-slot chunks.
+            const int nch = (int)((__reduce_max_sync(kFull, work ? (unsigned)nown : 0u) + 7u) >> 3);
             float x[kSubCap];
 #pragma unroll
-            for (int q = 0; q < kSubCap; ++q) x[q] = (work && q < nown) ? __uint_as_float(own[q].x) : -INFINITY;
+            for (int ch = 0; ch < kSubCap / 8; ++ch) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) x[8 * ch + u] = -INFINITY;
+                if (ch < nch) {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int q = 8 * ch + u;
+                        x[q] = lds_f32_or(own_s + 8u * q, work && q < nown, -INFINITY);
+                    }
+                }
+            }
 
             // 1. split at the K-th best approximate score
             float hi8[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) hi8[u] = -INFINITY;
 #pragma unroll
-            for (int q = 0; q < kSubCap; ++q) hi8[q & 7] = fmaxf(hi8[q & 7], x[q]);
+            for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                if (ch < nch) {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) hi8[u] = fmaxf(hi8[u], x[8 * ch + u]);
+                }
+            }
             float hi = fmaxf(fmaxf(fmaxf(hi8[0], hi8[1]), fmaxf(hi8[2], hi8[3])),
                              fmaxf(fmaxf(hi8[4], hi8[5]), fmaxf(hi8[6], hi8[7])));
             hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, 1));
-            int cnt_lo = count_ge<kSubCap>(x, lo);
+            int cnt_lo = count_ge_chunks<kSubCap>(x, lo, nch);
             cnt_lo += __shfl_xor_sync(kFull, cnt_lo, 1);
             if (work && !all_in && cnt_lo < K) {
                 to_fallback = true;  // cannot happen: lb is reached by K candidates
@@ -740,7 +802,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             for (int it = 0; it < 40; ++it) {
                 if (__all_sync(kFull, done)) break;
                 const float mid = lo + 0.5f * (hi - lo);
-                int c = count_ge<kSubCap>(x, mid);
+                int c = count_ge_chunks<kSubCap>(x, mid, nch);
                 c += __shfl_xor_sync(kFull, c, 1);
                 if (!done) {
                     if (!(mid > lo && mid < hi)) {
@@ -761,10 +823,16 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 kmax8[u] = -INFINITY;
             }
 #pragma unroll
-            for (int q = 0; q < kSubCap; ++q) {
-                const bool ge = x[q] >= lo;
-                kmin8[q & 7] = ge ? fminf(kmin8[q & 7], x[q]) : kmin8[q & 7];
-                kmax8[q & 7] = ge ? kmax8[q & 7] : fmaxf(kmax8[q & 7], x[q]);
+            for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                if (ch < nch) {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const float xq = x[8 * ch + u];
+                        const bool ge = xq >= lo;
+                        kmin8[u] = ge ? fminf(kmin8[u], xq) : kmin8[u];
+                        kmax8[u] = ge ? kmax8[u] : fmaxf(kmax8[u], xq);
+                    }
+                }
             }
             float xk = kmin8[0], xk1 = kmax8[0];
 #pragma unroll
@@ -788,9 +856,15 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             {
                 int ni8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, nb8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-                for (int q = 0; q < kSubCap; ++q) {
-                    ni8[q & 7] += x[q] > U ? 1 : 0;
-                    nb8[q & 7] += (x[q] >= W && x[q] <= U) ? 1 : 0;
+                for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                    if (ch < nch) {
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const float xq = x[8 * ch + u];
+                            ni8[u] += xq > U ? 1 : 0;
+                            nb8[u] += (xq >= W && xq <= U) ? 1 : 0;
+                        }
+                    }
                 }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
@@ -812,12 +886,18 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)frow * kMaxBand;  // MMAs are done with sA
             uint2* myslots = scratch + fh * (kMaxBand / 2);
             if (rescore) {
-                uint2* wp = myslots;
+                uint32_t wa = smem_u32(myslots);
 #pragma unroll
-                for (int q = 0; q < kSubCap; ++q) {
-                    const bool inb = x[q] >= W && x[q] <= U;
-                    if (inb) *wp = make_uint2((uint32_t)q, 0u);
-                    wp += inb ? 1 : 0;
+                for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                    if (ch < nch) {
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const int q = 8 * ch + u;
+                            const bool inb = x[q] >= W && x[q] <= U;
+                            sts_u32_if(wa, (uint32_t)q, inb);
+                            wa += inb ? 8u : 0u;
+                        }
+                    }
                 }
             }
             const int nbmax = __reduce_max_sync(kFull, rescore ? (unsigned)own_nb : 0u);
@@ -856,20 +936,29 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             // 3. compact kept keys in place, then merge the two lists
             int nsel = 0;
             if (work) {
-                uint2* wp = own;
+                uint32_t wa = own_s + 4u;  // .y of the next kept slot
                 int bidx = 0;
 #pragma unroll
-                for (int q = 0; q < kSubCap; ++q) {
-                    // scores re-read from the list: x[] is not kept live across the band work
-                    const uint2 e = own[q];
-                    const float sq = q < nown ? __uint_as_float(e.x) : -INFINITY;
-                    const bool inb = sq >= W && sq <= U;
-                    const bool keep = sq > U || (inb && (!rescore || ((selmask >> bidx) & 1u)));
-                    bidx += inb ? 1 : 0;
-                    if (keep) wp->y = e.y;
-                    wp += keep ? 1 : 0;
+                for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                    if (ch < nch) {
+                        // scores re-read from the list, a chunk at a time (x[] is not kept
+                        // live across the band work); loads before the chunk's stores
+                        uint2 e8[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) e8[u] = lds_u2(own_s + 8u * (8 * ch + u));
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const int q = 8 * ch + u;
+                            const float sq = q < nown ? __uint_as_float(e8[u].x) : -INFINITY;
+                            const bool inb = sq >= W && sq <= U;
+                            const bool keep = sq > U || (inb && (!rescore || ((selmask >> bidx) & 1u)));
+                            bidx += inb ? 1 : 0;
+                            sts_u32_if(wa, e8[u].y, keep);
+                            wa += keep ? 8u : 0u;
+                        }
+                    }
                 }
-                nsel = (int)(wp - own);
+                nsel = (int)((wa - own_s - 4u) >> 3);
             }
             const int nsel_oth = __shfl_xor_sync(kFull, nsel, 1);
             __syncwarp();
@@ -879,34 +968,68 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const int mfront = (ntot + 1) >> 1;
             const int mcount = fh ? ntot - mfront : mfront;
             const int steps = (int)__reduce_max_sync(kFull, work ? (unsigned)mcount : 0u);
+            // The merged rows are staged in the (now idle) k' tile ring, 256 B per row
+            // with the 16-byte groups XOR-swizzled by row, then written out with
+            // coalesced 16-byte stores.
+            const uint32_t stage_s = smem_u32(sB);
             {
-                const uint2* LA = frowbuf;
-                const uint2* LB = frowbuf + kSubCap;
+                const uint32_t LA = smem_u32(frowbuf) + 4u;             // .y fields
+                const uint32_t LB = LA + 8u * kSubCap;
                 const int dir = fh ? -1 : 1;
                 int ia = fh ? nA - 1 : 0, ib = fh ? nB - 1 : 0;
                 // lane 2r takes the smaller key each step, lane 2r+1 the larger:
                 // compare on j for the front and on -j for the back
                 const int sgn = fh ? -1 : 1;
-                int ja = (work && ia >= 0 && ia < nA) ? (int)LA[ia].y : -1;
-                int jb = (work && ib >= 0 && ib < nB) ? (int)LB[ib].y : -1;
-                int32_t* orow = p.out + orow_id * K;
+                int ja = (work && ia >= 0 && ia < nA) ? (int)lds_u32(LA + 8u * ia) : -1;
+                int jb = (work && ib >= 0 && ib < nB) ? (int)lds_u32(LB + 8u * ib) : -1;
+                const uint32_t srow = stage_s + 256u * frow;
+                const int swz = (frow & 7) << 2;
                 for (int st = 0; st < steps; ++st) {
                     if (work && st < mcount) {
                         const int ka = ja < 0 ? INT_MAX : sgn * ja;
                         const int kb = jb < 0 ? INT_MAX : sgn * jb;
                         const bool ta = ka < kb;
-                        orow[fh ? ntot - 1 - st : st] = ta ? ja : jb;
+                        const int col = fh ? ntot - 1 - st : st;
+                        sts_f32(srow + 4u * (uint32_t)(col ^ swz), __int_as_float(ta ? ja : jb));
                         if (ta) {
                             ia += dir;
-                            ja = (ia >= 0 && ia < nA) ? (int)LA[ia].y : -1;
+                            ja = (ia >= 0 && ia < nA) ? (int)lds_u32(LA + 8u * ia) : -1;
                         } else {
                             ib += dir;
-                            jb = (ib >= 0 && ib < nB) ? (int)LB[ib].y : -1;
+                            jb = (ib >= 0 && ib < nB) ? (int)lds_u32(LB + 8u * ib) : -1;
                         }
                     }
                 }
                 if (work && fh) {
-                    for (int q = ntot; q < K; ++q) orow[q] = -1;
+                    for (int q = ntot; q < K; ++q) sts_f32(srow + 4u * (uint32_t)(q ^ swz), __int_as_float(-1));
+                }
+            }
+            __syncwarp();
+            {
+                // this warp's 16 rows: r0 + 16 * hf + rin, finished by lane pair rin
+                const unsigned workmask = __ballot_sync(kFull, work);
+                const int rbase = r0 + 16 * hf;
+                if ((K & 3) == 0) {
+                    const int per_row = K >> 2;
+                    for (int f = lane; f < 16 * per_row; f += 32) {
+                        const int rin = f / per_row, v = f - rin * per_row;
+                        if ((workmask >> (2 * rin)) & 1u) {
+                            const int rrow = rbase + rin;
+                            const uint4 val = lds_u4(stage_s + 256u * rrow + 16u * (uint32_t)(v ^ (rrow & 7)));
+                            const size_t oid = (size_t)bh * Nq + (size_t)(i0 + rrow);
+                            *(reinterpret_cast<uint4*>(p.out + oid * K) + v) = val;
+                        }
+                    }
+                } else {
+                    for (int f = lane; f < 16 * K; f += 32) {
+                        const int rin = f / K, c = f - rin * K;
+                        if ((workmask >> (2 * rin)) & 1u) {
+                            const int rrow = rbase + rin;
+                            const uint32_t val = lds_u32(stage_s + 256u * rrow + 4u * (uint32_t)(c ^ ((rrow & 7) << 2)));
+                            const size_t oid = (size_t)bh * Nq + (size_t)(i0 + rrow);
+                            p.out[oid * K + c] = (int32_t)val;
+                        }
+                    }
                 }
             }
             if (to_fallback && fh == 0) {

@@ -22,6 +22,33 @@ __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
 __device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
     asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v));
 }
+__device__ __forceinline__ uint2 lds_u2(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+// *addr = v when pred (an explicitly predicated store: no branch).
+__device__ __forceinline__ void sts_u32_if(uint32_t addr, uint32_t v, bool pred) {
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n @p st.shared.u32 [%0], %1;\n}"
+                 ::"r"(addr), "r"(v), "r"(pred ? 1 : 0));
+}
+// value at addr when pred, else `otherwise` (an explicitly predicated load).
+__device__ __forceinline__ float lds_f32_or(uint32_t addr, bool pred, float otherwise) {
+    float v;
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n mov.f32 %0, %3;\n @p ld.shared.f32 %0, [%1];\n}"
+                 : "=f"(v) : "r"(addr), "r"(pred ? 1 : 0), "f"(otherwise));
+    return v;
+}
 
 // ----------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -114,6 +141,15 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 
 // 32 consecutive fp32 columns of this warp's 32 TMEM lanes (thread t <- lane base + t).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -148,6 +184,10 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(const void* smem_tile) {
 __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t ab_format, uint32_t M, uint32_t N) {
     return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
+
+// 32x32b TMEM load of N (16 or 32) consecutive columns into v.
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&v)[16]) { tmem_ld16(taddr, v); }
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&v)[32]) { tmem_ld32(taddr, v); }
 
 }  // namespace sm100
 }  // namespace ossa
