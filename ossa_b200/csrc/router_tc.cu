@@ -798,7 +798,10 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 to_fallback = true;  // cannot happen: lb is reached by K candidates
                 work = false;
             }
-            bool done = !work || all_in || cnt_lo == K;
+            // Stop at an exact split (K entries >= lo) or once the bracket is within
+            // delta: the boundary band then holds the few near-tied entries and the
+            // canonical rescoring below decides them.
+            bool done = !work || all_in || cnt_lo == K || hi - lo <= fdelta;
             for (int it = 0; it < 40; ++it) {
                 if (__all_sync(kFull, done)) break;
                 const float mid = lo + 0.5f * (hi - lo);
@@ -810,9 +813,10 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     } else if (c >= K) {
                         lo = mid;
                         cnt_lo = c;
-                        done = c == K;
+                        done = c == K || hi - lo <= fdelta;
                     } else {
                         hi = mid;
+                        done = hi - lo <= fdelta;
                     }
                 }
             }
