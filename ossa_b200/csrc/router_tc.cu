@@ -75,6 +75,8 @@ constexpr int kSubLimit = kSubCap - 16;  // past this after a 16-column step: ex
 constexpr int kRowStride = 2 * kSubCap + 1;  // uint2 entries per row; odd stride spreads banks
 constexpr int kWinLen = 96;         // bias window entries per copy (32 rows x 64 columns)
 constexpr int kWinCopy = 104;       // copy stride (floats): copies 8 banks apart
+constexpr int kWinPad = 4;          // leading slots of a copy: unmasked stores of x - s < 0 land there
+static_assert(kWinPad >= 3 && kWinPad % 4 == 0 && kWinPad + kWinLen <= kWinCopy, "window copy layout");
 constexpr int kTileBytes = kTileM * kR * 2;
 constexpr uint32_t kTmemCols = kAccBufs * kTileN;
 constexpr int kMaxK = 64;           // selection bound uses the K-th of 128 column-class maxima
@@ -466,7 +468,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         uint2* sub = rowbuf + hf * kSubCap;  // this thread's candidate sub-list
         float* wcp = win + ew * 4 * kWinCopy;
         const int s4 = lane & 3;
-        const float* mycopy = wcp + s4 * kWinCopy + (lane - s4) + (kHalfCols - 4);
+        const float* mycopy = wcp + s4 * kWinCopy + kWinPad + (lane - s4) + (kHalfCols - 4);
         const uint32_t mycopy_s = smem_u32(mycopy);  // its shared address
         const uint32_t wcp_s = smem_u32(wcp);
         const int lim = p.causal ? min(N, p.q0 + i + 1) : N;  // keys j < lim are eligible
@@ -492,13 +494,17 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             }
         };
         auto tile_prologue = [&](int t) -> bool {
+            // Copy s keeps w[y + s] at kWinPad + y.  Values x < kWinLen land at
+            // y = x - s in [-3, kWinLen), inside the copy's padding when negative,
+            // so those stores need no mask; only the last group is masked.
 #pragma unroll
             for (int u = 0; u < kWinVals; ++u) {
                 const int x = lane + 32 * u;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const int y = x - s;
-                    if (y >= 0 && y < kWinLen) sts_f32(wcp_s + 4u * (uint32_t)(s * kWinCopy + y), wv[u]);
+                    const uint32_t a = wcp_s + 4u * (uint32_t)(s * kWinCopy + kWinPad + x - s);
+                    if (32 * (u + 1) <= kWinLen) sts_f32(a, wv[u]);
+                    else sts_f32_if(a, wv[u], x - s < kWinLen);
                 }
             }
             __syncwarp();

@@ -22,6 +22,10 @@ __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
 __device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
     asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v));
 }
+__device__ __forceinline__ void sts_f32_if(uint32_t addr, float v, bool pred) {
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n @p st.shared.f32 [%0], %1;\n}"
+                 ::"r"(addr), "f"(v), "r"(pred ? 1 : 0));
+}
 __device__ __forceinline__ uint2 lds_u2(uint32_t addr) {
     uint2 v;
     asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
