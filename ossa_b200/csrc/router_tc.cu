@@ -80,6 +80,7 @@ static_assert(kWinPad >= 3 && kWinPad % 4 == 0 && kWinPad + kWinLen <= kWinCopy,
 constexpr int kTileBytes = kTileM * kR * 2;
 constexpr uint32_t kTmemCols = kAccBufs * kTileN;
 constexpr int kMaxK = 64;           // selection bound uses the K-th of 128 column-class maxima
+constexpr int kBoundSlack = 3;      // the pass-1 bound stops once K..K+3 class maxima are above it
 constexpr int kMaxBand = 16;        // boundary candidates rescored per row before falling back
 
 constexpr size_t kOffA = 0;
@@ -617,7 +618,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             lo = fminf(lo, __shfl_xor_sync(kFull, lo, 1));
             hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, 1));
             nfin += __shfl_xor_sync(kFull, nfin, 1);
-            bool done = nfin <= K;
+            bool done = nfin <= K + kBoundSlack;
             for (int it = 0; it < 32; ++it) {
                 if (__all_sync(kFull, done)) break;
                 const float mid = lo + 0.5f * (hi - lo);
@@ -628,7 +629,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         done = true;
                     } else if (c >= K) {
                         lo = mid;
-                        done = c == K;
+                        done = c <= K + kBoundSlack;  // any lo with >= K maxima above is a bound
                     } else {
                         hi = mid;
                     }
