@@ -495,6 +495,12 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             }
         };
         auto tile_prologue = [&](int t) -> bool {
+            // Take this tile's values out of wv first, so the next tile's loads into
+            // wv need not wait for the shared-memory stores to read their operands.
+            float cur[kWinVals];
+#pragma unroll
+            for (int u = 0; u < kWinVals; ++u) cur[u] = wv[u];
+            if (t + 1 < T2) fetch_window(((t + 1) % T) * kTileN);
             // Copy s keeps w[y + s] at kWinPad + y.  Values x < kWinLen land at
             // y = x - s in [-3, kWinLen), inside the copy's padding when negative,
             // so those stores need no mask; only the last group is masked.
@@ -504,12 +510,11 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
                     const uint32_t a = wcp_s + 4u * (uint32_t)(s * kWinCopy + kWinPad + x - s);
-                    if (32 * (u + 1) <= kWinLen) sts_f32(a, wv[u]);
-                    else sts_f32_if(a, wv[u], x - s < kWinLen);
+                    if (32 * (u + 1) <= kWinLen) sts_f32(a, cur[u]);
+                    else sts_f32_if(a, cur[u], x - s < kWinLen);
                 }
             }
             __syncwarp();
-            if (t + 1 < T2) fetch_window(((t + 1) % T) * kTileN);
             if (!__all_sync(kFull, mbar_wait(tfull + t % kAccBufs, (t / kAccBufs) & 1))) return false;
             tc_fence_after();
             return true;
@@ -806,9 +811,9 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 work = false;
             }
             // Stop at an exact split (K entries >= lo) or once the bracket is within
-            // delta: the boundary band then holds the few near-tied entries and the
+            // 4 delta: the boundary band then holds the few near-tied entries and the
             // canonical rescoring below decides them.
-            bool done = !work || all_in || cnt_lo == K || hi - lo <= fdelta;
+            bool done = !work || all_in || cnt_lo == K || hi - lo <= 4.f * fdelta;
             for (int it = 0; it < 40; ++it) {
                 if (__all_sync(kFull, done)) break;
                 const float mid = lo + 0.5f * (hi - lo);
@@ -820,10 +825,10 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     } else if (c >= K) {
                         lo = mid;
                         cnt_lo = c;
-                        done = c == K || hi - lo <= fdelta;
+                        done = c == K || hi - lo <= 4.f * fdelta;
                     } else {
                         hi = mid;
-                        done = hi - lo <= fdelta;
+                        done = hi - lo <= 4.f * fdelta;
                     }
                 }
             }

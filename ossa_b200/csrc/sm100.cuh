@@ -46,6 +46,12 @@ __device__ __forceinline__ void sts_u32_if(uint32_t addr, uint32_t v, bool pred)
     asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n @p st.shared.u32 [%0], %1;\n}"
                  ::"r"(addr), "r"(v), "r"(pred ? 1 : 0));
 }
+__device__ __forceinline__ uint32_t lds_u32_or(uint32_t addr, bool pred, uint32_t otherwise) {
+    uint32_t v;
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n mov.b32 %0, %3;\n @p ld.shared.u32 %0, [%1];\n}"
+                 : "=r"(v) : "r"(addr), "r"(pred ? 1 : 0), "r"(otherwise));
+    return v;
+}
 // value at addr when pred, else `otherwise` (an explicitly predicated load).
 __device__ __forceinline__ float lds_f32_or(uint32_t addr, bool pred, float otherwise) {
     float v;
