@@ -238,6 +238,114 @@ project_persistent_kernel(const T* __restrict__ x, const float* __restrict__ w, 
     cp_async_wait_all();
 }
 
+// bf16 rows, D = 128, R = 64 (the ContentRouter shape of the product path): 4 rows x 8
+// output columns per thread (columns cg*4.. and 32 + cg*4..), so a d-step reads one 8-byte
+// x group (4 bf16 rows) and two float4 of W per 32 FMA, and x stays bf16 in shared memory (converted on use, exactly).
+// The next tile's rows are prefetched into registers while the current one is multiplied.
+// Same per-output fmaf chain (d = 0..127 from 0.0f) as project_kernel.
+constexpr int kP2Cols = 8;                        // output columns per thread
+constexpr int kP2Rows = 4;                        // rows per thread
+constexpr int kP2CG = 64 / kP2Cols;               // 8 column groups
+constexpr int kP2RG = kProjThreads / kP2CG;       // 32 row groups
+constexpr int kP2Tile = kP2RG * kP2Rows;          // 128 rows per tile
+constexpr int kP2XS = kP2Tile + 8;                // bf16 stride of a transposed x row (272 B)
+constexpr int kP2Vec = kP2Tile * 128 / 8 / kProjThreads;  // 16-byte row pieces per thread (8)
+constexpr size_t kP2Smem = 128 * 64 * sizeof(float) + 128 * kP2XS * sizeof(__nv_bfloat16);
+
+__global__ void __launch_bounds__(kProjThreads, 2)
+project_bf16_d128_r64_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+                             float* __restrict__ out, long long rows, long long ntiles) {
+    extern __shared__ float4 smem4[];
+    float* Ws = reinterpret_cast<float*>(smem4);                          // [128][64]
+    __nv_bfloat16* Xs = reinterpret_cast<__nv_bfloat16*>(Ws + 128 * 64);  // [128][kP2XS]
+    const int tid = threadIdx.x;
+    const int cg = tid % kP2CG;
+    const int rg = tid / kP2CG;
+    for (int e = tid; e < 64 * 128; e += kProjThreads) {
+        const int d = e / 64, c = e - d * 64;
+        Ws[d * 64 + c] = __ldg(w + (size_t)c * 128 + d);
+    }
+    uint4 pre[kP2Vec];
+    auto fetch = [&](long long tile) {
+#pragma unroll
+        for (int u = 0; u < kP2Vec; ++u) {
+            // consecutive threads take consecutive rows: conflict-free transposed stores
+            const int e = tid + u * kProjThreads;
+            const int vcol = e / kP2Tile, r = e - vcol * kP2Tile;
+            const long long gr = tile * kP2Tile + r;
+            pre[u] = gr < rows ? __ldg(reinterpret_cast<const uint4*>(x + gr * 128) + vcol) : make_uint4(0, 0, 0, 0);
+        }
+    };
+    long long tile = blockIdx.x;
+    if (tile < ntiles) fetch(tile);
+    for (; tile < ntiles; tile += gridDim.x) {
+        __syncthreads();  // the previous tile's products are done with Xs (and Ws is ready)
+#pragma unroll
+        for (int u = 0; u < kP2Vec; ++u) {
+            const int e = tid + u * kProjThreads;
+            const int vcol = e / kP2Tile, r = e - vcol * kP2Tile;
+            const uint32_t wds[4] = {pre[u].x, pre[u].y, pre[u].z, pre[u].w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                Xs[(vcol * 8 + 2 * t) * kP2XS + r] = __ushort_as_bfloat16((unsigned short)(wds[t] & 0xffffu));
+                Xs[(vcol * 8 + 2 * t + 1) * kP2XS + r] = __ushort_as_bfloat16((unsigned short)(wds[t] >> 16));
+            }
+        }
+        __syncthreads();
+        if (tile + gridDim.x < ntiles) fetch(tile + gridDim.x);
+        float acc[kP2Rows][kP2Cols];
+#pragma unroll
+        for (int a = 0; a < kP2Rows; ++a)
+#pragma unroll
+            for (int c = 0; c < kP2Cols; ++c) acc[a][c] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < 128; ++d) {
+            const uint2 xr = *reinterpret_cast<const uint2*>(Xs + d * kP2XS + rg * kP2Rows);
+            float xa[4];
+            unpack_bf16x2(xr.x, xa[0], xa[1]);
+            unpack_bf16x2(xr.y, xa[2], xa[3]);
+            // columns cg*4 .. +3 and 32 + cg*4 .. +3: each float4 read of the warp spans
+            // 128 consecutive bytes (no bank conflicts)
+            const float4 w0 = *reinterpret_cast<const float4*>(Ws + d * 64 + cg * 4);
+            const float4 w1 = *reinterpret_cast<const float4*>(Ws + d * 64 + 32 + cg * 4);
+            const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int a = 0; a < kP2Rows; ++a)
+#pragma unroll
+                for (int c = 0; c < kP2Cols; ++c) acc[a][c] = fmaf(xa[a], wa[c], acc[a][c]);
+        }
+#pragma unroll
+        for (int a = 0; a < kP2Rows; ++a) {
+            const long long gr = tile * kP2Tile + rg * kP2Rows + a;
+            if (gr < rows) {
+                *reinterpret_cast<float4*>(out + gr * 64 + cg * 4) =
+                    make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+                *reinterpret_cast<float4*>(out + gr * 64 + 32 + cg * 4) =
+                    make_float4(acc[a][4], acc[a][5], acc[a][6], acc[a][7]);
+            }
+        }
+    }
+}
+
+cudaError_t launch_bf16_d128_r64(const ProjectArgs& a, cudaStream_t stream) {
+    auto kern = project_bf16_d128_r64_kernel;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kP2Smem);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 0, per_sm = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kProjThreads, kP2Smem)) != cudaSuccess)
+        return e;
+    const long long ntiles = (a.rows + kP2Tile - 1) / kP2Tile;
+    if (ntiles == 0) return cudaSuccess;
+    const long long grid = std::min<long long>(ntiles, (long long)sms * std::max(1, per_sm));
+    kern<<<(unsigned)grid, kProjThreads, kP2Smem, stream>>>(static_cast<const __nv_bfloat16*>(a.x), a.w, a.out,
+                                                           a.rows, ntiles);
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) note_launch();
+    return err;
+}
+
 template <typename T, int R>
 constexpr size_t persistent_smem_bytes();
 
@@ -272,6 +380,9 @@ constexpr size_t persistent_smem_bytes() {
 
 template <typename T, int R>
 cudaError_t launch_r(const ProjectArgs& a, cudaStream_t stream) {
+    if constexpr (sizeof(T) == 2 && R == 64) {
+        if (a.D == 128 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0) return launch_bf16_d128_r64(a, stream);
+    }
     if constexpr (persistent_smem_bytes<T, R>() <= 200 * 1024) {
         if (a.D <= kDChunk && a.D % ChunkLoader<T>::VEC == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0)
             return launch_persistent<T, R>(a, stream);
