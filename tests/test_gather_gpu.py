@@ -176,3 +176,45 @@ def test_full_size_config2_properties():
                                         v[b:b + 1].float().cpu(), idx[b:b + 1, :, rows].cpu(),
                                         positions=rows)
         _close(out[b:b + 1, :, rows], sub, torch.bfloat16)
+
+
+def _router_form_indices(B, H, Hkv, N, K, overlap, seed):
+    """Index rows in the router's canonical form (valid keys strictly ascending, then
+    -1 padding) whose heads share a controlled fraction of their keys; some keys lie
+    after the query (masked when causal)."""
+    rng = np.random.default_rng(seed)
+    G = H // Hkv
+    idx = np.full((B, H, N, K), -1, dtype=np.int64)
+    for b in range(B):
+        for g in range(Hkv):
+            for i in range(N):
+                n = int(rng.integers(0, K + 1)) if i % 17 else K
+                shared = rng.choice(N, size=int(overlap * n), replace=False)
+                for hh in range(G):
+                    rest = np.setdiff1d(rng.choice(N, size=min(N, 2 * n), replace=False), shared)[: n - len(shared)]
+                    keys = np.sort(np.concatenate([shared, rest]))
+                    idx[b, g * G + hh, i, : len(keys)] = keys
+    return torch.from_numpy(idx)
+
+
+@pytest.mark.parametrize("overlap", [1.0, 0.6, 0.0])
+@pytest.mark.parametrize("K", [64, 37, 128])
+@pytest.mark.parametrize("causal", [True, False])
+def test_grouped_gather_router_form_rows(overlap, K, causal):
+    """Index rows in the router's output form (ascending keys, -1 padding) whose GQA
+    heads share part of their keys: the output matches the oracle, and the GQA-native
+    and repeated-heads layouts agree."""
+    B, H, Hkv, N, D = 2, 12, 2, 200, 128
+    g = cases.gen(K * 10 + int(overlap * 10) + causal)
+    s = 1.0 / math.sqrt(D)
+    q = (torch.randn(B, H, N, D, generator=g) * s).bfloat16()
+    k = (torch.randn(B, Hkv, N, D, generator=g) * s).bfloat16()
+    v = (torch.randn(B, Hkv, N, D, generator=g) * s).bfloat16()
+    idx = _router_form_indices(B, H, Hkv, N, K, overlap, seed=K + causal)
+    for dt in (torch.int32, torch.int64):
+        out = topk_attention(q.to(DEV), k.to(DEV), v.to(DEV), topk_indices=idx.to(dt).to(DEV), causal=causal)
+        ref = rp.masked_index_attention(q.float(), k.float(), v.float(), idx, causal=causal)
+        _close(out, ref, torch.bfloat16)
+        per_head = topk_attention(q.to(DEV), k.repeat_interleave(6, 1).to(DEV), v.repeat_interleave(6, 1).to(DEV),
+                                  topk_indices=idx.to(dt).to(DEV), causal=causal)
+        torch.testing.assert_close(out.float(), per_head.float(), atol=2e-3, rtol=2e-3)
