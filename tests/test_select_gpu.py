@@ -259,3 +259,32 @@ def test_tensor_core_selector_non_finite_rows():
     got, fb, status = router_topk_with_status(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
     assert status == 0 and fb >= 2 * N
     _assert_same(got, oracle.router_topk(q, k, wq, wk, pb, N, K))
+
+
+def test_long_context_tensor_core_selector():
+    """Long sequence (N = 16384, the tensor-core selector with 128 key tiles per
+    query block at the end): identical to the exact selector, sampled rows to the
+    oracle."""
+    B, H, Hkv, N, D, r, K = 1, 4, 2, 16384, 128, 64, 64
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=16, scale=1.0 / math.sqrt(D))
+    q, k = q.bfloat16(), k.bfloat16()
+    wq, wk, pb = _weights(D, r, N, seed=16)
+    tc, ex, fb, status = _run_both(q, k, wq, wk, pb, N, K, True)
+    assert status == 0
+    assert torch.equal(tc, ex), f"{(tc != ex).any(-1).sum().item()} rows differ"
+    rows = np.concatenate([np.arange(0, B * H * N, 4099), np.array([N - 1, 2 * N - 1, B * H * N - 1])]).astype(np.int64)
+    ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows, causal=True)
+    _assert_same(tc.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
+
+
+def test_long_context_k128_exact_selector():
+    """Config 5's shape at its smallest length (N = 32768, K = 128, the exact
+    CUDA-core selector): sampled rows against the oracle."""
+    B, H, Hkv, N, D, r, K = 1, 2, 1, 32768, 128, 64, 128
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=32, scale=1.0 / math.sqrt(D))
+    q, k = q.bfloat16(), k.bfloat16()
+    wq, wk, pb = _weights(D, r, N, seed=32)
+    got = router_topk(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
+    rows = np.array([0, 1, 127, 128, 4096, 20000, N - 1, N, 2 * N - 1], dtype=np.int64)
+    ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows, causal=True)
+    _assert_same(got.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
