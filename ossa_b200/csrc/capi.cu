@@ -73,19 +73,20 @@ struct RouterLayout {
 
 constexpr size_t kCountersBytes = 256;
 
-// Nq query rows per (b, h) against Nk keys per (b, kv head).
-RouterLayout router_layout(int B, int H, int Hkv, int Nq, int Nk, int r) {
+// Nq query rows per (b, h) against Nk keys per (b, kv head); K = 0 for scoring
+// without selection.
+RouterLayout router_layout(int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
     RouterLayout l;
     const size_t qp = (size_t)B * H * Nq * r * sizeof(float);
     const size_t kp = (size_t)B * Hkv * Nk * r * sizeof(float);
     l.qp_off = kCountersBytes;
     l.kp_off = l.qp_off + align_up(qp);
     l.tc_off = l.kp_off + align_up(kp);
-    l.total = l.tc_off + (r == 64 ? align_up(ossa::router_tc_workspace_bytes(B, H, Hkv, Nq, Nk)) : 0);
+    l.total = l.tc_off + (r == 64 ? align_up(ossa::router_tc_workspace_bytes(B, H, Hkv, Nq, Nk, K)) : 0);
     return l;
 }
 
-// The tensor-core selector serves r = 64, K <= 64 and at least one full tile of
+// The tensor-core selector serves r = 64, K <= 128 and at least one full tile of
 // query and key rows; OSSA_ROUTER_SELECT=exact forces the CUDA-core exact selector
 // (both produce identical indices; the switch exists to cross-check them).
 bool use_tensor_core_select(int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
@@ -104,7 +105,7 @@ int check_rows(int Nq, int Nk, int q0) {
 
 int check_router(const void* q, const void* k, int dtype, const float* wq, const float* wk,
                  const float* pos_bias, int B, int H, int Hkv, int Nq, int Nk, int q0, int D, int r,
-                 int seq_len_cfg, const void* out, void* ws, size_t ws_bytes) {
+                 int seq_len_cfg, int K, const void* out, void* ws, size_t ws_bytes) {
     int st = check_heads(B, H, Hkv, Nk);
     if (st) return st;
     if ((st = check_rows(Nq, Nk, q0))) return st;
@@ -119,7 +120,7 @@ int check_router(const void* q, const void* k, int dtype, const float* wq, const
         return fail(OSSA_ERR_INVALID, "null pointer argument");
     if (!aligned16(q) || !aligned16(k) || !aligned16(out))
         return fail(OSSA_ERR_INVALID, "q, k and the output must be 16-byte aligned");
-    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r);
+    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K);
     if (!ws || ws_bytes < l.total || !aligned16(ws))
         return fail(OSSA_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required, got %zu",
                     l.total, ws ? ws_bytes : (size_t)0);
@@ -129,7 +130,7 @@ int check_router(const void* q, const void* k, int dtype, const float* wq, const
 int project_both(const void* q, const void* k, int dtype, const float* wq, const float* wk,
                  int B, int H, int Hkv, int Nq, int Nk, int D, int r, void* ws, cudaStream_t stream,
                  float** qp_out, float** kp_out) {
-    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r);
+    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, 0);  // qp_off, kp_off do not depend on K
     char* base = static_cast<char*>(ws);
     float* qp = reinterpret_cast<float*>(base + l.qp_off);
     float* kp = reinterpret_cast<float*>(base + l.kp_off);
@@ -198,9 +199,8 @@ int ossa_router_status(const void* workspace, int* fallback_rows, int* status) {
 }
 
 size_t ossa_router_workspace_size_rows(int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
-    (void)K;
     if (B < 0 || H <= 0 || Hkv <= 0 || Nq < 0 || Nk < 0 || r <= 0) return 0;
-    return router_layout(B, H, Hkv, Nq, Nk, r).total;
+    return router_layout(B, H, Hkv, Nq, Nk, r, K).total;
 }
 
 size_t ossa_router_workspace_size(int B, int H, int Hkv, int N, int r, int K) {
@@ -211,8 +211,8 @@ int ossa_router_topk_rows(const void* q, const void* k, int dtype, const float* 
                           const float* pos_bias, int B, int H, int Hkv, int Nq, int Nk, int D, int r,
                           int seq_len_cfg, int K, int causal, int q_start, int32_t* idx_out, void* workspace,
                           size_t workspace_bytes, ossa_stream_t stream) {
-    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, Nq, Nk, q_start, D, r, seq_len_cfg, idx_out,
-                          workspace, workspace_bytes);
+    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, Nq, Nk, q_start, D, r, seq_len_cfg, K,
+                          idx_out, workspace, workspace_bytes);
     if (st) return st;
     if (K <= 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
     if (!ossa::score_topk_supported(r, K))
@@ -226,7 +226,7 @@ int ossa_router_topk_rows(const void* q, const void* k, int dtype, const float* 
     if (st) return st;
     const float scale = (float)(1.0 / sqrt((double)r));
     if (use_tensor_core_select(B, H, Hkv, Nq, Nk, r, K)) {
-        const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r);
+        const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K);
         ossa::RouterTcArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, Nk, K, causal ? 1 : 0, scale,
                              idx_out, static_cast<char*>(workspace) + l.tc_off,
                              reinterpret_cast<int*>(workspace)};
@@ -253,7 +253,7 @@ int ossa_router_score(const void* q, const void* k, int dtype, const float* wq, 
                       const float* pos_bias, int B, int H, int Hkv, int N, int D, int r,
                       int seq_len_cfg, float* scores_out, void* workspace, size_t workspace_bytes,
                       ossa_stream_t stream) {
-    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, N, 0, D, r, seq_len_cfg,
+    int st = check_router(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, N, 0, D, r, seq_len_cfg, 0,
                           scores_out, workspace, workspace_bytes);
     if (st) return st;
     if ((long long)B * H * N == 0) return OSSA_OK;

@@ -76,7 +76,7 @@ cudaError_t launch_score_dense(const ScoreDenseArgs& a, cudaStream_t stream);
 
 namespace ossa {
 
-// Tensor-core (tcgen05) router selection, r = 64.  qp32/kp32: canonical fp32
+// Tensor-core (tcgen05) router selection, r = 64, K <= 128.  qp32/kp32: canonical fp32
 // projections; ws: router_tc_workspace_bytes of scratch; counters: two ints
 // (rows sent to the exact fallback, status word: 0 = ok, nonzero = a bounded
 // wait expired), zeroed by the caller before the launch.
@@ -94,7 +94,7 @@ struct RouterTcArgs {
     int q0 = 0;  // position of query row 0 in the key sequence
 };
 bool router_tc_supported(int r, int K);
-size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N);
+size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K);
 cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream);
 
 }  // namespace ossa

@@ -49,6 +49,8 @@
 
 #include <cfloat>
 #include <climits>
+#include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -83,6 +85,16 @@ constexpr int kMaxK = 64;           // selection bound uses the K-th of 128 colu
 constexpr int kBoundSlack = 3;      // the pass-1 bound stops once K..K+3 class maxima are above it
 constexpr int kMaxBand = 16;        // boundary candidates rescored per row before falling back
 
+// Wide selection (64 < K <= 128): pass 1 keeps 256 column classes (key tile
+// parity x column), whose K-th largest maximum bounds the K-th best score; the
+// candidate sub-lists (about 1.4 K entries per row) live in global memory and a
+// warp-per-row kernel (wide_final_kernel) makes the final choice.
+constexpr int kWideMaxK = 128;
+constexpr int kWideCap = 160;              // global candidate sub-list capacity (per row and column half)
+constexpr int kWideLimit = kWideCap - 16;  // past this after a 16-column step: exact fallback
+constexpr int kWideEPL = 2 * kWideCap / 32;  // candidate entries per lane in the final kernel
+constexpr int kClsStride = 2 * kTileN + 1;   // floats per row of class maxima; odd stride spreads banks
+
 constexpr size_t kOffA = 0;
 constexpr size_t kOffB = kOffA + kTileBytes;
 constexpr size_t kOffWin = kOffB + (size_t)kStages * kTileBytes;
@@ -94,6 +106,8 @@ constexpr int kNumBars = 2 * kStages + 1 + 2 * kAccBufs + 1;
 constexpr size_t kOffSlot = kOffBar + kNumBars * sizeof(uint64_t);
 constexpr size_t kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert((size_t)kTileM * kClsStride * 4 + kTileM * 4 <= (size_t)kTileM * kRowStride * sizeof(uint2),
+              "the wide selection's class maxima and bounds fit in the candidate area");
 static_assert(kOffB % 1024 == 0 && kTileBytes % 1024 == 0, "swizzled tiles need 1 KB alignment");
 
 constexpr float kTwoPowM22 = 2.384185791015625e-07f;  // 2^-22
@@ -230,6 +244,8 @@ struct TcParams {
     int* fb_count;
     int32_t* fb_list;
     int* status;
+    uint2* lists;  // wide selection: (score, key) sub-lists, kWideCap per row and column half
+    int* counts;   // wide selection: sub-list lengths, -1 sends the row to the exact fallback
     int L, H, Hkv, N, K, causal, nqb;
     int Nq, q0;  // query rows per (b, h) and the key-sequence position of row 0
     float scale;
@@ -338,6 +354,93 @@ __device__ __forceinline__ void bisect_kth(const float (&x)[NX], int K, float wi
     }
 }
 
+// A lower bound on the K-th largest class maximum of a row whose maxima are
+// spread over G consecutive lanes (kHalfCols per lane, -inf for empty classes):
+// bisection on the value until K..K+kBoundSlack maxima are >= lo (or the bracket
+// cannot be split).  K distinct keys reach the result, so it is a lower bound on
+// the row's K-th best approximate score; -inf when fewer than K are finite.
+template <int G>
+__device__ __forceinline__ float group_class_bound(const float (&y)[kHalfCols], int K) {
+    float lo8[8], hi8[8];
+    int nf8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        lo8[u] = INFINITY;
+        hi8[u] = -INFINITY;
+        nf8[u] = 0;
+    }
+#pragma unroll
+    for (int c = 0; c < kHalfCols; ++c) {
+        const bool f = y[c] > -INFINITY;
+        nf8[c & 7] += f ? 1 : 0;
+        lo8[c & 7] = f ? fminf(lo8[c & 7], y[c]) : lo8[c & 7];
+        hi8[c & 7] = fmaxf(hi8[c & 7], y[c]);
+    }
+    float lo = lo8[0], hi = hi8[0];
+    int nfin = nf8[0];
+#pragma unroll
+    for (int u = 1; u < 8; ++u) {
+        lo = fminf(lo, lo8[u]);
+        hi = fmaxf(hi, hi8[u]);
+        nfin += nf8[u];
+    }
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1) {
+        lo = fminf(lo, __shfl_xor_sync(kFull, lo, o));
+        hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, o));
+        nfin += __shfl_xor_sync(kFull, nfin, o);
+    }
+    bool done = nfin <= K + kBoundSlack;
+    for (int it = 0; it < 32; ++it) {
+        if (__all_sync(kFull, done)) break;
+        const float mid = lo + 0.5f * (hi - lo);
+        int c = count_ge<kHalfCols>(y, mid);
+#pragma unroll
+        for (int o = 1; o < G; o <<= 1) c += __shfl_xor_sync(kFull, c, o);
+        if (!done) {
+            if (!(mid > lo && mid < hi)) {
+                done = true;
+            } else if (c >= K) {
+                lo = mid;
+                done = c <= K + kBoundSlack;  // any lo with >= K maxima above is a bound
+            } else {
+                hi = mid;
+            }
+        }
+    }
+    return nfin < K ? -INFINITY : lo;
+}
+
+// Candidate append: store (sc, key) at a and advance a by one entry when
+// sc >= theta (and, in the masked form, col < climit).  The address chain only
+// carries the add; the compare is repeated off it.  Shared-memory lists take a
+// 32-bit shared address, global lists a generic 64-bit one.
+__device__ __forceinline__ void append_ge(uint32_t& a, float sc, float theta, uint32_t key) {
+    asm volatile("{\n .reg .pred p;\n setp.ge.f32 p, %1, %2;\n"
+                 " @p st.shared.v2.b32 [%0], {%1, %3};\n}" :: "r"(a), "f"(sc), "f"(theta), "r"(key));
+    a += sc >= theta ? 8u : 0u;
+}
+__device__ __forceinline__ void append_ge(uint64_t& a, float sc, float theta, uint32_t key) {
+    asm volatile("{\n .reg .pred p;\n setp.ge.f32 p, %1, %2;\n"
+                 " @p st.global.v2.b32 [%0], {%1, %3};\n}" :: "l"(a), "f"(sc), "f"(theta), "r"(key));
+    a += sc >= theta ? 8ull : 0ull;
+}
+__device__ __forceinline__ void append_ge_lt(uint32_t& a, float sc, float theta, uint32_t key, int col,
+                                             int climit) {
+    asm volatile("{\n .reg .pred p, e;\n setp.ge.f32 p, %1, %2;\n setp.lt.s32 e, %4, %5;\n"
+                 " and.pred p, p, e;\n @p st.shared.v2.b32 [%0], {%1, %3};\n}"
+                 :: "r"(a), "f"(sc), "f"(theta), "r"(key), "r"(col), "r"(climit));
+    a += (sc >= theta && col < climit) ? 8u : 0u;
+}
+__device__ __forceinline__ void append_ge_lt(uint64_t& a, float sc, float theta, uint32_t key, int col,
+                                             int climit) {
+    asm volatile("{\n .reg .pred p, e;\n setp.ge.f32 p, %1, %2;\n setp.lt.s32 e, %4, %5;\n"
+                 " and.pred p, p, e;\n @p st.global.v2.b32 [%0], {%1, %3};\n}"
+                 :: "l"(a), "f"(sc), "f"(theta), "r"(key), "r"(col), "r"(climit));
+    a += (sc >= theta && col < climit) ? 8ull : 0ull;
+}
+
+template <bool kWide>
 __global__ void __launch_bounds__(kThreads, 1)
 router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const TcParams p) {
@@ -348,6 +451,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint8_t* sB = smem + kOffB;
     float* win = reinterpret_cast<float*>(smem + kOffWin);
     uint2* buf = reinterpret_cast<uint2*>(smem + kOffBuf);
+    [[maybe_unused]] float* cls = reinterpret_cast<float*>(smem + kOffBuf);  // wide: class maxima per row
+    [[maybe_unused]] float* lbw = cls + kTileM * kClsStride;                 // wide: bound per row
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint64_t* full = bars;
     uint64_t* empty = bars + kStages;
@@ -370,6 +475,15 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const int jend = p.causal ? min(N, i0g + kTileM) : N;
     const int T = (jend + kTileN - 1) / kTileN;  // key tiles per pass
     const int T2 = 2 * T;                          // two passes over the same key tiles
+    // Key tile of step t.  Pass 2 (t >= T) walks the tiles in order, and so does
+    // pass 1 of the narrow selection; the wide selection's pass 1 takes the even
+    // tiles first and the odd ones after, so each parity has its own class maxima.
+    const int Te = (T + 1) >> 1;
+    auto tile_of = [T, Te](int t) -> int {
+        if (t >= T) return t - T;
+        if constexpr (kWide) return t < Te ? 2 * t : 2 * (t - Te) + 1;
+        return t;
+    };
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
@@ -408,7 +522,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 if (t >= kStages) ok = mbar_wait(empty + s, ((t / kStages) - 1) & 1);
                 if (!ok) break;
                 mbar_arrive_expect_tx(full + s, kTileBytes);
-                tma_load_2d(sB + (size_t)s * kTileBytes, &tmB, full + s, 0, krow0 + (t % T) * kTileN);
+                tma_load_2d(sB + (size_t)s * kTileBytes, &tmB, full + s, 0, krow0 + tile_of(t) * kTileN);
                 issued = t + 1;
             }
             // the loads of the last stages are never waited on by a refill: make
@@ -500,7 +614,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             float cur[kWinVals];
 #pragma unroll
             for (int u = 0; u < kWinVals; ++u) cur[u] = wv[u];
-            if (t + 1 < T2) fetch_window(((t + 1) % T) * kTileN);
+            if (t + 1 < T2) fetch_window(tile_of(t + 1) * kTileN);
             // Copy s keeps w[y + s] at kWinPad + y.  Values x < kWinLen land at
             // y = x - s in [-3, kWinLen), inside the copy's padding when negative,
             // so those stores need no mask; only the last group is masked.
@@ -526,7 +640,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
         for (int c = 0; c < kHalfCols; ++c) cm[c] = -INFINITY;
         for (int t = 0; t < T && ok; ++t) {
-            const int j0 = t * kTileN;
+            const int j0 = tile_of(t) * kTileN;
             const int ab = t % kAccBufs;
             if (!tile_prologue(t)) {
                 ok = false;
@@ -576,82 +690,83 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 }
             }
             __syncwarp();  // window copies are rewritten for the next tile
-        }
-
-        // End of pass 1: the 128 class maxima of a row lie in two warps (64 each).
-        // They go through the (still empty) candidate area to a lane pair of one
-        // warp: lanes 2r and 2r+1 of warp hf take row r0 + 16*hf + r, one half
-        // each, and bisect on the value until exactly K maxima are >= lo (or the
-        // bracket cannot be split).  lo is then a lower bound on the row's K-th
-        // best approximate score (K distinct keys reach it), and every exact
-        // top-K key scores at least lo - 2*delta.  The bound goes back through
-        // the row's spare list entry.
-        float* xch = reinterpret_cast<float*>(sub);
+            if constexpr (kWide) {
+                if (t == Te - 1) {
+                    // even tiles done: their class maxima go to shared memory
+                    float* crow = cls + row * kClsStride + hf * kHalfCols;
 #pragma unroll
-        for (int c = 0; c < kHalfCols; ++c) xch[c] = cm[c];
-        named_bar_sync(pair_bar, 64);
-        {
-            const int brow = r0 + 16 * hf + (lane >> 1);
-            const int bhalf = lane & 1;
-            const float* cls = reinterpret_cast<const float*>(buf + (size_t)brow * kRowStride + bhalf * kSubCap);
-            float y[kHalfCols];
-#pragma unroll
-            for (int c = 0; c < kHalfCols; ++c) y[c] = cls[c ^ bhalf];  // the pair reads different banks
-            float lo8[8], hi8[8];
-            int nf8[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                lo8[u] = INFINITY;
-                hi8[u] = -INFINITY;
-                nf8[u] = 0;
-            }
-#pragma unroll
-            for (int c = 0; c < kHalfCols; ++c) {
-                const bool f = y[c] > -INFINITY;
-                nf8[c & 7] += f ? 1 : 0;
-                lo8[c & 7] = f ? fminf(lo8[c & 7], y[c]) : lo8[c & 7];
-                hi8[c & 7] = fmaxf(hi8[c & 7], y[c]);
-            }
-            float lo = lo8[0], hi = hi8[0];
-            int nfin = nf8[0];
-#pragma unroll
-            for (int u = 1; u < 8; ++u) {
-                lo = fminf(lo, lo8[u]);
-                hi = fmaxf(hi, hi8[u]);
-                nfin += nf8[u];
-            }
-            lo = fminf(lo, __shfl_xor_sync(kFull, lo, 1));
-            hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, 1));
-            nfin += __shfl_xor_sync(kFull, nfin, 1);
-            bool done = nfin <= K + kBoundSlack;
-            for (int it = 0; it < 32; ++it) {
-                if (__all_sync(kFull, done)) break;
-                const float mid = lo + 0.5f * (hi - lo);
-                int c = count_ge<kHalfCols>(y, mid);
-                c += __shfl_xor_sync(kFull, c, 1);
-                if (!done) {
-                    if (!(mid > lo && mid < hi)) {
-                        done = true;
-                    } else if (c >= K) {
-                        lo = mid;
-                        done = c <= K + kBoundSlack;  // any lo with >= K maxima above is a bound
-                    } else {
-                        hi = mid;
+                    for (int c = 0; c < kHalfCols; ++c) {
+                        crow[c] = cm[c];
+                        cm[c] = -INFINITY;
                     }
                 }
             }
-            const float lbv = nfin < K ? -INFINITY : lo;
-            if (bhalf == 0) buf[(size_t)brow * kRowStride + (kRowStride - 1)].x = __float_as_uint(lbv);
         }
-        named_bar_sync(pair_bar, 64);  // bounds published; class maxima read before sub-lists are written
+
+        float lb = -INFINITY;
+        if constexpr (!kWide) {
+            // End of pass 1: the 128 class maxima of a row lie in two warps (64
+            // each).  They go through the (still empty) candidate area to a lane
+            // pair of one warp: lanes 2r and 2r+1 of warp hf take row r0 + 16*hf + r,
+            // one half each (group_class_bound).  Every exact top-K key scores at
+            // least the bound - 2*delta.  The bound goes back through the row's
+            // spare list entry.
+            float* xch = reinterpret_cast<float*>(sub);
+#pragma unroll
+            for (int c = 0; c < kHalfCols; ++c) xch[c] = cm[c];
+            named_bar_sync(pair_bar, 64);
+            {
+                const int brow = r0 + 16 * hf + (lane >> 1);
+                const int bhalf = lane & 1;
+                const float* bcls = reinterpret_cast<const float*>(buf + (size_t)brow * kRowStride + bhalf * kSubCap);
+                float y[kHalfCols];
+#pragma unroll
+                for (int c = 0; c < kHalfCols; ++c) y[c] = bcls[c ^ bhalf];  // the pair reads different banks
+                const float lbv = group_class_bound<2>(y, K);
+                if (bhalf == 0) buf[(size_t)brow * kRowStride + (kRowStride - 1)].x = __float_as_uint(lbv);
+            }
+            named_bar_sync(pair_bar, 64);  // bounds published; class maxima read before sub-lists are written
+            lb = __uint_as_float(rowbuf[kRowStride - 1].x);
+        } else {
+            // End of pass 1 (wide): a row's 256 class maxima (even/odd tiles x two
+            // column halves, 64 each) are in shared memory; four lanes per row
+            // bound them, the quadrant's 32 rows in two batches of 16.
+            float* crow = cls + row * kClsStride + kTileN + hf * kHalfCols;
+#pragma unroll
+            for (int c = 0; c < kHalfCols; ++c) crow[c] = cm[c];
+            named_bar_sync(pair_bar, 64);
+#pragma unroll 1
+            for (int bt = 0; bt < 2; ++bt) {
+                const int brow = r0 + 16 * bt + 8 * hf + (lane >> 2);
+                const int t4 = lane & 3;
+                const float* src = cls + brow * kClsStride + t4 * kHalfCols;
+                float y[kHalfCols];
+                // rotated by 8 per lane of the group: the warp's 32 reads hit 32 banks
+#pragma unroll
+                for (int c = 0; c < kHalfCols; ++c) y[c] = src[(c + 8 * t4) & (kHalfCols - 1)];
+                const float lbv = group_class_bound<4>(y, K);
+                if (t4 == 0) lbw[brow] = lbv;
+            }
+            named_bar_sync(pair_bar, 64);
+            lb = lbw[row];
+        }
         float theta = __int_as_float(0x7fc00000);  // NaN admits nothing
         if (ok && !fb) {
-            const float lb = __uint_as_float(rowbuf[kRowStride - 1].x);
             // fewer than K eligible keys: admit every finite score (masked keys are -inf)
             theta = lb == -INFINITY ? -FLT_MAX : lb - (2.f * delta + fabsf(lb) * kTwoPowM22);
         }
 
         // ---------------- pass 2: collect candidates s >= theta into the sub-list
+        // Narrow: the sub-list sits in shared memory (32-bit shared address).
+        // Wide: it sits in global memory, kWideCap entries per row and half.
+        using Addr = std::conditional_t<kWide, uint64_t, uint32_t>;
+        constexpr int kLimit = kWide ? kWideLimit : kSubLimit;
+        Addr list_base;
+        if constexpr (kWide)
+            list_base = (uint64_t)__cvta_generic_to_global(
+                p.lists + (((size_t)bh * Nq + (size_t)(i < Nq ? i : 0)) * 2 + hf) * kWideCap);
+        else
+            list_base = smem_u32(sub);
         int cnt = 0;
         for (int t = T; t < T2 && ok; ++t) {
             const int j0 = (t - T) * kTileN;
@@ -664,14 +779,14 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const bool full_tile = j0 + cbase + kHalfCols <= N;
             const int climit = lim - j0 - cbase;
             const uint32_t jb = (uint32_t)(j0 + cbase);
-            // 32-bit shared-memory write address and an explicitly predicated
-            // st.shared: the per-column append then costs one store and one add
-            uint32_t waddr = smem_u32(sub) + 8u * (uint32_t)cnt;
+            // Write address and an explicitly predicated store: the per-column
+            // append costs one store and one add.
+            const Addr sub_s = list_base;
+            Addr waddr = sub_s + (Addr)(8u * (uint32_t)cnt);
             // After every 16 columns: a sub-list that could overflow during the next
-            // 16 sends its row to the exact fallback (kSubLimit = kSubCap - 16).
-            const uint32_t sub_s = smem_u32(sub);
+            // 16 sends its row to the exact fallback (kLimit = capacity - 16).
             auto overflow_check = [&]() {
-                if ((int)((waddr - sub_s) >> 3) > kSubLimit) {
+                if ((int)((waddr - sub_s) >> 3) > kLimit) {
                     fb = true;
                     theta = __int_as_float(0x7fc00000);
                     waddr = sub_s;
@@ -700,12 +815,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
                         for (int d = 0; d < 4; ++d) {
                             const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
-                            // append (score, key) when score >= theta; the address chain
-                            // only carries the add (the compare is repeated off it)
-                            asm volatile("{\n .reg .pred p;\n setp.ge.f32 p, %1, %2;\n"
-                                         " @p st.shared.v2.b32 [%0], {%1, %3};\n}"
-                                         :: "r"(waddr), "f"(sc), "f"(theta), "r"(jb + (uint32_t)(c + d)));
-                            waddr += sc >= theta ? 8u : 0u;
+                            append_ge(waddr, sc, theta, jb + (uint32_t)(c + d));
                         }
                         if ((q & 3) == 3) overflow_check();
                     }
@@ -717,11 +827,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
                         for (int d = 0; d < 4; ++d) {
                             const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
-                            asm volatile("{\n .reg .pred p, e;\n setp.ge.f32 p, %1, %2;\n setp.lt.s32 e, %4, %5;\n"
-                                         " and.pred p, p, e;\n @p st.shared.v2.b32 [%0], {%1, %3};\n}"
-                                         :: "r"(waddr), "f"(sc), "f"(theta), "r"(jb + (uint32_t)(c + d)), "r"(c + d),
-                                            "r"(climit));
-                            waddr += (sc >= theta && c + d < climit) ? 8u : 0u;
+                            append_ge_lt(waddr, sc, theta, jb + (uint32_t)(c + d), c + d, climit);
                         }
                         if ((q & 3) == 3) overflow_check();
                     }
@@ -732,325 +838,330 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         if (!ok) atomicOr(p.status, 4);
 
-        // ---------------------------------------------- per-row final selection
-        // Publish both sub-list counts (-1: exact fallback); then the lane pair
-        // (2r, 2r+1) of warp hf finishes row r0 + 16*hf + r, each lane owning one
-        // sub-list (both are in ascending key order).
-        //  1. bisection on the approximate scores from [lb, max] until exactly K
-        //     are >= lo; x_K = min{s >= lo}, x_K1 = max{s < lo}.  Entries above
-        //     U = x_K1 + 2*delta are certainly in the exact top K, entries below
-        //     W = x_K - 2*delta certainly not (with a bracket [lo, hi] instead
-        //     when the scores do not split: U = hi + 2*delta, W = lo - 2*delta).
-        //  2. entries in [W, U] (usually none) are rescored with the canonical
-        //     fp32 formula and the best K - #(s > U) of them by (score desc,
-        //     key asc) are kept.
-        //  3. each lane compacts its kept keys in place; lane 2r merges the two
-        //     lists from the front, lane 2r+1 from the back, into the output row.
-        // Quadrant metadata lives in the window of its column-half-0 warp: only
-        // the quadrant's two warps touch it, and both are past their last window
-        // read once the first barrier below completes.
-        int* qmeta = reinterpret_cast<int*>(win + (ew & 3) * 4 * kWinCopy);
-        named_bar_sync(pair_bar, 64);
-        qmeta[2 * lane + hf] = fb ? -1 : cnt;
-        named_bar_sync(pair_bar, 64);
-        {
-            const int frow = r0 + 16 * hf + (lane >> 1);
-            const int fh = lane & 1;
-            const int fi = i0 + frow;
-            const bool active = ok && fi < Nq;
-            const int ca = qmeta[2 * (frow - r0)], cb = qmeta[2 * (frow - r0) + 1];
-            uint2* frowbuf = buf + (size_t)frow * kRowStride;
-            uint2* own = frowbuf + fh * kSubCap;
-            const int nown = fh ? cb : ca;
-            bool to_fallback = active && (ca < 0 || cb < 0);
-            bool work = active && !to_fallback;
-            const int tot = ca + cb;
-            const bool all_in = tot <= K;
-            const size_t orow_id = (size_t)bh * Nq + (size_t)(fi < Nq ? fi : 0);
-            float fdelta = 0.f, lo = 0.f;
-            if (work) {
-                fdelta = p.rowinfo[orow_id].y;
-                lo = __uint_as_float(frowbuf[kRowStride - 1].x);
-            }
-            const uint32_t own_s = smem_u32(own);
-            // Slots past the warp's longest sub-list hold -inf in every lane and
-            // change no count or extremum below: loops stop after nch 8-slot chunks.
-            const int nch = (int)((__reduce_max_sync(kFull, work ? (unsigned)nown : 0u) + 7u) >> 3);
-            float x[kSubCap];
-#pragma unroll
-            for (int ch = 0; ch < kSubCap / 8; ++ch) {
-#pragma unroll
-                for (int u = 0; u < 8; ++u) x[8 * ch + u] = -INFINITY;
-                if (ch < nch) {
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        const int q = 8 * ch + u;
-                        x[q] = lds_f32_or(own_s + 8u * q, work && q < nown, -INFINITY);
-                    }
-                }
-            }
-
-            // 1. split at the K-th best approximate score
-            float hi8[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) hi8[u] = -INFINITY;
-#pragma unroll
-            for (int ch = 0; ch < kSubCap / 8; ++ch) {
-                if (ch < nch) {
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) hi8[u] = fmaxf(hi8[u], x[8 * ch + u]);
-                }
-            }
-            float hi = fmaxf(fmaxf(fmaxf(hi8[0], hi8[1]), fmaxf(hi8[2], hi8[3])),
-                             fmaxf(fmaxf(hi8[4], hi8[5]), fmaxf(hi8[6], hi8[7])));
-            hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, 1));
-            int cnt_lo = count_ge_chunks<kSubCap>(x, lo, nch);
-            cnt_lo += __shfl_xor_sync(kFull, cnt_lo, 1);
-            if (work && !all_in && cnt_lo < K) {
-                to_fallback = true;  // cannot happen: lb is reached by K candidates
-                work = false;
-            }
-            // Stop at an exact split (K entries >= lo) or once the bracket is within
-            // 4 delta: the boundary band then holds the few near-tied entries and the
-            // canonical rescoring below decides them.
-            bool done = !work || all_in || cnt_lo == K || hi - lo <= 4.f * fdelta;
-            for (int it = 0; it < 40; ++it) {
-                if (__all_sync(kFull, done)) break;
-                const float mid = lo + 0.5f * (hi - lo);
-                int c = count_ge_chunks<kSubCap>(x, mid, nch);
-                c += __shfl_xor_sync(kFull, c, 1);
-                if (!done) {
-                    if (!(mid > lo && mid < hi)) {
-                        done = true;
-                    } else if (c >= K) {
-                        lo = mid;
-                        cnt_lo = c;
-                        done = c == K || hi - lo <= 4.f * fdelta;
-                    } else {
-                        hi = mid;
-                        done = hi - lo <= 4.f * fdelta;
-                    }
-                }
-            }
-            float kmin8[8], kmax8[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                kmin8[u] = INFINITY;
-                kmax8[u] = -INFINITY;
-            }
-#pragma unroll
-            for (int ch = 0; ch < kSubCap / 8; ++ch) {
-                if (ch < nch) {
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        const float xq = x[8 * ch + u];
-                        const bool ge = xq >= lo;
-                        kmin8[u] = ge ? fminf(kmin8[u], xq) : kmin8[u];
-                        kmax8[u] = ge ? kmax8[u] : fmaxf(kmax8[u], xq);
-                    }
-                }
-            }
-            float xk = kmin8[0], xk1 = kmax8[0];
-#pragma unroll
-            for (int u = 1; u < 8; ++u) {
-                xk = fminf(xk, kmin8[u]);
-                xk1 = fmaxf(xk1, kmax8[u]);
-            }
-            xk = fminf(xk, __shfl_xor_sync(kFull, xk, 1));
-            xk1 = fmaxf(xk1, __shfl_xor_sync(kFull, xk1, 1));
-            float U = -INFINITY, W = INFINITY;  // all_in: keep every entry, empty band
-            if (work && !all_in) {
-                const bool split = cnt_lo == K && xk1 > -INFINITY;
-                const float top = split ? xk1 : hi;
-                const float bot = split ? xk : lo;
-                const float sl = fmaxf(fabsf(top), fabsf(bot));
-                const float m2 = 2.f * fdelta + (sl + 2.f * fdelta) * kTwoPowM22;
-                U = top + m2;
-                W = bot - m2;
-            }
-            int n_in = 0, own_nb = 0;
+        if constexpr (kWide) {
+            // the warp-per-row wide_final_kernel finishes the row from its two lists
+            if (ok && i < Nq) p.counts[((size_t)bh * Nq + i) * 2 + hf] = fb ? -1 : cnt;
+        } else {
+            // ---------------------------------------------- per-row final selection
+            // Publish both sub-list counts (-1: exact fallback); then the lane pair
+            // (2r, 2r+1) of warp hf finishes row r0 + 16*hf + r, each lane owning one
+            // sub-list (both are in ascending key order).
+            //  1. bisection on the approximate scores from [lb, max] until exactly K
+            //     are >= lo; x_K = min{s >= lo}, x_K1 = max{s < lo}.  Entries above
+            //     U = x_K1 + 2*delta are certainly in the exact top K, entries below
+            //     W = x_K - 2*delta certainly not (with a bracket [lo, hi] instead
+            //     when the scores do not split: U = hi + 2*delta, W = lo - 2*delta).
+            //  2. entries in [W, U] (usually none) are rescored with the canonical
+            //     fp32 formula and the best K - #(s > U) of them by (score desc,
+            //     key asc) are kept.
+            //  3. each lane compacts its kept keys in place; lane 2r merges the two
+            //     lists from the front, lane 2r+1 from the back, into the output row.
+            // Quadrant metadata lives in the window of its column-half-0 warp: only
+            // the quadrant's two warps touch it, and both are past their last window
+            // read once the first barrier below completes.
+            int* qmeta = reinterpret_cast<int*>(win + (ew & 3) * 4 * kWinCopy);
+            named_bar_sync(pair_bar, 64);
+            qmeta[2 * lane + hf] = fb ? -1 : cnt;
+            named_bar_sync(pair_bar, 64);
             {
-                int ni8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, nb8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
+                const int frow = r0 + 16 * hf + (lane >> 1);
+                const int fh = lane & 1;
+                const int fi = i0 + frow;
+                const bool active = ok && fi < Nq;
+                const int ca = qmeta[2 * (frow - r0)], cb = qmeta[2 * (frow - r0) + 1];
+                uint2* frowbuf = buf + (size_t)frow * kRowStride;
+                uint2* own = frowbuf + fh * kSubCap;
+                const int nown = fh ? cb : ca;
+                bool to_fallback = active && (ca < 0 || cb < 0);
+                bool work = active && !to_fallback;
+                const int tot = ca + cb;
+                const bool all_in = tot <= K;
+                const size_t orow_id = (size_t)bh * Nq + (size_t)(fi < Nq ? fi : 0);
+                float fdelta = 0.f, lo = 0.f;
+                if (work) {
+                    fdelta = p.rowinfo[orow_id].y;
+                    lo = __uint_as_float(frowbuf[kRowStride - 1].x);
+                }
+                const uint32_t own_s = smem_u32(own);
+                // Slots past the warp's longest sub-list hold -inf in every lane and
+                // change no count or extremum below: loops stop after nch 8-slot chunks.
+                const int nch = (int)((__reduce_max_sync(kFull, work ? (unsigned)nown : 0u) + 7u) >> 3);
+                float x[kSubCap];
+    #pragma unroll
+                for (int ch = 0; ch < kSubCap / 8; ++ch) {
+    #pragma unroll
+                    for (int u = 0; u < 8; ++u) x[8 * ch + u] = -INFINITY;
+                    if (ch < nch) {
+    #pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const int q = 8 * ch + u;
+                            x[q] = lds_f32_or(own_s + 8u * q, work && q < nown, -INFINITY);
+                        }
+                    }
+                }
+
+                // 1. split at the K-th best approximate score
+                float hi8[8];
+    #pragma unroll
+                for (int u = 0; u < 8; ++u) hi8[u] = -INFINITY;
+    #pragma unroll
                 for (int ch = 0; ch < kSubCap / 8; ++ch) {
                     if (ch < nch) {
-#pragma unroll
+    #pragma unroll
+                        for (int u = 0; u < 8; ++u) hi8[u] = fmaxf(hi8[u], x[8 * ch + u]);
+                    }
+                }
+                float hi = fmaxf(fmaxf(fmaxf(hi8[0], hi8[1]), fmaxf(hi8[2], hi8[3])),
+                                 fmaxf(fmaxf(hi8[4], hi8[5]), fmaxf(hi8[6], hi8[7])));
+                hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, 1));
+                int cnt_lo = count_ge_chunks<kSubCap>(x, lo, nch);
+                cnt_lo += __shfl_xor_sync(kFull, cnt_lo, 1);
+                if (work && !all_in && cnt_lo < K) {
+                    to_fallback = true;  // cannot happen: lb is reached by K candidates
+                    work = false;
+                }
+                // Stop at an exact split (K entries >= lo) or once the bracket is within
+                // 4 delta: the boundary band then holds the few near-tied entries and the
+                // canonical rescoring below decides them.
+                bool done = !work || all_in || cnt_lo == K || hi - lo <= 4.f * fdelta;
+                for (int it = 0; it < 40; ++it) {
+                    if (__all_sync(kFull, done)) break;
+                    const float mid = lo + 0.5f * (hi - lo);
+                    int c = count_ge_chunks<kSubCap>(x, mid, nch);
+                    c += __shfl_xor_sync(kFull, c, 1);
+                    if (!done) {
+                        if (!(mid > lo && mid < hi)) {
+                            done = true;
+                        } else if (c >= K) {
+                            lo = mid;
+                            cnt_lo = c;
+                            done = c == K || hi - lo <= 4.f * fdelta;
+                        } else {
+                            hi = mid;
+                            done = hi - lo <= 4.f * fdelta;
+                        }
+                    }
+                }
+                float kmin8[8], kmax8[8];
+    #pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    kmin8[u] = INFINITY;
+                    kmax8[u] = -INFINITY;
+                }
+    #pragma unroll
+                for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                    if (ch < nch) {
+    #pragma unroll
                         for (int u = 0; u < 8; ++u) {
                             const float xq = x[8 * ch + u];
-                            ni8[u] += xq > U ? 1 : 0;
-                            nb8[u] += (xq >= W && xq <= U) ? 1 : 0;
+                            const bool ge = xq >= lo;
+                            kmin8[u] = ge ? fminf(kmin8[u], xq) : kmin8[u];
+                            kmax8[u] = ge ? kmax8[u] : fmaxf(kmax8[u], xq);
                         }
                     }
                 }
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    n_in += ni8[u];
-                    own_nb += nb8[u];
+                float xk = kmin8[0], xk1 = kmax8[0];
+    #pragma unroll
+                for (int u = 1; u < 8; ++u) {
+                    xk = fminf(xk, kmin8[u]);
+                    xk1 = fmaxf(xk1, kmax8[u]);
                 }
-            }
-            n_in += __shfl_xor_sync(kFull, n_in, 1);
-            const int oth_nb = __shfl_xor_sync(kFull, own_nb, 1);
-            const int need = K - n_in;
-            bool rescore = work && !all_in && own_nb + oth_nb != need;
-            if (rescore && (own_nb > kMaxBand / 2 || oth_nb > kMaxBand / 2)) {
-                to_fallback = true;
-                work = false;
-                rescore = false;
-            }
+                xk = fminf(xk, __shfl_xor_sync(kFull, xk, 1));
+                xk1 = fmaxf(xk1, __shfl_xor_sync(kFull, xk1, 1));
+                float U = -INFINITY, W = INFINITY;  // all_in: keep every entry, empty band
+                if (work && !all_in) {
+                    const bool split = cnt_lo == K && xk1 > -INFINITY;
+                    const float top = split ? xk1 : hi;
+                    const float bot = split ? xk : lo;
+                    const float sl = fmaxf(fabsf(top), fabsf(bot));
+                    const float m2 = 2.f * fdelta + (sl + 2.f * fdelta) * kTwoPowM22;
+                    U = top + m2;
+                    W = bot - m2;
+                }
+                int n_in = 0, own_nb = 0;
+                {
+                    int ni8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, nb8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    #pragma unroll
+                    for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                        if (ch < nch) {
+    #pragma unroll
+                            for (int u = 0; u < 8; ++u) {
+                                const float xq = x[8 * ch + u];
+                                ni8[u] += xq > U ? 1 : 0;
+                                nb8[u] += (xq >= W && xq <= U) ? 1 : 0;
+                            }
+                        }
+                    }
+    #pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        n_in += ni8[u];
+                        own_nb += nb8[u];
+                    }
+                }
+                n_in += __shfl_xor_sync(kFull, n_in, 1);
+                const int oth_nb = __shfl_xor_sync(kFull, own_nb, 1);
+                const int need = K - n_in;
+                bool rescore = work && !all_in && own_nb + oth_nb != need;
+                if (rescore && (own_nb > kMaxBand / 2 || oth_nb > kMaxBand / 2)) {
+                    to_fallback = true;
+                    work = false;
+                    rescore = false;
+                }
 
-            // 2. canonical rescoring of the boundary band
-            uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)frow * kMaxBand;  // MMAs are done with sA
-            uint2* myslots = scratch + fh * (kMaxBand / 2);
-            if (rescore) {
-                uint32_t wa = smem_u32(myslots);
-#pragma unroll
-                for (int ch = 0; ch < kSubCap / 8; ++ch) {
-                    if (ch < nch) {
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) {
-                            const int q = 8 * ch + u;
-                            const bool inb = x[q] >= W && x[q] <= U;
-                            sts_u32_if(wa, (uint32_t)q, inb);
-                            wa += inb ? 8u : 0u;
+                // 2. canonical rescoring of the boundary band
+                uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)frow * kMaxBand;  // MMAs are done with sA
+                uint2* myslots = scratch + fh * (kMaxBand / 2);
+                if (rescore) {
+                    uint32_t wa = smem_u32(myslots);
+    #pragma unroll
+                    for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                        if (ch < nch) {
+    #pragma unroll
+                            for (int u = 0; u < 8; ++u) {
+                                const int q = 8 * ch + u;
+                                const bool inb = x[q] >= W && x[q] <= U;
+                                sts_u32_if(wa, (uint32_t)q, inb);
+                                wa += inb ? 8u : 0u;
+                            }
                         }
                     }
                 }
-            }
-            const int nbmax = __reduce_max_sync(kFull, rescore ? (unsigned)own_nb : 0u);
-            if (nbmax > 0) {
-                __syncwarp();
-                const float* qrow = p.qp32 + orow_id * kR;
-                const float* kbase = p.kp32 + (size_t)(b * Hkv + g) * N * kR;
-                for (int u = 0; u < nbmax; ++u) {
-                    if (rescore && u < own_nb) {
-                        const int jj = (int)own[myslots[u].x].y;
-                        const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, p.q0 + fi, jj,
-                                                                     p.scale);
-                        myslots[u] = make_uint2(order_key(ex), (uint32_t)jj);
+                const int nbmax = __reduce_max_sync(kFull, rescore ? (unsigned)own_nb : 0u);
+                if (nbmax > 0) {
+                    __syncwarp();
+                    const float* qrow = p.qp32 + orow_id * kR;
+                    const float* kbase = p.kp32 + (size_t)(b * Hkv + g) * N * kR;
+                    for (int u = 0; u < nbmax; ++u) {
+                        if (rescore && u < own_nb) {
+                            const int jj = (int)own[myslots[u].x].y;
+                            const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, p.q0 + fi, jj,
+                                                                         p.scale);
+                            myslots[u] = make_uint2(order_key(ex), (uint32_t)jj);
+                        }
+                    }
+                    __syncwarp();
+                }
+                uint32_t selmask = 0u;
+                if (rescore) {
+                    const uint2* oslots = scratch + (1 - fh) * (kMaxBand / 2);
+                    for (int a2 = 0; a2 < own_nb; ++a2) {
+                        const uint2 ea = myslots[a2];
+                        int rank = 0;
+                        for (int c2 = 0; c2 < own_nb; ++c2) {
+                            const uint2 e = myslots[c2];
+                            rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
+                        }
+                        for (int c2 = 0; c2 < oth_nb; ++c2) {
+                            const uint2 e = oslots[c2];
+                            rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
+                        }
+                        if (rank < need) selmask |= 1u << a2;
                     }
                 }
-                __syncwarp();
-            }
-            uint32_t selmask = 0u;
-            if (rescore) {
-                const uint2* oslots = scratch + (1 - fh) * (kMaxBand / 2);
-                for (int a2 = 0; a2 < own_nb; ++a2) {
-                    const uint2 ea = myslots[a2];
-                    int rank = 0;
-                    for (int c2 = 0; c2 < own_nb; ++c2) {
-                        const uint2 e = myslots[c2];
-                        rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
-                    }
-                    for (int c2 = 0; c2 < oth_nb; ++c2) {
-                        const uint2 e = oslots[c2];
-                        rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
-                    }
-                    if (rank < need) selmask |= 1u << a2;
-                }
-            }
 
-            // 3. compact kept keys in place, then merge the two lists
-            int nsel = 0;
-            if (work) {
-                uint32_t wa = own_s + 4u;  // .y of the next kept slot
-                int bidx = 0;
-#pragma unroll
-                for (int ch = 0; ch < kSubCap / 8; ++ch) {
-                    if (ch < nch) {
-                        // scores re-read from the list, a chunk at a time (x[] is not kept
-                        // live across the band work); loads before the chunk's stores
-                        uint2 e8[8];
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) e8[u] = lds_u2(own_s + 8u * (8 * ch + u));
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) {
-                            const int q = 8 * ch + u;
-                            const float sq = q < nown ? __uint_as_float(e8[u].x) : -INFINITY;
-                            const bool inb = sq >= W && sq <= U;
-                            const bool keep = sq > U || (inb && (!rescore || ((selmask >> bidx) & 1u)));
-                            bidx += inb ? 1 : 0;
-                            sts_u32_if(wa, e8[u].y, keep);
-                            wa += keep ? 8u : 0u;
+                // 3. compact kept keys in place, then merge the two lists
+                int nsel = 0;
+                if (work) {
+                    uint32_t wa = own_s + 4u;  // .y of the next kept slot
+                    int bidx = 0;
+    #pragma unroll
+                    for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                        if (ch < nch) {
+                            // scores re-read from the list, a chunk at a time (x[] is not kept
+                            // live across the band work); loads before the chunk's stores
+                            uint2 e8[8];
+    #pragma unroll
+                            for (int u = 0; u < 8; ++u) e8[u] = lds_u2(own_s + 8u * (8 * ch + u));
+    #pragma unroll
+                            for (int u = 0; u < 8; ++u) {
+                                const int q = 8 * ch + u;
+                                const float sq = q < nown ? __uint_as_float(e8[u].x) : -INFINITY;
+                                const bool inb = sq >= W && sq <= U;
+                                const bool keep = sq > U || (inb && (!rescore || ((selmask >> bidx) & 1u)));
+                                bidx += inb ? 1 : 0;
+                                sts_u32_if(wa, e8[u].y, keep);
+                                wa += keep ? 8u : 0u;
+                            }
+                        }
+                    }
+                    nsel = (int)((wa - own_s - 4u) >> 3);
+                }
+                const int nsel_oth = __shfl_xor_sync(kFull, nsel, 1);
+                __syncwarp();
+                const int nA = fh ? nsel_oth : nsel;
+                const int nB = fh ? nsel : nsel_oth;
+                const int ntot = nA + nB;
+                const int mfront = (ntot + 1) >> 1;
+                const int mcount = fh ? ntot - mfront : mfront;
+                const int steps = (int)__reduce_max_sync(kFull, work ? (unsigned)mcount : 0u);
+                // The merged rows are staged in the (now idle) k' tile ring, 256 B per row
+                // with the 16-byte groups XOR-swizzled by row, then written out with
+                // coalesced 16-byte stores.
+                const uint32_t stage_s = smem_u32(sB);
+                {
+                    const uint32_t LA = smem_u32(frowbuf) + 4u;             // .y fields
+                    const uint32_t LB = LA + 8u * kSubCap;
+                    const int dir = fh ? -1 : 1;
+                    int ia = fh ? nA - 1 : 0, ib = fh ? nB - 1 : 0;
+                    // lane 2r takes the smaller key each step, lane 2r+1 the larger:
+                    // compare on j for the front and on -j for the back
+                    const int sgn = fh ? -1 : 1;
+                    int ja = (work && ia >= 0 && ia < nA) ? (int)lds_u32(LA + 8u * ia) : -1;
+                    int jb = (work && ib >= 0 && ib < nB) ? (int)lds_u32(LB + 8u * ib) : -1;
+                    const uint32_t srow = stage_s + 256u * frow;
+                    const int swz = (frow & 7) << 2;
+                    for (int st = 0; st < steps; ++st) {
+                        if (work && st < mcount) {
+                            const int ka = ja < 0 ? INT_MAX : sgn * ja;
+                            const int kb = jb < 0 ? INT_MAX : sgn * jb;
+                            const bool ta = ka < kb;
+                            const int col = fh ? ntot - 1 - st : st;
+                            sts_f32(srow + 4u * (uint32_t)(col ^ swz), __int_as_float(ta ? ja : jb));
+                            if (ta) {
+                                ia += dir;
+                                ja = (ia >= 0 && ia < nA) ? (int)lds_u32(LA + 8u * ia) : -1;
+                            } else {
+                                ib += dir;
+                                jb = (ib >= 0 && ib < nB) ? (int)lds_u32(LB + 8u * ib) : -1;
+                            }
+                        }
+                    }
+                    if (work && fh) {
+                        for (int q = ntot; q < K; ++q) sts_f32(srow + 4u * (uint32_t)(q ^ swz), __int_as_float(-1));
+                    }
+                }
+                __syncwarp();
+                {
+                    // this warp's 16 rows: r0 + 16 * hf + rin, finished by lane pair rin
+                    const unsigned workmask = __ballot_sync(kFull, work);
+                    const int rbase = r0 + 16 * hf;
+                    if ((K & 3) == 0) {
+                        const int per_row = K >> 2;
+                        for (int f = lane; f < 16 * per_row; f += 32) {
+                            const int rin = f / per_row, v = f - rin * per_row;
+                            if ((workmask >> (2 * rin)) & 1u) {
+                                const int rrow = rbase + rin;
+                                const uint4 val = lds_u4(stage_s + 256u * rrow + 16u * (uint32_t)(v ^ (rrow & 7)));
+                                const size_t oid = (size_t)bh * Nq + (size_t)(i0 + rrow);
+                                *(reinterpret_cast<uint4*>(p.out + oid * K) + v) = val;
+                            }
+                        }
+                    } else {
+                        for (int f = lane; f < 16 * K; f += 32) {
+                            const int rin = f / K, c = f - rin * K;
+                            if ((workmask >> (2 * rin)) & 1u) {
+                                const int rrow = rbase + rin;
+                                const uint32_t val = lds_u32(stage_s + 256u * rrow + 4u * (uint32_t)(c ^ ((rrow & 7) << 2)));
+                                const size_t oid = (size_t)bh * Nq + (size_t)(i0 + rrow);
+                                p.out[oid * K + c] = (int32_t)val;
+                            }
                         }
                     }
                 }
-                nsel = (int)((wa - own_s - 4u) >> 3);
-            }
-            const int nsel_oth = __shfl_xor_sync(kFull, nsel, 1);
-            __syncwarp();
-            const int nA = fh ? nsel_oth : nsel;
-            const int nB = fh ? nsel : nsel_oth;
-            const int ntot = nA + nB;
-            const int mfront = (ntot + 1) >> 1;
-            const int mcount = fh ? ntot - mfront : mfront;
-            const int steps = (int)__reduce_max_sync(kFull, work ? (unsigned)mcount : 0u);
-            // The merged rows are staged in the (now idle) k' tile ring, 256 B per row
-            // with the 16-byte groups XOR-swizzled by row, then written out with
-            // coalesced 16-byte stores.
-            const uint32_t stage_s = smem_u32(sB);
-            {
-                const uint32_t LA = smem_u32(frowbuf) + 4u;             // .y fields
-                const uint32_t LB = LA + 8u * kSubCap;
-                const int dir = fh ? -1 : 1;
-                int ia = fh ? nA - 1 : 0, ib = fh ? nB - 1 : 0;
-                // lane 2r takes the smaller key each step, lane 2r+1 the larger:
-                // compare on j for the front and on -j for the back
-                const int sgn = fh ? -1 : 1;
-                int ja = (work && ia >= 0 && ia < nA) ? (int)lds_u32(LA + 8u * ia) : -1;
-                int jb = (work && ib >= 0 && ib < nB) ? (int)lds_u32(LB + 8u * ib) : -1;
-                const uint32_t srow = stage_s + 256u * frow;
-                const int swz = (frow & 7) << 2;
-                for (int st = 0; st < steps; ++st) {
-                    if (work && st < mcount) {
-                        const int ka = ja < 0 ? INT_MAX : sgn * ja;
-                        const int kb = jb < 0 ? INT_MAX : sgn * jb;
-                        const bool ta = ka < kb;
-                        const int col = fh ? ntot - 1 - st : st;
-                        sts_f32(srow + 4u * (uint32_t)(col ^ swz), __int_as_float(ta ? ja : jb));
-                        if (ta) {
-                            ia += dir;
-                            ja = (ia >= 0 && ia < nA) ? (int)lds_u32(LA + 8u * ia) : -1;
-                        } else {
-                            ib += dir;
-                            jb = (ib >= 0 && ib < nB) ? (int)lds_u32(LB + 8u * ib) : -1;
-                        }
-                    }
+                if (to_fallback && fh == 0) {
+                    const int pos = atomicAdd(p.fb_count, 1);
+                    p.fb_list[pos] = (int32_t)orow_id;
                 }
-                if (work && fh) {
-                    for (int q = ntot; q < K; ++q) sts_f32(srow + 4u * (uint32_t)(q ^ swz), __int_as_float(-1));
-                }
-            }
-            __syncwarp();
-            {
-                // this warp's 16 rows: r0 + 16 * hf + rin, finished by lane pair rin
-                const unsigned workmask = __ballot_sync(kFull, work);
-                const int rbase = r0 + 16 * hf;
-                if ((K & 3) == 0) {
-                    const int per_row = K >> 2;
-                    for (int f = lane; f < 16 * per_row; f += 32) {
-                        const int rin = f / per_row, v = f - rin * per_row;
-                        if ((workmask >> (2 * rin)) & 1u) {
-                            const int rrow = rbase + rin;
-                            const uint4 val = lds_u4(stage_s + 256u * rrow + 16u * (uint32_t)(v ^ (rrow & 7)));
-                            const size_t oid = (size_t)bh * Nq + (size_t)(i0 + rrow);
-                            *(reinterpret_cast<uint4*>(p.out + oid * K) + v) = val;
-                        }
-                    }
-                } else {
-                    for (int f = lane; f < 16 * K; f += 32) {
-                        const int rin = f / K, c = f - rin * K;
-                        if ((workmask >> (2 * rin)) & 1u) {
-                            const int rrow = rbase + rin;
-                            const uint32_t val = lds_u32(stage_s + 256u * rrow + 4u * (uint32_t)(c ^ ((rrow & 7) << 2)));
-                            const size_t oid = (size_t)bh * Nq + (size_t)(i0 + rrow);
-                            p.out[oid * K + c] = (int32_t)val;
-                        }
-                    }
-                }
-            }
-            if (to_fallback && fh == 0) {
-                const int pos = atomicAdd(p.fb_count, 1);
-                p.fb_list[pos] = (int32_t)orow_id;
             }
         }
     }
@@ -1157,6 +1268,185 @@ exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, co
     }
 }
 
+// ------------------------------------------ wide selection: per-row final choice
+
+struct WideFinalParams {
+    const uint2* lists;
+    const int* counts;
+    const float2* rowinfo;
+    const float* bias;
+    const float* qp32;
+    const float* kp32;
+    int32_t* out;
+    int* fb_count;
+    int32_t* fb_list;
+    long long rows;
+    int L, H, Hkv, N, K, Nq, q0;
+    float scale;
+};
+
+// One warp per query row.  The row's two candidate sub-lists A and B (one per
+// column half, keys ascending, at most kWideCap each) are loaded as entry
+// q = lane + 32 e of A ++ B.  With more than K candidates, the K-th best
+// approximate score x_K splits them: let top = the best score below x_K when
+// exactly K entries reach x_K, else x_K itself, and m2 = 2 delta plus rounding
+// slack.  Entries above U = top + m2 are certainly in the exact top K, entries
+// below W = x_K - m2 certainly not; when the band [W, U] holds more entries than
+// the free slots, its entries are rescored with the canonical fp32 formula and
+// the best by (score desc, key asc) fill the slots.  The kept keys of A and B
+// are then merged by rank into ascending order, -1 padded.  Rows whose lists
+// overflowed, whose inputs are not finite, or whose band holds more than 32
+// entries go to the exact fallback list.
+__global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p) {
+    __shared__ int skept[8][2][kWideMaxK];
+    __shared__ int sband[8][32];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = lanemask_lt();
+    const int K = p.K;
+    for (long long row = (long long)blockIdx.x * 8 + warp; row < p.rows; row += (long long)gridDim.x * 8) {
+        const int ca = p.counts[2 * row], cb = p.counts[2 * row + 1];
+        bool fallback = ca < 0 || cb < 0 || ca > kWideCap || cb > kWideCap;
+        if (!fallback) {
+            const uint2* LA = p.lists + (size_t)row * (2 * kWideCap);
+            const uint2* LB = LA + kWideCap;
+            const int tot = ca + cb;
+            float sv[kWideEPL];
+            uint32_t jv[kWideEPL];
+            bool val[kWideEPL], keep[kWideEPL];
+#pragma unroll
+            for (int e = 0; e < kWideEPL; ++e) {
+                const int q = lane + 32 * e;
+                val[e] = q < tot;
+                uint2 t = make_uint2(0u, 0u);
+                if (val[e]) t = q < ca ? LA[q] : LB[q - ca];
+                sv[e] = __uint_as_float(t.x);
+                jv[e] = t.y;
+                keep[e] = val[e];
+            }
+            if (tot > K) {
+                uint32_t u[kWideEPL];
+#pragma unroll
+                for (int e = 0; e < kWideEPL; ++e) u[e] = order_key(sv[e]);
+                uint32_t T;
+                int ties;
+                warp_kth_key<kWideEPL>(u, val, K, T, ties);
+                unsigned nge = 0;
+                uint32_t below = 0u;  // order keys of finite scores are never 0
+#pragma unroll
+                for (int e = 0; e < kWideEPL; ++e) {
+                    if (val[e]) {
+                        if (u[e] >= T) ++nge;
+                        else below = max(below, u[e]);
+                    }
+                }
+                nge = __reduce_add_sync(kFull, nge);
+                below = __reduce_max_sync(kFull, below);
+                const float xk = key_to_float(T);
+                const float top = ((int)nge == K && below != 0u) ? key_to_float(below) : xk;
+                const float fdelta = p.rowinfo[row].y;
+                const float sl = fmaxf(fabsf(top), fabsf(xk));
+                const float m2 = 2.f * fdelta + (sl + 2.f * fdelta) * kTwoPowM22;
+                const float U = top + m2, W = xk - m2;
+                unsigned n_in = 0, nb = 0;
+                bool band[kWideEPL];
+#pragma unroll
+                for (int e = 0; e < kWideEPL; ++e) {
+                    band[e] = val[e] && sv[e] >= W && sv[e] <= U;
+                    n_in += (val[e] && sv[e] > U) ? 1u : 0u;
+                    nb += band[e] ? 1u : 0u;
+                }
+                n_in = __reduce_add_sync(kFull, n_in);
+                nb = __reduce_add_sync(kFull, nb);
+                const int need = K - (int)n_in;
+                if ((int)nb == need) {
+#pragma unroll
+                    for (int e = 0; e < kWideEPL; ++e) keep[e] = val[e] && sv[e] >= W;
+                } else if (nb > 32u) {
+                    fallback = true;
+                } else {
+                    // band entries to lanes 0..nb-1, in (e, lane) order
+                    const long long bh = row / p.Nq;
+                    const int ipos = p.q0 + (int)(row - bh * p.Nq);
+                    const int b = (int)(bh / p.H);
+                    const int g = (int)(bh - (long long)b * p.H) / (p.H / p.Hkv);
+                    int slot[kWideEPL];
+                    int base = 0;
+#pragma unroll
+                    for (int e = 0; e < kWideEPL; ++e) {
+                        const unsigned bal = __ballot_sync(kFull, band[e]);
+                        slot[e] = base + __popc(bal & lt);
+                        if (band[e]) sband[warp][slot[e]] = (int)jv[e];
+                        base += __popc(bal);
+                    }
+                    __syncwarp();
+                    uint32_t ek = 0u;
+                    int jj = INT_MAX;
+                    if (lane < (int)nb) {
+                        jj = sband[warp][lane];
+                        const float ex = canonical_score(p.qp32 + (size_t)row * kR,
+                                                         p.kp32 + ((size_t)(b * p.Hkv + g) * p.N + jj) * kR, p.bias,
+                                                         p.L, ipos, jj, p.scale);
+                        ek = order_key(ex);
+                    }
+                    int rank = 0;
+                    for (int l2 = 0; l2 < (int)nb; ++l2) {
+                        const uint32_t e2 = __shfl_sync(kFull, ek, l2);
+                        const int j2 = __shfl_sync(kFull, jj, l2);
+                        rank += (e2 > ek || (e2 == ek && j2 < jj)) ? 1 : 0;
+                    }
+                    const unsigned sel = __ballot_sync(kFull, lane < (int)nb && rank < need);
+#pragma unroll
+                    for (int e = 0; e < kWideEPL; ++e)
+                        keep[e] = val[e] && (sv[e] > U || (band[e] && ((sel >> slot[e]) & 1u)));
+                    __syncwarp();  // sband is rewritten for the next row
+                }
+            }
+            if (!fallback) {
+                // kept keys of each list, compacted in list order (ascending keys)
+                int* SA = skept[warp][0];
+                int* SB = skept[warp][1];
+                int na = 0, nbk = 0;
+                int li[kWideEPL];
+#pragma unroll
+                for (int e = 0; e < kWideEPL; ++e) {
+                    const bool isA = lane + 32 * e < ca;
+                    const bool kA = keep[e] && isA, kB = keep[e] && !isA;
+                    const unsigned balA = __ballot_sync(kFull, kA);
+                    const unsigned balB = __ballot_sync(kFull, kB);
+                    li[e] = isA ? na + __popc(balA & lt) : nbk + __popc(balB & lt);
+                    if (kA && li[e] < kWideMaxK) SA[li[e]] = (int)jv[e];
+                    if (kB && li[e] < kWideMaxK) SB[li[e]] = (int)jv[e];
+                    na += __popc(balA);
+                    nbk += __popc(balB);
+                }
+                __syncwarp();
+                int32_t* orow = p.out + row * K;
+#pragma unroll
+                for (int e = 0; e < kWideEPL; ++e) {
+                    if (keep[e]) {
+                        const bool isA = lane + 32 * e < ca;
+                        const int* other = isA ? SB : SA;
+                        int lo = 0, hi = min(isA ? nbk : na, kWideMaxK);
+                        while (lo < hi) {  // keys of the other list below this one
+                            const int mid = (lo + hi) >> 1;
+                            if (other[mid] < (int)jv[e]) lo = mid + 1; else hi = mid;
+                        }
+                        const int pos = li[e] + lo;
+                        if (pos < K) orow[pos] = (int32_t)jv[e];
+                    }
+                }
+                for (int q = na + nbk + lane; q < K; q += 32) orow[q] = -1;
+                __syncwarp();  // skept is rewritten for the next row
+            }
+        }
+        if (fallback && lane == 0) {
+            const int pos = atomicAdd(p.fb_count, 1);
+            p.fb_list[pos] = (int32_t)row;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1195,13 +1485,15 @@ cudaError_t record(cudaError_t e) {
 
 }  // namespace
 
-bool router_tc_supported(int r, int K) { return r == kR && K >= 1 && K <= kMaxK; }
+bool router_tc_supported(int r, int K) { return r == kR && K >= 1 && K <= kWideMaxK; }
 
-size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N) {
+size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K) {
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
     const size_t rq = (size_t)B * H * Nq, rk = (size_t)B * Hkv * N;
-    return al(rq * kR * 2) + al(rk * kR * 2) + al(rq * sizeof(float2)) + al((3 * (size_t)B * Hkv + 2) * 4) +
-           al(rq * 4);
+    size_t total = al(rq * kR * 2) + al(rk * kR * 2) + al(rq * sizeof(float2)) +
+                   al((3 * (size_t)B * Hkv + 2) * 4) + al(rq * 4);
+    if (K > kMaxK) total += al(rq * 2 * kWideCap * sizeof(uint2)) + al(rq * 2 * sizeof(int));
+    return total;
 }
 
 cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
@@ -1219,6 +1511,15 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     uint32_t* gstats = stats + 3 * (size_t)a.B * a.Hkv;
     w += al((3 * (size_t)a.B * a.Hkv + 2) * 4);
     int32_t* fb_list = reinterpret_cast<int32_t*>(w);
+    w += al(rq * 4);
+    const bool wide = a.K > kMaxK;
+    uint2* lists = nullptr;
+    int* counts = nullptr;
+    if (wide) {
+        lists = reinterpret_cast<uint2*>(w);
+        w += al(rq * 2 * kWideCap * sizeof(uint2));
+        counts = reinterpret_cast<int*>(w);
+    }
     int* counters = a.counters;  // [0] fallback rows, [1] status
 
     cudaError_t e = cudaMemsetAsync(stats, 0, (3 * (size_t)a.B * a.Hkv + 2) * 4, stream);
@@ -1240,7 +1541,8 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     }
     CUtensorMap tmA, tmB;
     if (!make_row_map(&tmA, q16, rq) || !make_row_map(&tmB, k16, rk)) return cudaErrorInvalidValue;
-    e = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    e = cudaFuncSetAttribute(wide ? router_tc_kernel<true> : router_tc_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e != cudaSuccess) return e;
     TcParams prm;
     prm.rowinfo = rowinfo;
@@ -1251,6 +1553,8 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.fb_count = counters;
     prm.fb_list = fb_list;
     prm.status = counters + 1;
+    prm.lists = lists;
+    prm.counts = counts;
     prm.L = a.L;
     prm.H = a.H;
     prm.Hkv = a.Hkv;
@@ -1262,9 +1566,39 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.nqb = (Nq + kTileM - 1) / kTileM;
     prm.scale = a.scale;
     const long long nblk = (long long)prm.nqb * a.B * a.H;
-    router_tc_kernel<<<(unsigned)nblk, kThreads, kSmemBytes, stream>>>(tmA, tmB, prm);
+    if (!wide) {
+        router_tc_kernel<false><<<(unsigned)nblk, kThreads, kSmemBytes, stream>>>(tmA, tmB, prm);
+        if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        exact_rows_kernel<4><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0,
+                                                          a.K, a.scale, a.causal, counters, fb_list, a.out);
+        return record(cudaGetLastError());
+    }
+    router_tc_kernel<true><<<(unsigned)nblk, kThreads, kSmemBytes, stream>>>(tmA, tmB, prm);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-    exact_rows_kernel<4><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0, a.K,
+    WideFinalParams fp;
+    fp.lists = lists;
+    fp.counts = counts;
+    fp.rowinfo = rowinfo;
+    fp.bias = a.bias;
+    fp.qp32 = a.qp32;
+    fp.kp32 = a.kp32;
+    fp.out = a.out;
+    fp.fb_count = counters;
+    fp.fb_list = fb_list;
+    fp.rows = (long long)rq;
+    fp.L = a.L;
+    fp.H = a.H;
+    fp.Hkv = a.Hkv;
+    fp.N = a.N;
+    fp.K = a.K;
+    fp.Nq = Nq;
+    fp.q0 = a.q0;
+    fp.scale = a.scale;
+    const long long fblk = std::min<long long>(((long long)rq + 7) / 8, 148LL * 8);
+    wide_final_kernel<<<(unsigned)fblk, 256, 0, stream>>>(fp);
+    if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+    // K + 32 candidates per warp must fit: 6 entries per lane for K <= 160
+    exact_rows_kernel<6><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0, a.K,
                                                       a.scale, a.causal, counters, fb_list, a.out);
     return record(cudaGetLastError());
 }

@@ -194,7 +194,7 @@ def test_full_size_config2_selection():
 
 
 def _run_both(q, k, wq, wk, pb, L, K, causal=True):
-    """Tensor-core selector (default for r = 64, K <= 96) and, forced through
+    """Tensor-core selector (default for r = 64, K <= 128) and, forced through
     OSSA_ROUTER_SELECT=exact, the CUDA-core exact selector on the same inputs."""
     import os
 
@@ -208,7 +208,11 @@ def _run_both(q, k, wq, wk, pb, L, K, causal=True):
     return tc, ex, fb, status
 
 
-@pytest.mark.parametrize("N,K,causal", [(2048, 64, True), (777, 32, True), (640, 64, False), (300, 48, True), (4096, 16, True)])
+@pytest.mark.parametrize("N,K,causal", [
+    (2048, 64, True), (777, 32, True), (640, 64, False), (300, 48, True), (4096, 16, True),
+    # wide selection (64 < K <= 128): 256 column classes, global candidate lists
+    (2048, 128, True), (777, 100, True), (640, 128, False), (4096, 96, True), (1500, 65, True),
+])
 def test_tensor_core_and_exact_selectors_agree(N, K, causal):
     B, H, Hkv, D, r = 2, 12, 2, 128, 64
     q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=N + K, scale=1.0 / math.sqrt(D))
@@ -222,10 +226,11 @@ def test_tensor_core_and_exact_selectors_agree(N, K, causal):
     _assert_same(tc.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
 
 
-def test_tensor_core_selector_content_dominated_scores():
+@pytest.mark.parametrize("K", [64, 128])
+def test_tensor_core_selector_content_dominated_scores(K):
     """Trained-router-like regime: content scores dominate the position bias, so
     the boundary band is decided by the q'.k' products the tensor cores compute."""
-    B, H, Hkv, N, D, r, K = 1, 12, 2, 1024, 128, 64, 64
+    B, H, Hkv, N, D, r = 1, 12, 2, 1024, 128, 64
     q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=77)
     wq, wk, pb = _weights(D, r, N, seed=8, bias_scale=0.01)
     wq, wk = wq * 4, wk * 4
@@ -234,10 +239,11 @@ def test_tensor_core_selector_content_dominated_scores():
     _assert_same(tc, oracle.router_topk(q, k, wq, wk, pb, N, K))
 
 
-def test_tensor_core_selector_ties_go_to_exact_fallback():
+@pytest.mark.parametrize("N,K", [(256, 64), (512, 128)])
+def test_tensor_core_selector_ties_go_to_exact_fallback(N, K):
     """All scores tie: every row's candidate list overflows and is recomputed by
     the exact warp-per-row selector; the result is still the lowest indices."""
-    B, H, Hkv, N, D, r, L, K = 1, 4, 2, 256, 64, 64, 256, 64
+    B, H, Hkv, D, r, L = 1, 4, 2, 64, 64, 256
     q = torch.randn(B, H, N, D)
     k = torch.randn(B, Hkv, N, D)
     wq = torch.zeros(r, D)
@@ -248,11 +254,12 @@ def test_tensor_core_selector_ties_go_to_exact_fallback():
     _assert_same(got, oracle.router_topk(q, k, wq, wk, pb, L, K))
 
 
-def test_tensor_core_selector_non_finite_rows():
+@pytest.mark.parametrize("K", [16, 128])
+def test_tensor_core_selector_non_finite_rows(K):
     """A key with an infinite component makes every score of that (b, kv head)
     non-finite: those rows go to the exact selector, which ranks NaN first as
     torch.topk does."""
-    B, H, Hkv, N, D, r, K = 1, 4, 2, 200, 64, 64, 16
+    B, H, Hkv, N, D, r = 1, 4, 2, 200, 64, 64
     q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=5)
     k[0, 1, 50, 7] = float("inf")
     wq, wk, pb = _weights(D, r, N, seed=6)
@@ -277,14 +284,17 @@ def test_long_context_tensor_core_selector():
     _assert_same(tc.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
 
 
-def test_long_context_k128_exact_selector():
-    """Config 5's shape at its smallest length (N = 32768, K = 128, the exact
-    CUDA-core selector): sampled rows against the oracle."""
+def test_long_context_k128_selectors():
+    """Long-context shape at its smallest length (N = 32768, K = 128): the wide
+    tensor-core selection equals the exact CUDA-core selector on every row, and
+    sampled rows equal the oracle."""
     B, H, Hkv, N, D, r, K = 1, 2, 1, 32768, 128, 64, 128
     q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=32, scale=1.0 / math.sqrt(D))
     q, k = q.bfloat16(), k.bfloat16()
     wq, wk, pb = _weights(D, r, N, seed=32)
-    got = router_topk(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
+    tc, ex, fb, status = _run_both(q, k, wq, wk, pb, N, K, True)
+    assert status == 0
+    assert torch.equal(tc, ex), f"{(tc != ex).any(-1).sum().item()} rows differ"
     rows = np.array([0, 1, 127, 128, 4096, 20000, N - 1, N, 2 * N - 1], dtype=np.int64)
     ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows, causal=True)
-    _assert_same(got.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
+    _assert_same(tc.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
