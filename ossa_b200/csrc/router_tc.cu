@@ -17,13 +17,15 @@
 //     tensor core and the canonical fmaf chain far less; 2^-8 leaves 4x margin).
 //  2. warp 0 (one thread) streams 128-key tiles of k'16 with TMA (128-byte
 //     swizzle) through a 2-stage ring; warp 1 (one thread) issues
-//     tcgen05.mma.kind::f16 128x128x64 into one of 4 TMEM accumulators; eight
-//     epilogue warps (two per TMEM lane quadrant, each owning 64 of the 128
+//     tcgen05.mma.kind::f16 128x128x64 into one of 4 TMEM accumulators and, with
+//     bulk copies, the tile's pos_bias window into the matching window buffer;
+//     eight epilogue warps (two per TMEM lane quadrant, each owning 64 of the 128
 //     columns; one query row per thread) drain a finished accumulator with
 //     tcgen05.ld, release it, and score
 //        s = acc * m_i + pos_bias[clamp(i - j + L, 0, 2L - 1)]
-//     (pos_bias staged per warp and tile as four shifted copies so each thread
-//     reads 4 consecutive offsets with one aligned 16-byte load).
+//     (the window holds the tile's 255 bias terms as four shifted copies, cut
+//     from a per-call bias line with the causal -inf already applied, so each
+//     thread reads 4 consecutive offsets with one aligned 16-byte load).
 //  3. Two passes over the same key tiles (the MMA runs twice; the epilogue is
 //     the bottleneck, not the tensor core).  Pass 1 keeps, per row, the maximum
 //     score of each column class (key index mod 128).  The K-th largest of those
@@ -75,10 +77,15 @@ constexpr int kChunk = 32;          // accumulator columns per tcgen05.ld in the
 constexpr int kSubCap = 80;         // candidate sub-list capacity (per row and column half)
 constexpr int kSubLimit = kSubCap - 16;  // past this after a 16-column step: exact fallback
 constexpr int kRowStride = 2 * kSubCap + 1;  // uint2 entries per row; odd stride spreads banks
-constexpr int kWinLen = 96;         // bias window entries per copy (32 rows x 64 columns)
-constexpr int kWinCopy = 104;       // copy stride (floats): copies 8 banks apart
-constexpr int kWinPad = 4;          // leading slots of a copy: unmasked stores of x - s < 0 land there
-static_assert(kWinPad >= 3 && kWinPad % 4 == 0 && kWinPad + kWinLen <= kWinCopy, "window copy layout");
+// pos_bias window of one tile, shared by the CTA: w[x] = bias term at offset
+// i - j = x - 127 from the tile's corner, as four copies shifted by s = 0..3
+// (copy s holds w[s .. s + kWinLen - 1]) so that every thread reads the terms of
+// 4 consecutive columns with one aligned 16-byte load.
+constexpr int kWinLen = 2 * kTileN - 4;  // 252 terms per copy (x = row - col + 127 <= 254)
+constexpr int kWinCopy = kWinLen + 12;   // copy stride in floats, = 8 (mod 32): copies 8 banks apart
+constexpr int kWinBytes = 4 * kWinCopy * 4;
+constexpr uint32_t kWinTx = 4u * kWinLen * 4u;  // bytes one tile's window brings in
+static_assert(kWinCopy % 32 == 8 && (kWinLen * 4) % 16 == 0 && (kWinCopy * 4) % 16 == 0, "window layout");
 constexpr int kTileBytes = kTileM * kR * 2;
 constexpr uint32_t kTmemCols = kAccBufs * kTileN;
 constexpr int kMaxK = 64;           // selection bound uses the K-th of 128 column-class maxima
@@ -98,11 +105,10 @@ constexpr int kClsStride = 2 * kTileN + 1;   // floats per row of class maxima; 
 constexpr size_t kOffA = 0;
 constexpr size_t kOffB = kOffA + kTileBytes;
 constexpr size_t kOffWin = kOffB + (size_t)kStages * kTileBytes;
-constexpr size_t kOffBuf = kOffWin + (size_t)kEpiWarps * 4 * kWinCopy * sizeof(float);
+constexpr size_t kOffBuf = kOffWin + (size_t)kAccBufs * kWinBytes;  // one window per accumulator
 constexpr size_t kOffBar = kOffBuf + (size_t)kTileM * kRowStride * sizeof(uint2);
 static_assert(kChunk % 16 == 0, "the overflow check runs every 16 columns");
-static_assert(4 * kWinCopy >= 2 * 32, "a quadrant's row metadata reuses one warp's window");
-constexpr int kNumBars = 2 * kStages + 1 + 2 * kAccBufs + 1;
+constexpr int kNumBars = 2 * kStages + 1 + 3 * kAccBufs + 1;
 constexpr size_t kOffSlot = kOffBar + kNumBars * sizeof(uint64_t);
 constexpr size_t kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -156,6 +162,27 @@ __global__ void bias_stats_kernel(const float* __restrict__ bias, int n, uint32_
         atomicMax(gstats + 0, mm);
         if (b) atomicOr(gstats + 1, 1u);
     }
+}
+
+// The pos_bias line of one call as four copies shifted by s = 0..3: copy s holds
+// at index k the bias term of offset o = a_min + k + s (o = i - j + L): -inf when
+// causal and o < L (a key after its query), else pos_bias[clamp(o, 0, 2L - 1)].
+// Tile windows are then plain aligned bulk copies out of it.
+__global__ void bias_line_kernel(const float* __restrict__ bias, int L, int causal, long long a_min, int ext_len,
+                                 float* __restrict__ out) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= 4LL * ext_len) return;
+    const int s = (int)(t / ext_len);
+    const long long o = a_min + (t - (long long)s * ext_len) + s;
+    float v = -INFINITY;
+    if (!(causal && o < L)) v = __ldg(bias + (o < 0 ? 0 : (o > 2LL * L - 1 ? 2LL * L - 1 : o)));
+    out[t] = v;
+}
+
+// Floats per copy of the bias line: tile (qb, key tile) reads kWinLen of them
+// from kTileN * (qb + tiles_n - 1 - key tile).
+__host__ __device__ constexpr int bias_line_len(int nqb, int tiles_n) {
+    return kTileN * (nqb + tiles_n - 2) + kWinLen;
 }
 
 // Power-of-two exponent e with max_abs * 2^e in [2^12, 2^13).
@@ -244,10 +271,12 @@ struct TcParams {
     int* fb_count;
     int32_t* fb_list;
     int* status;
+    const float* bext;  // four shifted copies of the pos_bias line, ext_len floats each
     uint2* lists;  // wide selection: (score, key) sub-lists, kWideCap per row and column half
     int* counts;   // wide selection: sub-list lengths, -1 sends the row to the exact fallback
     int L, H, Hkv, N, K, causal, nqb;
     int Nq, q0;  // query rows per (b, h) and the key-sequence position of row 0
+    int tiles_n, ext_len;  // key tiles per (b, kv head); floats per bias-line copy
     float scale;
 };
 
@@ -459,7 +488,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint64_t* afull = bars + 2 * kStages;
     uint64_t* tfull = afull + 1;
     uint64_t* tempty = tfull + kAccBufs;
-    uint64_t* mdone = tempty + kAccBufs;
+    uint64_t* wfull = tempty + kAccBufs;  // the tile's pos_bias window has landed
+    uint64_t* mdone = wfull + kAccBufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffSlot);
 
     const int N = p.N, H = p.H, Hkv = p.Hkv, Nq = p.Nq;
@@ -496,6 +526,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         for (int s = 0; s < kAccBufs; ++s) {
             mbar_init(tfull + s, 1);
             mbar_init(tempty + s, kEpiWarps);
+            mbar_init(wfull + s, 1);
         }
         mbar_init(mdone, 1);
         fence_mbar_init();
@@ -536,12 +567,35 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_f16(0u, kTileM, kTileN);
             const uint64_t adesc = umma_desc_sw128(sA);
+            // The pos_bias window of step t goes to window buffer t % kAccBufs once the
+            // accumulator of that index is free (every epilogue warp is done with
+            // both): one bulk copy per shifted copy of the bias line.  The line is
+            // laid out so that tile (qb, key tile) starts kTileN * (qb + tiles_n - 1 -
+            // key tile) floats into each copy.
+            const float* bline = p.bext + (size_t)kTileN * (qb + p.tiles_n - 1);
+            auto load_window = [&](int t) {
+                const int ab = t % kAccBufs;
+                const float* src = bline - (size_t)kTileN * tile_of(t);
+                float* dst = win + (size_t)ab * (kWinBytes / 4);
+                mbar_arrive_expect_tx(wfull + ab, kWinTx);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    bulk_load(dst + c * kWinCopy, src + (size_t)c * p.ext_len, kWinLen * 4, wfull + ab);
+            };
+            const int wfirst = min(T2, kAccBufs);
+            for (int t = 0; t < wfirst; ++t) load_window(t);
+            int wissued = wfirst;
             bool ok = mbar_wait(afull, 0);
             for (int t = 0; t < T2 && ok; ++t) {
                 const int s = t % kStages;
                 const int ab = t % kAccBufs;
+                if (t >= kAccBufs) {
+                    ok = mbar_wait(tempty + ab, ((t / kAccBufs) - 1) & 1);
+                    if (!ok) break;
+                    load_window(t);
+                    wissued = t + 1;
+                }
                 ok = mbar_wait(full + s, (t / kStages) & 1);
-                if (ok && t >= kAccBufs) ok = mbar_wait(tempty + ab, ((t / kAccBufs) - 1) & 1);
                 if (!ok) break;
                 tc_fence_after();
                 const uint64_t bdesc = umma_desc_sw128(sB + (size_t)s * kTileBytes);
@@ -554,6 +608,9 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             }
             mma_commit(mdone);  // completes once every MMA issued above has finished
             mbar_wait(mdone, 0);
+            // windows the epilogue never waited for (error path) land before the CTA retires
+            for (int t = max(0, wissued - kAccBufs); t < wissued; ++t)
+                mbar_wait(wfull + t % kAccBufs, (t / kAccBufs) & 1);
             if (!ok) atomicOr(p.status, 2);
         }
     } else {
@@ -581,59 +638,24 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         uint2* rowbuf = buf + (size_t)row * kRowStride;
         uint2* sub = rowbuf + hf * kSubCap;  // this thread's candidate sub-list
-        float* wcp = win + ew * 4 * kWinCopy;
+        // pos_bias terms of columns cbase + cl .. + 3 (cl a multiple of 4): copy
+        // s4 = row & 3 of the tile's window at position row - s4 + 124 - cbase - cl,
+        // i.e. w[row - (cbase + cl + 3) + 127 .. row - (cbase + cl) + 127], in reverse
         const int s4 = lane & 3;
-        const float* mycopy = wcp + s4 * kWinCopy + kWinPad + (lane - s4) + (kHalfCols - 4);
-        const uint32_t mycopy_s = smem_u32(mycopy);  // its shared address
-        const uint32_t wcp_s = smem_u32(wcp);
+        const uint32_t wrd_s = smem_u32(win) + 4u * (uint32_t)(s4 * kWinCopy + row - s4 + (kTileN - 4) - cbase);
         const int lim = p.causal ? min(N, p.q0 + i + 1) : N;  // keys j < lim are eligible
         bool ok = true;
 
-        // Tile prologue shared by both passes: stage this warp's pos_bias window
-        // (copy s holds w[y + s], w[x] = bias[clamp(i0g + r0 - j0 - 63 - cbase + x + L)],
-        // so column c of row lane reads w[lane - (c - cbase) + 63]) and wait for the
-        // tile's accumulator.  Returns false if the bounded wait expired.
-        // The bias values of tile t + 1 are fetched from global memory while tile
-        // t is processed (wv), so staging never waits on that load.
-        constexpr int kWinVals = (kWinLen + 3 + 31) / 32;
-        float wv[kWinVals];
-        auto fetch_window = [&](int j0) {
-            const int obase = i0g + r0 - j0 - (kHalfCols - 1) - cbase + L;
-#pragma unroll
-            for (int u = 0; u < kWinVals; ++u) {
-                const int braw = obase + lane + 32 * u;  // i - j + L for this window slot
-                const int bi = braw < 0 ? 0 : (braw > 2 * L - 1 ? 2 * L - 1 : braw);
-                // causal: a key after the query (i - j < 0) gets -inf, so full tiles
-                // need no per-column mask
-                wv[u] = (p.causal && braw < L) ? -INFINITY : __ldg(p.bias + bi);
-            }
-        };
+        // Tile prologue shared by both passes: wait for the tile's pos_bias window
+        // and its accumulator.  Returns false if a bounded wait expired.
         auto tile_prologue = [&](int t) -> bool {
-            // Take this tile's values out of wv first, so the next tile's loads into
-            // wv need not wait for the shared-memory stores to read their operands.
-            float cur[kWinVals];
-#pragma unroll
-            for (int u = 0; u < kWinVals; ++u) cur[u] = wv[u];
-            if (t + 1 < T2) fetch_window(tile_of(t + 1) * kTileN);
-            // Copy s keeps w[y + s] at kWinPad + y.  Values x < kWinLen land at
-            // y = x - s in [-3, kWinLen), inside the copy's padding when negative,
-            // so those stores need no mask; only the last group is masked.
-#pragma unroll
-            for (int u = 0; u < kWinVals; ++u) {
-                const int x = lane + 32 * u;
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const uint32_t a = wcp_s + 4u * (uint32_t)(s * kWinCopy + kWinPad + x - s);
-                    if (32 * (u + 1) <= kWinLen) sts_f32(a, cur[u]);
-                    else sts_f32_if(a, cur[u], x - s < kWinLen);
-                }
-            }
-            __syncwarp();
-            if (!__all_sync(kFull, mbar_wait(tfull + t % kAccBufs, (t / kAccBufs) & 1))) return false;
+            const int ab = t % kAccBufs;
+            const uint32_t par = (uint32_t)(t / kAccBufs) & 1u;
+            const bool got = mbar_wait(wfull + ab, par) && mbar_wait(tfull + ab, par);
+            if (!__all_sync(kFull, got)) return false;
             tc_fence_after();
             return true;
         };
-        fetch_window(0);
 
         // ---------------- pass 1: maximum score per column class (key index mod 128)
         float cm[kHalfCols];
@@ -647,6 +669,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 break;
             }
             const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN + cbase);
+            const uint32_t mycopy_s = wrd_s + (uint32_t)(ab * kWinBytes);
             // columns past the last key need the explicit mask (the tile reads on
             // into the next head's keys); causally masked keys score -inf anyway
             const bool full_tile = j0 + cbase + kHalfCols <= N;
@@ -689,7 +712,6 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     }
                 }
             }
-            __syncwarp();  // window copies are rewritten for the next tile
             if constexpr (kWide) {
                 if (t == Te - 1) {
                     // even tiles done: their class maxima go to shared memory
@@ -776,6 +798,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 break;
             }
             const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN + cbase);
+            const uint32_t mycopy_s = wrd_s + (uint32_t)(ab * kWinBytes);
             const bool full_tile = j0 + cbase + kHalfCols <= N;
             const int climit = lim - j0 - cbase;
             const uint32_t jb = (uint32_t)(j0 + cbase);
@@ -834,7 +857,6 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 }
             }
             cnt = (int)((waddr - sub_s) >> 3);
-            __syncwarp();  // window copies are rewritten for the next tile
         }
         if (!ok) atomicOr(p.status, 4);
 
@@ -856,20 +878,18 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             //     key asc) are kept.
             //  3. each lane compacts its kept keys in place; lane 2r merges the two
             //     lists from the front, lane 2r+1 from the back, into the output row.
-            // Quadrant metadata lives in the window of its column-half-0 warp: only
-            // the quadrant's two warps touch it, and both are past their last window
-            // read once the first barrier below completes.
-            int* qmeta = reinterpret_cast<int*>(win + (ew & 3) * 4 * kWinCopy);
-            named_bar_sync(pair_bar, 64);
-            qmeta[2 * lane + hf] = fb ? -1 : cnt;
+            // A row's two counts go to the .y word of its spare list entry (.x holds
+            // the bound), 16 bits per column half.
+            reinterpret_cast<int16_t*>(&rowbuf[kRowStride - 1].y)[hf] = (int16_t)(fb ? -1 : cnt);
             named_bar_sync(pair_bar, 64);
             {
                 const int frow = r0 + 16 * hf + (lane >> 1);
                 const int fh = lane & 1;
                 const int fi = i0 + frow;
                 const bool active = ok && fi < Nq;
-                const int ca = qmeta[2 * (frow - r0)], cb = qmeta[2 * (frow - r0) + 1];
                 uint2* frowbuf = buf + (size_t)frow * kRowStride;
+                const int16_t* fmeta = reinterpret_cast<const int16_t*>(&frowbuf[kRowStride - 1].y);
+                const int ca = fmeta[0], cb = fmeta[1];
                 uint2* own = frowbuf + fh * kSubCap;
                 const int nown = fh ? cb : ca;
                 bool to_fallback = active && (ca < 0 || cb < 0);
@@ -1490,8 +1510,10 @@ bool router_tc_supported(int r, int K) { return r == kR && K >= 1 && K <= kWideM
 size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K) {
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
     const size_t rq = (size_t)B * H * Nq, rk = (size_t)B * Hkv * N;
+    const int nqb = (Nq + kTileM - 1) / kTileM, tiles_n = (N + kTileN - 1) / kTileN;
     size_t total = al(rq * kR * 2) + al(rk * kR * 2) + al(rq * sizeof(float2)) +
-                   al((3 * (size_t)B * Hkv + 2) * 4) + al(rq * 4);
+                   al((3 * (size_t)B * Hkv + 2) * 4) + al(rq * 4) +
+                   (nqb > 0 && tiles_n > 0 ? al(4 * (size_t)bias_line_len(nqb, tiles_n) * 4) : 0);
     if (K > kMaxK) total += al(rq * 2 * kWideCap * sizeof(uint2)) + al(rq * 2 * sizeof(int));
     return total;
 }
@@ -1512,6 +1534,10 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     w += al((3 * (size_t)a.B * a.Hkv + 2) * 4);
     int32_t* fb_list = reinterpret_cast<int32_t*>(w);
     w += al(rq * 4);
+    const int nqb = (Nq + kTileM - 1) / kTileM, tiles_n = (a.N + kTileN - 1) / kTileN;
+    const int ext_len = bias_line_len(nqb, tiles_n);
+    float* bext = reinterpret_cast<float*>(w);
+    w += al(4 * (size_t)ext_len * 4);
     const bool wide = a.K > kMaxK;
     uint2* lists = nullptr;
     int* counts = nullptr;
@@ -1538,6 +1564,13 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
         qprep_kernel<<<(unsigned)((rq + 127) / 128), 128, 0, stream>>>(a.qp32, q16, rowinfo, (long long)rq, a.H,
                                                                       a.Hkv, Nq, a.scale, stats, gstats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        // offset of bias-line index 0: tile (qb, key tile) starts at i - j + L =
+        // q0 + kTileN * (qb - key tile) - 127 + L
+        const long long a_min = (long long)a.q0 + a.L - (kTileN - 1) - (long long)kTileN * (tiles_n - 1);
+        const long long nb = 4LL * ext_len;
+        bias_line_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, stream>>>(a.bias, a.L, a.causal, a_min, ext_len,
+                                                                          bext);
+        if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     }
     CUtensorMap tmA, tmB;
     if (!make_row_map(&tmA, q16, rq) || !make_row_map(&tmB, k16, rk)) return cudaErrorInvalidValue;
@@ -1555,6 +1588,9 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.status = counters + 1;
     prm.lists = lists;
     prm.counts = counts;
+    prm.bext = bext;
+    prm.tiles_n = tiles_n;
+    prm.ext_len = ext_len;
     prm.L = a.L;
     prm.H = a.H;
     prm.Hkv = a.Hkv;
