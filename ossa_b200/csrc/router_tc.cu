@@ -1,10 +1,10 @@
 // Router top-K selection on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
 // Replaces ContentRouter.score + causal mask + torch.topk (ossa/router.py:171-190,
-// ossa/bench/sparse_forward.py:180-202) for proj_dim r = 64 and K <= 64, with the
-// same result as the exact CUDA-core selector: the K best keys by canonical fp32
-// score (fmaf chains, see score_topk.cu), lowest key index first on ties, emitted
-// in ascending key order and -1 padded.
+// ossa/bench/sparse_forward.py:180-202) for proj_dim r = 64 and K <= 128, with
+// the same result as the exact CUDA-core selector: the K best keys by canonical
+// fp32 score (fmaf chains, see score_topk.cu), lowest key index first on ties,
+// emitted in ascending key order and -1 padded.
 //
 // Pipeline (one CTA = 128 query rows of one (b, h), one CTA per SM):
 //  1. prep kernels turn the canonical fp32 projections q', k' into fp16 copies
@@ -14,30 +14,34 @@
 //     |approx score - canonical score| <= delta_i:
 //        delta_i = scale * 2^-8 * |q'_i| * max_j |k'_j| + 2^-22 * (max|bias| + scale * |q'_i| * max_j |k'_j|)
 //     (fp16 input rounding contributes <= 2^-10 |q'||k'|, fp32 accumulation in the
-//     tensor core and the canonical fmaf chain far less; 2^-8 leaves 4x margin).
+//     tensor core and the canonical fmaf chain far less; 2^-8 leaves 4x margin),
+//     and the call's pos_bias window images (window_table_kernel).
 //  2. warp 0 (one thread) streams 128-key tiles of k'16 with TMA (128-byte
-//     swizzle) through a 2-stage ring; warp 1 (one thread) issues
-//     tcgen05.mma.kind::f16 128x128x64 into one of 4 TMEM accumulators and, with
-//     bulk copies, the tile's pos_bias window into the matching window buffer;
-//     eight epilogue warps (two per TMEM lane quadrant, each owning 64 of the 128
-//     columns; one query row per thread) drain a finished accumulator with
-//     tcgen05.ld, release it, and score
+//     swizzle) through a 4- or 6-stage ring; warp 1 (one thread) issues
+//     tcgen05.mma.kind::f16 128x128x64 into one of 4 TMEM accumulators; warp 2
+//     (one thread) brings the tile's pos_bias window into the matching window
+//     buffer with one bulk copy, completing on the same barrier as the MMA (each
+//     of these threads spends tens of cycles per issued TMA/MMA instruction, so
+//     the three streams are kept apart); eight epilogue warps (two per TMEM
+//     lane quadrant, each owning 64 of the 128 columns; one query row per
+//     thread) drain a finished accumulator with tcgen05.ld, release it, and score
 //        s = acc * m_i + pos_bias[clamp(i - j + L, 0, 2L - 1)]
-//     (the window holds the tile's 255 bias terms as four shifted copies, cut
-//     from a per-call bias line with the causal -inf already applied, so each
-//     thread reads 4 consecutive offsets with one aligned 16-byte load).
+//     (the window holds the tile's 255 bias terms as four shifted copies with
+//     the causal -inf already applied, so each thread reads the terms of 4
+//     consecutive columns with one aligned 16-byte load).
 //  3. Two passes over the same key tiles (the MMA runs twice; the epilogue is
 //     the bottleneck, not the tensor core).  Pass 1 keeps, per row, the maximum
-//     score of each column class (key index mod 128).  The K-th largest of those
-//     128 maxima is a valid lower bound on the row's K-th best score (K distinct
-//     keys reach it), so theta = bound - 2*delta_i can only drop keys outside
-//     the exact top K.  Pass 2 appends every score >= theta to the thread's
-//     candidate sub-list (about 1.3 K entries per row on random data).
-//  4. End of row (one thread per row): bisection on the candidates' approximate
-//     scores brackets the K-th best T; entries above T + 2*delta_i are certainly
-//     selected, entries below T - 2*delta_i certainly not, and the few in between
-//     are rescored with the canonical fp32 formula; the remaining slots go to
-//     them by (score desc, j asc).  Output in ascending key order.
+//     score of each column class: key index mod 128 (K <= 64), or key tile
+//     parity x column, 256 classes (K <= 128).  The K-th largest class maximum
+//     is a valid lower bound on the row's K-th best score (K distinct keys reach
+//     it), so theta = bound - 2*delta_i can only drop keys outside the exact top
+//     K.  Pass 2 appends every score >= theta to the thread's candidate sub-list
+//     in global memory (about 1.3-1.4 K entries per row on random data).
+//  4. final_select_kernel, one warp per row: the K-th best approximate score x_K
+//     splits the candidates; entries above the split + 2*delta_i are certainly
+//     selected, entries below x_K - 2*delta_i certainly not, and the few in
+//     between are rescored with the canonical fp32 formula; the remaining slots
+//     go to them by (score desc, j asc).  Output in ascending key order.
 //  5. Rows whose sub-list would overflow (massive near-ties), whose boundary
 //     band is too wide, or whose inputs are not finite are appended to a list
 //     and recomputed afterwards by an exact warp-per-row selector
@@ -68,53 +72,64 @@ using namespace sm100;
 constexpr int kR = 64;              // projection dim = MMA K
 constexpr int kTileM = 128;         // query rows per CTA
 constexpr int kTileN = 128;         // keys per MMA tile
-constexpr int kStages = 2;          // k' tile ring
 constexpr int kAccBufs = 4;         // TMEM accumulators (128 columns each)
 constexpr int kEpiWarps = 8;        // two per TMEM lane quadrant, 64 columns each
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kCtlWarps = 3;        // k' loads, MMA issue, window loads
+constexpr int kThreads = 32 * (kCtlWarps + kEpiWarps);
 constexpr int kHalfCols = kTileN / 2;
-constexpr int kChunk = 32;          // accumulator columns per tcgen05.ld in the epilogue
-constexpr int kSubCap = 80;         // candidate sub-list capacity (per row and column half)
-constexpr int kSubLimit = kSubCap - 16;  // past this after a 16-column step: exact fallback
-constexpr int kRowStride = 2 * kSubCap + 1;  // uint2 entries per row; odd stride spreads banks
-// pos_bias window of one tile, shared by the CTA: w[x] = bias term at offset
-// i - j = x - 127 from the tile's corner, as four copies shifted by s = 0..3
-// (copy s holds w[s .. s + kWinLen - 1]) so that every thread reads the terms of
+// pos_bias window of one tile, shared by the CTA: u[z] = bias term of column
+// col for row `row` at z = col - row + 127, as four copies shifted by s = 0..3
+// (copy s holds u[s .. s + kWinLen - 1]) so that every thread reads the terms of
 // 4 consecutive columns with one aligned 16-byte load.
-constexpr int kWinLen = 2 * kTileN - 4;  // 252 terms per copy (x = row - col + 127 <= 254)
+constexpr int kWinLen = 2 * kTileN - 4;  // 252 terms per copy (z <= 254)
 constexpr int kWinCopy = kWinLen + 12;   // copy stride in floats, = 8 (mod 32): copies 8 banks apart
 constexpr int kWinBytes = 4 * kWinCopy * 4;
-constexpr uint32_t kWinTx = 4u * kWinLen * 4u;  // bytes one tile's window brings in
 static_assert(kWinCopy % 32 == 8 && (kWinLen * 4) % 16 == 0 && (kWinCopy * 4) % 16 == 0, "window layout");
 constexpr int kTileBytes = kTileM * kR * 2;
 constexpr uint32_t kTmemCols = kAccBufs * kTileN;
-constexpr int kMaxK = 64;           // selection bound uses the K-th of 128 column-class maxima
 constexpr int kBoundSlack = 3;      // the pass-1 bound stops once K..K+3 class maxima are above it
-constexpr int kMaxBand = 16;        // boundary candidates rescored per row before falling back
+constexpr int kMaxBand = 32;        // wide: boundary candidates rescored per row (one per lane) before falling back
+constexpr int kMaxBandNarrow = 8;   // narrow: boundary candidates rescored per sub-list before falling back
 
-// Wide selection (64 < K <= 128): pass 1 keeps 256 column classes (key tile
-// parity x column), whose K-th largest maximum bounds the K-th best score; the
-// candidate sub-lists (about 1.4 K entries per row) live in global memory and a
-// warp-per-row kernel (wide_final_kernel) makes the final choice.
-constexpr int kWideMaxK = 128;
-constexpr int kWideCap = 160;              // global candidate sub-list capacity (per row and column half)
-constexpr int kWideLimit = kWideCap - 16;  // past this after a 16-column step: exact fallback
-constexpr int kWideEPL = 2 * kWideCap / 32;  // candidate entries per lane in the final kernel
-constexpr int kClsStride = 2 * kTileN + 1;   // floats per row of class maxima; odd stride spreads banks
-
-constexpr size_t kOffA = 0;
-constexpr size_t kOffB = kOffA + kTileBytes;
-constexpr size_t kOffWin = kOffB + (size_t)kStages * kTileBytes;
-constexpr size_t kOffBuf = kOffWin + (size_t)kAccBufs * kWinBytes;  // one window per accumulator
-constexpr size_t kOffBar = kOffBuf + (size_t)kTileM * kRowStride * sizeof(uint2);
-static_assert(kChunk % 16 == 0, "the overflow check runs every 16 columns");
-constexpr int kNumBars = 2 * kStages + 1 + 3 * kAccBufs + 1;
-constexpr size_t kOffSlot = kOffBar + kNumBars * sizeof(uint64_t);
-constexpr size_t kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
-static_assert(kSmemBytes <= 232448, "shared memory budget");
-static_assert((size_t)kTileM * kClsStride * 4 + kTileM * 4 <= (size_t)kTileM * kRowStride * sizeof(uint2),
-              "the wide selection's class maxima and bounds fit in the candidate area");
-static_assert(kOffB % 1024 == 0 && kTileBytes % 1024 == 0, "swizzled tiles need 1 KB alignment");
+// Two variants.  Narrow (K <= 64): the pass-1 bound is the K-th largest of 128
+// column-class maxima (key mod 128); the candidate sub-lists (about 1.3 K per
+// row on random data) sit in shared memory and the epilogue warps make the final
+// choice in the kernel.  Wide (64 < K <= 128): 256 classes (key tile parity x
+// column; pass 1 visits the even tiles, then the odd ones); the sub-lists (about
+// 1.4 K per row) sit in global memory and a warp-per-row kernel
+// (final_select_kernel) makes the final choice.
+template <bool kWide>
+struct TcCfg {
+    static constexpr int kMaxK = kWide ? 128 : 64;
+    static constexpr int kStages = kWide ? 4 : 2;  // k' tile ring
+    static constexpr int kCap = kWide ? 160 : 80;  // sub-list capacity per row and column half
+    static constexpr int kLimit = kCap - 16;       // past this after a 16-column step: exact fallback
+    // narrow: kRowStride uint2 per row in shared memory (both sub-lists and a
+    // spare entry for the row's bound and counts; the odd stride spreads banks);
+    // the class maxima go through the still empty sub-list area.
+    static constexpr int kRowStride = 2 * kCap + 1;
+    // wide: class maxima kClsStride floats per row (odd: spreads banks), then the
+    // per-row bounds; sub-lists in global memory, contiguous per row and half,
+    // 2 * kTileM * kCap entries per query block.
+    static constexpr int kClsStride = 2 * kTileN + 1;
+    static constexpr size_t kOffA = 0;
+    static constexpr size_t kOffB = kOffA + kTileBytes;
+    static constexpr size_t kOffWin = kOffB + (size_t)kStages * kTileBytes;
+    static constexpr size_t kOffBuf = kOffWin + (size_t)kAccBufs * kWinBytes;
+    static constexpr size_t kBufBytes =
+        kWide ? (size_t)kTileM * (kClsStride + 1) * 4 : (size_t)kTileM * kRowStride * sizeof(uint2);
+    static constexpr size_t kOffBar = (kOffBuf + kBufBytes + 7) / 8 * 8;
+    static constexpr int kNumBars = 2 * kStages + 1 + 2 * kAccBufs + 1;
+    static constexpr size_t kOffSlot = kOffBar + (size_t)kNumBars * 8;
+    static constexpr size_t kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+    static_assert(kOffB % 1024 == 0 && kTileBytes % 1024 == 0, "swizzled tiles need 1 KB alignment");
+    static_assert(kOffWin % 16 == 0, "bulk copies need 16-byte aligned destinations");
+    static_assert(kWide || 2 * kTileM * kMaxBandNarrow * 8 <= kTileBytes, "rescoring slots fit in the q' tile");
+    static_assert(kWide || kTileM * 256 <= kStages * kTileBytes, "output staging fits in the k' ring");
+};
+constexpr int kWideMaxK = TcCfg<true>::kMaxK;
+constexpr int kNarrowMaxK = TcCfg<false>::kMaxK;
 
 constexpr float kTwoPowM22 = 2.384185791015625e-07f;  // 2^-22
 
@@ -164,26 +179,28 @@ __global__ void bias_stats_kernel(const float* __restrict__ bias, int n, uint32_
     }
 }
 
-// The pos_bias line of one call as four copies shifted by s = 0..3: copy s holds
-// at index k the bias term of offset o = a_min + k + s (o = i - j + L): -inf when
+// The pos_bias windows of one call, one per tile diagonal d = nqb - 1 - qb + key
+// tile: the exact shared-memory image of the tile's window (kWinBytes), so one
+// bulk copy brings it in.  Copy s of window d holds, at position y < kWinLen, the
+// bias term of offset o = o_max - kTileN * d - y - s (o = i - j + L; offsets
+// descend so that ascending positions are ascending key columns): -inf when
 // causal and o < L (a key after its query), else pos_bias[clamp(o, 0, 2L - 1)].
-// Tile windows are then plain aligned bulk copies out of it.
-__global__ void bias_line_kernel(const float* __restrict__ bias, int L, int causal, long long a_min, int ext_len,
-                                 float* __restrict__ out) {
+__global__ void window_table_kernel(const float* __restrict__ bias, int L, int causal, long long o_max, int ndiag,
+                                    float* __restrict__ out) {
+    constexpr int kPer = 4 * kWinCopy;
     const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= 4LL * ext_len) return;
-    const int s = (int)(t / ext_len);
-    const long long o = a_min + (t - (long long)s * ext_len) + s;
-    float v = -INFINITY;
-    if (!(causal && o < L)) v = __ldg(bias + (o < 0 ? 0 : (o > 2LL * L - 1 ? 2LL * L - 1 : o)));
+    if (t >= (long long)ndiag * kPer) return;
+    const int d = (int)(t / kPer);
+    const int r = (int)(t - (long long)d * kPer);
+    const int s = r / kWinCopy, y = r - s * kWinCopy;
+    const long long o = o_max - (long long)kTileN * d - y - s;
+    float v = 0.f;  // copy padding
+    if (y < kWinLen) v = (causal && o < L) ? -INFINITY : __ldg(bias + (o < 0 ? 0 : (o > 2LL * L - 1 ? 2LL * L - 1 : o)));
     out[t] = v;
 }
 
-// Floats per copy of the bias line: tile (qb, key tile) reads kWinLen of them
-// from kTileN * (qb + tiles_n - 1 - key tile).
-__host__ __device__ constexpr int bias_line_len(int nqb, int tiles_n) {
-    return kTileN * (nqb + tiles_n - 2) + kWinLen;
-}
+// Tile diagonals of a call: tile (qb, key tile) uses window nqb - 1 - qb + key tile.
+__host__ __device__ constexpr int window_count(int nqb, int tiles_n) { return nqb + tiles_n - 1; }
 
 // Power-of-two exponent e with max_abs * 2^e in [2^12, 2^13).
 __device__ __forceinline__ int scale_exponent(float max_abs) {
@@ -271,12 +288,11 @@ struct TcParams {
     int* fb_count;
     int32_t* fb_list;
     int* status;
-    const float* bext;  // four shifted copies of the pos_bias line, ext_len floats each
-    uint2* lists;  // wide selection: (score, key) sub-lists, kWideCap per row and column half
-    int* counts;   // wide selection: sub-list lengths, -1 sends the row to the exact fallback
+    const float* wtab;  // pos_bias window images, one per tile diagonal (kWinBytes each)
+    uint2* lists;  // wide: (score, key) sub-lists, TcCfg::kCap per row and column half
+    int* counts;   // wide: sub-list lengths, -1 sends the row to the exact fallback
     int L, H, Hkv, N, K, causal, nqb;
     int Nq, q0;  // query rows per (b, h) and the key-sequence position of row 0
-    int tiles_n, ext_len;  // key tiles per (b, kv head); floats per bias-line copy
     float scale;
 };
 
@@ -306,20 +322,6 @@ __device__ __forceinline__ float canonical_score(const float* __restrict__ qrow,
     return __fadd_rn(__fmul_rn(acc, scale), __ldg(bias + bi));
 }
 
-// Barrier over `count` threads (a multiple of 32) using hardware barrier `id`.
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-// Count of x[q] >= v (eight independent partial counts: no long add chain).
-template <int NX>
-__device__ __forceinline__ int count_ge(const float (&x)[NX], float v) {
-    int c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-    for (int q = 0; q < NX; ++q) c[q & 7] += x[q] >= v ? 1 : 0;
-    return ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
-}
-
 // count_ge over the first nch 8-entry chunks of x only (nch uniform across the warp).
 template <int NX>
 __device__ __forceinline__ int count_ge_chunks(const float (&x)[NX], float v, int nch) {
@@ -334,53 +336,18 @@ __device__ __forceinline__ int count_ge_chunks(const float (&x)[NX], float v, in
     return ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
 }
 
-// A lower bound on the K-th largest of x (padding entries are -inf): the result
-// v satisfies count(x >= v) >= K, found by bisection between the smallest and
-// largest finite values; -inf if fewer than K entries are finite.
-template <int NX>
-__device__ __forceinline__ float kth_lower_bound(const float (&x)[NX], int K, int iters) {
-    float lo8[8], hi8[8];
-    int nf8[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        lo8[u] = INFINITY;
-        hi8[u] = -INFINITY;
-        nf8[u] = 0;
-    }
-#pragma unroll
-    for (int q = 0; q < NX; ++q) {
-        const bool f = x[q] > -INFINITY;
-        nf8[q & 7] += f ? 1 : 0;
-        lo8[q & 7] = f ? fminf(lo8[q & 7], x[q]) : lo8[q & 7];
-        hi8[q & 7] = fmaxf(hi8[q & 7], x[q]);
-    }
-    float lo = lo8[0], hi = hi8[0];
-    int nfin = nf8[0];
-#pragma unroll
-    for (int u = 1; u < 8; ++u) {
-        lo = fminf(lo, lo8[u]);
-        hi = fmaxf(hi, hi8[u]);
-        nfin += nf8[u];
-    }
-    if (nfin < K) return -INFINITY;
-    for (int it = 0; it < iters; ++it) {
-        const float mid = lo + 0.5f * (hi - lo);
-        if (!(mid > lo && mid < hi)) break;
-        if (count_ge<NX>(x, mid) >= K) lo = mid; else hi = mid;
-    }
-    return lo;
+// Barrier over `count` threads (a multiple of 32) using hardware barrier `id`.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// Narrows [lo, hi] (count(x >= lo) >= K, count(x > hi) < K on entry) until
-// hi - lo <= width: afterwards the K-th largest of x lies in [lo, hi].
+// Count of x[q] >= v (eight independent partial counts: no long add chain).
 template <int NX>
-__device__ __forceinline__ void bisect_kth(const float (&x)[NX], int K, float width, int iters, float& lo,
-                                           float& hi) {
-    for (int it = 0; it < iters && hi - lo > width; ++it) {
-        const float mid = lo + 0.5f * (hi - lo);
-        if (!(mid > lo && mid < hi)) break;
-        if (count_ge<NX>(x, mid) >= K) lo = mid; else hi = mid;
-    }
+__device__ __forceinline__ int count_ge(const float (&x)[NX], float v) {
+    int c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int q = 0; q < NX; ++q) c[q & 7] += x[q] >= v ? 1 : 0;
+    return ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
 }
 
 // A lower bound on the K-th largest class maximum of a row whose maxima are
@@ -440,57 +407,105 @@ __device__ __forceinline__ float group_class_bound(const float (&y)[kHalfCols], 
     return nfin < K ? -INFINITY : lo;
 }
 
-// Candidate append: store (sc, key) at a and advance a by one entry when
-// sc >= theta (and, in the masked form, col < climit).  The address chain only
-// carries the add; the compare is repeated off it.  Shared-memory lists take a
-// 32-bit shared address, global lists a generic 64-bit one.
+// Candidate append: store (sc, key) at a and advance a by one entry (kStep
+// bytes) when sc >= theta (and, in the masked form, col < climit).  The address
+// chain only carries the add; the compare is repeated off it, so the compiler
+// can compute the next columns' compares ahead.  Shared-memory sub-lists take a
+// 32-bit shared address, global ones a 64-bit global address.
+template <uint32_t kStep>
 __device__ __forceinline__ void append_ge(uint32_t& a, float sc, float theta, uint32_t key) {
     asm volatile("{\n .reg .pred p;\n setp.ge.f32 p, %1, %2;\n"
                  " @p st.shared.v2.b32 [%0], {%1, %3};\n}" :: "r"(a), "f"(sc), "f"(theta), "r"(key));
-    a += sc >= theta ? 8u : 0u;
+    a += sc >= theta ? kStep : 0u;
 }
-__device__ __forceinline__ void append_ge(uint64_t& a, float sc, float theta, uint32_t key) {
-    asm volatile("{\n .reg .pred p;\n setp.ge.f32 p, %1, %2;\n"
-                 " @p st.global.v2.b32 [%0], {%1, %3};\n}" :: "l"(a), "f"(sc), "f"(theta), "r"(key));
-    a += sc >= theta ? 8ull : 0ull;
-}
+template <uint32_t kStep>
 __device__ __forceinline__ void append_ge_lt(uint32_t& a, float sc, float theta, uint32_t key, int col,
                                              int climit) {
     asm volatile("{\n .reg .pred p, e;\n setp.ge.f32 p, %1, %2;\n setp.lt.s32 e, %4, %5;\n"
                  " and.pred p, p, e;\n @p st.shared.v2.b32 [%0], {%1, %3};\n}"
                  :: "r"(a), "f"(sc), "f"(theta), "r"(key), "r"(col), "r"(climit));
-    a += (sc >= theta && col < climit) ? 8u : 0u;
+    a += (sc >= theta && col < climit) ? kStep : 0u;
 }
+template <uint64_t kStep>
+__device__ __forceinline__ void append_ge(uint64_t& a, float sc, float theta, uint32_t key) {
+    asm volatile("{\n .reg .pred p;\n setp.ge.f32 p, %1, %2;\n"
+                 " @p st.global.v2.b32 [%0], {%1, %3};\n}" :: "l"(a), "f"(sc), "f"(theta), "r"(key));
+    a += sc >= theta ? kStep : 0ull;
+}
+template <uint64_t kStep>
 __device__ __forceinline__ void append_ge_lt(uint64_t& a, float sc, float theta, uint32_t key, int col,
                                              int climit) {
     asm volatile("{\n .reg .pred p, e;\n setp.ge.f32 p, %1, %2;\n setp.lt.s32 e, %4, %5;\n"
                  " and.pred p, p, e;\n @p st.global.v2.b32 [%0], {%1, %3};\n}"
                  :: "l"(a), "f"(sc), "f"(theta), "r"(key), "r"(col), "r"(climit));
-    a += (sc >= theta && col < climit) ? 8ull : 0ull;
+    a += (sc >= theta && col < climit) ? kStep : 0ull;
+}
+
+// Scores of two adjacent columns in one instruction: (acc0, acc1) * (m, m) +
+// (b0, b1) with fma.rn.f32x2, each element rounded exactly as fmaf.  mm holds
+// m in both halves.
+__device__ __forceinline__ float2 score2(uint32_t acc0, uint32_t acc1, uint64_t mm, float b0, float b1) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rc, {%5, %6};\n"
+        " fma.rn.f32x2 rd, ra, %4, rc;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y) : "r"(acc0), "r"(acc1), "l"(mm), "f"(b0), "f"(b1));
+    return d;
+}
+
+// Scores one 64-column half tile in 16-column chunks, software-pipelined:
+// chunk h + 1's accumulator columns (tcgen05.ld) and pos_bias terms (ld.shared
+// from wsrc upwards, x..w = columns c..c+3) are in flight while chunk h is
+// scored by fn(h, v, bw).
+// The accumulator is released on `tempty` once its last chunk has landed.
+template <typename Fn>
+__device__ __forceinline__ void score_half_tile(uint32_t taddr, uint32_t wsrc, uint64_t* tempty, int lane, Fn&& fn) {
+    constexpr int kC = 16, kNC = kHalfCols / kC;
+    uint32_t v[2][kC];
+    float4 bw[2][kC / 4];
+    tmem_ld16(taddr, v[0]);
+#pragma unroll
+    for (int q = 0; q < kC / 4; ++q) bw[0][q] = lds_f4(wsrc + 16u * (uint32_t)q);
+#pragma unroll
+    for (int h = 0; h < kNC; ++h) {
+        tmem_wait_ld();
+        reg_fence(v[h & 1]);
+        if (h + 1 < kNC) {
+            tmem_ld16(taddr + (uint32_t)(kC * (h + 1)), v[(h + 1) & 1]);
+#pragma unroll
+            for (int q = 0; q < kC / 4; ++q) bw[(h + 1) & 1][q] = lds_f4(wsrc + 4u * (uint32_t)(kC * (h + 1) + 4 * q));
+        } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty);
+        }
+        fn(h, v[h & 1], bw[h & 1]);
+    }
 }
 
 template <bool kWide>
 __global__ void __launch_bounds__(kThreads, 1)
 router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const TcParams p) {
+    using Cfg = TcCfg<kWide>;
+    constexpr int kStages = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-    uint8_t* sA = smem + kOffA;
-    uint8_t* sB = smem + kOffB;
-    float* win = reinterpret_cast<float*>(smem + kOffWin);
-    uint2* buf = reinterpret_cast<uint2*>(smem + kOffBuf);
-    [[maybe_unused]] float* cls = reinterpret_cast<float*>(smem + kOffBuf);  // wide: class maxima per row
-    [[maybe_unused]] float* lbw = cls + kTileM * kClsStride;                 // wide: bound per row
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint8_t* sA = smem + Cfg::kOffA;
+    uint8_t* sB = smem + Cfg::kOffB;
+    float* win = reinterpret_cast<float*>(smem + Cfg::kOffWin);
+    // narrow: sub-lists; wide: class maxima and bounds (see TcCfg)
+    [[maybe_unused]] uint2* buf = reinterpret_cast<uint2*>(smem + Cfg::kOffBuf);
+    [[maybe_unused]] float* cls = reinterpret_cast<float*>(smem + Cfg::kOffBuf);
+    [[maybe_unused]] float* lbw = cls + kTileM * Cfg::kClsStride;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
     uint64_t* full = bars;
     uint64_t* empty = bars + kStages;
     uint64_t* afull = bars + 2 * kStages;
     uint64_t* tfull = afull + 1;
     uint64_t* tempty = tfull + kAccBufs;
-    uint64_t* wfull = tempty + kAccBufs;  // the tile's pos_bias window has landed
-    uint64_t* mdone = wfull + kAccBufs;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffSlot);
+    uint64_t* mdone = tempty + kAccBufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffSlot);
 
     const int N = p.N, H = p.H, Hkv = p.Hkv, Nq = p.Nq;
     const int BH = gridDim.x / p.nqb;
@@ -524,9 +539,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         mbar_init(afull, 1);
         for (int s = 0; s < kAccBufs; ++s) {
-            mbar_init(tfull + s, 1);
+            mbar_init(tfull + s, 2);  // MMA commit + the window's bulk copy
             mbar_init(tempty + s, kEpiWarps);
-            mbar_init(wfull + s, 1);
         }
         mbar_init(mdone, 1);
         fence_mbar_init();
@@ -567,35 +581,12 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_f16(0u, kTileM, kTileN);
             const uint64_t adesc = umma_desc_sw128(sA);
-            // The pos_bias window of step t goes to window buffer t % kAccBufs once the
-            // accumulator of that index is free (every epilogue warp is done with
-            // both): one bulk copy per shifted copy of the bias line.  The line is
-            // laid out so that tile (qb, key tile) starts kTileN * (qb + tiles_n - 1 -
-            // key tile) floats into each copy.
-            const float* bline = p.bext + (size_t)kTileN * (qb + p.tiles_n - 1);
-            auto load_window = [&](int t) {
-                const int ab = t % kAccBufs;
-                const float* src = bline - (size_t)kTileN * tile_of(t);
-                float* dst = win + (size_t)ab * (kWinBytes / 4);
-                mbar_arrive_expect_tx(wfull + ab, kWinTx);
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    bulk_load(dst + c * kWinCopy, src + (size_t)c * p.ext_len, kWinLen * 4, wfull + ab);
-            };
-            const int wfirst = min(T2, kAccBufs);
-            for (int t = 0; t < wfirst; ++t) load_window(t);
-            int wissued = wfirst;
             bool ok = mbar_wait(afull, 0);
             for (int t = 0; t < T2 && ok; ++t) {
                 const int s = t % kStages;
                 const int ab = t % kAccBufs;
-                if (t >= kAccBufs) {
-                    ok = mbar_wait(tempty + ab, ((t / kAccBufs) - 1) & 1);
-                    if (!ok) break;
-                    load_window(t);
-                    wissued = t + 1;
-                }
                 ok = mbar_wait(full + s, (t / kStages) & 1);
+                if (ok && t >= kAccBufs) ok = mbar_wait(tempty + ab, ((t / kAccBufs) - 1) & 1);
                 if (!ok) break;
                 tc_fence_after();
                 const uint64_t bdesc = umma_desc_sw128(sB + (size_t)s * kTileBytes);
@@ -608,24 +599,47 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             }
             mma_commit(mdone);  // completes once every MMA issued above has finished
             mbar_wait(mdone, 0);
-            // windows the epilogue never waited for (error path) land before the CTA retires
-            for (int t = max(0, wissued - kAccBufs); t < wissued; ++t)
-                mbar_wait(wfull + t % kAccBufs, (t / kAccBufs) & 1);
             if (!ok) atomicOr(p.status, 2);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------ window loads
+        // The pos_bias window of step t goes to window buffer t % kAccBufs once the
+        // accumulator of that index is free (every epilogue warp is done with
+        // both), as one bulk copy of its precomputed image that completes on the
+        // accumulator's tfull barrier (its second arrival, after the MMA commit).
+        if (lane == 0) {
+            const float* wbase = p.wtab + (size_t)(p.nqb - 1 - qb) * (4 * kWinCopy);
+            bool ok = true;
+            int issued = 0;
+            for (int t = 0; t < T2; ++t) {
+                const int ab = t % kAccBufs;
+                if (t >= kAccBufs) ok = mbar_wait(tempty + ab, ((t / kAccBufs) - 1) & 1);
+                if (!ok) break;
+                mbar_arrive_expect_tx(tfull + ab, kWinBytes);
+                bulk_load(win + (size_t)ab * (kWinBytes / 4), wbase + (size_t)tile_of(t) * (4 * kWinCopy), kWinBytes,
+                          tfull + ab);
+                issued = t + 1;
+            }
+            // copies the epilogue never waited for (error path) land before the CTA
+            // retires: their barrier phases complete, or the bounded waits run out
+            // long after the bytes have arrived
+            if (!ok)
+                for (int t = max(0, issued - kAccBufs); t < issued; ++t)
+                    mbar_wait(tfull + t % kAccBufs, (t / kAccBufs) & 1);
+            if (!ok) atomicOr(p.status, 8);
         }
     } else {
         // ------------------------------------------------ epilogue: scoring + selection
         // Eight warps: warp (quadrant qd, half hf) owns TMEM lanes 32*qd.. (query
         // rows) and accumulator columns 64*hf.. of every tile; each row is served
         // by two threads, one per column half, with one candidate sub-list each.
-        const int ew = warp - 2;             // 0..7
+        const int ew = warp - kCtlWarps;     // 0..7
         const int qd = warp & 3;             // TMEM lane quadrant this warp may access
         const int hf = ew >> 2;              // column half
         const int r0 = qd * 32;
         const int row = r0 + lane;
         const int i = i0 + row;              // local query row
         const int K = p.K;
-        const int L = p.L;
         const int cbase = hf * kHalfCols;    // first tile column of this thread
         const uint32_t pair_bar = 1u + (uint32_t)qd;  // named barrier of the quadrant's two warps
         float m = 0.f, delta = 0.f;
@@ -636,22 +650,21 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             delta = ri.y;
             if (!(m == m)) fb = true;
         }
-        uint2* rowbuf = buf + (size_t)row * kRowStride;
-        uint2* sub = rowbuf + hf * kSubCap;  // this thread's candidate sub-list
-        // pos_bias terms of columns cbase + cl .. + 3 (cl a multiple of 4): copy
-        // s4 = row & 3 of the tile's window at position row - s4 + 124 - cbase - cl,
-        // i.e. w[row - (cbase + cl + 3) + 127 .. row - (cbase + cl) + 127], in reverse
-        const int s4 = lane & 3;
-        const uint32_t wrd_s = smem_u32(win) + 4u * (uint32_t)(s4 * kWinCopy + row - s4 + (kTileN - 4) - cbase);
+        const uint64_t mm = ((uint64_t)__float_as_uint(m) << 32) | __float_as_uint(m);  // (m, m)
+        // The window holds u[z], z = col - row + 127 (the bias term of column col
+        // for this row), copy s holding u[s ..].  Columns cbase + cl .. + 3 (cl a
+        // multiple of 4) are copy s4 = 3 - (row & 3) at position
+        // cbase + cl - (row - (row & 3)) + 124, in column order.
+        const int s4 = 3 - (lane & 3);
+        const uint32_t wrd_s =
+            smem_u32(win) + 4u * (uint32_t)(s4 * kWinCopy + cbase - (row - (lane & 3)) + (kTileN - 4));
         const int lim = p.causal ? min(N, p.q0 + i + 1) : N;  // keys j < lim are eligible
         bool ok = true;
 
-        // Tile prologue shared by both passes: wait for the tile's pos_bias window
-        // and its accumulator.  Returns false if a bounded wait expired.
+        // Tile prologue shared by both passes: wait for the tile's accumulator and
+        // pos_bias window (one barrier).  Returns false if the bounded wait expired.
         auto tile_prologue = [&](int t) -> bool {
-            const int ab = t % kAccBufs;
-            const uint32_t par = (uint32_t)(t / kAccBufs) & 1u;
-            const bool got = mbar_wait(wfull + ab, par) && mbar_wait(tfull + ab, par);
+            const bool got = mbar_wait(tfull + t % kAccBufs, (uint32_t)(t / kAccBufs) & 1u);
             if (!__all_sync(kFull, got)) return false;
             tc_fence_after();
             return true;
@@ -674,48 +687,41 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             // into the next head's keys); causally masked keys score -inf anyway
             const bool full_tile = j0 + cbase + kHalfCols <= N;
             const int climit = lim - j0 - cbase;  // local columns c < climit are eligible
-            // 32-column chunks: the chunk's accumulator columns and its bias values
-            // are loaded together, so the shared-memory latency is paid once per
-            // chunk rather than once per 4 columns.
+            if (full_tile) {
+                score_half_tile(taddr, mycopy_s, tempty + ab, lane,
+                                [&](int h, const uint32_t (&v)[16], const float4 (&bw)[4]) {
 #pragma unroll
-            for (int h2 = 0; h2 < kHalfCols / kChunk; ++h2) {
-                uint32_t v[kChunk];
-                float4 bw[kChunk / 4];
-                tmem_ld_chunk(taddr + (uint32_t)(kChunk * h2), v);
-#pragma unroll
-                for (int q = 0; q < kChunk / 4; ++q) bw[q] = lds_f4(mycopy_s - 4u * (uint32_t)(kChunk * h2 + 4 * q));
-                tmem_wait_ld();
-                if (h2 == kHalfCols / kChunk - 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(tempty + ab);
-                }
-                if (full_tile) {
-#pragma unroll
-                    for (int q = 0; q < kChunk / 4; ++q) {
-                        const int c = kChunk * h2 + 4 * q;
-                        cm[c + 0] = fmaxf(cm[c + 0], fmaf(__uint_as_float(v[4 * q + 0]), m, bw[q].w));
-                        cm[c + 1] = fmaxf(cm[c + 1], fmaf(__uint_as_float(v[4 * q + 1]), m, bw[q].z));
-                        cm[c + 2] = fmaxf(cm[c + 2], fmaf(__uint_as_float(v[4 * q + 2]), m, bw[q].y));
-                        cm[c + 3] = fmaxf(cm[c + 3], fmaf(__uint_as_float(v[4 * q + 3]), m, bw[q].x));
+                    for (int q = 0; q < 4; ++q) {
+                        const int c = 16 * h + 4 * q;
+                        const float2 s01 = score2(v[4 * q + 0], v[4 * q + 1], mm, bw[q].x, bw[q].y);
+                        const float2 s23 = score2(v[4 * q + 2], v[4 * q + 3], mm, bw[q].z, bw[q].w);
+                        cm[c + 0] = fmaxf(cm[c + 0], s01.x);
+                        cm[c + 1] = fmaxf(cm[c + 1], s01.y);
+                        cm[c + 2] = fmaxf(cm[c + 2], s23.x);
+                        cm[c + 3] = fmaxf(cm[c + 3], s23.y);
                     }
-                } else {
+                });
+            } else {
+                score_half_tile(taddr, mycopy_s, tempty + ab, lane,
+                                [&](int h, const uint32_t (&v)[16], const float4 (&bw)[4]) {
 #pragma unroll
-                    for (int q = 0; q < kChunk / 4; ++q) {
-                        const int c = kChunk * h2 + 4 * q;
-                        const float b4[4] = {bw[q].w, bw[q].z, bw[q].y, bw[q].x};
+                    for (int q = 0; q < 4; ++q) {
+                        const int c = 16 * h + 4 * q;
+                        const float2 s01 = score2(v[4 * q + 0], v[4 * q + 1], mm, bw[q].x, bw[q].y);
+                        const float2 s23 = score2(v[4 * q + 2], v[4 * q + 3], mm, bw[q].z, bw[q].w);
+                        const float s4v[4] = {s01.x, s01.y, s23.x, s23.y};
 #pragma unroll
                         for (int d = 0; d < 4; ++d) {
-                            const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
+                            const float sc = s4v[d];
                             cm[c + d] = fmaxf(cm[c + d], c + d < climit ? sc : -INFINITY);
                         }
                     }
-                }
+                });
             }
             if constexpr (kWide) {
                 if (t == Te - 1) {
                     // even tiles done: their class maxima go to shared memory
-                    float* crow = cls + row * kClsStride + hf * kHalfCols;
+                    float* crow = cls + row * Cfg::kClsStride + hf * kHalfCols;
 #pragma unroll
                     for (int c = 0; c < kHalfCols; ++c) {
                         crow[c] = cm[c];
@@ -725,35 +731,35 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             }
         }
 
+        // End of pass 1: a group of lanes per row bounds the row's class maxima
+        // (group_class_bound): every exact top-K key scores at least the bound -
+        // 2*delta.
+        [[maybe_unused]] uint2* rowbuf = buf + (size_t)row * Cfg::kRowStride;  // narrow
+        [[maybe_unused]] uint2* sub = rowbuf + hf * Cfg::kCap;  // narrow: this thread's sub-list
         float lb = -INFINITY;
         if constexpr (!kWide) {
-            // End of pass 1: the 128 class maxima of a row lie in two warps (64
-            // each).  They go through the (still empty) candidate area to a lane
-            // pair of one warp: lanes 2r and 2r+1 of warp hf take row r0 + 16*hf + r,
-            // one half each (group_class_bound).  Every exact top-K key scores at
-            // least the bound - 2*delta.  The bound goes back through the row's
-            // spare list entry.
+            // 128 maxima, 64 per column half, exchanged through the still empty
+            // sub-lists: lanes 2r and 2r+1 of warp hf take row r0 + 16*hf + r, one
+            // half each; the bound goes back through the row's spare entry
             float* xch = reinterpret_cast<float*>(sub);
 #pragma unroll
             for (int c = 0; c < kHalfCols; ++c) xch[c] = cm[c];
             named_bar_sync(pair_bar, 64);
-            {
-                const int brow = r0 + 16 * hf + (lane >> 1);
-                const int bhalf = lane & 1;
-                const float* bcls = reinterpret_cast<const float*>(buf + (size_t)brow * kRowStride + bhalf * kSubCap);
-                float y[kHalfCols];
+            const int brow = r0 + 16 * hf + (lane >> 1);
+            const int bhalf = lane & 1;
+            const float* bcls = reinterpret_cast<const float*>(buf + (size_t)brow * Cfg::kRowStride + bhalf * Cfg::kCap);
+            float y[kHalfCols];
 #pragma unroll
-                for (int c = 0; c < kHalfCols; ++c) y[c] = bcls[c ^ bhalf];  // the pair reads different banks
-                const float lbv = group_class_bound<2>(y, K);
-                if (bhalf == 0) buf[(size_t)brow * kRowStride + (kRowStride - 1)].x = __float_as_uint(lbv);
-            }
+            for (int c = 0; c < kHalfCols; ++c) y[c] = bcls[c ^ bhalf];  // the pair reads different banks
+            const float lbv = group_class_bound<2>(y, K);
+            if (bhalf == 0) buf[(size_t)brow * Cfg::kRowStride + (Cfg::kRowStride - 1)].x = __float_as_uint(lbv);
             named_bar_sync(pair_bar, 64);  // bounds published; class maxima read before sub-lists are written
-            lb = __uint_as_float(rowbuf[kRowStride - 1].x);
+            lb = __uint_as_float(rowbuf[Cfg::kRowStride - 1].x);
         } else {
-            // End of pass 1 (wide): a row's 256 class maxima (even/odd tiles x two
-            // column halves, 64 each) are in shared memory; four lanes per row
-            // bound them, the quadrant's 32 rows in two batches of 16.
-            float* crow = cls + row * kClsStride + kTileN + hf * kHalfCols;
+            // 256 maxima (even/odd tiles x two column halves, 64 each; the even ones
+            // are already in shared memory); four lanes per row, the quadrant's 32
+            // rows in two batches of 16
+            float* crow = cls + row * Cfg::kClsStride + kTileN + hf * kHalfCols;
 #pragma unroll
             for (int c = 0; c < kHalfCols; ++c) crow[c] = cm[c];
             named_bar_sync(pair_bar, 64);
@@ -761,7 +767,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             for (int bt = 0; bt < 2; ++bt) {
                 const int brow = r0 + 16 * bt + 8 * hf + (lane >> 2);
                 const int t4 = lane & 3;
-                const float* src = cls + brow * kClsStride + t4 * kHalfCols;
+                const float* src = cls + brow * Cfg::kClsStride + t4 * kHalfCols;
                 float y[kHalfCols];
                 // rotated by 8 per lane of the group: the warp's 32 reads hit 32 banks
 #pragma unroll
@@ -779,14 +785,14 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
 
         // ---------------- pass 2: collect candidates s >= theta into the sub-list
-        // Narrow: the sub-list sits in shared memory (32-bit shared address).
-        // Wide: it sits in global memory, kWideCap entries per row and half.
+        // (narrow: shared memory; wide: global memory, contiguous per row and half)
         using Addr = std::conditional_t<kWide, uint64_t, uint32_t>;
-        constexpr int kLimit = kWide ? kWideLimit : kSubLimit;
+        constexpr int kLimit = Cfg::kLimit;
+        constexpr Addr kStep = 8;  // bytes per entry
         Addr list_base;
         if constexpr (kWide)
             list_base = (uint64_t)__cvta_generic_to_global(
-                p.lists + (((size_t)bh * Nq + (size_t)(i < Nq ? i : 0)) * 2 + hf) * kWideCap);
+                p.lists + ((size_t)bh * p.nqb + qb) * (2 * kTileM * (size_t)Cfg::kCap) + (size_t)(2 * row + hf) * Cfg::kCap);
         else
             list_base = smem_u32(sub);
         int cnt = 0;
@@ -805,63 +811,55 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             // Write address and an explicitly predicated store: the per-column
             // append costs one store and one add.
             const Addr sub_s = list_base;
-            Addr waddr = sub_s + (Addr)(8u * (uint32_t)cnt);
+            Addr waddr = sub_s + kStep * (uint32_t)cnt;
             // After every 16 columns: a sub-list that could overflow during the next
             // 16 sends its row to the exact fallback (kLimit = capacity - 16).
             auto overflow_check = [&]() {
-                if ((int)((waddr - sub_s) >> 3) > kLimit) {
+                if ((int)((waddr - sub_s) / kStep) > kLimit) {
                     fb = true;
                     theta = __int_as_float(0x7fc00000);
                     waddr = sub_s;
                 }
             };
-            // 32-column chunks, each loading its accumulator columns and bias values
-            // together (as in pass 1).
+            if (full_tile) {
+                score_half_tile(taddr, mycopy_s, tempty + ab, lane,
+                                [&](int h, const uint32_t (&v)[16], const float4 (&bw)[4]) {
 #pragma unroll
-            for (int h2 = 0; h2 < kHalfCols / kChunk; ++h2) {
-                uint32_t v[kChunk];
-                float4 bw[kChunk / 4];
-                tmem_ld_chunk(taddr + (uint32_t)(kChunk * h2), v);
-#pragma unroll
-                for (int q = 0; q < kChunk / 4; ++q) bw[q] = lds_f4(mycopy_s - 4u * (uint32_t)(kChunk * h2 + 4 * q));
-                tmem_wait_ld();
-                if (h2 == kHalfCols / kChunk - 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(tempty + ab);
-                }
-                if (full_tile) {
-#pragma unroll
-                    for (int q = 0; q < kChunk / 4; ++q) {
-                        const int c = kChunk * h2 + 4 * q;
-                        const float b4[4] = {bw[q].w, bw[q].z, bw[q].y, bw[q].x};
+                    for (int q = 0; q < 4; ++q) {
+                        const int c = 16 * h + 4 * q;
+                        const float b4[4] = {bw[q].x, bw[q].y, bw[q].z, bw[q].w};
 #pragma unroll
                         for (int d = 0; d < 4; ++d) {
+                            // scalar FMAs here: the packed form measured slower in this loop
                             const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
-                            append_ge(waddr, sc, theta, jb + (uint32_t)(c + d));
+                            append_ge<kStep>(waddr, sc, theta, jb + (uint32_t)(c + d));
                         }
-                        if ((q & 3) == 3) overflow_check();
                     }
-                } else {
+                    overflow_check();
+                });
+            } else {
+                score_half_tile(taddr, mycopy_s, tempty + ab, lane,
+                                [&](int h, const uint32_t (&v)[16], const float4 (&bw)[4]) {
 #pragma unroll
-                    for (int q = 0; q < kChunk / 4; ++q) {
-                        const int c = kChunk * h2 + 4 * q;
-                        const float b4[4] = {bw[q].w, bw[q].z, bw[q].y, bw[q].x};
+                    for (int q = 0; q < 4; ++q) {
+                        const int c = 16 * h + 4 * q;
+                        const float b4[4] = {bw[q].x, bw[q].y, bw[q].z, bw[q].w};
 #pragma unroll
                         for (int d = 0; d < 4; ++d) {
+                            // scalar FMAs here: the packed form measured slower in this loop
                             const float sc = fmaf(__uint_as_float(v[4 * q + d]), m, b4[d]);
-                            append_ge_lt(waddr, sc, theta, jb + (uint32_t)(c + d), c + d, climit);
+                            append_ge_lt<kStep>(waddr, sc, theta, jb + (uint32_t)(c + d), c + d, climit);
                         }
-                        if ((q & 3) == 3) overflow_check();
                     }
-                }
+                    overflow_check();
+                });
             }
-            cnt = (int)((waddr - sub_s) >> 3);
+            cnt = (int)((waddr - sub_s) / kStep);
         }
         if (!ok) atomicOr(p.status, 4);
 
         if constexpr (kWide) {
-            // the warp-per-row wide_final_kernel finishes the row from its two lists
+            // final_select_kernel finishes the row from its two lists
             if (ok && i < Nq) p.counts[((size_t)bh * Nq + i) * 2 + hf] = fb ? -1 : cnt;
         } else {
             // ---------------------------------------------- per-row final selection
@@ -880,17 +878,17 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             //     lists from the front, lane 2r+1 from the back, into the output row.
             // A row's two counts go to the .y word of its spare list entry (.x holds
             // the bound), 16 bits per column half.
-            reinterpret_cast<int16_t*>(&rowbuf[kRowStride - 1].y)[hf] = (int16_t)(fb ? -1 : cnt);
+            reinterpret_cast<int16_t*>(&rowbuf[Cfg::kRowStride - 1].y)[hf] = (int16_t)(fb ? -1 : cnt);
             named_bar_sync(pair_bar, 64);
             {
                 const int frow = r0 + 16 * hf + (lane >> 1);
                 const int fh = lane & 1;
                 const int fi = i0 + frow;
                 const bool active = ok && fi < Nq;
-                uint2* frowbuf = buf + (size_t)frow * kRowStride;
-                const int16_t* fmeta = reinterpret_cast<const int16_t*>(&frowbuf[kRowStride - 1].y);
+                uint2* frowbuf = buf + (size_t)frow * Cfg::kRowStride;
+                const int16_t* fmeta = reinterpret_cast<const int16_t*>(&frowbuf[Cfg::kRowStride - 1].y);
                 const int ca = fmeta[0], cb = fmeta[1];
-                uint2* own = frowbuf + fh * kSubCap;
+                uint2* own = frowbuf + fh * Cfg::kCap;
                 const int nown = fh ? cb : ca;
                 bool to_fallback = active && (ca < 0 || cb < 0);
                 bool work = active && !to_fallback;
@@ -900,15 +898,15 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 float fdelta = 0.f, lo = 0.f;
                 if (work) {
                     fdelta = p.rowinfo[orow_id].y;
-                    lo = __uint_as_float(frowbuf[kRowStride - 1].x);
+                    lo = __uint_as_float(frowbuf[Cfg::kRowStride - 1].x);
                 }
                 const uint32_t own_s = smem_u32(own);
                 // Slots past the warp's longest sub-list hold -inf in every lane and
                 // change no count or extremum below: loops stop after nch 8-slot chunks.
                 const int nch = (int)((__reduce_max_sync(kFull, work ? (unsigned)nown : 0u) + 7u) >> 3);
-                float x[kSubCap];
+                float x[Cfg::kCap];
     #pragma unroll
-                for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                for (int ch = 0; ch < Cfg::kCap / 8; ++ch) {
     #pragma unroll
                     for (int u = 0; u < 8; ++u) x[8 * ch + u] = -INFINITY;
                     if (ch < nch) {
@@ -925,7 +923,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     #pragma unroll
                 for (int u = 0; u < 8; ++u) hi8[u] = -INFINITY;
     #pragma unroll
-                for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                for (int ch = 0; ch < Cfg::kCap / 8; ++ch) {
                     if (ch < nch) {
     #pragma unroll
                         for (int u = 0; u < 8; ++u) hi8[u] = fmaxf(hi8[u], x[8 * ch + u]);
@@ -934,7 +932,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 float hi = fmaxf(fmaxf(fmaxf(hi8[0], hi8[1]), fmaxf(hi8[2], hi8[3])),
                                  fmaxf(fmaxf(hi8[4], hi8[5]), fmaxf(hi8[6], hi8[7])));
                 hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, 1));
-                int cnt_lo = count_ge_chunks<kSubCap>(x, lo, nch);
+                int cnt_lo = count_ge_chunks<Cfg::kCap>(x, lo, nch);
                 cnt_lo += __shfl_xor_sync(kFull, cnt_lo, 1);
                 if (work && !all_in && cnt_lo < K) {
                     to_fallback = true;  // cannot happen: lb is reached by K candidates
@@ -947,7 +945,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 for (int it = 0; it < 40; ++it) {
                     if (__all_sync(kFull, done)) break;
                     const float mid = lo + 0.5f * (hi - lo);
-                    int c = count_ge_chunks<kSubCap>(x, mid, nch);
+                    int c = count_ge_chunks<Cfg::kCap>(x, mid, nch);
                     c += __shfl_xor_sync(kFull, c, 1);
                     if (!done) {
                         if (!(mid > lo && mid < hi)) {
@@ -969,7 +967,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     kmax8[u] = -INFINITY;
                 }
     #pragma unroll
-                for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                for (int ch = 0; ch < Cfg::kCap / 8; ++ch) {
                     if (ch < nch) {
     #pragma unroll
                         for (int u = 0; u < 8; ++u) {
@@ -1002,7 +1000,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 {
                     int ni8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, nb8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     #pragma unroll
-                    for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                    for (int ch = 0; ch < Cfg::kCap / 8; ++ch) {
                         if (ch < nch) {
     #pragma unroll
                             for (int u = 0; u < 8; ++u) {
@@ -1022,19 +1020,19 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 const int oth_nb = __shfl_xor_sync(kFull, own_nb, 1);
                 const int need = K - n_in;
                 bool rescore = work && !all_in && own_nb + oth_nb != need;
-                if (rescore && (own_nb > kMaxBand / 2 || oth_nb > kMaxBand / 2)) {
+                if (rescore && (own_nb > (2 * kMaxBandNarrow) / 2 || oth_nb > (2 * kMaxBandNarrow) / 2)) {
                     to_fallback = true;
                     work = false;
                     rescore = false;
                 }
 
                 // 2. canonical rescoring of the boundary band
-                uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)frow * kMaxBand;  // MMAs are done with sA
-                uint2* myslots = scratch + fh * (kMaxBand / 2);
+                uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)frow * (2 * kMaxBandNarrow);  // MMAs are done with sA
+                uint2* myslots = scratch + fh * ((2 * kMaxBandNarrow) / 2);
                 if (rescore) {
                     uint32_t wa = smem_u32(myslots);
     #pragma unroll
-                    for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                    for (int ch = 0; ch < Cfg::kCap / 8; ++ch) {
                         if (ch < nch) {
     #pragma unroll
                             for (int u = 0; u < 8; ++u) {
@@ -1054,7 +1052,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     for (int u = 0; u < nbmax; ++u) {
                         if (rescore && u < own_nb) {
                             const int jj = (int)own[myslots[u].x].y;
-                            const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, L, p.q0 + fi, jj,
+                            const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, p.L, p.q0 + fi, jj,
                                                                          p.scale);
                             myslots[u] = make_uint2(order_key(ex), (uint32_t)jj);
                         }
@@ -1063,7 +1061,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 }
                 uint32_t selmask = 0u;
                 if (rescore) {
-                    const uint2* oslots = scratch + (1 - fh) * (kMaxBand / 2);
+                    const uint2* oslots = scratch + (1 - fh) * ((2 * kMaxBandNarrow) / 2);
                     for (int a2 = 0; a2 < own_nb; ++a2) {
                         const uint2 ea = myslots[a2];
                         int rank = 0;
@@ -1085,7 +1083,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     uint32_t wa = own_s + 4u;  // .y of the next kept slot
                     int bidx = 0;
     #pragma unroll
-                    for (int ch = 0; ch < kSubCap / 8; ++ch) {
+                    for (int ch = 0; ch < Cfg::kCap / 8; ++ch) {
                         if (ch < nch) {
                             // scores re-read from the list, a chunk at a time (x[] is not kept
                             // live across the band work); loads before the chunk's stores
@@ -1120,7 +1118,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 const uint32_t stage_s = smem_u32(sB);
                 {
                     const uint32_t LA = smem_u32(frowbuf) + 4u;             // .y fields
-                    const uint32_t LB = LA + 8u * kSubCap;
+                    const uint32_t LB = LA + 8u * Cfg::kCap;
                     const int dir = fh ? -1 : 1;
                     int ia = fh ? nA - 1 : 0, ib = fh ? nB - 1 : 0;
                     // lane 2r takes the smaller key each step, lane 2r+1 the larger:
@@ -1288,9 +1286,9 @@ exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, co
     }
 }
 
-// ------------------------------------------ wide selection: per-row final choice
+// ------------------------------------------------------ per-row final choice
 
-struct WideFinalParams {
+struct FinalParams {
     const uint2* lists;
     const int* counts;
     const float2* rowinfo;
@@ -1301,12 +1299,12 @@ struct WideFinalParams {
     int* fb_count;
     int32_t* fb_list;
     long long rows;
-    int L, H, Hkv, N, K, Nq, q0;
+    int L, H, Hkv, N, K, Nq, q0, nqb;
     float scale;
 };
 
 // One warp per query row.  The row's two candidate sub-lists A and B (one per
-// column half, keys ascending, at most kWideCap each) are loaded as entry
+// column half, keys ascending, at most kCap each) are loaded as entry
 // q = lane + 32 e of A ++ B.  With more than K candidates, the K-th best
 // approximate score x_K splits them: let top = the best score below x_K when
 // exactly K entries reach x_K, else x_K itself, and m2 = 2 delta plus rounding
@@ -1315,10 +1313,13 @@ struct WideFinalParams {
 // the free slots, its entries are rescored with the canonical fp32 formula and
 // the best by (score desc, key asc) fill the slots.  The kept keys of A and B
 // are then merged by rank into ascending order, -1 padded.  Rows whose lists
-// overflowed, whose inputs are not finite, or whose band holds more than 32
-// entries go to the exact fallback list.
-__global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p) {
-    __shared__ int skept[8][2][kWideMaxK];
+// overflowed, whose inputs are not finite, or whose band holds more than
+// kMaxBand entries go to the exact fallback list.
+template <int kCap, int kMaxOut>
+__global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) {
+    constexpr int kEPL = 2 * kCap / 32;  // candidate entries per lane
+    static_assert(kEPL * 32 == 2 * kCap && kMaxBand <= 32, "list and band layout");
+    __shared__ int skept[8][2][kMaxOut];
     __shared__ int sband[8][32];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1326,16 +1327,19 @@ __global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p
     const int K = p.K;
     for (long long row = (long long)blockIdx.x * 8 + warp; row < p.rows; row += (long long)gridDim.x * 8) {
         const int ca = p.counts[2 * row], cb = p.counts[2 * row + 1];
-        bool fallback = ca < 0 || cb < 0 || ca > kWideCap || cb > kWideCap;
+        bool fallback = ca < 0 || cb < 0 || ca > kCap || cb > kCap;
         if (!fallback) {
-            const uint2* LA = p.lists + (size_t)row * (2 * kWideCap);
-            const uint2* LB = LA + kWideCap;
+            const long long bh = row / p.Nq;
+            const int il = (int)(row - bh * p.Nq);
+            const uint2* LA = p.lists + ((size_t)bh * p.nqb + il / kTileM) * (2 * kTileM * (size_t)kCap) +
+                              (size_t)(2 * (il % kTileM)) * kCap;  // contiguous sub-lists (wide layout)
+            const uint2* LB = LA + kCap;
             const int tot = ca + cb;
-            float sv[kWideEPL];
-            uint32_t jv[kWideEPL];
-            bool val[kWideEPL], keep[kWideEPL];
+            float sv[kEPL];
+            uint32_t jv[kEPL];
+            bool val[kEPL], keep[kEPL];
 #pragma unroll
-            for (int e = 0; e < kWideEPL; ++e) {
+            for (int e = 0; e < kEPL; ++e) {
                 const int q = lane + 32 * e;
                 val[e] = q < tot;
                 uint2 t = make_uint2(0u, 0u);
@@ -1345,16 +1349,16 @@ __global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p
                 keep[e] = val[e];
             }
             if (tot > K) {
-                uint32_t u[kWideEPL];
+                uint32_t u[kEPL];
 #pragma unroll
-                for (int e = 0; e < kWideEPL; ++e) u[e] = order_key(sv[e]);
+                for (int e = 0; e < kEPL; ++e) u[e] = order_key(sv[e]);
                 uint32_t T;
                 int ties;
-                warp_kth_key<kWideEPL>(u, val, K, T, ties);
+                warp_kth_key<kEPL>(u, val, K, T, ties);
                 unsigned nge = 0;
                 uint32_t below = 0u;  // order keys of finite scores are never 0
 #pragma unroll
-                for (int e = 0; e < kWideEPL; ++e) {
+                for (int e = 0; e < kEPL; ++e) {
                     if (val[e]) {
                         if (u[e] >= T) ++nge;
                         else below = max(below, u[e]);
@@ -1369,9 +1373,9 @@ __global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p
                 const float m2 = 2.f * fdelta + (sl + 2.f * fdelta) * kTwoPowM22;
                 const float U = top + m2, W = xk - m2;
                 unsigned n_in = 0, nb = 0;
-                bool band[kWideEPL];
+                bool band[kEPL];
 #pragma unroll
-                for (int e = 0; e < kWideEPL; ++e) {
+                for (int e = 0; e < kEPL; ++e) {
                     band[e] = val[e] && sv[e] >= W && sv[e] <= U;
                     n_in += (val[e] && sv[e] > U) ? 1u : 0u;
                     nb += band[e] ? 1u : 0u;
@@ -1381,8 +1385,8 @@ __global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p
                 const int need = K - (int)n_in;
                 if ((int)nb == need) {
 #pragma unroll
-                    for (int e = 0; e < kWideEPL; ++e) keep[e] = val[e] && sv[e] >= W;
-                } else if (nb > 32u) {
+                    for (int e = 0; e < kEPL; ++e) keep[e] = val[e] && sv[e] >= W;
+                } else if (nb > (unsigned)kMaxBand) {
                     fallback = true;
                 } else {
                     // band entries to lanes 0..nb-1, in (e, lane) order
@@ -1390,10 +1394,10 @@ __global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p
                     const int ipos = p.q0 + (int)(row - bh * p.Nq);
                     const int b = (int)(bh / p.H);
                     const int g = (int)(bh - (long long)b * p.H) / (p.H / p.Hkv);
-                    int slot[kWideEPL];
+                    int slot[kEPL];
                     int base = 0;
 #pragma unroll
-                    for (int e = 0; e < kWideEPL; ++e) {
+                    for (int e = 0; e < kEPL; ++e) {
                         const unsigned bal = __ballot_sync(kFull, band[e]);
                         slot[e] = base + __popc(bal & lt);
                         if (band[e]) sband[warp][slot[e]] = (int)jv[e];
@@ -1417,7 +1421,7 @@ __global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p
                     }
                     const unsigned sel = __ballot_sync(kFull, lane < (int)nb && rank < need);
 #pragma unroll
-                    for (int e = 0; e < kWideEPL; ++e)
+                    for (int e = 0; e < kEPL; ++e)
                         keep[e] = val[e] && (sv[e] > U || (band[e] && ((sel >> slot[e]) & 1u)));
                     __syncwarp();  // sband is rewritten for the next row
                 }
@@ -1427,27 +1431,27 @@ __global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p
                 int* SA = skept[warp][0];
                 int* SB = skept[warp][1];
                 int na = 0, nbk = 0;
-                int li[kWideEPL];
+                int li[kEPL];
 #pragma unroll
-                for (int e = 0; e < kWideEPL; ++e) {
+                for (int e = 0; e < kEPL; ++e) {
                     const bool isA = lane + 32 * e < ca;
                     const bool kA = keep[e] && isA, kB = keep[e] && !isA;
                     const unsigned balA = __ballot_sync(kFull, kA);
                     const unsigned balB = __ballot_sync(kFull, kB);
                     li[e] = isA ? na + __popc(balA & lt) : nbk + __popc(balB & lt);
-                    if (kA && li[e] < kWideMaxK) SA[li[e]] = (int)jv[e];
-                    if (kB && li[e] < kWideMaxK) SB[li[e]] = (int)jv[e];
+                    if (kA && li[e] < kMaxOut) SA[li[e]] = (int)jv[e];
+                    if (kB && li[e] < kMaxOut) SB[li[e]] = (int)jv[e];
                     na += __popc(balA);
                     nbk += __popc(balB);
                 }
                 __syncwarp();
                 int32_t* orow = p.out + row * K;
 #pragma unroll
-                for (int e = 0; e < kWideEPL; ++e) {
+                for (int e = 0; e < kEPL; ++e) {
                     if (keep[e]) {
                         const bool isA = lane + 32 * e < ca;
                         const int* other = isA ? SB : SA;
-                        int lo = 0, hi = min(isA ? nbk : na, kWideMaxK);
+                        int lo = 0, hi = min(isA ? nbk : na, kMaxOut);
                         while (lo < hi) {  // keys of the other list below this one
                             const int mid = (lo + hi) >> 1;
                             if (other[mid] < (int)jv[e]) lo = mid + 1; else hi = mid;
@@ -1466,6 +1470,7 @@ __global__ void __launch_bounds__(256) wide_final_kernel(const WideFinalParams p
         }
     }
 }
+
 
 // ------------------------------------------------------------------ host side
 
@@ -1513,8 +1518,13 @@ size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K) {
     const int nqb = (Nq + kTileM - 1) / kTileM, tiles_n = (N + kTileN - 1) / kTileN;
     size_t total = al(rq * kR * 2) + al(rk * kR * 2) + al(rq * sizeof(float2)) +
                    al((3 * (size_t)B * Hkv + 2) * 4) + al(rq * 4) +
-                   (nqb > 0 && tiles_n > 0 ? al(4 * (size_t)bias_line_len(nqb, tiles_n) * 4) : 0);
-    if (K > kMaxK) total += al(rq * 2 * kWideCap * sizeof(uint2)) + al(rq * 2 * sizeof(int));
+                   (nqb > 0 && tiles_n > 0 ? al((size_t)window_count(nqb, tiles_n) * kWinBytes) : 0);
+    if (K > kNarrowMaxK) {
+        // wide: sub-lists for every row slot of every query block (the last block
+        // padded) and their lengths
+        const size_t lrows = (size_t)B * H * nqb * kTileM;
+        total += al(lrows * 2 * (size_t)TcCfg<true>::kCap * sizeof(uint2)) + al(rq * 2 * sizeof(int));
+    }
     return total;
 }
 
@@ -1535,15 +1545,15 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     int32_t* fb_list = reinterpret_cast<int32_t*>(w);
     w += al(rq * 4);
     const int nqb = (Nq + kTileM - 1) / kTileM, tiles_n = (a.N + kTileN - 1) / kTileN;
-    const int ext_len = bias_line_len(nqb, tiles_n);
-    float* bext = reinterpret_cast<float*>(w);
-    w += al(4 * (size_t)ext_len * 4);
-    const bool wide = a.K > kMaxK;
+    const int ndiag = window_count(nqb, tiles_n);
+    float* wtab = reinterpret_cast<float*>(w);
+    w += al((size_t)ndiag * kWinBytes);
+    const bool wide = a.K > kNarrowMaxK;
     uint2* lists = nullptr;
     int* counts = nullptr;
     if (wide) {
         lists = reinterpret_cast<uint2*>(w);
-        w += al(rq * 2 * kWideCap * sizeof(uint2));
+        w += al((size_t)a.B * a.H * nqb * kTileM * 2 * (size_t)TcCfg<true>::kCap * sizeof(uint2));
         counts = reinterpret_cast<int*>(w);
     }
     int* counters = a.counters;  // [0] fallback rows, [1] status
@@ -1564,18 +1574,20 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
         qprep_kernel<<<(unsigned)((rq + 127) / 128), 128, 0, stream>>>(a.qp32, q16, rowinfo, (long long)rq, a.H,
                                                                       a.Hkv, Nq, a.scale, stats, gstats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-        // offset of bias-line index 0: tile (qb, key tile) starts at i - j + L =
-        // q0 + kTileN * (qb - key tile) - 127 + L
-        const long long a_min = (long long)a.q0 + a.L - (kTileN - 1) - (long long)kTileN * (tiles_n - 1);
-        const long long nb = 4LL * ext_len;
-        bias_line_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, stream>>>(a.bias, a.L, a.causal, a_min, ext_len,
-                                                                          bext);
+        // offset of bias-line index 0: the window of tile (qb, key tile) starts at
+        // i - j + L = q0 + kTileN * (qb - key tile) + 127 + L (its first column
+        // against its last row)
+        const long long o_max = (long long)a.q0 + (long long)kTileN * (nqb - 1) + (kTileN - 1) + a.L;
+        const long long nb = (long long)ndiag * 4 * kWinCopy;
+        window_table_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, stream>>>(a.bias, a.L, a.causal, o_max, ndiag,
+                                                                             wtab);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     }
     CUtensorMap tmA, tmB;
     if (!make_row_map(&tmA, q16, rq) || !make_row_map(&tmB, k16, rk)) return cudaErrorInvalidValue;
+    const int smem_bytes = (int)(wide ? TcCfg<true>::kSmemBytes : TcCfg<false>::kSmemBytes);
     e = cudaFuncSetAttribute(wide ? router_tc_kernel<true> : router_tc_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     TcParams prm;
     prm.rowinfo = rowinfo;
@@ -1588,9 +1600,7 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.status = counters + 1;
     prm.lists = lists;
     prm.counts = counts;
-    prm.bext = bext;
-    prm.tiles_n = tiles_n;
-    prm.ext_len = ext_len;
+    prm.wtab = wtab;
     prm.L = a.L;
     prm.H = a.H;
     prm.Hkv = a.Hkv;
@@ -1603,15 +1613,16 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.scale = a.scale;
     const long long nblk = (long long)prm.nqb * a.B * a.H;
     if (!wide) {
-        router_tc_kernel<false><<<(unsigned)nblk, kThreads, kSmemBytes, stream>>>(tmA, tmB, prm);
+        router_tc_kernel<false><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        // rows sent to the exact selector (K + 32 candidates per warp: 4 entries per lane)
         exact_rows_kernel<4><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0,
                                                           a.K, a.scale, a.causal, counters, fb_list, a.out);
         return record(cudaGetLastError());
     }
-    router_tc_kernel<true><<<(unsigned)nblk, kThreads, kSmemBytes, stream>>>(tmA, tmB, prm);
+    router_tc_kernel<true><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-    WideFinalParams fp;
+    FinalParams fp;
     fp.lists = lists;
     fp.counts = counts;
     fp.rowinfo = rowinfo;
@@ -1629,11 +1640,12 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     fp.K = a.K;
     fp.Nq = Nq;
     fp.q0 = a.q0;
+    fp.nqb = prm.nqb;
     fp.scale = a.scale;
-    const long long fblk = std::min<long long>(((long long)rq + 7) / 8, 148LL * 8);
-    wide_final_kernel<<<(unsigned)fblk, 256, 0, stream>>>(fp);
+    const unsigned fblk = (unsigned)std::min<long long>(((long long)rq + 7) / 8, 148LL * 8);
+    final_select_kernel<TcCfg<true>::kCap, kWideMaxK><<<fblk, 256, 0, stream>>>(fp);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-    // K + 32 candidates per warp must fit: 6 entries per lane for K <= 160
+    // rows sent to the exact selector (K + 32 candidates per warp: 6 entries per lane for K <= 160)
     exact_rows_kernel<6><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0, a.K,
                                                       a.scale, a.causal, counters, fb_list, a.out);
     return record(cudaGetLastError());

@@ -158,7 +158,8 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-// 32 consecutive fp32 columns of this warp's 32 TMEM lanes (thread t <- lane base + t).
+// 16 (tmem_ld16) or 32 (tmem_ld32) consecutive fp32 columns of this warp's 32 TMEM lanes
+// (thread t <- lane base + t).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -182,6 +183,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Pins the registers of a tcgen05.ld to this point: placed after tmem_wait_ld,
+// it keeps the compiler from moving their uses above the wait.
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&v)[N]) {
+#pragma unroll
+    for (int k = 0; k < N; ++k) asm volatile("" : "+r"(v[k]));
+}
 
 // UMMA shared-memory descriptor for a K-major operand tile stored with the
 // 128-byte swizzle (rows of 128 bytes, 8-row / 1024-byte swizzle atoms, atoms
