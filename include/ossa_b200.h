@@ -84,7 +84,10 @@ OSSA_API int ossa_topk_attention_fwd(const void* q, const void* k, const void* v
 /*
  * Bytes of workspace ossa_router_topk / ossa_router_score need for this shape.
  * Replaces nothing in the reference (its router materialises (B,H,N,N) logits,
- * ossa/router.py:182-189); the workspace holds the projected q'/k' rows.
+ * ossa/router.py:182-189); the workspace holds the projected q'/k' rows and the
+ * selector's scratch (fp16 copies, per-row bounds, position-bias windows; for
+ * 64 < K <= 128 also the candidate lists, 2.5 KB per query row).  It depends on
+ * K: size it with the K of the call.
  */
 OSSA_API size_t ossa_router_workspace_size(int B, int H, int Hkv, int N, int r, int K);
 

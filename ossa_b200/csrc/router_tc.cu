@@ -350,6 +350,18 @@ __device__ __forceinline__ int count_ge(const float (&x)[NX], float v) {
     return ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
 }
 
+// Next probe of a search for the value v where count(x >= v) reaches `target`:
+// linear interpolation of the count between (lo, c_lo) and (hi, c_hi), kept in
+// the middle 7/8 of the bracket so that every step shrinks it.  On the class
+// maxima (spread smoothly between their min and max) it takes fewer steps than
+// bisection; correctness never depends on where it probes.
+__device__ __forceinline__ float interp_probe(float lo, float hi, int c_lo, int c_hi, float target) {
+    const float den = (float)(c_lo - c_hi);
+    float t = den > 0.f ? __fdividef((float)c_lo - target, den) : 0.5f;
+    t = fminf(fmaxf(t, 0.0625f), 0.9375f);
+    return lo + t * (hi - lo);
+}
+
 // A lower bound on the K-th largest class maximum of a row whose maxima are
 // spread over G consecutive lanes (kHalfCols per lane, -inf for empty classes):
 // bisection on the value until K..K+kBoundSlack maxima are >= lo (or the bracket
@@ -387,9 +399,10 @@ __device__ __forceinline__ float group_class_bound(const float (&y)[kHalfCols], 
         nfin += __shfl_xor_sync(kFull, nfin, o);
     }
     bool done = nfin <= K + kBoundSlack;
+    int c_lo = nfin, c_hi = 1;  // count(y >= lo), an estimate of count(y >= hi)
     for (int it = 0; it < 32; ++it) {
         if (__all_sync(kFull, done)) break;
-        const float mid = lo + 0.5f * (hi - lo);
+        const float mid = interp_probe(lo, hi, c_lo, c_hi, (float)K + 0.5f * kBoundSlack);
         int c = count_ge<kHalfCols>(y, mid);
 #pragma unroll
         for (int o = 1; o < G; o <<= 1) c += __shfl_xor_sync(kFull, c, o);
@@ -398,9 +411,11 @@ __device__ __forceinline__ float group_class_bound(const float (&y)[kHalfCols], 
                 done = true;
             } else if (c >= K) {
                 lo = mid;
+                c_lo = c;
                 done = c <= K + kBoundSlack;  // any lo with >= K maxima above is a bound
             } else {
                 hi = mid;
+                c_hi = c;
             }
         }
     }
@@ -942,6 +957,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 // 4 delta: the boundary band then holds the few near-tied entries and the
                 // canonical rescoring below decides them.
                 bool done = !work || all_in || cnt_lo == K || hi - lo <= 4.f * fdelta;
+                // (plain bisection: the candidates bunch up near lb, where interpolation
+                // on the count probes badly)
                 for (int it = 0; it < 40; ++it) {
                     if (__all_sync(kFull, done)) break;
                     const float mid = lo + 0.5f * (hi - lo);
