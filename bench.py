@@ -271,7 +271,9 @@ def run_ours(args) -> None:
     select_roof["frac"] = select_roof["achieved"] / select_roof["peak"]
     dominant = gather_roof if gat_tot >= sel_tot else select_roof
     roof = dict(dominant)
-    roof["kernel"] = "gather_attn_fwd" if dominant is gather_roof else "router projection + score_topk"
+    roof["kernel"] = ("gather_attn_fwd" if dominant is gather_roof else
+                      "router selection step (router_topk: projections, prep, router_tc_kernel, fallback), "
+                      "timed with events around the call")
     roof["peak_source"] = f"{peaks['source']} (MEASURED_PEAKS.json burst)" if peaks["source"] == "measured" \
         else "fallback"
     roof["algorithmic"] = (f"{gbytes} B per launch (33,536 B per query-head at K=64)"

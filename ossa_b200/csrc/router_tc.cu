@@ -225,55 +225,59 @@ __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict
     *reinterpret_cast<uint2*>(k16 + off) = pk;
 }
 
-// One thread per query row: scaled fp16 row, epilogue multiplier and error bound.
-__global__ void qprep_kernel(const float* __restrict__ qp, __half* __restrict__ q16, float2* __restrict__ rowinfo,
-                             long long rows, int H, int Hkv, int Nq, float scale,
-                             const uint32_t* __restrict__ stats, const uint32_t* __restrict__ gstats) {
-    const long long row = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (row >= rows) return;
-    const long long bh = row / Nq;
+// Eight threads per query row (8 of its 64 values each, coalesced loads and
+// stores): scaled fp16 row, epilogue multiplier and error bound.
+__global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp, __half* __restrict__ q16,
+                                                    float2* __restrict__ rowinfo, long long rows, int H, int Hkv,
+                                                    int Nq, float scale, const uint32_t* __restrict__ stats,
+                                                    const uint32_t* __restrict__ gstats) {
+    const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+    const int part = threadIdx.x & 7;
+    const bool live = row < rows;  // whole 8-lane groups share it
+    const long long rr = live ? row : 0;
+    const long long bh = rr / Nq;
     const int b = (int)(bh / H);
     const int h = (int)(bh - (long long)b * H);
     const int bg = b * Hkv + h / (H / Hkv);
-    const float4* r = reinterpret_cast<const float4*>(qp + row * kR);
-    float4 x[kR / 4];
-    float mabs = 0.f, ss = 0.f;
-    bool bad = false;
+    const float4* r = reinterpret_cast<const float4*>(qp + rr * kR) + 2 * part;
+    const float4 x0 = __ldg(r), x1 = __ldg(r + 1);
+    float mabs = fmaxf(fmaxf(fmaxf(fabsf(x0.x), fabsf(x0.y)), fmaxf(fabsf(x0.z), fabsf(x0.w))),
+                       fmaxf(fmaxf(fabsf(x1.x), fabsf(x1.y)), fmaxf(fabsf(x1.z), fabsf(x1.w))));
+    float ss = fmaf(x0.x, x0.x, fmaf(x0.y, x0.y, fmaf(x0.z, x0.z, x0.w * x0.w)));
+    ss = fmaf(x1.x, x1.x, fmaf(x1.y, x1.y, fmaf(x1.z, x1.z, fmaf(x1.w, x1.w, ss))));
+    unsigned bad = (isfinite(x0.x) && isfinite(x0.y) && isfinite(x0.z) && isfinite(x0.w) && isfinite(x1.x) &&
+                    isfinite(x1.y) && isfinite(x1.z) && isfinite(x1.w)) ? 0u : 1u;
 #pragma unroll
-    for (int c = 0; c < kR / 4; ++c) {
-        x[c] = __ldg(r + c);
-        mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(x[c].x), fabsf(x[c].y)), fmaxf(fabsf(x[c].z), fabsf(x[c].w))));
-        ss = fmaf(x[c].x, x[c].x, fmaf(x[c].y, x[c].y, fmaf(x[c].z, x[c].z, fmaf(x[c].w, x[c].w, ss))));
-        bad |= !(isfinite(x[c].x) && isfinite(x[c].y) && isfinite(x[c].z) && isfinite(x[c].w));
+    for (int o = 1; o < 8; o <<= 1) {
+        mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, o));
+        ss += __shfl_xor_sync(kFull, ss, o);
+        bad |= __shfl_xor_sync(kFull, bad, o);
     }
+    if (!live) return;
     const int eq = scale_exponent(mabs);
+    __half2 h0 = __floats2half2_rn(ldexpf(x0.x, eq), ldexpf(x0.y, eq));
+    __half2 h1 = __floats2half2_rn(ldexpf(x0.z, eq), ldexpf(x0.w, eq));
+    __half2 h2 = __floats2half2_rn(ldexpf(x1.x, eq), ldexpf(x1.y, eq));
+    __half2 h3 = __floats2half2_rn(ldexpf(x1.z, eq), ldexpf(x1.w, eq));
+    uint4 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&h0);
+    pk.y = *reinterpret_cast<uint32_t*>(&h1);
+    pk.z = *reinterpret_cast<uint32_t*>(&h2);
+    pk.w = *reinterpret_cast<uint32_t*>(&h3);
+    reinterpret_cast<uint4*>(q16 + rr * kR)[part] = pk;
+    if (part != 0) return;
     const int ek = scale_exponent(__uint_as_float(stats[3 * bg + 0]));
     const float kmax = __uint_as_float(stats[3 * bg + 1]);
     const float bmax = __uint_as_float(gstats[0]);
-    bad |= stats[3 * bg + 2] != 0u || gstats[1] != 0u;
-    uint4* o = reinterpret_cast<uint4*>(q16 + row * kR);
-#pragma unroll
-    for (int c = 0; c < kR / 8; ++c) {
-        const float4 a = x[2 * c], bq = x[2 * c + 1];
-        __half2 h0 = __floats2half2_rn(ldexpf(a.x, eq), ldexpf(a.y, eq));
-        __half2 h1 = __floats2half2_rn(ldexpf(a.z, eq), ldexpf(a.w, eq));
-        __half2 h2 = __floats2half2_rn(ldexpf(bq.x, eq), ldexpf(bq.y, eq));
-        __half2 h3 = __floats2half2_rn(ldexpf(bq.z, eq), ldexpf(bq.w, eq));
-        uint4 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&h0);
-        pk.y = *reinterpret_cast<uint32_t*>(&h1);
-        pk.z = *reinterpret_cast<uint32_t*>(&h2);
-        pk.w = *reinterpret_cast<uint32_t*>(&h3);
-        o[c] = pk;
-    }
+    const bool nonfinite = bad != 0u || stats[3 * bg + 2] != 0u || gstats[1] != 0u;
     const float m = ldexpf(scale, -(eq + ek));
     const float qn = sqrtf(ss) * 1.0001f;
     const float cross = scale * qn * kmax;
     const float delta = scale * 0.00390625f * qn * kmax + kTwoPowM22 * (bmax + cross) + 1e-30f;
-    if (bad || !isfinite(delta) || !(m >= 1.1754944e-38f) || !isfinite(m)) {
-        rowinfo[row] = make_float2(__int_as_float(0x7fc00000), 0.f);  // NaN multiplier: exact fallback
+    if (nonfinite || !isfinite(delta) || !(m >= 1.1754944e-38f) || !isfinite(m)) {
+        rowinfo[rr] = make_float2(__int_as_float(0x7fc00000), 0.f);  // NaN multiplier: exact fallback
     } else {
-        rowinfo[row] = make_float2(m, delta);
+        rowinfo[rr] = make_float2(m, delta);
     }
 }
 
@@ -1588,7 +1592,7 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
         dim3 g2((a.N * (kR / 4) + 255) / 256, BG);
         kconvert_kernel<<<g2, 256, 0, stream>>>(a.kp32, k16, a.N, stats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-        qprep_kernel<<<(unsigned)((rq + 127) / 128), 128, 0, stream>>>(a.qp32, q16, rowinfo, (long long)rq, a.H,
+        qprep_kernel<<<(unsigned)((rq * 8 + 255) / 256), 256, 0, stream>>>(a.qp32, q16, rowinfo, (long long)rq, a.H,
                                                                       a.Hkv, Nq, a.scale, stats, gstats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
         // offset of bias-line index 0: the window of tile (qb, key tile) starts at

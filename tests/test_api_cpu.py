@@ -121,3 +121,40 @@ def test_host_pipeline_argument_checks():
         routed_attention_from_host(q, k, k, w, w, pb, 8, 4, torch.zeros_like(q), chunk=0)
     with pytest.raises(ValueError, match="CUDA"):
         routed_attention_from_host(q, k, k, w, w, pb, 8, 4, torch.zeros_like(q))
+
+
+def test_full_model_runner_config_and_routers():
+    """The full-model prefill runner builds the Qwen2.5-1.5B architecture and one
+    seeded Xavier-uniform router per layer (checked on the CPU at 2 layers)."""
+    import math
+
+    from ossa_b200.bench import full_model
+
+    cfg = full_model.qwen25_15b_config(4096)
+    assert (cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers) == (1536, 8960, 28)
+    assert (cfg.num_attention_heads, cfg.num_key_value_heads, cfg.vocab_size) == (12, 2, 151936)
+    rope = getattr(cfg, "rope_parameters", None) or {"rope_theta": getattr(cfg, "rope_theta", None)}
+    assert rope["rope_theta"] == 1e6 and cfg.hidden_size // cfg.num_attention_heads == 128
+
+    class _Attn:
+        head_dim = 128
+
+    class _Layer:
+        self_attn = _Attn()
+
+    class _Model:
+        config = cfg
+
+        class model:  # noqa: N801 - mirrors the Hugging Face attribute path
+            layers = [_Layer(), _Layer()]
+
+    a = full_model.build_routers(_Model, 4096, "cpu", seed=5)
+    b = full_model.build_routers(_Model, 4096, "cpu", seed=5)
+    assert sorted(a) == [0, 1]
+    bound = math.sqrt(6.0 / (64 + 128))
+    for li in a:
+        wq = a[li].q_proj[0].weight.detach()
+        assert wq.shape == (64, 128) and float(wq.abs().max()) <= bound
+        assert a[li].pos_bias.weight.shape == (2 * 4096, 1)
+        assert torch.equal(wq, b[li].q_proj[0].weight.detach())
+    assert not torch.equal(a[0].q_proj[0].weight, a[1].q_proj[0].weight)

@@ -77,3 +77,15 @@ def test_patched_bf16_model_runs_and_tracks_fp32():
     assert torch.isfinite(b).all()
     cos = torch.nn.functional.cosine_similarity(a.flatten(0, 1), b.flatten(0, 1), dim=-1)
     assert cos.mean() > 0.99
+
+
+def test_full_model_runner_small(capsys):
+    """The full-model prefill runner end to end on a 2-layer cut of the
+    architecture: one JSON line with a positive rate and finite logits."""
+    import json
+
+    from ossa_b200.bench import full_model
+
+    full_model.main(["--batch", "2", "--seq", "512", "--layers", "2", "--steps", "1", "--warmup", "1"])
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["value"] > 0 and line["logits_finite"] and line["config"]["layers"] == 2
