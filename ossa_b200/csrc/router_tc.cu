@@ -11,10 +11,11 @@
 //     scaled by powers of two (q' per row, k' per (b, kv head)) so every value
 //     sits in [2^12, 2^13) at most, plus per row the epilogue multiplier
 //     m_i = scale * 2^-(e_q + e_k) and an error bound delta_i with
-//     |approx score - canonical score| <= delta_i:
-//        delta_i = scale * 2^-8 * |q'_i| * max_j |k'_j| + 2^-22 * (max|bias| + scale * |q'_i| * max_j |k'_j|)
-//     (fp16 input rounding contributes <= 2^-10 |q'||k'|, fp32 accumulation in the
-//     tensor core and the canonical fmaf chain far less; 2^-8 leaves 4x margin),
+//     |approx score - canonical score| <= delta_i, built from the measured fp16
+//     conversion errors dq_i = fp16(q'_i) - q'_i and dk_j (Cauchy-Schwarz):
+//        delta_i = scale * (|q'_i| max|dk| + |dq_i| max|k'| + |dq_i| max|dk|)
+//                  + scale * 2^-13 * |q'_i| * max_j |k'_j|   (fp32 accumulation: tensor core, fmaf chain)
+//                  + 2^-22 * (max|bias| + scale * |q'_i| * max_j |k'_j|)   (final roundings)
 //     and the call's pos_bias window images (window_table_kernel).
 //  2. warp 0 (one thread) streams 128-key tiles of k'16 with TMA (128-byte
 //     swizzle) through a 4- or 6-stage ring; warp 1 (one thread) issues
@@ -42,10 +43,11 @@
 //     selected, entries below x_K - 2*delta_i certainly not, and the few in
 //     between are rescored with the canonical fp32 formula; the remaining slots
 //     go to them by (score desc, j asc).  Output in ascending key order.
-//  5. Rows whose sub-list would overflow (massive near-ties), whose boundary
-//     band is too wide, or whose inputs are not finite are appended to a list
-//     and recomputed afterwards by an exact warp-per-row selector
-//     (exact_rows_kernel).
+//     However wide the band (large |q'||k'| make delta wide), it is decided by
+//     canonical rescoring of the row's candidates, never by a full-row scan.
+//  5. Rows whose sub-list would overflow (massive near-ties) or whose inputs are
+//     not finite are appended to a list and recomputed afterwards by an exact
+//     warp-per-row selector (exact_rows_kernel).
 //
 // Every wait on an mbarrier is bounded (~1 s); on expiry the kernel records a
 // nonzero status word, lets the other roles finish their bounded waits, waits
@@ -89,7 +91,6 @@ constexpr int kTileBytes = kTileM * kR * 2;
 constexpr uint32_t kTmemCols = kAccBufs * kTileN;
 constexpr int kBoundSlack = 3;      // the pass-1 bound stops once K..K+3 class maxima are above it
 constexpr int kMaxBand = 32;        // wide: boundary candidates rescored per row (one per lane) before falling back
-constexpr int kMaxBandNarrow = 8;   // narrow: boundary candidates rescored per sub-list before falling back
 
 // Two variants.  Narrow (K <= 64): the pass-1 bound is the K-th largest of 128
 // column-class maxima (key mod 128); the candidate sub-lists (about 1.3 K per
@@ -125,7 +126,6 @@ struct TcCfg {
     static_assert(kSmemBytes <= 232448, "shared memory budget");
     static_assert(kOffB % 1024 == 0 && kTileBytes % 1024 == 0, "swizzled tiles need 1 KB alignment");
     static_assert(kOffWin % 16 == 0, "bulk copies need 16-byte aligned destinations");
-    static_assert(kWide || 2 * kTileM * kMaxBandNarrow * 8 <= kTileBytes, "rescoring slots fit in the q' tile");
     static_assert(kWide || kTileM * 256 <= kStages * kTileBytes, "output staging fits in the k' ring");
 };
 constexpr int kWideMaxK = TcCfg<true>::kMaxK;
@@ -135,7 +135,10 @@ constexpr float kTwoPowM22 = 2.384185791015625e-07f;  // 2^-22
 
 // ---------------------------------------------------------------- prep kernels
 
-// stats[3*bg + 0] = max |k'| bits, [3*bg + 1] = max_j |k'_j|_2 bits, [3*bg + 2] = non-finite flag.
+// Per (b, kv head) statistics, kStatWords words each: [0] max |k'| bits,
+// [1] max_j |k'_j|_2 bits, [2] non-finite flag, [3] max_j |fp16(k'_j) - k'_j|_2 bits
+// (the largest conversion error of a key row, written by kconvert_kernel).
+constexpr int kStatWords = 4;
 __global__ void kstats_kernel(const float* __restrict__ kp, int N, uint32_t* __restrict__ stats) {
     const int bg = blockIdx.y;
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
@@ -156,9 +159,9 @@ __global__ void kstats_kernel(const float* __restrict__ kp, int N, uint32_t* __r
     uint32_t m2 = __reduce_max_sync(kFull, __float_as_uint(bad ? 0.f : nrm));
     unsigned b = __reduce_or_sync(kFull, bad ? 1u : 0u);
     if ((threadIdx.x & 31) == 0) {
-        atomicMax(stats + 3 * bg + 0, m1);
-        atomicMax(stats + 3 * bg + 1, m2);
-        if (b) atomicOr(stats + 3 * bg + 2, 1u);
+        atomicMax(stats + kStatWords * bg + 0, m1);
+        atomicMax(stats + kStatWords * bg + 1, m2);
+        if (b) atomicOr(stats + kStatWords * bg + 2, 1u);
     }
 }
 
@@ -209,20 +212,35 @@ __device__ __forceinline__ int scale_exponent(float max_abs) {
     return max_abs > 0.f ? 13 - ex : 0;
 }
 
+// fp16 copy of k' scaled by the (b, kv head) power of two, one float4 per thread
+// (16 threads per key row), and the norm of each row's conversion error, whose
+// maximum goes to stats[kStatWords*bg + 3].
 __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict__ k16, int N,
-                                const uint32_t* __restrict__ stats) {
+                                uint32_t* __restrict__ stats) {
     const int bg = blockIdx.y;
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;  // one float4 per thread
-    if (t >= N * (kR / 4)) return;
-    const int e = scale_exponent(__uint_as_float(stats[3 * bg + 0]));
-    const size_t off = (size_t)bg * N * kR + (size_t)t * 4;
-    const float4 x = __ldg(reinterpret_cast<const float4*>(kp + off));
-    __half2 lo = __floats2half2_rn(ldexpf(x.x, e), ldexpf(x.y, e));
-    __half2 hi = __floats2half2_rn(ldexpf(x.z, e), ldexpf(x.w, e));
-    uint2 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&lo);
-    pk.y = *reinterpret_cast<uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(k16 + off) = pk;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = t < N * (kR / 4);  // whole 16-thread rows share it (N * 16 threads)
+    const int e = scale_exponent(__uint_as_float(stats[kStatWords * bg + 0]));
+    float ss = 0.f;
+    if (live) {
+        const size_t off = (size_t)bg * N * kR + (size_t)t * 4;
+        const float4 x = __ldg(reinterpret_cast<const float4*>(kp + off));
+        __half2 lo = __floats2half2_rn(ldexpf(x.x, e), ldexpf(x.y, e));
+        __half2 hi = __floats2half2_rn(ldexpf(x.z, e), ldexpf(x.w, e));
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(k16 + off) = pk;
+        // conversion errors in unscaled units (power-of-two scaling and the
+        // difference of two values within a factor of 2 are exact)
+        const float2 fl = __half22float2(lo), fh = __half22float2(hi);
+        const float d0 = ldexpf(fl.x, -e) - x.x, d1 = ldexpf(fl.y, -e) - x.y;
+        const float d2 = ldexpf(fh.x, -e) - x.z, d3 = ldexpf(fh.y, -e) - x.w;
+        ss = fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, d3 * d3)));
+    }
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(kFull, ss, o);
+    if (live && (threadIdx.x & 15) == 0) atomicMax(stats + kStatWords * bg + 3, __float_as_uint(sqrtf(ss) * 1.0001f));
 }
 
 // Eight threads per query row (8 of its 64 values each, coalesced loads and
@@ -265,15 +283,35 @@ __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp
     pk.z = *reinterpret_cast<uint32_t*>(&h2);
     pk.w = *reinterpret_cast<uint32_t*>(&h3);
     reinterpret_cast<uint4*>(q16 + rr * kR)[part] = pk;
+    // conversion errors of this part of the row, in unscaled units (exact)
+    float dd = 0.f;
+    {
+        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+        const float2 f2 = __half22float2(h2), f3 = __half22float2(h3);
+        const float e0 = ldexpf(f0.x, -eq) - x0.x, e1 = ldexpf(f0.y, -eq) - x0.y;
+        const float e2 = ldexpf(f1.x, -eq) - x0.z, e3 = ldexpf(f1.y, -eq) - x0.w;
+        const float e4 = ldexpf(f2.x, -eq) - x1.x, e5 = ldexpf(f2.y, -eq) - x1.y;
+        const float e6 = ldexpf(f3.x, -eq) - x1.z, e7 = ldexpf(f3.y, -eq) - x1.w;
+        dd = fmaf(e0, e0, fmaf(e1, e1, fmaf(e2, e2, fmaf(e3, e3, fmaf(e4, e4, fmaf(e5, e5, fmaf(e6, e6, e7 * e7)))))));
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) dd += __shfl_xor_sync(0xffu << (threadIdx.x & 24), dd, o);
     if (part != 0) return;
-    const int ek = scale_exponent(__uint_as_float(stats[3 * bg + 0]));
-    const float kmax = __uint_as_float(stats[3 * bg + 1]);
+    const int ek = scale_exponent(__uint_as_float(stats[kStatWords * bg + 0]));
+    const float kmax = __uint_as_float(stats[kStatWords * bg + 1]);
+    const float dkmax = __uint_as_float(stats[kStatWords * bg + 3]);
     const float bmax = __uint_as_float(gstats[0]);
-    const bool nonfinite = bad != 0u || stats[3 * bg + 2] != 0u || gstats[1] != 0u;
+    const bool nonfinite = bad != 0u || stats[kStatWords * bg + 2] != 0u || gstats[1] != 0u;
     const float m = ldexpf(scale, -(eq + ek));
     const float qn = sqrtf(ss) * 1.0001f;
+    const float dq = sqrtf(dd) * 1.0001f;
     const float cross = scale * qn * kmax;
-    const float delta = scale * 0.00390625f * qn * kmax + kTwoPowM22 * (bmax + cross) + 1e-30f;
+    // |approx - canonical| <= scale * |q'.dk + dq.k' + dq.dk| (fp16 conversion,
+    // Cauchy-Schwarz with the measured errors) + scale * 2^-13 |q'| max|k'| (fp32
+    // accumulation in the tensor core and in the canonical chain: 64 terms at a few
+    // ulp each) + 2^-22 (max|bias| + cross) (the final roundings)
+    const float delta = scale * (qn * dkmax + dq * kmax + dq * dkmax) * 1.0001f + scale * 1.220703125e-4f * qn * kmax +
+                        kTwoPowM22 * (bmax + cross) + 1e-30f;
     if (nonfinite || !isfinite(delta) || !(m >= 1.1754944e-38f) || !isfinite(m)) {
         rowinfo[rr] = make_float2(__int_as_float(0x7fc00000), 0.f);  // NaN multiplier: exact fallback
     } else {
@@ -300,30 +338,28 @@ struct TcParams {
     float scale;
 };
 
-// Canonical fp32 score of (query row qrow, key row krow) at offset i - j.
+// Canonical fp32 score of (query row qrow, key row krow) at offset i - j: the
+// fmaf chain over d = 0..63 in order.  The key row's 16 loads are issued
+// together (one memory round trip; the query row is reused and cached).
 __device__ __forceinline__ float canonical_score(const float* __restrict__ qrow, const float* __restrict__ krow,
                                                  const float* __restrict__ bias, int L, int i, int j,
                                                  float scale) {
-    float acc = 0.f;
+    float4 bk[kR / 4];
 #pragma unroll
-    for (int c0 = 0; c0 < kR; c0 += 16) {
-        float4 a[4], bk[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            a[u] = __ldg(reinterpret_cast<const float4*>(qrow + c0) + u);
-            bk[u] = __ldg(reinterpret_cast<const float4*>(krow + c0) + u);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            acc = fmaf(a[u].x, bk[u].x, acc);
-            acc = fmaf(a[u].y, bk[u].y, acc);
-            acc = fmaf(a[u].z, bk[u].z, acc);
-            acc = fmaf(a[u].w, bk[u].w, acc);
-        }
-    }
+    for (int u = 0; u < kR / 4; ++u) bk[u] = __ldg(reinterpret_cast<const float4*>(krow) + u);
     int bi = i - j + L;
     bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
-    return __fadd_rn(__fmul_rn(acc, scale), __ldg(bias + bi));
+    const float bv = __ldg(bias + bi);
+    float acc = 0.f;
+#pragma unroll
+    for (int u = 0; u < kR / 4; ++u) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(qrow) + u);
+        acc = fmaf(a.x, bk[u].x, acc);
+        acc = fmaf(a.y, bk[u].y, acc);
+        acc = fmaf(a.z, bk[u].z, acc);
+        acc = fmaf(a.w, bk[u].w, acc);
+    }
+    return __fadd_rn(__fmul_rn(acc, scale), bv);
 }
 
 // count_ge over the first nch 8-entry chunks of x only (nch uniform across the warp).
@@ -1040,69 +1076,77 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 n_in += __shfl_xor_sync(kFull, n_in, 1);
                 const int oth_nb = __shfl_xor_sync(kFull, own_nb, 1);
                 const int need = K - n_in;
-                bool rescore = work && !all_in && own_nb + oth_nb != need;
-                if (rescore && (own_nb > (2 * kMaxBandNarrow) / 2 || oth_nb > (2 * kMaxBandNarrow) / 2)) {
-                    to_fallback = true;
-                    work = false;
-                    rescore = false;
-                }
+                const bool rescore = work && !all_in && own_nb + oth_nb != need;
 
-                // 2. canonical rescoring of the boundary band
-                uint2* scratch = reinterpret_cast<uint2*>(sA) + (size_t)frow * (2 * kMaxBandNarrow);  // MMAs are done with sA
-                uint2* myslots = scratch + fh * ((2 * kMaxBandNarrow) / 2);
+                // 2. canonical rescoring of the boundary band, in place: a band entry's
+                // score word becomes the order key of its canonical score; bm marks the
+                // band entries of this lane's sub-list, sm the ones selected
+                constexpr int kMaskWords = (Cfg::kCap + 31) / 32;
+                uint32_t bm[kMaskWords], sm[kMaskWords];
+    #pragma unroll
+                for (int w = 0; w < kMaskWords; ++w) {
+                    bm[w] = 0u;
+                    sm[w] = 0u;
+                }
                 if (rescore) {
-                    uint32_t wa = smem_u32(myslots);
     #pragma unroll
                     for (int ch = 0; ch < Cfg::kCap / 8; ++ch) {
                         if (ch < nch) {
     #pragma unroll
                             for (int u = 0; u < 8; ++u) {
                                 const int q = 8 * ch + u;
-                                const bool inb = x[q] >= W && x[q] <= U;
-                                sts_u32_if(wa, (uint32_t)q, inb);
-                                wa += inb ? 8u : 0u;
+                                bm[q >> 5] |= (x[q] >= W && x[q] <= U) ? 1u << (q & 31) : 0u;
                             }
                         }
                     }
-                }
-                const int nbmax = __reduce_max_sync(kFull, rescore ? (unsigned)own_nb : 0u);
-                if (nbmax > 0) {
-                    __syncwarp();
                     const float* qrow = p.qp32 + orow_id * kR;
                     const float* kbase = p.kp32 + (size_t)(b * Hkv + g) * N * kR;
-                    for (int u = 0; u < nbmax; ++u) {
-                        if (rescore && u < own_nb) {
-                            const int jj = (int)own[myslots[u].x].y;
-                            const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, p.L, p.q0 + fi, jj,
-                                                                         p.scale);
-                            myslots[u] = make_uint2(order_key(ex), (uint32_t)jj);
+    #pragma unroll
+                    for (int w = 0; w < kMaskWords; ++w) {
+                        for (uint32_t m = bm[w]; m != 0u; m &= m - 1u) {
+                            const int q = 32 * w + __ffs(m) - 1;
+                            const int jj = (int)lds_u32(own_s + 8u * q + 4u);
+                            const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, p.L, p.q0 + fi,
+                                                             jj, p.scale);
+                            sts_f32(own_s + 8u * q, __uint_as_float(order_key(ex)));
                         }
                     }
-                    __syncwarp();
                 }
-                uint32_t selmask = 0u;
+                __syncwarp();
+                // rank each own band entry among the band entries of both sub-lists by
+                // (canonical score desc, key asc); the first `need` are kept
+                uint32_t obm[kMaskWords];
+    #pragma unroll
+                for (int w = 0; w < kMaskWords; ++w) obm[w] = __shfl_xor_sync(kFull, bm[w], 1);
                 if (rescore) {
-                    const uint2* oslots = scratch + (1 - fh) * ((2 * kMaxBandNarrow) / 2);
-                    for (int a2 = 0; a2 < own_nb; ++a2) {
-                        const uint2 ea = myslots[a2];
-                        int rank = 0;
-                        for (int c2 = 0; c2 < own_nb; ++c2) {
-                            const uint2 e = myslots[c2];
-                            rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
+                    const uint32_t oth_s = smem_u32(frowbuf + (1 - fh) * Cfg::kCap);
+    #pragma unroll
+                    for (int w = 0; w < kMaskWords; ++w) {
+                        for (uint32_t m = bm[w]; m != 0u; m &= m - 1u) {
+                            const int qa = 32 * w + __ffs(m) - 1;
+                            const uint2 ea = lds_u2(own_s + 8u * qa);
+                            int rank = 0;
+    #pragma unroll
+                            for (int w2 = 0; w2 < kMaskWords; ++w2) {
+                                for (uint32_t m2 = bm[w2]; m2 != 0u; m2 &= m2 - 1u) {
+                                    const uint2 e = lds_u2(own_s + 8u * (32 * w2 + __ffs(m2) - 1));
+                                    rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
+                                }
+                                for (uint32_t m2 = obm[w2]; m2 != 0u; m2 &= m2 - 1u) {
+                                    const uint2 e = lds_u2(oth_s + 8u * (32 * w2 + __ffs(m2) - 1));
+                                    rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
+                                }
+                            }
+                            if (rank < need) sm[w] |= 1u << (qa & 31);
                         }
-                        for (int c2 = 0; c2 < oth_nb; ++c2) {
-                            const uint2 e = oslots[c2];
-                            rank += (e.x > ea.x || (e.x == ea.x && e.y < ea.y)) ? 1 : 0;
-                        }
-                        if (rank < need) selmask |= 1u << a2;
                     }
                 }
+                __syncwarp();  // the partner is done reading this sub-list before it is compacted
 
                 // 3. compact kept keys in place, then merge the two lists
                 int nsel = 0;
                 if (work) {
                     uint32_t wa = own_s + 4u;  // .y of the next kept slot
-                    int bidx = 0;
     #pragma unroll
                     for (int ch = 0; ch < Cfg::kCap / 8; ++ch) {
                         if (ch < nch) {
@@ -1114,10 +1158,12 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     #pragma unroll
                             for (int u = 0; u < 8; ++u) {
                                 const int q = 8 * ch + u;
+                                // band entries (rescored in place) by their selection bit,
+                                // the others by their approximate score: above U (certain),
+                                // or at least W when the whole band is kept
                                 const float sq = q < nown ? __uint_as_float(e8[u].x) : -INFINITY;
-                                const bool inb = sq >= W && sq <= U;
-                                const bool keep = sq > U || (inb && (!rescore || ((selmask >> bidx) & 1u)));
-                                bidx += inb ? 1 : 0;
+                                const bool inbm = (bm[q >> 5] >> (q & 31)) & 1u;
+                                const bool keep = inbm ? ((sm[q >> 5] >> (q & 31)) & 1u) != 0u : (sq > U || sq >= W);
                                 sts_u32_if(wa, e8[u].y, keep);
                                 wa += keep ? 8u : 0u;
                             }
@@ -1333,9 +1379,10 @@ struct FinalParams {
 // below W = x_K - m2 certainly not; when the band [W, U] holds more entries than
 // the free slots, its entries are rescored with the canonical fp32 formula and
 // the best by (score desc, key asc) fill the slots.  The kept keys of A and B
-// are then merged by rank into ascending order, -1 padded.  Rows whose lists
-// overflowed, whose inputs are not finite, or whose band holds more than
-// kMaxBand entries go to the exact fallback list.
+// are then merged by rank into ascending order, -1 padded.  When the band holds
+// more than kMaxBand entries, every candidate is rescored canonically and the
+// exact top K is taken among them.  Rows whose lists overflowed or whose inputs
+// are not finite go to the exact fallback list.
 template <int kCap, int kMaxOut>
 __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) {
     constexpr int kEPL = 2 * kCap / 32;  // candidate entries per lane
@@ -1408,7 +1455,40 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
 #pragma unroll
                     for (int e = 0; e < kEPL; ++e) keep[e] = val[e] && sv[e] >= W;
                 } else if (nb > (unsigned)kMaxBand) {
-                    fallback = true;
+                    // band wider than a lane each: rescore every candidate with the
+                    // canonical formula and take the exact top K among them (the list
+                    // holds every key that can be in it), ties to the lower key index
+                    const long long bh = row / p.Nq;
+                    const int ipos = p.q0 + (int)(row - bh * p.Nq);
+                    const int b = (int)(bh / p.H);
+                    const int g = (int)(bh - (long long)b * p.H) / (p.H / p.Hkv);
+                    const float* qrow = p.qp32 + (size_t)row * kR;
+                    const float* kbase = p.kp32 + (size_t)(b * p.Hkv + g) * p.N * kR;
+                    uint32_t ek[kEPL];
+#pragma unroll
+                    for (int e = 0; e < kEPL; ++e)
+                        ek[e] = val[e] ? order_key(canonical_score(qrow, kbase + (size_t)jv[e] * kR, p.bias, p.L, ipos,
+                                                                   (int)jv[e], p.scale))
+                                       : 0u;
+                    uint32_t Te;
+                    int ties;
+                    warp_kth_key<kEPL>(ek, val, K, Te, ties);
+                    // the K best are {ek > Te} plus the `ties` lowest keys with ek == Te
+                    bool taken[kEPL];
+#pragma unroll
+                    for (int e = 0; e < kEPL; ++e) taken[e] = false;
+                    for (int tsel = 0; tsel < ties; ++tsel) {
+                        uint32_t jmin = 0xffffffffu;
+#pragma unroll
+                        for (int e = 0; e < kEPL; ++e)
+                            if (val[e] && ek[e] == Te && !taken[e]) jmin = min(jmin, jv[e]);
+                        jmin = __reduce_min_sync(kFull, jmin);
+#pragma unroll
+                        for (int e = 0; e < kEPL; ++e)
+                            if (val[e] && ek[e] == Te && jv[e] == jmin) taken[e] = true;
+                    }
+#pragma unroll
+                    for (int e = 0; e < kEPL; ++e) keep[e] = val[e] && (ek[e] > Te || taken[e]);
                 } else {
                     // band entries to lanes 0..nb-1, in (e, lane) order
                     const long long bh = row / p.Nq;
@@ -1538,7 +1618,7 @@ size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K) {
     const size_t rq = (size_t)B * H * Nq, rk = (size_t)B * Hkv * N;
     const int nqb = (Nq + kTileM - 1) / kTileM, tiles_n = (N + kTileN - 1) / kTileN;
     size_t total = al(rq * kR * 2) + al(rk * kR * 2) + al(rq * sizeof(float2)) +
-                   al((3 * (size_t)B * Hkv + 2) * 4) + al(rq * 4) +
+                   al((kStatWords * (size_t)B * Hkv + 2) * 4) + al(rq * 4) +
                    (nqb > 0 && tiles_n > 0 ? al((size_t)window_count(nqb, tiles_n) * kWinBytes) : 0);
     if (K > kNarrowMaxK) {
         // wide: sub-lists for every row slot of every query block (the last block
@@ -1561,8 +1641,8 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     float2* rowinfo = reinterpret_cast<float2*>(w);
     w += al(rq * sizeof(float2));
     uint32_t* stats = reinterpret_cast<uint32_t*>(w);
-    uint32_t* gstats = stats + 3 * (size_t)a.B * a.Hkv;
-    w += al((3 * (size_t)a.B * a.Hkv + 2) * 4);
+    uint32_t* gstats = stats + kStatWords * (size_t)a.B * a.Hkv;
+    w += al((kStatWords * (size_t)a.B * a.Hkv + 2) * 4);
     int32_t* fb_list = reinterpret_cast<int32_t*>(w);
     w += al(rq * 4);
     const int nqb = (Nq + kTileM - 1) / kTileM, tiles_n = (a.N + kTileN - 1) / kTileN;
@@ -1579,7 +1659,7 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     }
     int* counters = a.counters;  // [0] fallback rows, [1] status
 
-    cudaError_t e = cudaMemsetAsync(stats, 0, (3 * (size_t)a.B * a.Hkv + 2) * 4, stream);
+    cudaError_t e = cudaMemsetAsync(stats, 0, (kStatWords * (size_t)a.B * a.Hkv + 2) * 4, stream);
     if (e != cudaSuccess) return e;
 
     const int BG = a.B * a.Hkv;

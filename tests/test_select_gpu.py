@@ -298,3 +298,23 @@ def test_long_context_k128_selectors():
     rows = np.array([0, 1, 127, 128, 4096, 20000, N - 1, N, 2 * N - 1], dtype=np.int64)
     ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows, causal=True)
     _assert_same(tc.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
+
+
+@pytest.mark.parametrize("K", [64, 128])
+def test_tensor_core_selector_wide_error_band(K):
+    """Model-like magnitudes (q, k entries of unit scale, Xavier router weights:
+    |q'|, |k'| around 7 to 10): the rigorous fp16 error bound then spans a dozen
+    or more candidates at the K-th boundary.  They are decided by canonical
+    rescoring of the candidates, not by the full-row exact fallback, and the
+    result equals the exact selector and the oracle."""
+    B, H, Hkv, N, D, r = 1, 12, 2, 2048, 128, 64
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=40 + K, scale=0.6)
+    q, k = q.bfloat16(), k.bfloat16()
+    wq, wk, pb = _weights(D, r, N, seed=41 + K)
+    tc, ex, fb, status = _run_both(q, k, wq, wk, pb, N, K, True)
+    assert status == 0
+    assert torch.equal(tc, ex), f"{(tc != ex).any(-1).sum().item()} rows differ"
+    assert fb < 0.01 * B * H * N, f"{fb} rows fell back to the full-row exact selector"
+    rows = np.concatenate([np.arange(0, B * H * N, 1021), np.array([N - 1, B * H * N - 1])]).astype(np.int64)
+    ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows, causal=True)
+    _assert_same(tc.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
