@@ -212,9 +212,17 @@ __device__ __forceinline__ int scale_exponent(float max_abs) {
     return max_abs > 0.f ? 13 - ex : 0;
 }
 
+// x * 2^e for the scalings above, with f = 2^e from pow2f: a multiply by the
+// exact power of two when 2^e and 2^-e are normal floats (then the product equals
+// ldexpf(x, e)), ldexpf otherwise.
+__device__ __forceinline__ float pow2f(int e) {
+    return (e > -126 && e < 127) ? __int_as_float((e + 127) << 23) : 0.f;
+}
+__device__ __forceinline__ float scale2(float x, int e, float f) { return f != 0.f ? x * f : ldexpf(x, e); }
+
 // fp16 copy of k' scaled by the (b, kv head) power of two, one float4 per thread
 // (16 threads per key row), and the norm of each row's conversion error, whose
-// maximum goes to stats[kStatWords*bg + 3].
+// maximum goes to stats[kStatWords*bg + 3].  Blocks of 256 threads.
 __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict__ k16, int N,
                                 uint32_t* __restrict__ stats) {
     const int bg = blockIdx.y;
@@ -225,8 +233,9 @@ __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict
     if (live) {
         const size_t off = (size_t)bg * N * kR + (size_t)t * 4;
         const float4 x = __ldg(reinterpret_cast<const float4*>(kp + off));
-        __half2 lo = __floats2half2_rn(ldexpf(x.x, e), ldexpf(x.y, e));
-        __half2 hi = __floats2half2_rn(ldexpf(x.z, e), ldexpf(x.w, e));
+        const float up = pow2f(e), dn = pow2f(-e);
+        __half2 lo = __floats2half2_rn(scale2(x.x, e, up), scale2(x.y, e, up));
+        __half2 hi = __floats2half2_rn(scale2(x.z, e, up), scale2(x.w, e, up));
         uint2 pk;
         pk.x = *reinterpret_cast<uint32_t*>(&lo);
         pk.y = *reinterpret_cast<uint32_t*>(&hi);
@@ -234,13 +243,24 @@ __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict
         // conversion errors in unscaled units (power-of-two scaling and the
         // difference of two values within a factor of 2 are exact)
         const float2 fl = __half22float2(lo), fh = __half22float2(hi);
-        const float d0 = ldexpf(fl.x, -e) - x.x, d1 = ldexpf(fl.y, -e) - x.y;
-        const float d2 = ldexpf(fh.x, -e) - x.z, d3 = ldexpf(fh.y, -e) - x.w;
+        const float d0 = scale2(fl.x, -e, dn) - x.x, d1 = scale2(fl.y, -e, dn) - x.y;
+        const float d2 = scale2(fh.x, -e, dn) - x.z, d3 = scale2(fh.y, -e, dn) - x.w;
         ss = fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, d3 * d3)));
     }
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(kFull, ss, o);
-    if (live && (threadIdx.x & 15) == 0) atomicMax(stats + kStatWords * bg + 3, __float_as_uint(sqrtf(ss) * 1.0001f));
+    // maximum over the block's rows, then one atomic per block (same-address
+    // atomics from every warp serialise)
+    __shared__ uint32_t wmax[8];
+    const uint32_t nrm = live ? __float_as_uint(sqrtf(ss) * 1.0001f) : 0u;
+    const uint32_t m = __reduce_max_sync(kFull, nrm);
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t bmax = 0u;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) bmax = max(bmax, wmax[w]);
+        if (bmax != 0u) atomicMax(stats + kStatWords * bg + 3, bmax);
+    }
 }
 
 // Eight threads per query row (8 of its 64 values each, coalesced loads and
@@ -273,10 +293,11 @@ __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp
     }
     if (!live) return;
     const int eq = scale_exponent(mabs);
-    __half2 h0 = __floats2half2_rn(ldexpf(x0.x, eq), ldexpf(x0.y, eq));
-    __half2 h1 = __floats2half2_rn(ldexpf(x0.z, eq), ldexpf(x0.w, eq));
-    __half2 h2 = __floats2half2_rn(ldexpf(x1.x, eq), ldexpf(x1.y, eq));
-    __half2 h3 = __floats2half2_rn(ldexpf(x1.z, eq), ldexpf(x1.w, eq));
+    const float up = pow2f(eq), dn = pow2f(-eq);
+    __half2 h0 = __floats2half2_rn(scale2(x0.x, eq, up), scale2(x0.y, eq, up));
+    __half2 h1 = __floats2half2_rn(scale2(x0.z, eq, up), scale2(x0.w, eq, up));
+    __half2 h2 = __floats2half2_rn(scale2(x1.x, eq, up), scale2(x1.y, eq, up));
+    __half2 h3 = __floats2half2_rn(scale2(x1.z, eq, up), scale2(x1.w, eq, up));
     uint4 pk;
     pk.x = *reinterpret_cast<uint32_t*>(&h0);
     pk.y = *reinterpret_cast<uint32_t*>(&h1);
@@ -288,10 +309,10 @@ __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp
     {
         const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
         const float2 f2 = __half22float2(h2), f3 = __half22float2(h3);
-        const float e0 = ldexpf(f0.x, -eq) - x0.x, e1 = ldexpf(f0.y, -eq) - x0.y;
-        const float e2 = ldexpf(f1.x, -eq) - x0.z, e3 = ldexpf(f1.y, -eq) - x0.w;
-        const float e4 = ldexpf(f2.x, -eq) - x1.x, e5 = ldexpf(f2.y, -eq) - x1.y;
-        const float e6 = ldexpf(f3.x, -eq) - x1.z, e7 = ldexpf(f3.y, -eq) - x1.w;
+        const float e0 = scale2(f0.x, -eq, dn) - x0.x, e1 = scale2(f0.y, -eq, dn) - x0.y;
+        const float e2 = scale2(f1.x, -eq, dn) - x0.z, e3 = scale2(f1.y, -eq, dn) - x0.w;
+        const float e4 = scale2(f2.x, -eq, dn) - x1.x, e5 = scale2(f2.y, -eq, dn) - x1.y;
+        const float e6 = scale2(f3.x, -eq, dn) - x1.z, e7 = scale2(f3.y, -eq, dn) - x1.w;
         dd = fmaf(e0, e0, fmaf(e1, e1, fmaf(e2, e2, fmaf(e3, e3, fmaf(e4, e4, fmaf(e5, e5, fmaf(e6, e6, e7 * e7)))))));
     }
 #pragma unroll
