@@ -142,6 +142,23 @@ OSSA_API int ossa_oracle_topk(const void* q, const void* k, int dtype,
                      ossa_stream_t stream);
 
 /*
+ * The same oracle selection with a caller-provided workspace, which lets it run
+ * on the tensor-core selector (head_dim 128, K <= 128): fp16 tensor-core scores
+ * with a per-row error bound choose the candidates and the fp32 scores above
+ * decide among them, so the indices equal ossa_oracle_topk's bit for bit.
+ * Other shapes run the exact CUDA-core selector.  Replaces the same oracle
+ * selector (ossa/bench/sparse_forward.py:194-202).  The workspace size depends on
+ * the shape, K and dtype (ossa_oracle_workspace_size; 0 = invalid arguments);
+ * its first 8 bytes are the counters ossa_router_status reads.
+ */
+OSSA_API size_t ossa_oracle_workspace_size(int B, int H, int Hkv, int N, int D, int K, int dtype);
+OSSA_API int ossa_oracle_topk_ws(const void* q, const void* k, int dtype,
+                                 int B, int H, int Hkv, int N, int D, float scale,
+                                 int K, int causal, int32_t* idx_out,
+                                 void* workspace, size_t workspace_bytes,
+                                 ossa_stream_t stream);
+
+/*
  * ossa_router_topk without a caller-provided workspace.  No counterpart in the
  * reference: it exists for callers that cannot allocate device memory where
  * they launch this work (a host framework that owns every byte of device

@@ -130,6 +130,23 @@ def oracle_topk(q, k, K: int, scale: float | None = None, causal: bool = True,
     return _topk_rows(q, k, None, 1, s, K, causal, with_scores)
 
 
+def oracle_topk_rows(q, k, K: int, rows, scale: float | None = None, causal: bool = True) -> np.ndarray:
+    """Exact-dot top-K for selected rows only (rows: flat ids (b*H + h)*N + i),
+    (len(rows), K) int32: spot checks of full-size oracle selections."""
+    B, H, Hkv, N = _shape4(q, k)
+    rows = np.ascontiguousarray(rows, dtype=np.int64)
+    D = q.shape[-1]
+    qf = q.reshape(B * H * N, D)
+    qsel = _f32(qf[torch_index(rows)] if hasattr(qf, "detach") else qf[rows])
+    kf = _f32(k)
+    s = np.float32(1.0 / math.sqrt(D) if scale is None else scale)
+    out = np.empty((len(rows), K), dtype=np.int32)
+    lib().orc_topk_rows(_fp(qsel), _fp(kf), None, 1, B, H, Hkv, N, D, float(s), K, 1 if causal else 0,
+                        rows.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), len(rows),
+                        out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+    return out
+
+
 def router_topk_rows(q, k, wq, wk, pos_bias, seq_len: int, K: int, rows, causal: bool = True) -> np.ndarray:
     """Canonical router top-K for selected rows only.  rows: flat ids
     (b*H + h)*N + i.  Returns (len(rows), K) int32.  Only the listed query rows

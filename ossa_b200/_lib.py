@@ -37,6 +37,8 @@ EXPORTED = (
     "ossa_topk_attention_fwd_rows",
     "ossa_router_workspace_size_rows",
     "ossa_router_topk_rows",
+    "ossa_oracle_workspace_size",
+    "ossa_oracle_topk_ws",
 )
 
 _lock = threading.Lock()
@@ -79,6 +81,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ossa_router_workspace_size_rows.restype = sz
     lib.ossa_router_topk_rows.argtypes = [vp, vp, ci, vp, vp, vp] + [ci] * 11 + [vp, vp, sz, vp]
     lib.ossa_router_topk_rows.restype = ci
+    lib.ossa_oracle_workspace_size.argtypes = [ci] * 7
+    lib.ossa_oracle_workspace_size.restype = sz
+    lib.ossa_oracle_topk_ws.argtypes = [vp, vp, ci, ci, ci, ci, ci, ci, cf, ci, ci, vp, vp, sz, vp]
+    lib.ossa_oracle_topk_ws.restype = ci
 
 
 def lib() -> ctypes.CDLL:

@@ -97,6 +97,21 @@ bool use_tensor_core_select(int B, int H, int Hkv, int Nq, int Nk, int r, int K)
 
 bool supported_r(int r) { return r == 16 || r == 32 || r == 64 || r == 128; }
 
+// The oracle selection runs on the tensor-core kernel for head_dim 128, K <= 128
+// and at least one full tile of query and key rows; OSSA_ORACLE_SELECT=exact
+// forces the CUDA-core exact selector (identical indices; the switch exists to
+// cross-check them).
+bool use_tensor_core_oracle(int B, int H, int Hkv, int N, int D, int K) {
+    const char* env = getenv("OSSA_ORACLE_SELECT");
+    if (env && env[0] == 'e') return false;
+    return ossa::oracle_tc_supported(D, K) && (long long)B * Hkv * N >= 128 && (long long)B * H * N >= 128;
+}
+
+size_t oracle_workspace_bytes(int B, int H, int Hkv, int N, int D, int K, int dtype) {
+    if (!use_tensor_core_oracle(B, H, Hkv, N, D, K)) return kCountersBytes;
+    return kCountersBytes + align_up(ossa::oracle_tc_workspace_bytes(B, H, Hkv, N, K, dtype));
+}
+
 int check_rows(int Nq, int Nk, int q0) {
     if (Nq < 0 || q0 < 0 || (long long)q0 + Nq > (1ll << 30))
         return fail(OSSA_ERR_INVALID, "bad query rows Nq=%d q_start=%d (keys %d)", Nq, q0, Nk);
@@ -284,6 +299,43 @@ int ossa_oracle_topk(const void* q, const void* k, int dtype, int B, int H, int 
     ossa::ScoreTopkArgs a{q, k, dtype, nullptr, 1, B, H, Hkv, N, D, K, scale, causal ? 1 : 0, idx_out};
     return cuda_status(ossa::launch_score_topk(a, static_cast<cudaStream_t>(stream)),
                        "oracle top-K launch");
+}
+
+size_t ossa_oracle_workspace_size(int B, int H, int Hkv, int N, int D, int K, int dtype) {
+    if (B < 0 || H <= 0 || Hkv <= 0 || N < 0 || D <= 0 || K <= 0 || !valid_dtype(dtype)) return 0;
+    return oracle_workspace_bytes(B, H, Hkv, N, D, K, dtype);
+}
+
+int ossa_oracle_topk_ws(const void* q, const void* k, int dtype, int B, int H, int Hkv, int N, int D,
+                        float scale, int K, int causal, int32_t* idx_out, void* workspace,
+                        size_t workspace_bytes, ossa_stream_t stream) {
+    int st = check_heads(B, H, Hkv, N);
+    if (st) return st;
+    if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);
+    if (!supported_r(D))
+        return fail(OSSA_ERR_UNSUPPORTED, "oracle selection supports head_dim in {16,32,64,128}, got %d", D);
+    if (K <= 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
+    if (!ossa::score_topk_supported(D, K))
+        return fail(OSSA_ERR_UNSUPPORTED, "top-K selection supports K <= 160 (got K=%d)", K);
+    if (!isfinite(scale)) return fail(OSSA_ERR_INVALID, "scale must be finite");
+    if ((long long)B * H * N == 0) return OSSA_OK;
+    if (!q || !k || !idx_out) return fail(OSSA_ERR_INVALID, "null pointer argument");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(idx_out))
+        return fail(OSSA_ERR_INVALID, "q, k and the output must be 16-byte aligned");
+    const size_t need = oracle_workspace_bytes(B, H, Hkv, N, D, K, dtype);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+        return fail(OSSA_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required, got %zu", need,
+                    workspace ? workspace_bytes : (size_t)0);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    st = cuda_status(cudaMemsetAsync(workspace, 0, kCountersBytes, s), "workspace counters reset");
+    if (st) return st;
+    if (!use_tensor_core_oracle(B, H, Hkv, N, D, K)) {
+        ossa::ScoreTopkArgs a{q, k, dtype, nullptr, 1, B, H, Hkv, N, D, K, scale, causal ? 1 : 0, idx_out};
+        return cuda_status(ossa::launch_score_topk(a, s), "oracle top-K launch");
+    }
+    ossa::OracleTcArgs a{q, k, dtype, B, H, Hkv, N, K, causal ? 1 : 0, scale, idx_out,
+                         static_cast<char*>(workspace) + kCountersBytes, reinterpret_cast<int*>(workspace)};
+    return cuda_status(ossa::launch_oracle_tc(a, s), "tensor-core oracle top-K launch");
 }
 
 }  // extern "C"

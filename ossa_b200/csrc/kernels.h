@@ -97,4 +97,22 @@ bool router_tc_supported(int r, int K);
 size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K);
 cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream);
 
+// The oracle selector (exact scaled q.k scores, no pos_bias) on the same
+// tensor-core kernel, for head_dim kOracleD: fp16 scores find the candidates,
+// fp32 canonical scores decide them (indices identical to launch_score_topk).
+constexpr int kOracleD = 128;
+struct OracleTcArgs {
+    const void* q;  // [B, H, N, D] rows, dtype
+    const void* k;  // [B, Hkv, N, D] rows, dtype
+    int dtype;
+    int B, H, Hkv, N, K, causal;
+    float scale;
+    int32_t* out;
+    void* ws;       // oracle_tc_workspace_bytes
+    int* counters;  // two ints, zeroed before the launch
+};
+bool oracle_tc_supported(int D, int K);
+size_t oracle_tc_workspace_bytes(int B, int H, int Hkv, int N, int K, int dtype);
+cudaError_t launch_oracle_tc(const OracleTcArgs& a, cudaStream_t stream);
+
 }  // namespace ossa

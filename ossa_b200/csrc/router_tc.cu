@@ -87,7 +87,6 @@ constexpr int kWinLen = 2 * kTileN - 4;  // 252 terms per copy (z <= 254)
 constexpr int kWinCopy = kWinLen + 12;   // copy stride in floats, = 8 (mod 32): copies 8 banks apart
 constexpr int kWinBytes = 4 * kWinCopy * 4;
 static_assert(kWinCopy % 32 == 8 && (kWinLen * 4) % 16 == 0 && (kWinCopy * 4) % 16 == 0, "window layout");
-constexpr int kTileBytes = kTileM * kR * 2;
 constexpr uint32_t kTmemCols = kAccBufs * kTileN;
 constexpr int kBoundSlack = 3;      // the pass-1 bound stops once K..K+3 class maxima are above it
 constexpr int kMaxBand = 32;        // wide: boundary candidates rescored per row (one per lane) before falling back
@@ -99,34 +98,48 @@ constexpr int kMaxBand = 32;        // wide: boundary candidates rescored per ro
 // column; pass 1 visits the even tiles, then the odd ones); the sub-lists (about
 // 1.4 K per row) sit in global memory and a warp-per-row kernel
 // (final_select_kernel) makes the final choice.
-template <bool kWide>
+// Variants.  kD is the contraction width: 64 for the router's projections, 128
+// for the exact-dot oracle selector (q . k at head_dim 128, no position bias).
+// A kD = 128 tile is stored as two 128 x 64 sub-tiles (one TMA box and one
+// swizzle atom column each), so the K = 128 contraction walks two descriptor
+// bases.  With kD = 128 the operand tiles double, so the candidate lists always
+// go to global memory and the wide variant stores its class maxima as fp16,
+// rounded down (still a lower bound).
+template <bool kWide, int kD = 64>
 struct TcCfg {
+    static_assert(kD == 64 || kD == 128, "contraction width");
     static constexpr int kMaxK = kWide ? 128 : 64;
-    static constexpr int kStages = kWide ? 4 : 2;  // k' tile ring
+    static constexpr bool kGlobal = kWide || kD > 64;       // candidate lists in global memory
+    static constexpr bool kClsHalf = kWide && kD > 64;      // class maxima as fp16
+    static constexpr int kTileB = kTileM * kD * 2;          // bytes of one q' or k' tile
+    static constexpr int kStages = kD > 64 ? 3 : (kWide ? 4 : 2);  // k' tile ring
     static constexpr int kCap = kWide ? 160 : 80;  // sub-list capacity per row and column half
     static constexpr int kLimit = kCap - 16;       // past this after a 16-column step: exact fallback
-    // narrow: kRowStride uint2 per row in shared memory (both sub-lists and a
-    // spare entry for the row's bound and counts; the odd stride spreads banks);
-    // the class maxima go through the still empty sub-list area.
+    // shared-memory lists (narrow, kD = 64): kRowStride uint2 per row (both
+    // sub-lists and a spare entry for the row's bound and counts; the odd stride
+    // spreads banks); the class maxima go through the still empty sub-list area.
     static constexpr int kRowStride = 2 * kCap + 1;
-    // wide: class maxima kClsStride floats per row (odd: spreads banks), then the
-    // per-row bounds; sub-lists in global memory, contiguous per row and half,
-    // 2 * kTileM * kCap entries per query block.
-    static constexpr int kClsStride = 2 * kTileN + 1;
+    // global lists: class maxima kClsStride entries per row (wide: 256 classes,
+    // odd stride; narrow: 128, stride 2 (mod 32) banks), then the per-row bounds;
+    // sub-lists contiguous per row and half, 2 * kTileM * kCap entries per query
+    // block.
+    static constexpr int kClsStride = kWide ? 2 * kTileN + 1 : kTileN + 2;
+    static constexpr size_t kClsBytes = (size_t)kTileM * kClsStride * (kClsHalf ? 2 : 4);
     static constexpr size_t kOffA = 0;
-    static constexpr size_t kOffB = kOffA + kTileBytes;
-    static constexpr size_t kOffWin = kOffB + (size_t)kStages * kTileBytes;
+    static constexpr size_t kOffB = kOffA + kTileB;
+    static constexpr size_t kOffWin = kOffB + (size_t)kStages * kTileB;
     static constexpr size_t kOffBuf = kOffWin + (size_t)kAccBufs * kWinBytes;
+    static constexpr size_t kOffLb = kOffBuf + (kClsBytes + 15) / 16 * 16;  // global lists: bound per row
     static constexpr size_t kBufBytes =
-        kWide ? (size_t)kTileM * (kClsStride + 1) * 4 : (size_t)kTileM * kRowStride * sizeof(uint2);
+        kGlobal ? (kOffLb - kOffBuf) + (size_t)kTileM * 4 : (size_t)kTileM * kRowStride * sizeof(uint2);
     static constexpr size_t kOffBar = (kOffBuf + kBufBytes + 7) / 8 * 8;
     static constexpr int kNumBars = 2 * kStages + 1 + 2 * kAccBufs + 1;
     static constexpr size_t kOffSlot = kOffBar + (size_t)kNumBars * 8;
     static constexpr size_t kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
     static_assert(kSmemBytes <= 232448, "shared memory budget");
-    static_assert(kOffB % 1024 == 0 && kTileBytes % 1024 == 0, "swizzled tiles need 1 KB alignment");
+    static_assert(kOffB % 1024 == 0 && kTileB % 1024 == 0, "swizzled tiles need 1 KB alignment");
     static_assert(kOffWin % 16 == 0, "bulk copies need 16-byte aligned destinations");
-    static_assert(kWide || kTileM * 256 <= kStages * kTileBytes, "output staging fits in the k' ring");
+    static_assert(kGlobal || kTileM * 256 <= kStages * kTileB, "output staging fits in the k' ring");
 };
 constexpr int kWideMaxK = TcCfg<true>::kMaxK;
 constexpr int kNarrowMaxK = TcCfg<false>::kMaxK;
@@ -139,15 +152,16 @@ constexpr float kTwoPowM22 = 2.384185791015625e-07f;  // 2^-22
 // [1] max_j |k'_j|_2 bits, [2] non-finite flag, [3] max_j |fp16(k'_j) - k'_j|_2 bits
 // (the largest conversion error of a key row, written by kconvert_kernel).
 constexpr int kStatWords = 4;
+template <int kD>
 __global__ void kstats_kernel(const float* __restrict__ kp, int N, uint32_t* __restrict__ stats) {
     const int bg = blockIdx.y;
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     float mabs = 0.f, ss = 0.f;
     bool bad = false;
     if (j < N) {
-        const float4* r = reinterpret_cast<const float4*>(kp + ((size_t)bg * N + j) * kR);
+        const float4* r = reinterpret_cast<const float4*>(kp + ((size_t)bg * N + j) * kD);
 #pragma unroll
-        for (int c = 0; c < kR / 4; ++c) {
+        for (int c = 0; c < kD / 4; ++c) {
             const float4 x = __ldg(r + c);
             mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
             ss = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, ss))));
@@ -187,7 +201,8 @@ __global__ void bias_stats_kernel(const float* __restrict__ bias, int n, uint32_
 // bulk copy brings it in.  Copy s of window d holds, at position y < kWinLen, the
 // bias term of offset o = o_max - kTileN * d - y - s (o = i - j + L; offsets
 // descend so that ascending positions are ascending key columns): -inf when
-// causal and o < L (a key after its query), else pos_bias[clamp(o, 0, 2L - 1)].
+// causal and o < L (a key after its query), else pos_bias[clamp(o, 0, 2L - 1)]
+// (0 with no pos_bias: the oracle's plain scaled dot products).
 __global__ void window_table_kernel(const float* __restrict__ bias, int L, int causal, long long o_max, int ndiag,
                                     float* __restrict__ out) {
     constexpr int kPer = 4 * kWinCopy;
@@ -198,7 +213,9 @@ __global__ void window_table_kernel(const float* __restrict__ bias, int L, int c
     const int s = r / kWinCopy, y = r - s * kWinCopy;
     const long long o = o_max - (long long)kTileN * d - y - s;
     float v = 0.f;  // copy padding
-    if (y < kWinLen) v = (causal && o < L) ? -INFINITY : __ldg(bias + (o < 0 ? 0 : (o > 2LL * L - 1 ? 2LL * L - 1 : o)));
+    if (y < kWinLen)
+        v = (causal && o < L) ? -INFINITY
+                              : (bias ? __ldg(bias + (o < 0 ? 0 : (o > 2LL * L - 1 ? 2LL * L - 1 : o))) : 0.f);
     out[t] = v;
 }
 
@@ -221,17 +238,19 @@ __device__ __forceinline__ float pow2f(int e) {
 __device__ __forceinline__ float scale2(float x, int e, float f) { return f != 0.f ? x * f : ldexpf(x, e); }
 
 // fp16 copy of k' scaled by the (b, kv head) power of two, one float4 per thread
-// (16 threads per key row), and the norm of each row's conversion error, whose
-// maximum goes to stats[kStatWords*bg + 3].  Blocks of 256 threads.
+// (kD / 4 threads per key row), and the norm of each row's conversion error,
+// whose maximum goes to stats[kStatWords*bg + 3].  Blocks of 256 threads.
+template <int kD>
 __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict__ k16, int N,
                                 uint32_t* __restrict__ stats) {
+    constexpr int kTPR = kD / 4;  // threads per row
     const int bg = blockIdx.y;
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    const bool live = t < N * (kR / 4);  // whole 16-thread rows share it (N * 16 threads)
+    const bool live = (long long)t < (long long)N * kTPR;  // whole rows share it
     const int e = scale_exponent(__uint_as_float(stats[kStatWords * bg + 0]));
     float ss = 0.f;
     if (live) {
-        const size_t off = (size_t)bg * N * kR + (size_t)t * 4;
+        const size_t off = (size_t)bg * N * kD + (size_t)t * 4;
         const float4 x = __ldg(reinterpret_cast<const float4*>(kp + off));
         const float up = pow2f(e), dn = pow2f(-e);
         __half2 lo = __floats2half2_rn(scale2(x.x, e, up), scale2(x.y, e, up));
@@ -248,7 +267,7 @@ __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict
         ss = fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, d3 * d3)));
     }
 #pragma unroll
-    for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(kFull, ss, o);
+    for (int o = 1; o < kTPR; o <<= 1) ss += __shfl_xor_sync(kFull, ss, o);
     // maximum over the block's rows, then one atomic per block (same-address
     // atomics from every warp serialise)
     __shared__ uint32_t wmax[8];
@@ -263,12 +282,14 @@ __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict
     }
 }
 
-// Eight threads per query row (8 of its 64 values each, coalesced loads and
+// Eight threads per query row (kD / 8 values each, coalesced loads and
 // stores): scaled fp16 row, epilogue multiplier and error bound.
+template <int kD>
 __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp, __half* __restrict__ q16,
                                                     float2* __restrict__ rowinfo, long long rows, int H, int Hkv,
                                                     int Nq, float scale, const uint32_t* __restrict__ stats,
                                                     const uint32_t* __restrict__ gstats) {
+    constexpr int kV4 = kD / 32;  // float4 per thread
     const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
     const int part = threadIdx.x & 7;
     const bool live = row < rows;  // whole 8-lane groups share it
@@ -277,14 +298,17 @@ __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp
     const int b = (int)(bh / H);
     const int h = (int)(bh - (long long)b * H);
     const int bg = b * Hkv + h / (H / Hkv);
-    const float4* r = reinterpret_cast<const float4*>(qp + rr * kR) + 2 * part;
-    const float4 x0 = __ldg(r), x1 = __ldg(r + 1);
-    float mabs = fmaxf(fmaxf(fmaxf(fabsf(x0.x), fabsf(x0.y)), fmaxf(fabsf(x0.z), fabsf(x0.w))),
-                       fmaxf(fmaxf(fabsf(x1.x), fabsf(x1.y)), fmaxf(fabsf(x1.z), fabsf(x1.w))));
-    float ss = fmaf(x0.x, x0.x, fmaf(x0.y, x0.y, fmaf(x0.z, x0.z, x0.w * x0.w)));
-    ss = fmaf(x1.x, x1.x, fmaf(x1.y, x1.y, fmaf(x1.z, x1.z, fmaf(x1.w, x1.w, ss))));
-    unsigned bad = (isfinite(x0.x) && isfinite(x0.y) && isfinite(x0.z) && isfinite(x0.w) && isfinite(x1.x) &&
-                    isfinite(x1.y) && isfinite(x1.z) && isfinite(x1.w)) ? 0u : 1u;
+    const float4* r = reinterpret_cast<const float4*>(qp + rr * kD) + kV4 * part;
+    float4 x[kV4];
+    float mabs = 0.f, ss = 0.f;
+    unsigned bad = 0u;
+#pragma unroll
+    for (int v = 0; v < kV4; ++v) {
+        x[v] = __ldg(r + v);
+        mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(x[v].x), fabsf(x[v].y)), fmaxf(fabsf(x[v].z), fabsf(x[v].w))));
+        ss = fmaf(x[v].x, x[v].x, fmaf(x[v].y, x[v].y, fmaf(x[v].z, x[v].z, fmaf(x[v].w, x[v].w, ss))));
+        bad |= (isfinite(x[v].x) && isfinite(x[v].y) && isfinite(x[v].z) && isfinite(x[v].w)) ? 0u : 1u;
+    }
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) {
         mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, o));
@@ -294,29 +318,27 @@ __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp
     if (!live) return;
     const int eq = scale_exponent(mabs);
     const float up = pow2f(eq), dn = pow2f(-eq);
-    __half2 h0 = __floats2half2_rn(scale2(x0.x, eq, up), scale2(x0.y, eq, up));
-    __half2 h1 = __floats2half2_rn(scale2(x0.z, eq, up), scale2(x0.w, eq, up));
-    __half2 h2 = __floats2half2_rn(scale2(x1.x, eq, up), scale2(x1.y, eq, up));
-    __half2 h3 = __floats2half2_rn(scale2(x1.z, eq, up), scale2(x1.w, eq, up));
-    uint4 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&h0);
-    pk.y = *reinterpret_cast<uint32_t*>(&h1);
-    pk.z = *reinterpret_cast<uint32_t*>(&h2);
-    pk.w = *reinterpret_cast<uint32_t*>(&h3);
-    reinterpret_cast<uint4*>(q16 + rr * kR)[part] = pk;
-    // conversion errors of this part of the row, in unscaled units (exact)
+    // fp16 copy, and the conversion errors of this part of the row in unscaled
+    // units (power-of-two scaling and the difference of two values within a
+    // factor of 2 are exact)
     float dd = 0.f;
-    {
-        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
-        const float2 f2 = __half22float2(h2), f3 = __half22float2(h3);
-        const float e0 = scale2(f0.x, -eq, dn) - x0.x, e1 = scale2(f0.y, -eq, dn) - x0.y;
-        const float e2 = scale2(f1.x, -eq, dn) - x0.z, e3 = scale2(f1.y, -eq, dn) - x0.w;
-        const float e4 = scale2(f2.x, -eq, dn) - x1.x, e5 = scale2(f2.y, -eq, dn) - x1.y;
-        const float e6 = scale2(f3.x, -eq, dn) - x1.z, e7 = scale2(f3.y, -eq, dn) - x1.w;
-        dd = fmaf(e0, e0, fmaf(e1, e1, fmaf(e2, e2, fmaf(e3, e3, fmaf(e4, e4, fmaf(e5, e5, fmaf(e6, e6, e7 * e7)))))));
-    }
+    uint2 pk[kV4];
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) dd += __shfl_xor_sync(0xffu << (threadIdx.x & 24), dd, o);
+    for (int v = 0; v < kV4; ++v) {
+        const __half2 h0 = __floats2half2_rn(scale2(x[v].x, eq, up), scale2(x[v].y, eq, up));
+        const __half2 h1 = __floats2half2_rn(scale2(x[v].z, eq, up), scale2(x[v].w, eq, up));
+        pk[v].x = *reinterpret_cast<const uint32_t*>(&h0);
+        pk[v].y = *reinterpret_cast<const uint32_t*>(&h1);
+        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+        const float e0 = scale2(f0.x, -eq, dn) - x[v].x, e1 = scale2(f0.y, -eq, dn) - x[v].y;
+        const float e2 = scale2(f1.x, -eq, dn) - x[v].z, e3 = scale2(f1.y, -eq, dn) - x[v].w;
+        dd = fmaf(e0, e0, fmaf(e1, e1, fmaf(e2, e2, fmaf(e3, e3, dd))));
+    }
+    uint4* o = reinterpret_cast<uint4*>(q16 + rr * kD + (size_t)part * kV4 * 4);
+#pragma unroll
+    for (int v = 0; v < kV4; v += 2) o[v / 2] = make_uint4(pk[v].x, pk[v].y, pk[v + 1].x, pk[v + 1].y);
+#pragma unroll
+    for (int o2 = 1; o2 < 8; o2 <<= 1) dd += __shfl_xor_sync(0xffu << (threadIdx.x & 24), dd, o2);
     if (part != 0) return;
     const int ek = scale_exponent(__uint_as_float(stats[kStatWords * bg + 0]));
     const float kmax = __uint_as_float(stats[kStatWords * bg + 1]);
@@ -330,8 +352,9 @@ __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp
     // |approx - canonical| <= scale * |q'.dk + dq.k' + dq.dk| (fp16 conversion,
     // Cauchy-Schwarz with the measured errors) + scale * 2^-13 |q'| max|k'| (fp32
     // accumulation in the tensor core and in the canonical chain: 64 terms at a few
-    // ulp each) + 2^-22 (max|bias| + cross) (the final roundings)
-    const float delta = scale * (qn * dkmax + dq * kmax + dq * dkmax) * 1.0001f + scale * 1.220703125e-4f * qn * kmax +
+    // ulp each, twice that for 128) + 2^-22 (max|bias| + cross) (the final roundings)
+    constexpr float kAcc = 1.220703125e-4f * (kD / 64);
+    const float delta = scale * (qn * dkmax + dq * kmax + dq * dkmax) * 1.0001f + scale * kAcc * qn * kmax +
                         kTwoPowM22 * (bmax + cross) + 1e-30f;
     if (nonfinite || !isfinite(delta) || !(m >= 1.1754944e-38f) || !isfinite(m)) {
         rowinfo[rr] = make_float2(__int_as_float(0x7fc00000), 0.f);  // NaN multiplier: exact fallback
@@ -359,28 +382,37 @@ struct TcParams {
     float scale;
 };
 
-// Canonical fp32 score of (query row qrow, key row krow) at offset i - j: the
-// fmaf chain over d = 0..63 in order.  The key row's 16 loads are issued
-// together (one memory round trip; the query row is reused and cached).
+// Canonical fp32 score of (query row qrow, key row krow): the fmaf chain over
+// d = 0..kD-1 in order, times scale, plus (router) the position-bias term at
+// offset i - j.  Key-row loads go out 64 values at a time (one memory round
+// trip for kD = 64; the query row is reused and cached).
+template <int kD = kR, bool kBias = true>
 __device__ __forceinline__ float canonical_score(const float* __restrict__ qrow, const float* __restrict__ krow,
                                                  const float* __restrict__ bias, int L, int i, int j,
                                                  float scale) {
-    float4 bk[kR / 4];
-#pragma unroll
-    for (int u = 0; u < kR / 4; ++u) bk[u] = __ldg(reinterpret_cast<const float4*>(krow) + u);
-    int bi = i - j + L;
-    bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
-    const float bv = __ldg(bias + bi);
+    float bv = 0.f;
+    if constexpr (kBias) {
+        int bi = i - j + L;
+        bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
+        bv = __ldg(bias + bi);
+    }
     float acc = 0.f;
 #pragma unroll
-    for (int u = 0; u < kR / 4; ++u) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(qrow) + u);
-        acc = fmaf(a.x, bk[u].x, acc);
-        acc = fmaf(a.y, bk[u].y, acc);
-        acc = fmaf(a.z, bk[u].z, acc);
-        acc = fmaf(a.w, bk[u].w, acc);
+    for (int c0 = 0; c0 < kD / 4; c0 += 16) {
+        float4 bk[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) bk[u] = __ldg(reinterpret_cast<const float4*>(krow) + c0 + u);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(qrow) + c0 + u);
+            acc = fmaf(a.x, bk[u].x, acc);
+            acc = fmaf(a.y, bk[u].y, acc);
+            acc = fmaf(a.z, bk[u].z, acc);
+            acc = fmaf(a.w, bk[u].w, acc);
+        }
     }
-    return __fadd_rn(__fmul_rn(acc, scale), bv);
+    if constexpr (kBias) return __fadd_rn(__fmul_rn(acc, scale), bv);
+    else return __fmul_rn(acc, scale);
 }
 
 // count_ge over the first nch 8-entry chunks of x only (nch uniform across the warp).
@@ -422,6 +454,13 @@ __device__ __forceinline__ float interp_probe(float lo, float hi, int c_lo, int 
     t = fminf(fmaxf(t, 0.0625f), 0.9375f);
     return lo + t * (hi - lo);
 }
+
+// Class-maximum storage: fp32, or fp16 rounded toward -inf (a smaller value,
+// so the K-th largest stays a lower bound on the K-th best score).
+__device__ __forceinline__ void cls_put(float* p, float v) { *p = v; }
+__device__ __forceinline__ void cls_put(__half* p, float v) { *p = __float2half_rd(v); }
+__device__ __forceinline__ float cls_get(const float* p) { return *p; }
+__device__ __forceinline__ float cls_get(const __half* p) { return __half2float(*p); }
 
 // A lower bound on the K-th largest class maximum of a row whose maxima are
 // spread over G consecutive lanes (kHalfCols per lane, -inf for empty classes):
@@ -558,22 +597,25 @@ __device__ __forceinline__ void score_half_tile(uint32_t taddr, uint32_t wsrc, u
     }
 }
 
-template <bool kWide>
+template <bool kWide, int kD = 64>
 __global__ void __launch_bounds__(kThreads, 1)
 router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const TcParams p) {
-    using Cfg = TcCfg<kWide>;
+    using Cfg = TcCfg<kWide, kD>;
     constexpr int kStages = Cfg::kStages;
+    constexpr int kTB = Cfg::kTileB;
+    constexpr bool kGlobal = Cfg::kGlobal;
+    using ClsT = std::conditional_t<Cfg::kClsHalf, __half, float>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
     uint8_t* sA = smem + Cfg::kOffA;
     uint8_t* sB = smem + Cfg::kOffB;
     float* win = reinterpret_cast<float*>(smem + Cfg::kOffWin);
-    // narrow: sub-lists; wide: class maxima and bounds (see TcCfg)
+    // shared-memory lists, or class maxima and bounds (see TcCfg)
     [[maybe_unused]] uint2* buf = reinterpret_cast<uint2*>(smem + Cfg::kOffBuf);
-    [[maybe_unused]] float* cls = reinterpret_cast<float*>(smem + Cfg::kOffBuf);
-    [[maybe_unused]] float* lbw = cls + kTileM * Cfg::kClsStride;
+    [[maybe_unused]] ClsT* cls = reinterpret_cast<ClsT*>(smem + Cfg::kOffBuf);
+    [[maybe_unused]] float* lbw = reinterpret_cast<float*>(smem + Cfg::kOffLb);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
     uint64_t* full = bars;
     uint64_t* empty = bars + kStages;
@@ -634,16 +676,20 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
             bool ok = true;
-            mbar_arrive_expect_tx(afull, kTileBytes);
-            tma_load_2d(sA, &tmA, afull, 0, bh * Nq + i0);
+            // a tile is kD / 64 boxes of 128 rows x 64 columns (one 16 KB swizzle atom column each)
+            mbar_arrive_expect_tx(afull, kTB);
+#pragma unroll
+            for (int h = 0; h < kD / 64; ++h) tma_load_2d(sA + h * 16384, &tmA, afull, 64 * h, bh * Nq + i0);
             const int krow0 = (b * Hkv + g) * N;
             int issued = 0;
             for (int t = 0; t < T2; ++t) {
                 const int s = t % kStages;
                 if (t >= kStages) ok = mbar_wait(empty + s, ((t / kStages) - 1) & 1);
                 if (!ok) break;
-                mbar_arrive_expect_tx(full + s, kTileBytes);
-                tma_load_2d(sB + (size_t)s * kTileBytes, &tmB, full + s, 0, krow0 + tile_of(t) * kTileN);
+                mbar_arrive_expect_tx(full + s, kTB);
+#pragma unroll
+                for (int h = 0; h < kD / 64; ++h)
+                    tma_load_2d(sB + (size_t)s * kTB + h * 16384, &tmB, full + s, 64 * h, krow0 + tile_of(t) * kTileN);
                 issued = t + 1;
             }
             // the loads of the last stages are never waited on by a refill: make
@@ -656,7 +702,6 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_f16(0u, kTileM, kTileN);
-            const uint64_t adesc = umma_desc_sw128(sA);
             bool ok = mbar_wait(afull, 0);
             for (int t = 0; t < T2 && ok; ++t) {
                 const int s = t % kStages;
@@ -665,11 +710,14 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 if (ok && t >= kAccBufs) ok = mbar_wait(tempty + ab, ((t / kAccBufs) - 1) & 1);
                 if (!ok) break;
                 tc_fence_after();
-                const uint64_t bdesc = umma_desc_sw128(sB + (size_t)s * kTileBytes);
                 const uint32_t d = tmem + (uint32_t)(ab * kTileN);
 #pragma unroll
-                for (int k = 0; k < kR / 16; ++k)
-                    mma_f16(d, adesc + 2u * k, bdesc + 2u * k, idesc, k > 0 ? 1u : 0u);
+                for (int k = 0; k < kD / 16; ++k) {
+                    // 16 columns per MMA; a new 64-column atom column every 4
+                    const uint64_t ad = umma_desc_sw128(sA + (k >> 2) * 16384) + 2u * (k & 3);
+                    const uint64_t bd = umma_desc_sw128(sB + (size_t)s * kTB + (k >> 2) * 16384) + 2u * (k & 3);
+                    mma_f16(d, ad, bd, idesc, k > 0 ? 1u : 0u);
+                }
                 mma_commit(empty + s);
                 mma_commit(tfull + ab);
             }
@@ -797,10 +845,10 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             if constexpr (kWide) {
                 if (t == Te - 1) {
                     // even tiles done: their class maxima go to shared memory
-                    float* crow = cls + row * Cfg::kClsStride + hf * kHalfCols;
+                    ClsT* crow = cls + row * Cfg::kClsStride + hf * kHalfCols;
 #pragma unroll
                     for (int c = 0; c < kHalfCols; ++c) {
-                        crow[c] = cm[c];
+                        cls_put(crow + c, cm[c]);
                         cm[c] = -INFINITY;
                     }
                 }
@@ -813,7 +861,26 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         [[maybe_unused]] uint2* rowbuf = buf + (size_t)row * Cfg::kRowStride;  // narrow
         [[maybe_unused]] uint2* sub = rowbuf + hf * Cfg::kCap;  // narrow: this thread's sub-list
         float lb = -INFINITY;
-        if constexpr (!kWide) {
+        if constexpr (!kWide && kGlobal) {
+            // 128 maxima, 64 per column half, exchanged through the class-maxima
+            // area: lanes 2r and 2r+1 of warp hf take row r0 + 16*hf + r, one half each
+            ClsT* crow = cls + row * Cfg::kClsStride + hf * kHalfCols;
+#pragma unroll
+            for (int c = 0; c < kHalfCols; ++c) cls_put(crow + c, cm[c]);
+            named_bar_sync(pair_bar, 64);
+            const int brow = r0 + 16 * hf + (lane >> 1);
+            const int bhalf = lane & 1;
+            const ClsT* src = cls + brow * Cfg::kClsStride + bhalf * kHalfCols;
+            float y[kHalfCols];
+            // rotated by one for the odd lane: with a row stride of 2 (mod 32) banks
+            // the warp's 32 reads hit 32 banks
+#pragma unroll
+            for (int c = 0; c < kHalfCols; ++c) y[c] = cls_get(src + ((c + bhalf) & (kHalfCols - 1)));
+            const float lbv = group_class_bound<2>(y, K);
+            if (bhalf == 0) lbw[brow] = lbv;
+            named_bar_sync(pair_bar, 64);
+            lb = lbw[row];
+        } else if constexpr (!kWide) {
             // 128 maxima, 64 per column half, exchanged through the still empty
             // sub-lists: lanes 2r and 2r+1 of warp hf take row r0 + 16*hf + r, one
             // half each; the bound goes back through the row's spare entry
@@ -835,19 +902,19 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             // 256 maxima (even/odd tiles x two column halves, 64 each; the even ones
             // are already in shared memory); four lanes per row, the quadrant's 32
             // rows in two batches of 16
-            float* crow = cls + row * Cfg::kClsStride + kTileN + hf * kHalfCols;
+            ClsT* crow = cls + row * Cfg::kClsStride + kTileN + hf * kHalfCols;
 #pragma unroll
-            for (int c = 0; c < kHalfCols; ++c) crow[c] = cm[c];
+            for (int c = 0; c < kHalfCols; ++c) cls_put(crow + c, cm[c]);
             named_bar_sync(pair_bar, 64);
 #pragma unroll 1
             for (int bt = 0; bt < 2; ++bt) {
                 const int brow = r0 + 16 * bt + 8 * hf + (lane >> 2);
                 const int t4 = lane & 3;
-                const float* src = cls + brow * Cfg::kClsStride + t4 * kHalfCols;
+                const ClsT* src = cls + brow * Cfg::kClsStride + t4 * kHalfCols;
                 float y[kHalfCols];
-                // rotated by 8 per lane of the group: the warp's 32 reads hit 32 banks
+                // rotated by 8 per lane of the group: the warp's 32 fp32 reads hit 32 banks
 #pragma unroll
-                for (int c = 0; c < kHalfCols; ++c) y[c] = src[(c + 8 * t4) & (kHalfCols - 1)];
+                for (int c = 0; c < kHalfCols; ++c) y[c] = cls_get(src + ((c + 8 * t4) & (kHalfCols - 1)));
                 const float lbv = group_class_bound<4>(y, K);
                 if (t4 == 0) lbw[brow] = lbv;
             }
@@ -862,11 +929,11 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
         // ---------------- pass 2: collect candidates s >= theta into the sub-list
         // (narrow: shared memory; wide: global memory, contiguous per row and half)
-        using Addr = std::conditional_t<kWide, uint64_t, uint32_t>;
+        using Addr = std::conditional_t<kGlobal, uint64_t, uint32_t>;
         constexpr int kLimit = Cfg::kLimit;
         constexpr Addr kStep = 8;  // bytes per entry
         Addr list_base;
-        if constexpr (kWide)
+        if constexpr (kGlobal)
             list_base = (uint64_t)__cvta_generic_to_global(
                 p.lists + ((size_t)bh * p.nqb + qb) * (2 * kTileM * (size_t)Cfg::kCap) + (size_t)(2 * row + hf) * Cfg::kCap);
         else
@@ -934,7 +1001,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         if (!ok) atomicOr(p.status, 4);
 
-        if constexpr (kWide) {
+        if constexpr (kGlobal) {
             // final_select_kernel finishes the row from its two lists
             if (ok && i < Nq) p.counts[((size_t)bh * Nq + i) * 2 + hf] = fb ? -1 : cnt;
         } else {
@@ -1284,7 +1351,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
 // One warp per listed row: canonical scores on CUDA cores, streaming selection
 // with a per-warp candidate list (the same rule as the exact CTA selector).
-template <int EPL>
+template <int EPL, int kD = kR, bool kBias = true>
 __global__ void __launch_bounds__(256)
 exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, const float* __restrict__ bias,
                   int L, int H, int Hkv, int N, int Nq, int q0, int K, float scale, int causal,
@@ -1304,8 +1371,8 @@ exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, co
         const int b = (int)(bh / H);
         const int h = (int)(bh - (long long)b * H);
         const int g = h / (H / Hkv);
-        const float* qrow = qp + row * kR;
-        const float* kbase = kp + (size_t)(b * Hkv + g) * N * kR;
+        const float* qrow = qp + row * kD;
+        const float* kbase = kp + (size_t)(b * Hkv + g) * N * kD;
         const int n = causal ? min(i + 1, N) : N;
         uint32_t theta = 0u;
         int cnt = 0;
@@ -1313,7 +1380,7 @@ exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, co
             const int j = j0 + lane;
             uint32_t key = 0u;
             const bool valid = j < n;
-            if (valid) key = order_key(canonical_score(qrow, kbase + (size_t)j * kR, bias, L, i, j, scale));
+            if (valid) key = order_key(canonical_score<kD, kBias>(qrow, kbase + (size_t)j * kD, bias, L, i, j, scale));
             const bool adm = valid && key > theta;
             const unsigned bal = __ballot_sync(kFull, adm);
             if (adm) wb[cnt + __popc(bal & lt)] = make_uint2(key, (uint32_t)j);
@@ -1404,7 +1471,7 @@ struct FinalParams {
 // more than kMaxBand entries, every candidate is rescored canonically and the
 // exact top K is taken among them.  Rows whose lists overflowed or whose inputs
 // are not finite go to the exact fallback list.
-template <int kCap, int kMaxOut>
+template <int kCap, int kMaxOut, int kD = kR, bool kBias = true>
 __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) {
     constexpr int kEPL = 2 * kCap / 32;  // candidate entries per lane
     static_assert(kEPL * 32 == 2 * kCap && kMaxBand <= 32, "list and band layout");
@@ -1483,13 +1550,13 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                     const int ipos = p.q0 + (int)(row - bh * p.Nq);
                     const int b = (int)(bh / p.H);
                     const int g = (int)(bh - (long long)b * p.H) / (p.H / p.Hkv);
-                    const float* qrow = p.qp32 + (size_t)row * kR;
-                    const float* kbase = p.kp32 + (size_t)(b * p.Hkv + g) * p.N * kR;
+                    const float* qrow = p.qp32 + (size_t)row * kD;
+                    const float* kbase = p.kp32 + (size_t)(b * p.Hkv + g) * p.N * kD;
                     uint32_t ek[kEPL];
 #pragma unroll
                     for (int e = 0; e < kEPL; ++e)
-                        ek[e] = val[e] ? order_key(canonical_score(qrow, kbase + (size_t)jv[e] * kR, p.bias, p.L, ipos,
-                                                                   (int)jv[e], p.scale))
+                        ek[e] = val[e] ? order_key(canonical_score<kD, kBias>(qrow, kbase + (size_t)jv[e] * kD, p.bias,
+                                                                              p.L, ipos, (int)jv[e], p.scale))
                                        : 0u;
                     uint32_t Te;
                     int ties;
@@ -1530,9 +1597,9 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                     int jj = INT_MAX;
                     if (lane < (int)nb) {
                         jj = sband[warp][lane];
-                        const float ex = canonical_score(p.qp32 + (size_t)row * kR,
-                                                         p.kp32 + ((size_t)(b * p.Hkv + g) * p.N + jj) * kR, p.bias,
-                                                         p.L, ipos, jj, p.scale);
+                        const float ex = canonical_score<kD, kBias>(
+                            p.qp32 + (size_t)row * kD, p.kp32 + ((size_t)(b * p.Hkv + g) * p.N + jj) * kD, p.bias,
+                            p.L, ipos, jj, p.scale);
                         ek = order_key(ex);
                     }
                     int rank = 0;
@@ -1612,13 +1679,14 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// (rows x 64) fp16 row-major matrix -> 128 x 64 boxes with the 128-byte swizzle.
-bool make_row_map(CUtensorMap* map, const void* base, unsigned long long rows) {
+// (rows x cols) fp16 row-major matrix -> 128-row x 64-column boxes with the
+// 128-byte swizzle (a row of cols > 64 takes cols / 64 boxes).
+bool make_row_map(CUtensorMap* map, const void* base, unsigned long long rows, int cols) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)kR, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)kR * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kR, (cuuint32_t)kTileM};
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {64u, (cuuint32_t)kTileM};
     const cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1630,35 +1698,40 @@ cudaError_t record(cudaError_t e) {
     return e;
 }
 
-}  // namespace
-
-bool router_tc_supported(int r, int K) { return r == kR && K >= 1 && K <= kWideMaxK; }
-
-size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K) {
+// Workspace of one tensor-core selection over row length kD: fp16 copies of the
+// query and key rows, per-row multipliers and bounds, key and bias statistics,
+// the fallback list, the window images and (lists in global memory) the
+// candidate sub-lists of every row slot of every query block with their lengths.
+size_t tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K, int kD) {
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
     const size_t rq = (size_t)B * H * Nq, rk = (size_t)B * Hkv * N;
     const int nqb = (Nq + kTileM - 1) / kTileM, tiles_n = (N + kTileN - 1) / kTileN;
-    size_t total = al(rq * kR * 2) + al(rk * kR * 2) + al(rq * sizeof(float2)) +
+    size_t total = al(rq * kD * 2) + al(rk * kD * 2) + al(rq * sizeof(float2)) +
                    al((kStatWords * (size_t)B * Hkv + 2) * 4) + al(rq * 4) +
                    (nqb > 0 && tiles_n > 0 ? al((size_t)window_count(nqb, tiles_n) * kWinBytes) : 0);
-    if (K > kNarrowMaxK) {
-        // wide: sub-lists for every row slot of every query block (the last block
-        // padded) and their lengths
+    const bool wide = K > kNarrowMaxK;
+    if (wide || kD > 64) {
         const size_t lrows = (size_t)B * H * nqb * kTileM;
-        total += al(lrows * 2 * (size_t)TcCfg<true>::kCap * sizeof(uint2)) + al(rq * 2 * sizeof(int));
+        const int cap = wide ? TcCfg<true>::kCap : TcCfg<false>::kCap;
+        total += al(lrows * 2 * (size_t)cap * sizeof(uint2)) + al(rq * 2 * sizeof(int));
     }
     return total;
 }
 
-cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
+// One selection: prep kernels, the tensor-core kernel, then (lists in global
+// memory) the warp-per-row final choice, then the exact fallback rows.
+// kBias: router scores (pos_bias added); without it the oracle's scaled dot
+// products.
+template <int kD, bool kBias>
+cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
     const int Nq = a.Nq > 0 ? a.Nq : a.N;
     const size_t rq = (size_t)a.B * a.H * Nq, rk = (size_t)a.B * a.Hkv * a.N;
     char* w = static_cast<char*>(a.ws);
     __half* q16 = reinterpret_cast<__half*>(w);
-    w += al(rq * kR * 2);
+    w += al(rq * kD * 2);
     __half* k16 = reinterpret_cast<__half*>(w);
-    w += al(rk * kR * 2);
+    w += al(rk * kD * 2);
     float2* rowinfo = reinterpret_cast<float2*>(w);
     w += al(rq * sizeof(float2));
     uint32_t* stats = reinterpret_cast<uint32_t*>(w);
@@ -1671,11 +1744,13 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     float* wtab = reinterpret_cast<float*>(w);
     w += al((size_t)ndiag * kWinBytes);
     const bool wide = a.K > kNarrowMaxK;
+    const bool global_lists = wide || kD > 64;
+    const int cap = wide ? TcCfg<true>::kCap : TcCfg<false>::kCap;
     uint2* lists = nullptr;
     int* counts = nullptr;
-    if (wide) {
+    if (global_lists) {
         lists = reinterpret_cast<uint2*>(w);
-        w += al((size_t)a.B * a.H * nqb * kTileM * 2 * (size_t)TcCfg<true>::kCap * sizeof(uint2));
+        w += al((size_t)a.B * a.H * nqb * kTileM * 2 * (size_t)cap * sizeof(uint2));
         counts = reinterpret_cast<int*>(w);
     }
     int* counters = a.counters;  // [0] fallback rows, [1] status
@@ -1686,29 +1761,31 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     const int BG = a.B * a.Hkv;
     {
         dim3 grid((a.N + 255) / 256, BG);
-        kstats_kernel<<<grid, 256, 0, stream>>>(a.kp32, a.N, stats);
+        kstats_kernel<kD><<<grid, 256, 0, stream>>>(a.kp32, a.N, stats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-        bias_stats_kernel<<<8, 256, 0, stream>>>(a.bias, 2 * a.L, gstats);
+        if (kBias) {
+            bias_stats_kernel<<<8, 256, 0, stream>>>(a.bias, 2 * a.L, gstats);
+            if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        }
+        dim3 g2((unsigned)(((long long)a.N * (kD / 4) + 255) / 256), BG);
+        kconvert_kernel<kD><<<g2, 256, 0, stream>>>(a.kp32, k16, a.N, stats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-        dim3 g2((a.N * (kR / 4) + 255) / 256, BG);
-        kconvert_kernel<<<g2, 256, 0, stream>>>(a.kp32, k16, a.N, stats);
-        if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-        qprep_kernel<<<(unsigned)((rq * 8 + 255) / 256), 256, 0, stream>>>(a.qp32, q16, rowinfo, (long long)rq, a.H,
-                                                                      a.Hkv, Nq, a.scale, stats, gstats);
+        qprep_kernel<kD><<<(unsigned)((rq * 8 + 255) / 256), 256, 0, stream>>>(a.qp32, q16, rowinfo, (long long)rq,
+                                                                           a.H, a.Hkv, Nq, a.scale, stats, gstats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
         // offset of bias-line index 0: the window of tile (qb, key tile) starts at
         // i - j + L = q0 + kTileN * (qb - key tile) + 127 + L (its first column
         // against its last row)
         const long long o_max = (long long)a.q0 + (long long)kTileN * (nqb - 1) + (kTileN - 1) + a.L;
         const long long nb = (long long)ndiag * 4 * kWinCopy;
-        window_table_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, stream>>>(a.bias, a.L, a.causal, o_max, ndiag,
-                                                                             wtab);
+        window_table_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, stream>>>(kBias ? a.bias : nullptr, a.L,
+                                                                             a.causal, o_max, ndiag, wtab);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     }
     CUtensorMap tmA, tmB;
-    if (!make_row_map(&tmA, q16, rq) || !make_row_map(&tmB, k16, rk)) return cudaErrorInvalidValue;
-    const int smem_bytes = (int)(wide ? TcCfg<true>::kSmemBytes : TcCfg<false>::kSmemBytes);
-    e = cudaFuncSetAttribute(wide ? router_tc_kernel<true> : router_tc_kernel<false>,
+    if (!make_row_map(&tmA, q16, rq, kD) || !make_row_map(&tmB, k16, rk, kD)) return cudaErrorInvalidValue;
+    const int smem_bytes = (int)(wide ? TcCfg<true, kD>::kSmemBytes : TcCfg<false, kD>::kSmemBytes);
+    e = cudaFuncSetAttribute(wide ? router_tc_kernel<true, kD> : router_tc_kernel<false, kD>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     TcParams prm;
@@ -1731,18 +1808,20 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.causal = a.causal;
     prm.Nq = Nq;
     prm.q0 = a.q0;
-    prm.nqb = (Nq + kTileM - 1) / kTileM;
+    prm.nqb = nqb;
     prm.scale = a.scale;
-    const long long nblk = (long long)prm.nqb * a.B * a.H;
-    if (!wide) {
-        router_tc_kernel<false><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
+    const long long nblk = (long long)nqb * a.B * a.H;
+    if (!global_lists) {
+        router_tc_kernel<false, kD><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
         // rows sent to the exact selector (K + 32 candidates per warp: 4 entries per lane)
-        exact_rows_kernel<4><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0,
-                                                          a.K, a.scale, a.causal, counters, fb_list, a.out);
+        exact_rows_kernel<4, kD, kBias><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
+                                                                     Nq, a.q0, a.K, a.scale, a.causal, counters,
+                                                                     fb_list, a.out);
         return record(cudaGetLastError());
     }
-    router_tc_kernel<true><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
+    if (wide) router_tc_kernel<true, kD><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
+    else router_tc_kernel<false, kD><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     FinalParams fp;
     fp.lists = lists;
@@ -1762,15 +1841,86 @@ cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
     fp.K = a.K;
     fp.Nq = Nq;
     fp.q0 = a.q0;
-    fp.nqb = prm.nqb;
+    fp.nqb = nqb;
     fp.scale = a.scale;
     const unsigned fblk = (unsigned)std::min<long long>(((long long)rq + 7) / 8, 148LL * 8);
-    final_select_kernel<TcCfg<true>::kCap, kWideMaxK><<<fblk, 256, 0, stream>>>(fp);
+    if (wide) final_select_kernel<TcCfg<true>::kCap, kWideMaxK, kD, kBias><<<fblk, 256, 0, stream>>>(fp);
+    else final_select_kernel<TcCfg<false>::kCap, kNarrowMaxK, kD, kBias><<<fblk, 256, 0, stream>>>(fp);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     // rows sent to the exact selector (K + 32 candidates per warp: 6 entries per lane for K <= 160)
-    exact_rows_kernel<6><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0, a.K,
-                                                      a.scale, a.causal, counters, fb_list, a.out);
+    if (wide)
+        exact_rows_kernel<6, kD, kBias><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
+                                                                     Nq, a.q0, a.K, a.scale, a.causal, counters,
+                                                                     fb_list, a.out);
+    else
+        exact_rows_kernel<4, kD, kBias><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
+                                                                     Nq, a.q0, a.K, a.scale, a.causal, counters,
+                                                                     fb_list, a.out);
     return record(cudaGetLastError());
+}
+
+// bf16 rows -> fp32 rows (the oracle's canonical scores read fp32), 8 values per thread.
+__global__ void widen_bf16_kernel(const __nv_bfloat16* __restrict__ in, float* __restrict__ out, long long n8) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n8) return;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(in) + t);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        f[2 * u] = __uint_as_float(w[u] << 16);
+        f[2 * u + 1] = __uint_as_float(w[u] & 0xffff0000u);
+    }
+    float4* o = reinterpret_cast<float4*>(out) + 2 * t;
+    o[0] = make_float4(f[0], f[1], f[2], f[3]);
+    o[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+
+}  // namespace
+
+bool router_tc_supported(int r, int K) { return r == kR && K >= 1 && K <= kWideMaxK; }
+
+size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K) {
+    return tc_workspace_bytes(B, H, Hkv, Nq, N, K, kR);
+}
+
+cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) { return launch_tc<kR, true>(a, stream); }
+
+bool oracle_tc_supported(int D, int K) { return D == kOracleD && K >= 1 && K <= kWideMaxK; }
+
+size_t oracle_tc_workspace_bytes(int B, int H, int Hkv, int N, int K, int dtype) {
+    auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+    const size_t rq = (size_t)B * H * N, rk = (size_t)B * Hkv * N;
+    size_t total = al(tc_workspace_bytes(B, H, Hkv, N, N, K, kOracleD));
+    if (dtype != kF32) total += al(rq * kOracleD * 4) + al(rk * kOracleD * 4);
+    return total;
+}
+
+cudaError_t launch_oracle_tc(const OracleTcArgs& o, cudaStream_t stream) {
+    auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+    const size_t rq = (size_t)o.B * o.H * o.N, rk = (size_t)o.B * o.Hkv * o.N;
+    char* w = static_cast<char*>(o.ws);
+    const float* q32 = static_cast<const float*>(o.q);
+    const float* k32 = static_cast<const float*>(o.k);
+    char* tcws = w;
+    w += al(tc_workspace_bytes(o.B, o.H, o.Hkv, o.N, o.N, o.K, kOracleD));
+    if (o.dtype != kF32) {
+        float* qw = reinterpret_cast<float*>(w);
+        w += al(rq * kOracleD * 4);
+        float* kw = reinterpret_cast<float*>(w);
+        const long long nq8 = (long long)(rq * kOracleD / 8), nk8 = (long long)(rk * kOracleD / 8);
+        widen_bf16_kernel<<<(unsigned)((nq8 + 255) / 256), 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(o.q), qw, nq8);
+        cudaError_t e = record(cudaGetLastError());
+        if (e != cudaSuccess) return e;
+        widen_bf16_kernel<<<(unsigned)((nk8 + 255) / 256), 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(o.k), kw, nk8);
+        if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        q32 = qw;
+        k32 = kw;
+    }
+    RouterTcArgs a{q32, k32, nullptr, 1, o.B, o.H, o.Hkv, o.N, o.K, o.causal, o.scale, o.out, tcws, o.counters};
+    return launch_tc<kOracleD, false>(a, stream);
 }
 
 }  // namespace ossa

@@ -151,7 +151,12 @@ def router_scores(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.
 def oracle_topk(q: torch.Tensor, k: torch.Tensor, top_k: int, *, scale: float | None = None,
                 causal: bool = True) -> torch.Tensor:
     """Exact-dot selector (sparse_forward.py:194-202): top-K of (q . k) * scale,
-    fp32, no router.  Returns int32 (B, H, N, top_k)."""
+    fp32, no router.  Returns int32 (B, H, N, top_k).
+
+    At head_dim 128 and top_k <= 128 the selection runs on the tensor-core
+    selector (fp16 scores with a per-row error bound pick the candidates, fp32
+    scores decide them); the indices are the exact selector's bit for bit.
+    OSSA_ORACLE_SELECT=exact forces the CUDA-core exact selector."""
     B, H, Hkv, N, D = _check_qk(q, k)
     dev = _lib.require_cuda(q, k)
     if top_k < 0:
@@ -163,10 +168,14 @@ def oracle_topk(q: torch.Tensor, k: torch.Tensor, top_k: int, *, scale: float | 
     dt = _common_dtype(q, k)
     qc = _as_kernel_input(q, dt)
     kc = _as_kernel_input(k, dt)
+    L = _lib.lib()
+    code = _lib.dtype_code(qc)
+    ws_bytes = L.ossa_oracle_workspace_size(B, H, Hkv, N, D, int(top_k), code)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        st = _lib.lib().ossa_oracle_topk(qc.data_ptr(), kc.data_ptr(), _lib.dtype_code(qc), B, H, Hkv,
-                                         N, D, s, int(top_k), 1 if causal else 0, out.data_ptr(),
-                                         _lib.stream_ptr(dev))
+        st = L.ossa_oracle_topk_ws(qc.data_ptr(), kc.data_ptr(), code, B, H, Hkv, N, D, s, int(top_k),
+                                   1 if causal else 0, out.data_ptr(), ws.data_ptr(), ws_bytes,
+                                   _lib.stream_ptr(dev))
     _lib.check(st)
     return out
 

@@ -142,3 +142,13 @@ def test_oracle_topk_matches_torch_topk_random():
     s = torch.matmul(q, kr.transpose(-2, -1)) / math.sqrt(D)
     ref = torch.sort(s.topk(K, dim=-1).indices, dim=-1).values.numpy()
     assert np.array_equal(idx, ref.astype(np.int32))
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_oracle_topk_rows_matches_full_selection(causal):
+    """The row-subset oracle selector (used for full-size spot checks) returns
+    exactly the full selection's rows."""
+    q, k, _ = cases.qkv(1, 4, 2, 200, 128, seed=3, scale=1.0 / math.sqrt(128))
+    full = oracle.oracle_topk(q, k, 16, causal=causal).reshape(-1, 16)
+    rows = np.arange(0, 800, 7, dtype=np.int64)
+    assert (oracle.oracle_topk_rows(q, k, 16, rows, causal=causal) == full[rows]).all()
