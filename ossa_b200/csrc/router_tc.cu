@@ -571,12 +571,20 @@ __device__ __forceinline__ float2 score2(uint32_t acc0, uint32_t acc1, uint64_t 
 // chunk h + 1's accumulator columns (tcgen05.ld) and pos_bias terms (ld.shared
 // from wsrc upwards, x..w = columns c..c+3) are in flight while chunk h is
 // scored by fn(h, v, bw).
-// The accumulator is released on `tempty` once its last chunk has landed.
+// The accumulator and the window buffer are released on `tempty` after the last
+// chunk has been scored: the next MMA into this accumulator and the bulk copy of
+// the next window into this buffer start as soon as `tempty` completes.  Every
+// accumulator and window word of the half tile is OR-ed into `dep`, the warp
+// reduces it (each lane waits for its own loads) and the arrive's address depends
+// on the result, so no read of this tile can still be in flight at the release.
+// (A release issued before the last chunk was scored let the next tile's MMA
+// and window copy land under the last chunk's reads on B200.)
 template <typename Fn>
 __device__ __forceinline__ void score_half_tile(uint32_t taddr, uint32_t wsrc, uint64_t* tempty, int lane, Fn&& fn) {
     constexpr int kC = 16, kNC = kHalfCols / kC;
     uint32_t v[2][kC];
     float4 bw[2][kC / 4];
+    uint32_t dep = 0u;
     tmem_ld16(taddr, v[0]);
 #pragma unroll
     for (int q = 0; q < kC / 4; ++q) bw[0][q] = lds_f4(wsrc + 16u * (uint32_t)q);
@@ -588,13 +596,18 @@ __device__ __forceinline__ void score_half_tile(uint32_t taddr, uint32_t wsrc, u
             tmem_ld16(taddr + (uint32_t)(kC * (h + 1)), v[(h + 1) & 1]);
 #pragma unroll
             for (int q = 0; q < kC / 4; ++q) bw[(h + 1) & 1][q] = lds_f4(wsrc + 4u * (uint32_t)(kC * (h + 1) + 4 * q));
-        } else {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty);
         }
         fn(h, v[h & 1], bw[h & 1]);
+#pragma unroll
+        for (int q = 0; q < kC / 4; ++q) {
+            const float4 b = bw[h & 1][q];
+            dep |= ((__float_as_uint(b.x) | __float_as_uint(b.y)) | (__float_as_uint(b.z) | __float_as_uint(b.w))) |
+                   ((v[h & 1][4 * q] | v[h & 1][4 * q + 1]) | (v[h & 1][4 * q + 2] | v[h & 1][4 * q + 3]));
+        }
     }
+    tc_fence_before();
+    dep = __reduce_or_sync(kFull, dep);
+    if (lane == 0) mbar_arrive_after(tempty, dep);
 }
 
 template <bool kWide, int kD = 64>

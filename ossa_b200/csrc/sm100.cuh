@@ -94,6 +94,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Arrive once `dep` is available: the barrier address is computed from it (its
+// value does not change the address), so the arrive cannot issue before the
+// loads that produced `dep` have returned.
+__device__ __forceinline__ void mbar_arrive_after(uint64_t* bar, uint32_t dep) {
+    asm volatile(
+        "{\n .reg .b32 z;\n and.b32 z, %1, 0;\n add.u32 z, z, %0;\n"
+        " mbarrier.arrive.shared::cta.b64 _, [z];\n}" ::"r"(smem_u32(bar)), "r"(dep)
+        : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
