@@ -29,7 +29,7 @@ import os
 
 import torch
 
-from ..select import oracle_topk
+from ..select import oracle_topk, oracle_topk_with_status
 from ..topk_attention import topk_attention
 
 
@@ -68,6 +68,7 @@ def main(argv=None) -> None:
         for _ in range(max(1, args.warmup)):
             idx = oracle_topk(q, k, K)
             out = topk_attention(q, k, v, topk_indices=idx)
+        _, fallback_rows, status = oracle_topk_with_status(q, k, K)
         torch.cuda.synchronize()
         for e in ev:
             e[0].record(stream)
@@ -92,6 +93,7 @@ def main(argv=None) -> None:
         "select_ms": sel, "gather_ms": gat, "steps": args.steps, "warmup": args.warmup,
         "selector": "exact CUDA-core" if args.exact else "tensor-core (exact indices)",
         "equal_to_exact": equal, "output_finite": bool(torch.isfinite(out).all()),
+        "fallback_rows": fallback_rows, "status": status,
         "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "oracle top-K attention, unit-normal q/k plus a shared rank-8 component",
                    "batch": B, "heads": H, "kv_heads": Hkv, "seq_len": N, "head_dim": D, "top_k": K},

@@ -113,7 +113,9 @@ struct TcCfg {
     static constexpr bool kClsHalf = kWide && kD > 64;      // class maxima as fp16
     static constexpr int kTileB = kTileM * kD * 2;          // bytes of one q' or k' tile
     static constexpr int kStages = kD > 64 ? 3 : (kWide ? 4 : 2);  // k' tile ring
-    static constexpr int kCap = kWide ? 160 : 80;  // sub-list capacity per row and column half
+    // sub-list capacity per row and column half (global lists for kD = 128 take
+    // more room than the shared-memory lists of the narrow kD = 64 variant)
+    static constexpr int kCap = kWide ? 160 : (kD > 64 ? 96 : 80);
     static constexpr int kLimit = kCap - 16;       // past this after a 16-column step: exact fallback
     // shared-memory lists (narrow, kD = 64): kRowStride uint2 per row (both
     // sub-lists and a spare entry for the row's bound and counts; the odd stride
@@ -1523,7 +1525,7 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                 for (int e = 0; e < kEPL; ++e) u[e] = order_key(sv[e]);
                 uint32_t T;
                 int ties;
-                warp_kth_key<kEPL>(u, val, K, T, ties);
+                warp_kth_key_search<kEPL>(u, val, K, T, ties);
                 unsigned nge = 0;
                 uint32_t below = 0u;  // order keys of finite scores are never 0
 #pragma unroll
@@ -1573,7 +1575,7 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                                        : 0u;
                     uint32_t Te;
                     int ties;
-                    warp_kth_key<kEPL>(ek, val, K, Te, ties);
+                    warp_kth_key_search<kEPL>(ek, val, K, Te, ties);
                     // the K best are {ek > Te} plus the `ties` lowest keys with ek == Te
                     bool taken[kEPL];
 #pragma unroll
@@ -1633,36 +1635,52 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                 int* SA = skept[warp][0];
                 int* SB = skept[warp][1];
                 int na = 0, nbk = 0;
-                int li[kEPL];
 #pragma unroll
                 for (int e = 0; e < kEPL; ++e) {
                     const bool isA = lane + 32 * e < ca;
                     const bool kA = keep[e] && isA, kB = keep[e] && !isA;
                     const unsigned balA = __ballot_sync(kFull, kA);
                     const unsigned balB = __ballot_sync(kFull, kB);
-                    li[e] = isA ? na + __popc(balA & lt) : nbk + __popc(balB & lt);
-                    if (kA && li[e] < kMaxOut) SA[li[e]] = (int)jv[e];
-                    if (kB && li[e] < kMaxOut) SB[li[e]] = (int)jv[e];
+                    const int li = isA ? na + __popc(balA & lt) : nbk + __popc(balB & lt);
+                    if (kA && li < kMaxOut) SA[li] = (int)jv[e];
+                    if (kB && li < kMaxOut) SB[li] = (int)jv[e];
                     na += __popc(balA);
                     nbk += __popc(balB);
                 }
+                na = min(na, kMaxOut);
+                nbk = min(nbk, kMaxOut);
                 __syncwarp();
-                int32_t* orow = p.out + row * K;
+                // merge path: lane l writes output positions 4l .. 4l+3 (kMaxOut <= 128);
+                // the split of position 4l between the two ascending lists by binary
+                // search, then four merge steps
+                const int n = na + nbk;
+                const int p0 = 4 * lane;
+                int outv[4] = {-1, -1, -1, -1};
+                if (p0 < n) {
+                    int lo = max(0, p0 - nbk), hi = min(p0, na);
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        if (SA[mid] < SB[p0 - 1 - mid]) lo = mid + 1; else hi = mid;
+                    }
+                    int ia = lo, ib = p0 - lo;
 #pragma unroll
-                for (int e = 0; e < kEPL; ++e) {
-                    if (keep[e]) {
-                        const bool isA = lane + 32 * e < ca;
-                        const int* other = isA ? SB : SA;
-                        int lo = 0, hi = min(isA ? nbk : na, kMaxOut);
-                        while (lo < hi) {  // keys of the other list below this one
-                            const int mid = (lo + hi) >> 1;
-                            if (other[mid] < (int)jv[e]) lo = mid + 1; else hi = mid;
+                    for (int s2 = 0; s2 < 4; ++s2) {
+                        if (p0 + s2 < n) {
+                            const bool takeA = ib >= nbk || (ia < na && SA[ia] < SB[ib]);
+                            outv[s2] = takeA ? SA[ia] : SB[ib];
+                            ia += takeA ? 1 : 0;
+                            ib += takeA ? 0 : 1;
                         }
-                        const int pos = li[e] + lo;
-                        if (pos < K) orow[pos] = (int32_t)jv[e];
                     }
                 }
-                for (int q = na + nbk + lane; q < K; q += 32) orow[q] = -1;
+                int32_t* orow = p.out + row * K;
+                if ((K & 3) == 0) {
+                    if (p0 < K) *reinterpret_cast<int4*>(orow + p0) = make_int4(outv[0], outv[1], outv[2], outv[3]);
+                } else {
+#pragma unroll
+                    for (int s2 = 0; s2 < 4; ++s2)
+                        if (p0 + s2 < K) orow[p0 + s2] = outv[s2];
+                }
                 __syncwarp();  // skept is rewritten for the next row
             }
         }
@@ -1725,7 +1743,7 @@ size_t tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K, int kD) {
     const bool wide = K > kNarrowMaxK;
     if (wide || kD > 64) {
         const size_t lrows = (size_t)B * H * nqb * kTileM;
-        const int cap = wide ? TcCfg<true>::kCap : TcCfg<false>::kCap;
+        const int cap = wide ? TcCfg<true>::kCap : (kD > 64 ? TcCfg<false, 128>::kCap : TcCfg<false, 64>::kCap);
         total += al(lrows * 2 * (size_t)cap * sizeof(uint2)) + al(rq * 2 * sizeof(int));
     }
     return total;
@@ -1758,7 +1776,7 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     w += al((size_t)ndiag * kWinBytes);
     const bool wide = a.K > kNarrowMaxK;
     const bool global_lists = wide || kD > 64;
-    const int cap = wide ? TcCfg<true>::kCap : TcCfg<false>::kCap;
+    const int cap = wide ? TcCfg<true, kD>::kCap : TcCfg<false, kD>::kCap;
     uint2* lists = nullptr;
     int* counts = nullptr;
     if (global_lists) {
@@ -1857,8 +1875,8 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     fp.nqb = nqb;
     fp.scale = a.scale;
     const unsigned fblk = (unsigned)std::min<long long>(((long long)rq + 7) / 8, 148LL * 8);
-    if (wide) final_select_kernel<TcCfg<true>::kCap, kWideMaxK, kD, kBias><<<fblk, 256, 0, stream>>>(fp);
-    else final_select_kernel<TcCfg<false>::kCap, kNarrowMaxK, kD, kBias><<<fblk, 256, 0, stream>>>(fp);
+    if (wide) final_select_kernel<TcCfg<true, kD>::kCap, kWideMaxK, kD, kBias><<<fblk, 256, 0, stream>>>(fp);
+    else final_select_kernel<TcCfg<false, kD>::kCap, kNarrowMaxK, kD, kBias><<<fblk, 256, 0, stream>>>(fp);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     // rows sent to the exact selector (K + 32 candidates per warp: 6 entries per lane for K <= 160)
     if (wide)

@@ -72,6 +72,67 @@ __device__ __forceinline__ void warp_kth_key(const uint32_t (&u)[EPL], const boo
     ties = kk;
 }
 
+// The same result as warp_kth_key (T = the K-th largest valid key, `ties` = how
+// many entries equal to T belong to the K largest), found by searching the key
+// range instead of walking its bits.  The bracket [lo, hi) keeps
+// count(u >= lo) >= K > count(u >= hi); probes alternate between linear
+// interpolation of that count (a few probes on spread-out scores) and bisection
+// (at most 32 more probes on any input).  The search ends when count(u >= lo) is
+// exactly K, so the K largest are {u >= lo} and T is their minimum, or when the
+// bracket is one key wide, so T = lo.  Requires more than K valid entries.
+template <int EPL>
+__device__ __forceinline__ void warp_kth_key_search(const uint32_t (&u)[EPL], const bool (&val)[EPL], int K,
+                                                    uint32_t& T, int& ties) {
+    uint32_t mx = 0u, mn = 0xffffffffu;
+    unsigned nvalid = 0;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        if (val[e]) {
+            mx = max(mx, u[e]);
+            mn = min(mn, u[e]);
+            ++nvalid;
+        }
+    }
+    mx = __reduce_max_sync(kFull, mx);
+    mn = __reduce_min_sync(kFull, mn);
+    int clo = (int)__reduce_add_sync(kFull, nvalid);
+    uint64_t lo = mn, hi = (uint64_t)mx + 1u;  // count(u >= hi) = 0
+    int chi = 0;
+#pragma unroll 1
+    for (int it = 0; clo != K && hi - lo > 1u && it < 80; ++it) {
+        uint64_t pr;
+        if (it & 1) {
+            pr = lo + ((hi - lo) >> 1);
+        } else {
+            const float f = ((float)(clo - K) + 0.5f) / (float)(clo - chi);
+            pr = lo + (uint64_t)((double)f * (double)(hi - lo));
+            pr = pr <= lo ? lo + 1u : (pr >= hi ? hi - 1u : pr);
+        }
+        const uint32_t p32 = (uint32_t)pr;
+        unsigned c = 0;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) c += (val[e] && u[e] >= p32) ? 1u : 0u;
+        const int cc = (int)__reduce_add_sync(kFull, c);
+        if (cc >= K) {
+            lo = pr;
+            clo = cc;
+        } else {
+            hi = pr;
+            chi = cc;
+        }
+    }
+    const uint32_t lo32 = (uint32_t)lo;
+    uint32_t t = 0xffffffffu;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e)
+        if (val[e] && u[e] >= lo32) t = min(t, u[e]);
+    T = __reduce_min_sync(kFull, t);
+    unsigned gt = 0;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) gt += (val[e] && u[e] > T) ? 1u : 0u;
+    ties = K - (int)__reduce_add_sync(kFull, gt);
+}
+
 // keep[e] = the entry is among the K largest (see warp_kth_key's tie rule).
 template <int EPL>
 __device__ __forceinline__ void warp_topk_mask(const uint32_t (&u)[EPL], const bool (&val)[EPL], int K,

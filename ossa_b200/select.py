@@ -149,7 +149,7 @@ def router_scores(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.
 
 
 def oracle_topk(q: torch.Tensor, k: torch.Tensor, top_k: int, *, scale: float | None = None,
-                causal: bool = True) -> torch.Tensor:
+                causal: bool = True, with_status: bool = False):
     """Exact-dot selector (sparse_forward.py:194-202): top-K of (q . k) * scale,
     fp32, no router.  Returns int32 (B, H, N, top_k).
 
@@ -163,7 +163,7 @@ def oracle_topk(q: torch.Tensor, k: torch.Tensor, top_k: int, *, scale: float | 
         raise ValueError(f"top_k must be >= 0, got {top_k}")
     out = torch.empty((B, H, N, top_k), dtype=torch.int32, device=dev)
     if out.numel() == 0:
-        return out
+        return (out, 0, 0) if with_status else out
     s = float(1.0 / math.sqrt(D)) if scale is None else float(scale)
     dt = _common_dtype(q, k)
     qc = _as_kernel_input(q, dt)
@@ -177,7 +177,20 @@ def oracle_topk(q: torch.Tensor, k: torch.Tensor, top_k: int, *, scale: float | 
                                    1 if causal else 0, out.data_ptr(), ws.data_ptr(), ws_bytes,
                                    _lib.stream_ptr(dev))
     _lib.check(st)
+    if with_status:
+        fb, status = ctypes.c_int(0), ctypes.c_int(0)
+        with torch.cuda.device(dev):
+            _lib.check(L.ossa_router_status(ws.data_ptr(), ctypes.byref(fb), ctypes.byref(status)))
+        return out, fb.value, status.value
     return out
+
+
+def oracle_topk_with_status(q: torch.Tensor, k: torch.Tensor, top_k: int, *, scale: float | None = None,
+                            causal: bool = True):
+    """oracle_topk plus (rows sent to the full-row exact fallback, device status
+    word), read back synchronously; a nonzero status means a bounded device wait
+    expired and the indices are not valid."""
+    return oracle_topk(q, k, top_k, scale=scale, causal=causal, with_status=True)
 
 
 def with_diagonal(idx: torch.Tensor) -> torch.Tensor:
