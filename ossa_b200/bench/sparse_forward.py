@@ -126,26 +126,34 @@ def _patch_layer(model, plan: PatchPlan):
     return restore
 
 
-def _load_router(checkpoint: Path, model, layer: int, seq_len: int):
+def _load_router(checkpoint: Path, model, layer: int, seq_len: int, *, pos_bias: str = "exact"):
     """Loads a ContentRouter checkpoint ({"state_dict", "cfg"}, the reference's
     format, bench/content_train.py:172-175) sized for ``seq_len`` as the reference
-    does (sparse_forward.py:272-294).  The position table of a checkpoint trained
-    at another seq_len does not fit, exactly as in the reference."""
+    does (sparse_forward.py:272-294).  With ``pos_bias="exact"`` (the reference's
+    behaviour) a checkpoint trained at another seq_len does not fit.  With
+    ``pos_bias="extend"`` (additive) the router is built at its trained seq_len
+    and resized with ``ContentRouter.with_seq_len``: its scores at any offset
+    equal the trained router's clamped ones."""
+    if pos_bias not in ("exact", "extend"):
+        raise ValueError(f"pos_bias must be 'exact' or 'extend', got {pos_bias!r}")
     state = torch.load(checkpoint, map_location=next(model.parameters()).device, weights_only=False)
     cfg_dict = state["cfg"]
     state_dict = state["state_dict"]
     if not any(key.startswith("q_proj") or key.startswith("k_proj") for key in state_dict):
         raise TypeError("only ContentRouter checkpoints are supported (PerLayerRouter is out of scope)")
     layer_module = model.model.layers[layer].self_attn
+    trained = state_dict["pos_bias.weight"].shape[0] // 2
     cfg = ContentRouterConfig(
         head_dim=layer_module.head_dim,
         n_heads=layer_module.config.num_attention_heads,
-        seq_len=seq_len,
+        seq_len=trained if pos_bias == "extend" else seq_len,
         proj_dim=cfg_dict.get("proj_dim", 64),
     )
     router = ContentRouter(cfg).to(next(model.parameters()).device)
     router.load_state_dict(state_dict)
     router.eval()
+    if pos_bias == "extend" and trained != seq_len:
+        router = router.with_seq_len(seq_len).eval()
     return router
 
 

@@ -53,6 +53,30 @@ class ContentRouter(nn.Module):
     def _params(self):
         return self.q_proj[0].weight, self.k_proj[0].weight, self.pos_bias.weight
 
+    def with_seq_len(self, seq_len: int) -> "ContentRouter":
+        """A copy sized for ``seq_len`` that scores every (i, j) exactly as this
+        router does.  Additive: the reference sizes pos_bias as 2*seq_len and
+        leaves longer contexts to retraining (README "Long context").  This
+        router already clamps offsets i - j beyond +-seq_len to the table's edge
+        entries (router.py:183-188), so the copy's table holds entry
+        clamp(o - seq_len + S, 0, 2S - 1) of this one (S = this router's
+        seq_len) at index o: the edge entries repeat outward when growing, and
+        offsets within +-min(S, seq_len) keep their entries when shrinking.
+        Projection weights are shared values (copied)."""
+        if seq_len <= 0:
+            raise ValueError(f"seq_len must be positive, got {seq_len}")
+        S = self.cfg.seq_len
+        cfg = ContentRouterConfig(head_dim=self.cfg.head_dim, n_heads=self.cfg.n_heads, seq_len=seq_len,
+                                  proj_dim=self.cfg.proj_dim, layers=self.cfg.layers)
+        dev = self.pos_bias.weight.device
+        out = ContentRouter(cfg).to(dev)
+        with torch.no_grad():
+            out.q_proj[0].weight.copy_(self.q_proj[0].weight)
+            out.k_proj[0].weight.copy_(self.k_proj[0].weight)
+            src = (torch.arange(2 * seq_len, device=dev) - seq_len + S).clamp_(0, 2 * S - 1)
+            out.pos_bias.weight.copy_(self.pos_bias.weight[src])
+        return out.train(self.training)
+
     def score(self, q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
         """q: (B, H, N, D), k: (B, H or Hkv, N, D) -> (B, H, N, N) fp32 logits."""
         wq, wk, pb = self._params()

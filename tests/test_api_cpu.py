@@ -158,3 +158,50 @@ def test_full_model_runner_config_and_routers():
         assert a[li].pos_bias.weight.shape == (2 * 4096, 1)
         assert torch.equal(wq, b[li].q_proj[0].weight.detach())
     assert not torch.equal(a[0].q_proj[0].weight, a[1].q_proj[0].weight)
+
+
+def test_router_with_seq_len_scores_like_the_clamped_table(golden_dir, tmp_path):
+    """A router resized from its trained seq_len (512, the reference checkpoint)
+    to 1024 scores every (i, j) of a 1024-token input exactly as the trained
+    table does under the reference's clamped indexing; shrinking keeps every
+    in-range offset.  _load_router(pos_bias="extend") loads that way."""
+    import types
+
+    import cases
+    import oracle
+    from ossa_b200.bench.sparse_forward import _load_router
+
+    z = np.load(golden_dir / "router_ckpt_c1.npz")
+    r = ContentRouter(ContentRouterConfig(head_dim=128, n_heads=12, seq_len=512, proj_dim=64))
+    r.load_state_dict({"q_proj.0.weight": torch.from_numpy(z["wq"]), "k_proj.0.weight": torch.from_numpy(z["wk"]),
+                       "pos_bias.weight": torch.from_numpy(z["pos_bias"])})
+    q, k, _ = cases.qkv(1, 2, 1, 1024, 128, seed=11)
+    wq, wk, pb = (t.detach() for t in r._params())
+    ref = oracle.router_scores(q, k, wq, wk, pb, 512)
+    big = r.with_seq_len(1024)
+    assert big.pos_bias.weight.shape == (2048, 1)
+    got = oracle.router_scores(q, k, *(t.detach() for t in big._params()), 1024)
+    assert np.array_equal(got, ref)
+    small = r.with_seq_len(200)
+    qs, ks = q[:, :, :200], k[:, :, :200]
+    assert np.array_equal(oracle.router_scores(qs, ks, *(t.detach() for t in small._params()), 200),
+                          oracle.router_scores(qs, ks, wq, wk, pb, 512))
+
+    class Attn(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.head_dim = 128
+            self.config = types.SimpleNamespace(num_attention_heads=12)
+            self.w = torch.nn.Parameter(torch.zeros(1))
+
+    model = torch.nn.Module()
+    model.model = torch.nn.Module()
+    model.model.layers = torch.nn.ModuleList([torch.nn.Module()])
+    model.model.layers[0].self_attn = Attn()
+    ckpt = tmp_path / "router.pt"
+    torch.save({"cfg": {"proj_dim": 64}, "state_dict": r.state_dict()}, ckpt)
+    with pytest.raises(RuntimeError):
+        _load_router(ckpt, model, 0, 1024)  # the reference's behaviour: the table does not fit
+    loaded = _load_router(ckpt, model, 0, 1024, pos_bias="extend")
+    assert torch.equal(loaded.pos_bias.weight, big.pos_bias.weight)
+    assert not loaded.training
