@@ -64,12 +64,22 @@ int check_heads(int B, int H, int Hkv, int N) {
     return OSSA_OK;
 }
 
-// Workspace: [counters 256 B][q' fp32][k' fp32][tensor-core selection scratch].
-// The counters block (fallback row count, status word) sits at offset 0 so
-// ossa_router_status can find it for any shape.
+// Workspace: [counters 256 B][q' fp32][k' fp32][tensor-core selection scratch]
+// [split selection scratch (few query rows only)].  The counters block
+// (fallback row count, status word) sits at offset 0 so ossa_router_status can
+// find it for any shape.
 struct RouterLayout {
-    size_t qp_off, kp_off, tc_off, total;
+    size_t qp_off, kp_off, tc_off, split_off, total;
 };
+
+// Fewer query rows than one tensor-core tile against more keys than one split
+// range: the split selector (select_split.cu) instead of the CTA-per-128-rows
+// one, which would give each row a single thread.
+constexpr long long kSplitMaxRows = 128;
+constexpr int kSplitMinKeys = 2048;
+bool split_shape(int B, int H, int Nq, int Nk) {
+    return (long long)B * H * Nq < kSplitMaxRows && Nk >= kSplitMinKeys;
+}
 
 constexpr size_t kCountersBytes = 256;
 
@@ -82,13 +92,17 @@ RouterLayout router_layout(int B, int H, int Hkv, int Nq, int Nk, int r, int K) 
     l.qp_off = kCountersBytes;
     l.kp_off = l.qp_off + align_up(qp);
     l.tc_off = l.kp_off + align_up(kp);
-    l.total = l.tc_off + (r == 64 ? align_up(ossa::router_tc_workspace_bytes(B, H, Hkv, Nq, Nk, K)) : 0);
+    l.split_off = l.tc_off + (r == 64 ? align_up(ossa::router_tc_workspace_bytes(B, H, Hkv, Nq, Nk, K)) : 0);
+    l.total = l.split_off + (K > 0 && split_shape(B, H, Nq, Nk)
+                                 ? align_up(ossa::split_select_workspace_bytes((long long)B * H * Nq, Nk, K))
+                                 : 0);
     return l;
 }
 
 // The tensor-core selector serves r = 64, K <= 128 and at least one full tile of
 // query and key rows; OSSA_ROUTER_SELECT=exact forces the CUDA-core exact selector
-// (both produce identical indices; the switch exists to cross-check them).
+// of score_topk.cu in place of it and of the split selector (all produce identical
+// indices; the switch exists to cross-check them).
 bool use_tensor_core_select(int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
     const char* env = getenv("OSSA_ROUTER_SELECT");
     if (env && env[0] == 'e') return false;
@@ -248,6 +262,13 @@ int ossa_router_topk_rows(const void* q, const void* k, int dtype, const float* 
         a.Nq = Nq;
         a.q0 = q_start;
         return cuda_status(ossa::launch_router_tc(a, s), "tensor-core router top-K launch");
+    }
+    const char* env = getenv("OSSA_ROUTER_SELECT");
+    if (split_shape(B, H, Nq, Nk) && !(env && env[0] == 'e')) {
+        const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K);
+        ossa::SplitSelectArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, Nk, r, K, scale, causal ? 1 : 0,
+                                idx_out, Nq, q_start, static_cast<char*>(workspace) + l.split_off};
+        return cuda_status(ossa::launch_split_select(a, s), "split router top-K launch");
     }
     ossa::ScoreTopkArgs a{qp, kp, ossa::kF32, pos_bias, seq_len_cfg, B, H, Hkv, Nk, r, K, scale,
                           causal ? 1 : 0, idx_out};

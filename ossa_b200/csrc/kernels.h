@@ -60,6 +60,27 @@ struct ScoreTopkArgs {
 cudaError_t launch_score_topk(const ScoreTopkArgs& a, cudaStream_t stream);
 bool score_topk_supported(int R, int K);
 
+// The same exact selection for a few query rows against many keys (decode):
+// one warp per (row, range of keys), then one warp per row over the ranges'
+// winners.  qrows (B*H*Nq, R), krows (B*Hkv*N, R) fp32; ws holds
+// split_select_workspace_bytes(B*H*Nq, N, K).
+struct SplitSelectArgs {
+    const float* qrows;
+    const float* krows;
+    const float* bias;  // nullptr: no position term
+    int L;
+    int B, H, Hkv, N, R, K;
+    float scale;
+    int causal;
+    int32_t* out;  // (B*H*Nq, K)
+    int Nq;        // query rows per (b, h)
+    int q0;        // position of query row 0 in the key sequence
+    void* ws;
+};
+bool split_select_supported(int R, int K);
+size_t split_select_workspace_bytes(long long rows, int N, int K);
+cudaError_t launch_split_select(const SplitSelectArgs& a, cudaStream_t stream);
+
 // Dense fp32 scores (B, H, N, N) with the same score definition, no mask.
 struct ScoreDenseArgs {
     const float* qrows;

@@ -73,3 +73,46 @@ def test_rows_argument_checks():
         topk_attention(q, k, k, topk_indices=idx)  # row counts differ without q_start
     with pytest.raises(OssaError):
         topk_attention(q, k[:, :, :0], k[:, :, :0], topk_indices=idx, q_start=0)
+
+
+@pytest.mark.parametrize("r,K", [(64, 64), (64, 128), (32, 100), (64, 160), (128, 16)])
+@pytest.mark.parametrize("nq,where", [(1, "end"), (3, "end"), (1, "middle"), (2, "start")])
+@pytest.mark.parametrize("causal", [True, False])
+def test_decode_rows_split_selector(r, K, nq, where, causal):
+    """Few query rows against a long key sequence (decode): the split selector
+    (one warp per row and 1024-key range, then a merge over the ranges) gives
+    exactly the oracle's rows and the CTA selector's."""
+    import os
+
+    B, H, Hkv, N, D, L = 2, 6, 2, 5000, 128, 4096
+    q, k, _, wq, wk, pb = _inputs(B, H, Hkv, N, D, r, L, seed=r + K + nq)
+    q0 = {"end": N - nq, "middle": 2047, "start": 0}[where]
+    qd = q[:, :, q0:q0 + nq].contiguous().to(DEV)
+    args = (k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K)
+    got = router_topk(qd, *args, causal=causal, q_start=q0)
+    os.environ["OSSA_ROUTER_SELECT"] = "exact"
+    try:
+        cta = router_topk(qd, *args, causal=causal, q_start=q0)
+    finally:
+        del os.environ["OSSA_ROUTER_SELECT"]
+    assert torch.equal(got, cta)
+    rows = np.array([(bh * N + i) for bh in range(B * H) for i in range(q0, q0 + nq)])
+    ref = oracle.router_topk_rows(q, k, wq, wk, pb, L, K, rows, causal=causal)
+    np.testing.assert_array_equal(got.cpu().numpy().reshape(-1, K), ref)
+
+
+def test_decode_split_selector_ties_across_ranges():
+    """Equal keys on both sides of a 1024-key range boundary: the tie goes to the
+    lower key index across ranges, as in the oracle."""
+    B, H, Hkv, N, D, r, L, K = 1, 4, 1, 3000, 128, 64, 3000, 64
+    q, k, _, wq, wk, pb = _inputs(B, H, Hkv, N, D, r, L, seed=3)
+    pb = torch.zeros_like(pb)
+    q0, nq = N - 2, 2
+    # copies of the first row's best key, 81 equal scores straddling the boundary at 1024
+    best = int(oracle.router_topk_rows(q, k, wq, wk, pb, L, 1, np.array([q0]))[0, 0])
+    k[0, 0, 990:1070] = k[0, 0, best]
+    got = router_topk(q[:, :, q0:].contiguous().to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K,
+                      q_start=q0)
+    rows = np.array([(bh * N + i) for bh in range(B * H) for i in range(q0, q0 + nq)])
+    ref = oracle.router_topk_rows(q, k, wq, wk, pb, L, K, rows)
+    np.testing.assert_array_equal(got.cpu().numpy().reshape(-1, K), ref)
