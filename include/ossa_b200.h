@@ -202,6 +202,22 @@ OSSA_API int ossa_router_topk_rows(const void* q, const void* k, int dtype,
                                    void* workspace, size_t workspace_bytes,
                                    ossa_stream_t stream);
 
+/*
+ * Rotary position embedding fused with the head transpose of the patched
+ * layer (ossa/bench/sparse_forward.py:166-178: the q/k/v projections viewed as
+ * (B, Hx, N, D), then Qwen2's apply_rotary_pos_emb on q and k).  Additive, for
+ * the fused pre-processing of the patched layer:
+ *   x   (B, N, Hx, D)  the linear projection's output rows
+ *   cos, sin (1 or B, N, D) (cs_batched = 1 when they carry the batch), or both NULL
+ *   out (B, Hx, N, D) = x*cos + rotate_half(x)*sin, rotate_half = cat(-x2, x1),
+ *       each product and the sum rounded to the dtype as the eager ops round
+ *       them (bit-identical to the PyTorch expression); without cos/sin a
+ *       plain layout copy.
+ * dtype OSSA_F32 or OSSA_BF16; D a multiple of 8; pointers 16-byte aligned.
+ */
+OSSA_API int ossa_rope_to_heads(const void* x, const void* cos, const void* sin, int cs_batched, int dtype,
+                                int B, int N, int Hx, int D, void* out, ossa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,6 +39,7 @@ EXPORTED = (
     "ossa_router_topk_rows",
     "ossa_oracle_workspace_size",
     "ossa_oracle_topk_ws",
+    "ossa_rope_to_heads",
 )
 
 _lock = threading.Lock()
@@ -85,6 +86,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ossa_oracle_workspace_size.restype = sz
     lib.ossa_oracle_topk_ws.argtypes = [vp, vp, ci, ci, ci, ci, ci, ci, cf, ci, ci, vp, vp, sz, vp]
     lib.ossa_oracle_topk_ws.restype = ci
+    lib.ossa_rope_to_heads.argtypes = [vp, vp, vp, ci, ci, ci, ci, ci, ci, vp, vp]
+    lib.ossa_rope_to_heads.restype = ci
 
 
 def lib() -> ctypes.CDLL:

@@ -13,7 +13,10 @@ modules, then:
 * ``impl="mask"`` keeps the reference's mask-path semantics (top-K set plus the
   forced diagonal, :209-222) but evaluates them on the same O(N*K) kernel by
   appending the diagonal to each index row instead of a dense N x N softmax;
-* o_proj and the ``(out, None)`` return as the reference.
+* o_proj and the ``(out, None)`` return as the reference;
+* (additive) RoPE and the head transpose of q/k/v run as one kernel pass per
+  tensor (``rope_to_heads``), bit-identical to ``apply_rotary_pos_emb`` plus the
+  layout copies.
 
 Deliberate difference: the reference casts router logits to the model dtype
 before ``torch.topk`` (:193), which ties ~15% of rows at the K-th boundary in
@@ -31,6 +34,7 @@ from typing import Optional
 import torch
 
 from .. import select
+from ..rope import rope_to_heads
 from ..router import ContentRouter, ContentRouterConfig
 from ..topk_attention import topk_attention
 
@@ -82,8 +86,6 @@ def _patch_layer(model, plan: PatchPlan):
     if plan.mode == "dense" or not plan.layers:
         return lambda: None
 
-    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
-
     restores: list = []
     for layer_idx in plan.layers:
         layer_module = model.model.layers[layer_idx].self_attn
@@ -99,13 +101,12 @@ def _patch_layer(model, plan: PatchPlan):
                 n_heads = layer_module.config.num_attention_heads
                 n_kv_heads = layer_module.config.num_key_value_heads
 
-                q = layer_module.q_proj(hidden_states).view(B, N, n_heads, head_dim).transpose(1, 2)
-                k = layer_module.k_proj(hidden_states).view(B, N, n_kv_heads, head_dim).transpose(1, 2)
-                v = layer_module.v_proj(hidden_states).view(B, N, n_kv_heads, head_dim).transpose(1, 2)
-                if position_embeddings is not None:
-                    cos, sin = position_embeddings
-                    q, k = apply_rotary_pos_emb(q, k, cos, sin)
-                q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+                # projections, then RoPE and the (B, heads, N, D) layout in one kernel
+                # pass per tensor (bit-identical to apply_rotary_pos_emb + contiguous)
+                cos, sin = position_embeddings if position_embeddings is not None else (None, None)
+                q = rope_to_heads(layer_module.q_proj(hidden_states), n_heads, cos, sin)
+                k = rope_to_heads(layer_module.k_proj(hidden_states), n_kv_heads, cos, sin)
+                v = rope_to_heads(layer_module.v_proj(hidden_states), n_kv_heads)
 
                 with torch.no_grad():
                     idx = select_indices(plan, captured_idx, q, k)

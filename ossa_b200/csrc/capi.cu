@@ -322,6 +322,19 @@ int ossa_oracle_topk(const void* q, const void* k, int dtype, int B, int H, int 
                        "oracle top-K launch");
 }
 
+int ossa_rope_to_heads(const void* x, const void* cos, const void* sin, int cs_batched, int dtype, int B, int N,
+                       int Hx, int D, void* out, ossa_stream_t stream) {
+    if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);
+    if (B < 0 || N < 0 || Hx <= 0 || D <= 0 || D % 8 != 0)
+        return fail(OSSA_ERR_INVALID, "bad shape B=%d N=%d heads=%d D=%d (D must be a multiple of 8)", B, N, Hx, D);
+    if ((long long)B * N == 0) return OSSA_OK;
+    if (!x || !out || (!cos) != (!sin)) return fail(OSSA_ERR_INVALID, "null pointer argument");
+    if (!aligned16(x) || !aligned16(out) || (cos && (!aligned16(cos) || !aligned16(sin))))
+        return fail(OSSA_ERR_INVALID, "x, cos, sin and out must be 16-byte aligned");
+    ossa::RopeArgs a{x, cos, sin, cs_batched ? 1 : 0, dtype, B, N, Hx, D, out};
+    return cuda_status(ossa::launch_rope_heads(a, static_cast<cudaStream_t>(stream)), "rope launch");
+}
+
 size_t ossa_oracle_workspace_size(int B, int H, int Hkv, int N, int D, int K, int dtype) {
     if (B < 0 || H <= 0 || Hkv <= 0 || N < 0 || D <= 0 || K <= 0 || !valid_dtype(dtype)) return 0;
     return oracle_workspace_bytes(B, H, Hkv, N, D, K, dtype);

@@ -77,6 +77,19 @@ struct SplitSelectArgs {
     int q0;        // position of query row 0 in the key sequence
     void* ws;
 };
+// RoPE (x*cos + rotate_half(x)*sin, rounded as the eager ops) fused with the
+// (B, N, Hx, D) -> (B, Hx, N, D) layout change; cosv == nullptr: layout only.
+struct RopeArgs {
+    const void* x;     // (B, N, Hx, D)
+    const void* cosv;  // (1 or B, N, D) or nullptr
+    const void* sinv;
+    int cs_batched;    // cos/sin carry a batch dimension
+    int dtype;
+    int B, N, Hx, D;
+    void* out;         // (B, Hx, N, D)
+};
+cudaError_t launch_rope_heads(const RopeArgs& a, cudaStream_t stream);
+
 bool split_select_supported(int R, int K);
 size_t split_select_workspace_bytes(long long rows, int N, int K);
 cudaError_t launch_split_select(const SplitSelectArgs& a, cudaStream_t stream);

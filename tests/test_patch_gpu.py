@@ -89,3 +89,30 @@ def test_full_model_runner_small(capsys):
     full_model.main(["--batch", "2", "--seq", "512", "--layers", "2", "--steps", "1", "--warmup", "1"])
     line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert line["value"] > 0 and line["logits_finite"] and line["config"]["layers"] == 2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("B,cs_batch,D", [(2, 2, 128), (3, 1, 128), (1, 1, 64), (2, 2, 16)])
+def test_rope_to_heads_equals_eager_rope(dtype, B, cs_batch, D):
+    """The fused RoPE + head transpose returns exactly Qwen2's eager
+    apply_rotary_pos_emb on the (B, heads, N, D) view, made contiguous, and the
+    layout-only form exactly the contiguous view."""
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+
+    from ossa_b200.rope import rope_to_heads
+
+    g = torch.Generator().manual_seed(D + B)
+    N, Hq, Hkv = 77, 6, 2
+    xq = (torch.randn(B, N, Hq * D, generator=g) * 3).to(dtype).to(DEV)
+    xk = (torch.randn(B, N, Hkv * D, generator=g) * 3).to(dtype).to(DEV)
+    pos = torch.arange(N).float()
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2).float() / D))
+    emb = torch.cat([pos[:, None] * inv[None], pos[:, None] * inv[None]], dim=-1)
+    cos = emb.cos()[None].expand(cs_batch, N, D).to(dtype).to(DEV)
+    sin = emb.sin()[None].expand(cs_batch, N, D).to(dtype).to(DEV)
+    qv = xq.view(B, N, Hq, D).transpose(1, 2)
+    kv = xk.view(B, N, Hkv, D).transpose(1, 2)
+    rq, rk = apply_rotary_pos_emb(qv, kv, cos, sin)
+    assert torch.equal(rope_to_heads(xq, Hq, cos, sin), rq.contiguous())
+    assert torch.equal(rope_to_heads(xk, Hkv, cos, sin), rk.contiguous())
+    assert torch.equal(rope_to_heads(xk, Hkv), kv.contiguous())
