@@ -203,6 +203,24 @@ OSSA_API int ossa_router_topk_rows(const void* q, const void* k, int dtype,
                                    ossa_stream_t stream);
 
 /*
+ * Decode key cache.  No counterpart in the reference (its forward is
+ * prefill-only, ossa/bench/sparse_forward.py:157-160).  A decoder projects each
+ * new key once, k' = k Wk^T (router.py:180, the same fp32 chain as
+ * ossa_router_topk), into a cache it owns, and selects against the cached rows:
+ *   ossa_router_project_keys:  k (rows, D) dtype -> kp_out (rows, r) fp32
+ *   ossa_router_topk_rows_kp:  ossa_router_topk_rows with the keys given as
+ *       kp (B, Hkv, Nk, r) fp32 instead of k and wk; identical indices
+ *   ossa_router_workspace_size_kp: its workspace (no k' region).
+ */
+OSSA_API size_t ossa_router_workspace_size_kp(int B, int H, int Hkv, int Nq, int Nk, int r, int K);
+OSSA_API int ossa_router_project_keys(const void* k, int dtype, const float* wk, long long rows, int D, int r,
+                                      float* kp_out, ossa_stream_t stream);
+OSSA_API int ossa_router_topk_rows_kp(const void* q, int dtype, const float* wq, const float* kp,
+                                      const float* pos_bias, int B, int H, int Hkv, int Nq, int Nk, int D, int r,
+                                      int seq_len_cfg, int K, int causal, int q_start, int32_t* idx_out,
+                                      void* workspace, size_t workspace_bytes, ossa_stream_t stream);
+
+/*
  * Rotary position embedding fused with the head transpose of the patched
  * layer (ossa/bench/sparse_forward.py:166-178: the q/k/v projections viewed as
  * (B, Hx, N, D), then Qwen2's apply_rotary_pos_emb on q and k).  Additive, for

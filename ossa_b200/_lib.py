@@ -40,6 +40,9 @@ EXPORTED = (
     "ossa_oracle_workspace_size",
     "ossa_oracle_topk_ws",
     "ossa_rope_to_heads",
+    "ossa_router_workspace_size_kp",
+    "ossa_router_project_keys",
+    "ossa_router_topk_rows_kp",
 )
 
 _lock = threading.Lock()
@@ -88,6 +91,12 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ossa_oracle_topk_ws.restype = ci
     lib.ossa_rope_to_heads.argtypes = [vp, vp, vp, ci, ci, ci, ci, ci, ci, vp, vp]
     lib.ossa_rope_to_heads.restype = ci
+    lib.ossa_router_workspace_size_kp.argtypes = [ci] * 7
+    lib.ossa_router_workspace_size_kp.restype = sz
+    lib.ossa_router_project_keys.argtypes = [vp, ci, vp, ctypes.c_longlong, ci, ci, vp, vp]
+    lib.ossa_router_project_keys.restype = ci
+    lib.ossa_router_topk_rows_kp.argtypes = [vp, ci, vp, vp, vp] + [ci] * 11 + [vp, vp, sz, vp]
+    lib.ossa_router_topk_rows_kp.restype = ci
 
 
 def lib() -> ctypes.CDLL:

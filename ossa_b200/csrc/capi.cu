@@ -84,11 +84,12 @@ bool split_shape(int B, int H, int Nq, int Nk) {
 constexpr size_t kCountersBytes = 256;
 
 // Nq query rows per (b, h) against Nk keys per (b, kv head); K = 0 for scoring
-// without selection.
-RouterLayout router_layout(int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
+// without selection.  own_kp = false: the caller holds the projected keys (the
+// decode key cache), so the workspace has no k' region.
+RouterLayout router_layout(int B, int H, int Hkv, int Nq, int Nk, int r, int K, bool own_kp = true) {
     RouterLayout l;
     const size_t qp = (size_t)B * H * Nq * r * sizeof(float);
-    const size_t kp = (size_t)B * Hkv * Nk * r * sizeof(float);
+    const size_t kp = own_kp ? (size_t)B * Hkv * Nk * r * sizeof(float) : 0;
     l.qp_off = kCountersBytes;
     l.kp_off = l.qp_off + align_up(qp);
     l.tc_off = l.kp_off + align_up(kp);
@@ -134,7 +135,7 @@ int check_rows(int Nq, int Nk, int q0) {
 
 int check_router(const void* q, const void* k, int dtype, const float* wq, const float* wk,
                  const float* pos_bias, int B, int H, int Hkv, int Nq, int Nk, int q0, int D, int r,
-                 int seq_len_cfg, int K, const void* out, void* ws, size_t ws_bytes) {
+                 int seq_len_cfg, int K, const void* out, void* ws, size_t ws_bytes, bool own_kp = true) {
     int st = check_heads(B, H, Hkv, Nk);
     if (st) return st;
     if ((st = check_rows(Nq, Nk, q0))) return st;
@@ -149,7 +150,7 @@ int check_router(const void* q, const void* k, int dtype, const float* wq, const
         return fail(OSSA_ERR_INVALID, "null pointer argument");
     if (!aligned16(q) || !aligned16(k) || !aligned16(out))
         return fail(OSSA_ERR_INVALID, "q, k and the output must be 16-byte aligned");
-    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K);
+    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K, own_kp);
     if (!ws || ws_bytes < l.total || !aligned16(ws))
         return fail(OSSA_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required, got %zu",
                     l.total, ws ? ws_bytes : (size_t)0);
@@ -172,6 +173,34 @@ int project_both(const void* q, const void* k, int dtype, const float* wq, const
     *qp_out = qp;
     *kp_out = kp;
     return OSSA_OK;
+}
+
+// Selection of Nq query rows from projected q' (B*H*Nq, r) and k' (B*Hkv*Nk, r):
+// the tensor-core selector, the split selector (few rows, many keys) or the
+// CTA selector; `l` is the workspace layout of the call.
+int select_rows(const float* qp, const float* kp, const float* pos_bias, int B, int H, int Hkv, int Nq, int Nk,
+                int r, int seq_len_cfg, int K, int causal, int q_start, int32_t* idx_out, void* workspace,
+                const RouterLayout& l, cudaStream_t s) {
+    const float scale = (float)(1.0 / sqrt((double)r));
+    if (use_tensor_core_select(B, H, Hkv, Nq, Nk, r, K)) {
+        ossa::RouterTcArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, Nk, K, causal ? 1 : 0, scale,
+                             idx_out, static_cast<char*>(workspace) + l.tc_off,
+                             reinterpret_cast<int*>(workspace)};
+        a.Nq = Nq;
+        a.q0 = q_start;
+        return cuda_status(ossa::launch_router_tc(a, s), "tensor-core router top-K launch");
+    }
+    const char* env = getenv("OSSA_ROUTER_SELECT");
+    if (split_shape(B, H, Nq, Nk) && !(env && env[0] == 'e')) {
+        ossa::SplitSelectArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, Nk, r, K, scale, causal ? 1 : 0,
+                                idx_out, Nq, q_start, static_cast<char*>(workspace) + l.split_off};
+        return cuda_status(ossa::launch_split_select(a, s), "split router top-K launch");
+    }
+    ossa::ScoreTopkArgs a{qp, kp, ossa::kF32, pos_bias, seq_len_cfg, B, H, Hkv, Nk, r, K, scale,
+                          causal ? 1 : 0, idx_out};
+    a.Nq = Nq;
+    a.q0 = q_start;
+    return cuda_status(ossa::launch_score_topk(a, s), "router top-K launch");
 }
 
 }  // namespace
@@ -253,28 +282,48 @@ int ossa_router_topk_rows(const void* q, const void* k, int dtype, const float* 
     float *qp = nullptr, *kp = nullptr;
     st = project_both(q, k, dtype, wq, wk, B, H, Hkv, Nq, Nk, D, r, workspace, s, &qp, &kp);
     if (st) return st;
-    const float scale = (float)(1.0 / sqrt((double)r));
-    if (use_tensor_core_select(B, H, Hkv, Nq, Nk, r, K)) {
-        const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K);
-        ossa::RouterTcArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, Nk, K, causal ? 1 : 0, scale,
-                             idx_out, static_cast<char*>(workspace) + l.tc_off,
-                             reinterpret_cast<int*>(workspace)};
-        a.Nq = Nq;
-        a.q0 = q_start;
-        return cuda_status(ossa::launch_router_tc(a, s), "tensor-core router top-K launch");
-    }
-    const char* env = getenv("OSSA_ROUTER_SELECT");
-    if (split_shape(B, H, Nq, Nk) && !(env && env[0] == 'e')) {
-        const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K);
-        ossa::SplitSelectArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, Nk, r, K, scale, causal ? 1 : 0,
-                                idx_out, Nq, q_start, static_cast<char*>(workspace) + l.split_off};
-        return cuda_status(ossa::launch_split_select(a, s), "split router top-K launch");
-    }
-    ossa::ScoreTopkArgs a{qp, kp, ossa::kF32, pos_bias, seq_len_cfg, B, H, Hkv, Nk, r, K, scale,
-                          causal ? 1 : 0, idx_out};
-    a.Nq = Nq;
-    a.q0 = q_start;
-    return cuda_status(ossa::launch_score_topk(a, s), "router top-K launch");
+    return select_rows(qp, kp, pos_bias, B, H, Hkv, Nq, Nk, r, seq_len_cfg, K, causal, q_start, idx_out, workspace,
+                       router_layout(B, H, Hkv, Nq, Nk, r, K), s);
+}
+
+size_t ossa_router_workspace_size_kp(int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
+    if (B < 0 || H <= 0 || Hkv <= 0 || Nq < 0 || Nk < 0 || r <= 0) return 0;
+    return router_layout(B, H, Hkv, Nq, Nk, r, K, false).total;
+}
+
+int ossa_router_project_keys(const void* k, int dtype, const float* wk, long long rows, int D, int r,
+                             float* kp_out, ossa_stream_t stream) {
+    if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);
+    if (rows < 0 || D <= 0) return fail(OSSA_ERR_INVALID, "bad shape rows=%lld D=%d", rows, D);
+    if (!supported_r(r)) return fail(OSSA_ERR_UNSUPPORTED, "proj_dim r=%d not in {16,32,64,128}", r);
+    if (rows == 0) return OSSA_OK;
+    if (!k || !wk || !kp_out) return fail(OSSA_ERR_INVALID, "null pointer argument");
+    if (!aligned16(k) || !aligned16(kp_out)) return fail(OSSA_ERR_INVALID, "k and kp_out must be 16-byte aligned");
+    ossa::ProjectArgs pk{k, wk, kp_out, rows, D, r, dtype};
+    return cuda_status(ossa::launch_project(pk, static_cast<cudaStream_t>(stream)), "k projection launch");
+}
+
+int ossa_router_topk_rows_kp(const void* q, int dtype, const float* wq, const float* kp, const float* pos_bias,
+                             int B, int H, int Hkv, int Nq, int Nk, int D, int r, int seq_len_cfg, int K,
+                             int causal, int q_start, int32_t* idx_out, void* workspace, size_t workspace_bytes,
+                             ossa_stream_t stream) {
+    int st = check_router(q, kp, dtype, wq, wq, pos_bias, B, H, Hkv, Nq, Nk, q_start, D, r, seq_len_cfg, K,
+                          idx_out, workspace, workspace_bytes, false);
+    if (st) return st;
+    if (K <= 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
+    if (!ossa::score_topk_supported(r, K))
+        return fail(OSSA_ERR_UNSUPPORTED, "top-K selection supports K <= 160 (got K=%d)", K);
+    if ((long long)B * H * Nq == 0) return OSSA_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    st = cuda_status(cudaMemsetAsync(workspace, 0, kCountersBytes, s), "workspace counters reset");
+    if (st) return st;
+    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K, false);
+    float* qp = reinterpret_cast<float*>(static_cast<char*>(workspace) + l.qp_off);
+    ossa::ProjectArgs pa{q, wq, qp, (long long)B * H * Nq, D, r, dtype};
+    st = cuda_status(ossa::launch_project(pa, s), "q projection launch");
+    if (st) return st;
+    return select_rows(qp, kp, pos_bias, B, H, Hkv, Nq, Nk, r, seq_len_cfg, K, causal, q_start, idx_out, workspace,
+                       l, s);
 }
 
 int ossa_router_topk(const void* q, const void* k, int dtype, const float* wq, const float* wk,

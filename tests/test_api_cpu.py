@@ -205,3 +205,18 @@ def test_router_with_seq_len_scores_like_the_clamped_table(golden_dir, tmp_path)
     loaded = _load_router(ckpt, model, 0, 1024, pos_bias="extend")
     assert torch.equal(loaded.pos_bias.weight, big.pos_bias.weight)
     assert not loaded.training
+
+
+def test_router_key_cache_argument_checks():
+    from ossa_b200.decode import RouterKeyCache
+
+    r = ContentRouter(ContentRouterConfig(head_dim=16, n_heads=4, seq_len=32, proj_dim=16))
+    cache = RouterKeyCache(r, batch=1, kv_heads=2, capacity=8, device="cpu")
+    with pytest.raises(ValueError):
+        cache.append(torch.zeros(1, 2, 9, 16))      # past the capacity
+    with pytest.raises(ValueError):
+        cache.append(torch.zeros(1, 3, 2, 16))      # wrong head count
+    with pytest.raises(RuntimeError):
+        cache.append(torch.zeros(1, 2, 2, 16))      # CPU tensors are refused, no CPU path
+    with pytest.raises(ValueError):
+        cache.topk(torch.zeros(1, 4, 1, 16), 4)     # nothing cached yet

@@ -116,3 +116,35 @@ def test_decode_split_selector_ties_across_ranges():
     rows = np.array([(bh * N + i) for bh in range(B * H) for i in range(q0, q0 + nq)])
     ref = oracle.router_topk_rows(q, k, wq, wk, pb, L, K, rows)
     np.testing.assert_array_equal(got.cpu().numpy().reshape(-1, K), ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_router_key_cache_matches_router_topk(dtype):
+    """Decoding with projected keys cached once per position gives the indices of
+    router_topk on all keys so far, step after step (split selector for one new
+    row; tensor-core selector for a 256-row prefill block)."""
+    from ossa_b200 import ContentRouter, ContentRouterConfig
+    from ossa_b200.decode import RouterKeyCache
+
+    B, H, Hkv, N, D, r, L, K = 1, 12, 2, 2600, 128, 64, 4096, 64
+    q, k, _, wq, wk, pb = _inputs(B, H, Hkv, N, D, r, L, seed=21)
+    q, k = q.to(dtype).to(DEV), k.to(dtype).to(DEV)
+    router = ContentRouter(ContentRouterConfig(head_dim=D, n_heads=H, seq_len=L, proj_dim=r))
+    with torch.no_grad():
+        router.q_proj[0].weight.copy_(wq)
+        router.k_proj[0].weight.copy_(wk)
+        router.pos_bias.weight.copy_(pb)
+    router = router.to(DEV)
+    args = (wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K)
+    cache = RouterKeyCache(router, B, Hkv, capacity=N)
+    n0 = 2400
+    cache.append(k[:, :, :n0 - 256])
+    cache.append(k[:, :, n0 - 256:n0])
+    blk = q[:, :, n0 - 256:n0].contiguous()
+    assert torch.equal(cache.topk(blk, K), router_topk(blk, k[:, :, :n0].contiguous(), *args, q_start=n0 - 256))
+    for pos in range(n0, N, 50):
+        cache.append(k[:, :, cache.length:pos + 1])
+        qn = q[:, :, pos:pos + 1].contiguous()
+        got = cache.topk(qn, K)
+        ref = router_topk(qn, k[:, :, :pos + 1].contiguous(), *args, q_start=pos)
+        assert torch.equal(got, ref), f"position {pos}"
