@@ -14,9 +14,13 @@
 //     streaming warp list (threshold = the current K-th key, compaction in
 //     position order, as the exact fallback selector does); the winners go to
 //     global memory in ascending key order.
-//  2. split_merge_kernel: one warp per row streams the ranges' winners in range
-//     order, so keys still arrive in ascending order, through the same
-//     streaming list; the K best are written ascending, -1 padded.
+//  2. split_merge_kernel: one CTA per row.  Each range also reports its K-th
+//     best order key; the largest of them is a lower bound on the row's K-th
+//     best (that range alone has K keys at or above it), so only entries at or
+//     above it enter the lists.  Warp w streams the winners of a contiguous
+//     group of ranges, in range order, through the same streaming list; warp 0
+//     then streams the 8 group lists in group order (keys still ascending) and
+//     writes the K best ascending, -1 padded.
 // Every key of the exact top K is among its range's K best, and ties at the
 // K-th score go to the lower key index in both stages, so the result is the
 // exact top K by (score desc, key asc).
@@ -121,7 +125,7 @@ template <int R, bool kBias, int EPL>
 __global__ void __launch_bounds__(256)
 split_scan_kernel(const float* __restrict__ qp, const float* __restrict__ kp, const float* __restrict__ bias, int L,
                   int H, int Hkv, int N, int Nq, int q0, int K, float scale, int causal, long long rows, int nsplit,
-                  uint2* __restrict__ cand, int* __restrict__ ccount) {
+                  uint2* __restrict__ cand, int* __restrict__ ccount, uint32_t* __restrict__ ckth) {
     __shared__ uint2 sbuf[8][32 * EPL];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -148,39 +152,74 @@ split_scan_kernel(const float* __restrict__ qp, const float* __restrict__ kp, co
     }
     const int m = st.finish(lane, lt);
     uint2* dst = cand + (size_t)gw * K;
-    for (int t = lane; t < m; t += 32) dst[t] = st.wb[t];
-    if (lane == 0) ccount[gw] = m;
+    uint32_t kmin = 0xffffffffu;
+    for (int t = lane; t < m; t += 32) {
+        const uint2 e = st.wb[t];
+        dst[t] = e;
+        kmin = min(kmin, e.x);
+    }
+    kmin = __reduce_min_sync(kFull, kmin);
+    if (lane == 0) {
+        ccount[gw] = m;
+        ckth[gw] = m == K ? kmin : 0u;  // the range's K-th best key (0: fewer than K)
+    }
 }
 
 template <int EPL>
 __global__ void __launch_bounds__(256)
-split_merge_kernel(const uint2* __restrict__ cand, const int* __restrict__ ccount, long long rows, int nsplit, int K,
-                   int32_t* __restrict__ out) {
+split_merge_kernel(const uint2* __restrict__ cand, const int* __restrict__ ccount, const uint32_t* __restrict__ ckth,
+                   int nsplit, int K, int32_t* __restrict__ out) {
     __shared__ uint2 sbuf[8][32 * EPL];
+    __shared__ uint2 sfin[32 * EPL];
+    __shared__ uint32_t swk[8];
+    __shared__ int scnt[8];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const unsigned lt = lanemask_lt();
-    for (long long row = (long long)blockIdx.x * 8 + warp; row < rows; row += (long long)gridDim.x * 8) {
-        WarpStreamTopK<EPL> st{sbuf[warp], K};
-        const size_t base = (size_t)row * nsplit;
-        for (int s0 = 0; s0 < nsplit; s0 += 32) {
-            const int cv = s0 + lane < nsplit ? ccount[base + s0 + lane] : 0;
-            const int ns = min(32, nsplit - s0);
-            for (int u = 0; u < ns; ++u) {
-                const int c = __shfl_sync(kFull, cv, u);
-                const uint2* src = cand + (base + s0 + u) * K;
-                for (int t0 = 0; t0 < c; t0 += 32) {
-                    const int t = t0 + lane;
-                    const bool valid = t < c;
-                    const uint2 e = valid ? src[t] : make_uint2(0u, 0u);
-                    st.push(valid, e.x, e.y, lane, lt);
-                }
+    const long long row = blockIdx.x;
+    const size_t base = (size_t)row * nsplit;
+    // lower bound on the row's K-th best key: the largest per-range K-th key
+    uint32_t t0 = 0u;
+    for (int s2 = threadIdx.x; s2 < nsplit; s2 += blockDim.x) t0 = max(t0, ckth[base + s2]);
+    t0 = __reduce_max_sync(kFull, t0);
+    if (lane == 0) swk[warp] = t0;
+    __syncthreads();
+    t0 = swk[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) t0 = max(t0, swk[w]);
+    // warp w: ranges [w * per, (w + 1) * per)
+    const int per = (nsplit + 7) / 8;
+    WarpStreamTopK<EPL> st{sbuf[warp], K};
+    st.theta = t0 > 0u ? t0 - 1u : 0u;  // admits keys >= t0
+    const int s_lo = warp * per, s_hi = min(nsplit, s_lo + per);
+    for (int sp = s_lo; sp < s_hi; ++sp) {
+        const int c = ccount[base + sp];
+        const uint2* src = cand + (base + sp) * K;
+        for (int q0 = 0; q0 < c; q0 += 32) {
+            const int t = q0 + lane;
+            const bool valid = t < c;
+            const uint2 e = valid ? src[t] : make_uint2(0u, 0u);
+            st.push(valid, e.x, e.y, lane, lt);
+        }
+    }
+    const int m = st.finish(lane, lt);
+    if (lane == 0) scnt[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+        WarpStreamTopK<EPL> fin{sfin, K};
+        fin.theta = t0 > 0u ? t0 - 1u : 0u;
+        for (int w = 0; w < 8; ++w) {
+            const int c = scnt[w];
+            for (int q0 = 0; q0 < c; q0 += 32) {
+                const int t = q0 + lane;
+                const bool valid = t < c;
+                const uint2 e = valid ? sbuf[w][t] : make_uint2(0u, 0u);
+                fin.push(valid, e.x, e.y, lane, lt);
             }
         }
-        const int m = st.finish(lane, lt);
+        const int mf = fin.finish(lane, lt);
         int32_t* orow = out + row * K;
-        for (int t = lane; t < K; t += 32) orow[t] = t < m ? (int32_t)st.wb[t].y : -1;
-        __syncwarp();  // sbuf is rewritten for the next row
+        for (int t = lane; t < K; t += 32) orow[t] = t < mf ? (int32_t)sfin[t].y : -1;
     }
 }
 
@@ -193,15 +232,15 @@ cudaError_t launch_split(const SplitSelectArgs& a, cudaStream_t stream) {
     const int nsplit = split_count(a.N);
     uint2* cand = static_cast<uint2*>(a.ws);
     int* ccount = reinterpret_cast<int*>(cand + (size_t)rows * nsplit * a.K);
+    uint32_t* ckth = reinterpret_cast<uint32_t*>(ccount + (size_t)rows * nsplit);
     const long long warps = rows * nsplit;
     split_scan_kernel<R, kBias, EPL><<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(
         a.qrows, a.krows, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0, a.K, a.scale, a.causal, rows, nsplit, cand,
-        ccount);
+        ccount, ckth);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     note_launch();
-    const unsigned mblk = (unsigned)std::min<long long>((rows + 7) / 8, 148LL * 8);
-    split_merge_kernel<EPL><<<mblk, 256, 0, stream>>>(cand, ccount, rows, nsplit, a.K, a.out);
+    split_merge_kernel<EPL><<<(unsigned)rows, 256, 0, stream>>>(cand, ccount, ckth, nsplit, a.K, a.out);
     e = cudaGetLastError();
     if (e == cudaSuccess) note_launch();
     return e;
@@ -233,7 +272,7 @@ bool split_select_supported(int R, int K) {
 
 size_t split_select_workspace_bytes(long long rows, int N, int K) {
     const size_t n = (size_t)rows * split_count(N);
-    return n * (size_t)K * sizeof(uint2) + n * sizeof(int);
+    return n * (size_t)K * sizeof(uint2) + n * (sizeof(int) + sizeof(uint32_t));
 }
 
 cudaError_t launch_split_select(const SplitSelectArgs& a, cudaStream_t stream) {
