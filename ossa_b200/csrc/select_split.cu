@@ -36,37 +36,6 @@ namespace {
 
 constexpr int kSplitKeys = 1024;  // keys per warp range
 
-// Canonical score: fmaf chain over c = 0..R-1 from 0, times scale, plus the
-// position-bias term (the definition score_topk.cu selects on).
-template <int R, bool kBias>
-__device__ __forceinline__ float exact_score(const float* __restrict__ qrow, const float* __restrict__ krow,
-                                             const float* __restrict__ bias, int L, int i, int j, float scale) {
-    constexpr int V = R / 4;
-    constexpr int CH = V < 16 ? V : 16;
-    float acc = 0.f;
-#pragma unroll
-    for (int c0 = 0; c0 < V; c0 += CH) {
-        float4 bk[CH];
-#pragma unroll
-        for (int u = 0; u < CH; ++u) bk[u] = __ldg(reinterpret_cast<const float4*>(krow) + c0 + u);
-#pragma unroll
-        for (int u = 0; u < CH; ++u) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(qrow) + c0 + u);
-            acc = fmaf(a.x, bk[u].x, acc);
-            acc = fmaf(a.y, bk[u].y, acc);
-            acc = fmaf(a.z, bk[u].z, acc);
-            acc = fmaf(a.w, bk[u].w, acc);
-        }
-    }
-    if constexpr (kBias) {
-        int bi = i - j + L;
-        bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
-        return __fadd_rn(__fmul_rn(acc, scale), __ldg(bias + bi));
-    } else {
-        return __fmul_rn(acc, scale);
-    }
-}
-
 // Streaming top-K of one warp over entries pushed 32 at a time in ascending key
 // order.  An entry enters the list only if its order key beats the current
 // K-th key (a later entry that ties it has a higher key index and loses); a
@@ -121,15 +90,27 @@ struct WarpStreamTopK {
     }
 };
 
+// Four warps per CTA.  Each warp stages the k' rows of its next 32 keys in
+// shared memory, 64 columns at a time, with coalesced 16-byte loads (a lane
+// loading its own 256-byte row would touch 32 lines per instruction); the row
+// stride of CH + 4 floats makes each lane's 16-byte reads of its own row
+// conflict-free.  Lane l then continues key l's fmaf chain over the chunk, so
+// each score is the canonical one score_topk.cu selects on: the fmaf chain over
+// c = 0..R-1 in order from 0, times scale, plus the position-bias term.
+constexpr int kScanWarps = 4;
+
 template <int R, bool kBias, int EPL>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(32 * kScanWarps)
 split_scan_kernel(const float* __restrict__ qp, const float* __restrict__ kp, const float* __restrict__ bias, int L,
                   int H, int Hkv, int N, int Nq, int q0, int K, float scale, int causal, long long rows, int nsplit,
                   uint2* __restrict__ cand, int* __restrict__ ccount, uint32_t* __restrict__ ckth) {
-    __shared__ uint2 sbuf[8][32 * EPL];
+    constexpr int CH = R < 64 ? R : 64;  // columns per staged chunk
+    constexpr int ST = CH + 4;            // row stride in floats
+    __shared__ uint2 sbuf[kScanWarps][32 * EPL];
+    __shared__ __align__(16) float stile[kScanWarps][32 * ST];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const long long gw = (long long)blockIdx.x * 8 + warp;
+    const long long gw = (long long)blockIdx.x * kScanWarps + warp;
     if (gw >= rows * nsplit) return;  // whole warps
     const unsigned lt = lanemask_lt();
     const long long row = gw / nsplit;
@@ -142,13 +123,46 @@ split_scan_kernel(const float* __restrict__ qp, const float* __restrict__ kp, co
     const float* kbase = kp + (size_t)(b * Hkv + g) * N * R;
     const int n = causal ? min(i + 1, N) : N;
     const int j0 = sp * kSplitKeys, j1 = min(j0 + kSplitKeys, n);
+    float* tile = stile[warp];
     WarpStreamTopK<EPL> st{sbuf[warp], K};
     for (int jb = j0; jb < j1; jb += 32) {
+        const int nk = min(32, j1 - jb);  // keys in this group
+        float acc = 0.f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < R; c0 += CH) {
+            // stage rows jb .. jb + nk - 1, columns c0 .. c0 + CH - 1
+            constexpr int V = CH / 4;  // float4 per staged row
+#pragma unroll
+            for (int t = 0; t < V; ++t) {
+                const int f = lane + 32 * t;  // float4 index in the 32 x V block
+                const int rr = f / V, cv = f - rr * V;
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (rr < nk) x = __ldg(reinterpret_cast<const float4*>(kbase + (size_t)(jb + rr) * R + c0) + cv);
+                *reinterpret_cast<float4*>(tile + rr * ST + 4 * cv) = x;
+            }
+            __syncwarp();
+#pragma unroll
+            for (int u = 0; u < V; ++u) {
+                const float4 kk = *reinterpret_cast<const float4*>(tile + lane * ST + 4 * u);
+                const float4 a = __ldg(reinterpret_cast<const float4*>(qrow + c0) + u);
+                acc = fmaf(a.x, kk.x, acc);
+                acc = fmaf(a.y, kk.y, acc);
+                acc = fmaf(a.z, kk.z, acc);
+                acc = fmaf(a.w, kk.w, acc);
+            }
+            __syncwarp();  // the tile is restaged next
+        }
         const int j = jb + lane;
-        const bool valid = j < j1;
-        const uint32_t key =
-            valid ? order_key(exact_score<R, kBias>(qrow, kbase + (size_t)j * R, bias, L, i, j, scale)) : 0u;
-        st.push(valid, key, (uint32_t)j, lane, lt);
+        const bool valid = lane < nk;
+        float sc;
+        if constexpr (kBias) {
+            int bi = i - j + L;
+            bi = bi < 0 ? 0 : (bi > 2 * L - 1 ? 2 * L - 1 : bi);
+            sc = __fadd_rn(__fmul_rn(acc, scale), valid ? __ldg(bias + bi) : 0.f);
+        } else {
+            sc = __fmul_rn(acc, scale);
+        }
+        st.push(valid, valid ? order_key(sc) : 0u, (uint32_t)j, lane, lt);
     }
     const int m = st.finish(lane, lt);
     uint2* dst = cand + (size_t)gw * K;
@@ -234,7 +248,8 @@ cudaError_t launch_split(const SplitSelectArgs& a, cudaStream_t stream) {
     int* ccount = reinterpret_cast<int*>(cand + (size_t)rows * nsplit * a.K);
     uint32_t* ckth = reinterpret_cast<uint32_t*>(ccount + (size_t)rows * nsplit);
     const long long warps = rows * nsplit;
-    split_scan_kernel<R, kBias, EPL><<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(
+    split_scan_kernel<R, kBias, EPL><<<(unsigned)((warps + kScanWarps - 1) / kScanWarps), 32 * kScanWarps, 0,
+                                       stream>>>(
         a.qrows, a.krows, a.bias, a.L, a.H, a.Hkv, a.N, Nq, a.q0, a.K, a.scale, a.causal, rows, nsplit, cand,
         ccount, ckth);
     cudaError_t e = cudaGetLastError();
