@@ -14,6 +14,7 @@
 // (bf16: computed in fp32 and rounded to nearest even; fp32: no contraction),
 // so the result is bit-identical to the unfused PyTorch ops.
 // Without cos/sin the kernel is the plain layout copy (for v).
+#include <algorithm>
 #include <cstdint>
 
 #include "common.cuh"
@@ -59,69 +60,70 @@ struct RopeIO<__nv_bfloat16> {
     static __device__ __forceinline__ float rnd(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 };
 
-// One thread per 4 columns of the low half of a (b, n, h) row: columns
-// c .. c+3 and c + D/2 .. c + D/2 + 3.
+// One CTA per (b, n) position; thread t of it takes head h = t / (D/8) and
+// columns c .. c+3 and c + D/2 .. c + D/2 + 3 of the low and high halves
+// (c = 4 * (t mod D/8)).  32-bit index arithmetic only.
 template <typename T, bool kRope>
 __global__ void __launch_bounds__(256)
 rope_heads_kernel(const T* __restrict__ x, const T* __restrict__ cosv, const T* __restrict__ sinv, int cs_batched,
                   int B, int N, int Hx, int D, T* __restrict__ out) {
     using IO = RopeIO<T>;
-    const int hq = D / 8;  // threads per row
-    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long long total = (long long)B * N * Hx * hq;
-    if (t >= total) return;
-    const int part = (int)(t % hq);
-    const long long r = t / hq;  // (b, n, h) row of the input
-    const int h = (int)(r % Hx);
-    const long long bn = r / Hx;
-    const int n = (int)(bn % N);
-    const int b = (int)(bn / N);
-    const int c = 4 * part;
+    const int hq = D / 8;  // threads per head row
+    const int bn = blockIdx.x;
+    const int b = bn / N;
+    const int n = bn - b * N;
     const int half = D / 2;
-    const T* xr = x + r * D;
-    float lo[4], hi[4];
-    IO::load4(xr + c, lo);
-    IO::load4(xr + half + c, hi);
-    T* orow = out + (((long long)b * Hx + h) * N + n) * D;
-    if constexpr (kRope) {
-        const long long cr = ((long long)(cs_batched ? b : 0) * N + n) * D;
-        float cl[4], ch[4], sl[4], sh[4];
-        IO::load4(cosv + cr + c, cl);
-        IO::load4(cosv + cr + half + c, ch);
-        IO::load4(sinv + cr + c, sl);
-        IO::load4(sinv + cr + half + c, sh);
-        float ol[4], oh[4];
+    for (int t = threadIdx.x; t < Hx * hq; t += blockDim.x) {
+        const int h = t / hq;
+        const int c = 4 * (t - h * hq);
+        const T* xr = x + ((size_t)bn * Hx + h) * D;
+        float lo[4], hi[4];
+        IO::load4(xr + c, lo);
+        IO::load4(xr + half + c, hi);
+        T* orow = out + (((size_t)b * Hx + h) * N + n) * D;
+        if constexpr (kRope) {
+            const size_t cr = ((size_t)(cs_batched ? b : 0) * N + n) * D;
+            float cl[4], ch[4], sl[4], sh[4];
+            IO::load4(cosv + cr + c, cl);
+            IO::load4(cosv + cr + half + c, ch);
+            IO::load4(sinv + cr + c, sl);
+            IO::load4(sinv + cr + half + c, sh);
+            float ol[4], oh[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            // low half: x1*cos - x2*sin; high half: x2*cos + x1*sin
-            const float a1 = IO::rnd(__fmul_rn(lo[u], cl[u]));
-            const float b1 = IO::rnd(__fmul_rn(-hi[u], sl[u]));
-            ol[u] = IO::rnd(__fadd_rn(a1, b1));
-            const float a2 = IO::rnd(__fmul_rn(hi[u], ch[u]));
-            const float b2 = IO::rnd(__fmul_rn(lo[u], sh[u]));
-            oh[u] = IO::rnd(__fadd_rn(a2, b2));
+            for (int u = 0; u < 4; ++u) {
+                // low half: x1*cos - x2*sin; high half: x2*cos + x1*sin
+                const float a1 = IO::rnd(__fmul_rn(lo[u], cl[u]));
+                const float b1 = IO::rnd(__fmul_rn(-hi[u], sl[u]));
+                ol[u] = IO::rnd(__fadd_rn(a1, b1));
+                const float a2 = IO::rnd(__fmul_rn(hi[u], ch[u]));
+                const float b2 = IO::rnd(__fmul_rn(lo[u], sh[u]));
+                oh[u] = IO::rnd(__fadd_rn(a2, b2));
+            }
+            IO::store4(orow + c, ol);
+            IO::store4(orow + half + c, oh);
+        } else {
+            IO::store4(orow + c, lo);
+            IO::store4(orow + half + c, hi);
         }
-        IO::store4(orow + c, ol);
-        IO::store4(orow + half + c, oh);
-    } else {
-        IO::store4(orow + c, lo);
-        IO::store4(orow + half + c, hi);
     }
 }
 
 template <typename T>
 cudaError_t launch_t(const RopeArgs& a, cudaStream_t stream) {
-    const long long total = (long long)a.B * a.N * a.Hx * (a.D / 8);
-    if (total == 0) return cudaSuccess;
-    const unsigned grid = (unsigned)((total + 255) / 256);
+    const long long rows = (long long)a.B * a.N;
+    if (rows == 0) return cudaSuccess;
+    if (rows > 0x7fffffffLL) return cudaErrorInvalidValue;
+    const unsigned grid = (unsigned)rows;
+    const int per = a.Hx * (a.D / 8);  // threads' worth of work per position
+    const unsigned block = (unsigned)std::min(256, (per + 31) / 32 * 32);
     const T* x = static_cast<const T*>(a.x);
     T* out = static_cast<T*>(a.out);
     if (a.cosv)
-        rope_heads_kernel<T, true><<<grid, 256, 0, stream>>>(x, static_cast<const T*>(a.cosv),
+        rope_heads_kernel<T, true><<<grid, block, 0, stream>>>(x, static_cast<const T*>(a.cosv),
                                                             static_cast<const T*>(a.sinv), a.cs_batched, a.B, a.N,
                                                             a.Hx, a.D, out);
     else
-        rope_heads_kernel<T, false><<<grid, 256, 0, stream>>>(x, nullptr, nullptr, 0, a.B, a.N, a.Hx, a.D, out);
+        rope_heads_kernel<T, false><<<grid, block, 0, stream>>>(x, nullptr, nullptr, 0, a.B, a.N, a.Hx, a.D, out);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) note_launch();
     return e;
