@@ -238,6 +238,15 @@ project_persistent_kernel(const T* __restrict__ x, const float* __restrict__ w, 
     cp_async_wait_all();
 }
 
+// (acc0, acc1) = (fma(x, w0, acc0), fma(x, w1, acc1)) as one fma.rn.f32x2: two
+// IEEE fused multiply-adds, each rounded once, the same as two fmaf calls.
+__device__ __forceinline__ void fma2(float& acc0, float& acc1, float x, float w0, float w1) {
+    asm("{\n .reg .b64 ra, rb, rc;\n mov.b64 ra, {%2, %2};\n mov.b64 rb, {%3, %4};\n"
+        " mov.b64 rc, {%0, %1};\n fma.rn.f32x2 rc, ra, rb, rc;\n mov.b64 {%0, %1}, rc;\n}"
+        : "+f"(acc0), "+f"(acc1)
+        : "f"(x), "f"(w0), "f"(w1));
+}
+
 // bf16 rows, D = 128, R = 64 (the ContentRouter shape of the product path): 4 rows x 8
 // output columns per thread (columns cg*4.. and 32 + cg*4..), so a d-step reads one 8-byte
 // x group (4 bf16 rows) and two float4 of W per 32 FMA, and x stays bf16 in shared memory (converted on use, exactly).
@@ -308,11 +317,13 @@ project_bf16_d128_r64_kernel(const __nv_bfloat16* __restrict__ x, const float* _
             // 128 consecutive bytes (no bank conflicts)
             const float4 w0 = *reinterpret_cast<const float4*>(Ws + d * 64 + cg * 4);
             const float4 w1 = *reinterpret_cast<const float4*>(Ws + d * 64 + 32 + cg * 4);
+            // column pairs (c, c+1) through fma.rn.f32x2: each lane of the pair is
+            // rounded exactly as fmaf, so every output keeps its fmaf chain
             const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
             for (int a = 0; a < kP2Rows; ++a)
 #pragma unroll
-                for (int c = 0; c < kP2Cols; ++c) acc[a][c] = fmaf(xa[a], wa[c], acc[a][c]);
+                for (int c = 0; c < kP2Cols; c += 2) fma2(acc[a][c], acc[a][c + 1], xa[a], wa[c], wa[c + 1]);
         }
 #pragma unroll
         for (int a = 0; a < kP2Rows; ++a) {
