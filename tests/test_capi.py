@@ -87,3 +87,30 @@ def test_router_validation_and_workspace():
     assert L.ossa_router_topk(*big_k) == _lib.OSSA_ERR_UNSUPPORTED
     assert L.ossa_oracle_topk(16, 16, _lib.OSSA_BF16, 1, 12, 2, 64, 96, 0.1, 8, 1, 16, None) == \
         _lib.OSSA_ERR_UNSUPPORTED
+
+
+def test_rope_key_cache_and_oracle_ws_validation():
+    """The fused RoPE, the decode key-cache and the workspace oracle entry
+    points reject bad requests before any CUDA call."""
+    L = _lib.lib()
+    bf, inv, ws_err, uns = _lib.OSSA_BF16, _lib.OSSA_ERR_INVALID, _lib.OSSA_ERR_WORKSPACE, _lib.OSSA_ERR_UNSUPPORTED
+    # RoPE: D must be a multiple of 8; cos without sin; unaligned pointers
+    assert L.ossa_rope_to_heads(16, 16, 16, 0, bf, 1, 4, 2, 12, 16, None) == inv
+    assert L.ossa_rope_to_heads(16, 16, None, 0, bf, 1, 4, 2, 128, 16, None) == inv
+    assert L.ossa_rope_to_heads(8, None, None, 0, bf, 1, 4, 2, 128, 16, None) == inv
+    assert L.ossa_rope_to_heads(16, None, None, 0, 7, 1, 4, 2, 128, 16, None) == inv
+    assert L.ossa_rope_to_heads(None, None, None, 0, bf, 0, 4, 2, 128, None, None) == _lib.OSSA_OK  # empty
+    # key projection: unsupported r, null output
+    assert L.ossa_router_project_keys(16, bf, 16, 10, 128, 48, 16, None) == uns
+    assert L.ossa_router_project_keys(16, bf, 16, 10, 128, 64, None, None) == inv
+    # selection against cached keys: its workspace has no k' region, and too small a one is refused
+    full = L.ossa_router_workspace_size_rows(1, 12, 2, 1, 32768, 64, 64)
+    kp_only = L.ossa_router_workspace_size_kp(1, 12, 2, 1, 32768, 64, 64)
+    assert 0 < kp_only and full - kp_only >= 2 * 32768 * 64 * 4
+    args = [16, bf, 16, 16, 16, 1, 12, 2, 1, 32768, 128, 64, 32768, 64, 1, 32767, 16, 16, 64, None]
+    assert L.ossa_router_topk_rows_kp(*args) == ws_err
+    # the workspace oracle: bad K and an undersized workspace
+    n = L.ossa_oracle_workspace_size(1, 12, 2, 1024, 128, 64, bf)
+    assert n > 256
+    assert L.ossa_oracle_topk_ws(16, 16, bf, 1, 12, 2, 1024, 128, 0.088, 0, 1, 16, 16, n, None) == inv
+    assert L.ossa_oracle_topk_ws(16, 16, bf, 1, 12, 2, 1024, 128, 0.088, 64, 1, 16, 16, n - 16, None) == ws_err
