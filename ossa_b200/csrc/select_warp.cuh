@@ -134,12 +134,13 @@ __device__ __forceinline__ void warp_kth_key_search(const uint32_t (&u)[EPL], co
 }
 
 // keep[e] = the entry is among the K largest (see warp_kth_key's tie rule).
+// Requires more than K valid entries (every caller compacts a list only then).
 template <int EPL>
 __device__ __forceinline__ void warp_topk_mask(const uint32_t (&u)[EPL], const bool (&val)[EPL], int K,
                                                bool (&keep)[EPL], uint32_t* T_out = nullptr) {
     uint32_t T;
     int ties;
-    warp_kth_key<EPL>(u, val, K, T, ties);
+    warp_kth_key_search<EPL>(u, val, K, T, ties);
     const unsigned lt = lanemask_lt();
     int seen = 0;
 #pragma unroll
