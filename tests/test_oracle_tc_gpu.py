@@ -116,3 +116,30 @@ def test_tensor_core_oracle_ties_and_non_finite():
     assert status == 0
     _assert_same(tc, oracle.oracle_topk(q.cpu(), k.cpu(), K))
     assert torch.equal(tc, _exact(q, k, K))
+
+
+@pytest.mark.parametrize("K", [1, 3, 65])
+def test_tensor_core_oracle_small_and_odd_k(K):
+    """K = 1 and 3 (the smallest lists for the K-th score search and the merge
+    path) and K = 65 (the first wide K): equal to the exact selector and the CPU
+    oracle."""
+    B, H, Hkv, N, D = 1, 4, 2, 700, 128
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=90 + K, scale=1.0 / math.sqrt(D))
+    q, k = q.bfloat16().to(DEV), k.bfloat16().to(DEV)
+    tc, fb, status = _oracle_ws(q, k, K)
+    assert status == 0
+    assert torch.equal(tc, _exact(q, k, K))
+    _assert_same(tc, oracle.oracle_topk(q.cpu(), k.cpu(), K))
+
+
+def test_tensor_core_oracle_infinite_key():
+    """A key row holding +inf: every query that sees it scores it +inf or NaN
+    (inf * 0 terms), and such rows go to the full-row exact selector; the result
+    is still the oracle's."""
+    B, H, Hkv, N, D, K = 1, 2, 1, 400, 128, 32
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=17, scale=1.0 / math.sqrt(D))
+    k[0, 0, 150, 7] = float("inf")
+    q, k = q.to(DEV), k.to(DEV)
+    tc, fb, status = _oracle_ws(q, k, K)
+    assert status == 0
+    _assert_same(tc, oracle.oracle_topk(q.cpu(), k.cpu(), K))
