@@ -51,7 +51,7 @@ def checksum(*ts) -> np.ndarray:
 
 
 def c1_inputs():
-    """BASELINE config 1 shape: B=1, 12 query / 2 kv heads, D=128, N=512, N(0,1)."""
+    """The small single-layer CPU workload: B=1, 12 query / 2 kv heads, D=128, N=512, N(0,1)."""
     return qkv(1, 12, 2, 512, 128, seed=0)
 
 

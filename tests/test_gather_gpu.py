@@ -155,7 +155,7 @@ def test_noncontiguous_inputs():
 
 
 def test_full_size_config2_properties():
-    """BASELINE config 2 shape (B=8, 12/2 heads, D=128, N=4096, K=64, bf16):
+    """The single-layer bf16 workload (B=8, 12/2 heads, D=128, N=4096, K=64, bf16):
     a sample of rows against the oracle, plus linearity in V (scaling V by 2
     doubles the output exactly in fp32 arithmetic before bf16 rounding)."""
     B, H, Hkv, N, D, K = 8, 12, 2, 4096, 128, 64

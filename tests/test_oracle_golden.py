@@ -21,7 +21,7 @@ def _load(golden_dir, name):
 
 
 def test_checkpoint_router_c1_sets_and_logits(golden_dir):
-    """BASELINE config 1 (B=1, 12/2 heads, D=128, N=512, K=64, fp32) with the
+    """The small single-layer workload (B=1, 12/2 heads, D=128, N=512, K=64, fp32) with the
     reference's trained layer-14 router: identical index sets on every row and
     bit-identical logits on the stored rows."""
     z = _load(golden_dir, "router_ckpt_c1.npz")
