@@ -66,7 +66,7 @@ def main(ref_root: str) -> None:
 
     torch.set_num_threads(8)
 
-    # --- A: BASELINE config 1 with the trained layer-14 router -------------
+    # --- A: the small single-layer workload with the trained layer-14 router
     ck = torch.load(ref_root / "checkpoints" / "content_router_layer14.pt", map_location="cpu",
                     weights_only=False)
     q, k, v = cases.c1_inputs()

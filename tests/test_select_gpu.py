@@ -34,13 +34,13 @@ def _assert_same(got: torch.Tensor, ref: np.ndarray):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("B,H,Hkv,N,D,r,L,K", [
-    (1, 12, 2, 512, 128, 64, 512, 64),     # config 1 shape
+    (1, 12, 2, 512, 128, 64, 512, 64),     # the small single-layer shape
     (2, 6, 3, 200, 64, 32, 128, 16),       # ragged, clamped pos_bias
     (1, 4, 1, 1, 128, 64, 16, 8),          # single row
     (1, 2, 2, 65, 64, 16, 64, 64),         # K == N - 1
     (1, 4, 2, 300, 128, 128, 300, 100),    # K not a multiple of 32
     (1, 2, 1, 97, 32, 64, 40, 160),        # K > N: padded rows everywhere
-    (2, 12, 2, 1000, 128, 64, 1000, 128),  # config 5's K
+    (2, 12, 2, 1000, 128, 64, 1000, 128),  # the long-context K
 ])
 @pytest.mark.parametrize("causal", [True, False])
 def test_router_topk_bit_exact(dtype, B, H, Hkv, N, D, r, L, K, causal):
@@ -92,7 +92,7 @@ def test_oracle_topk_bit_exact(dtype, B, H, Hkv, N, D, K):
 
 
 def test_checkpoint_router_matches_reference(golden_dir):
-    """Config 1 with the reference's trained router: the GPU selection equals the
+    """The small single-layer workload (N=512) with the reference's trained router: the GPU selection equals the
     reference's own causal top-64 sets on all 6144 rows."""
     z = np.load(golden_dir / "router_ckpt_c1.npz")
     q, k, _ = cases.c1_inputs()
@@ -168,7 +168,7 @@ def test_nan_scores_rank_first():
 
 
 def test_full_size_config2_selection():
-    """Config 2 (B=8, 12/2 heads, D=128, N=4096, K=64, bf16, random router):
+    """The single-layer bf16 workload (B=8, 12/2 heads, D=128, N=4096, K=64, random router):
     structural properties on every row and exact oracle agreement on a sample of
     rows from every (b, h)."""
     B, H, Hkv, N, D, r, K = 8, 12, 2, 4096, 128, 64, 64
