@@ -205,7 +205,7 @@ OSSA_API int ossa_router_topk_rows(const void* q, const void* k, int dtype,
 /*
  * Decode key cache.  No counterpart in the reference (its forward is
  * prefill-only, ossa/bench/sparse_forward.py:157-160).  A decoder projects each
- * new key once, k' = k Wk^T (router.py:180, the same fp32 chain as
+ * new key once, k' = k Wk^T (ossa/router.py:180, the same fp32 chain as
  * ossa_router_topk), into a cache it owns, and selects against the cached rows:
  *   ossa_router_project_keys:  k (rows, D) dtype -> kp_out (rows, r) fp32
  *   ossa_router_topk_rows_kp:  ossa_router_topk_rows with the keys given as

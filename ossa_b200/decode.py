@@ -4,7 +4,7 @@ The reference's patched forward is prefill-only (ossa/bench/sparse_forward.py:
 157-160 ignores ``past_key_values``).  For decoding, each generated token adds
 one key per kv head; ``router_topk`` would project every cached key again at
 every step.  ``RouterKeyCache`` projects each key once, k' = k Wk^T (the fp32
-chain of router.py:180 that every selector scores with), into a preallocated
+chain of ossa/router.py:180 that every selector scores with), into a preallocated
 (B, Hkv, capacity, r) fp32 cache, and selects the new query rows against the
 cached rows with ``ossa_router_topk_rows_kp``.  The indices are identical to
 ``router_topk(q_new, k_all, ..., q_start=...)`` on the same keys.

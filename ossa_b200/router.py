@@ -10,7 +10,7 @@ Additive differences:
 * ``k`` may carry Hkv < H heads (GQA); the reference needs repeated heads.
 * ``topk(..., causal=True)`` masks keys j > i before selecting (the patched
   forward's behaviour, sparse_forward.py:200-202); the default ``causal=False``
-  is the reference's unmasked ``topk`` (router.py:202-203).
+  is the reference's unmasked ``topk`` (ossa/router.py:202-203).
 * ``topk`` returns each row's index set in ascending key order (torch.topk
   orders by score), padded with -1 where fewer than ``top_k`` keys are
   eligible under the causal mask.  ``index_dtype`` defaults to int64 like
@@ -58,7 +58,7 @@ class ContentRouter(nn.Module):
         router does.  Additive: the reference sizes pos_bias as 2*seq_len and
         leaves longer contexts to retraining (README "Long context").  This
         router already clamps offsets i - j beyond +-seq_len to the table's edge
-        entries (router.py:183-188), so the copy's table holds entry
+        entries (ossa/router.py:183-188), so the copy's table holds entry
         clamp(o - seq_len + S, 0, 2S - 1) of this one (S = this router's
         seq_len) at index o: the edge entries repeat outward when growing, and
         offsets within +-min(S, seq_len) keep their entries when shrinking.

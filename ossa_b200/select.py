@@ -50,7 +50,7 @@ def _common_dtype(q: torch.Tensor, k: torch.Tensor) -> torch.dtype:
 def router_topk(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,
                 pos_bias: torch.Tensor, seq_len: int, top_k: int, *,
                 causal: bool = True, q_start: Optional[int] = None) -> torch.Tensor:
-    """ContentRouter top-K (router.py:171-190 scores) -> int32 (B, H, N, top_k).
+    """ContentRouter top-K (ossa/router.py:171-190 scores) -> int32 (B, H, N, top_k).
 
     q: (B, H, N, D); k: (B, Hkv, N, D) with Hkv dividing H (or the repeated H
     heads).  wq, wk: (r, D) projection weights; pos_bias: (2*seq_len, 1) or
