@@ -147,6 +147,20 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
+def _config(world: int) -> dict:
+    """The workload description both arms print (same keys, so the two lines
+    describe the same job)."""
+    return {"workload": WORKLOAD_NAME, "global_batch": WORKLOAD["B"] * world, "seq_len": WORKLOAD["N"],
+            **WORKLOAD,
+            "l2": "flushed between steps (256 MB write, outside the timed events)",
+            "parallelism": f"replicas x{world} (batch-sharded, no data-path collective)"}
+
+
+# Long-context configurations reported beside the headline workload: B=1, 12/2
+# heads, head_dim 128, random-init router; seq 32k at K=64 and 64k/128k at K=128.
+LONG_CONTEXT = ((32768, 64), (65536, 128), (131072, 128))
+
+
 def _dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -172,8 +186,126 @@ def make_inputs(device, seed: int, w=WORKLOAD):
     return q, k, v, wq.to(device), wk.to(device), pb.to(device)
 
 
+def _max_over_ranks(vals, dev, world):
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return t.tolist()
+
+
+def run_long_context(dev, world, rank, steps: int, warmup: int) -> list:
+    """Selection and gather at long context (LONG_CONTEXT), every rank its two
+    zig-zag query blocks of the sequence (one process: the whole sequence).  Per
+    step: the NCCL all-gather of K and V (N > 1), router_topk and topk_attention
+    on the rank's rows, each timed with CUDA events on the launching stream; the
+    step time and each part are maxima over ranks.  Inputs are larger than L2 (q
+    alone is 100-400 MB), so no flush is needed between steps."""
+    from ossa_b200 import router_topk, topk_attention
+    from ossa_b200.bench.long_context import make_inputs
+    from ossa_b200.sequence_shard import gather_sequence, local_rows, zigzag_blocks
+
+    peaks = _peaks()
+    traffic = _traffic()
+    stream = torch.cuda.current_stream(dev)
+    out = []
+    for N, K in LONG_CONTEXT:
+        q, k, v, wq, wk, pb = make_inputs(N, dev, seed=7)
+        ql, kl, vl = local_rows(q, world, rank), local_rows(k, world, rank), local_rows(v, world, rank)
+        del q, k, v
+        blk = ql.shape[2] // 2
+        if world == 1:  # the whole sequence in one call
+            blocks, qbs = [(0, N)], [ql]
+        else:
+            blocks = zigzag_blocks(N, world, rank)
+            qbs = [ql[:, :, h * blk:(h + 1) * blk].contiguous() for h in range(2)]
+
+        def step(evs=None):
+            if evs:
+                evs[0].record(stream)
+            kf = gather_sequence(kl, world)
+            vf = gather_sequence(vl, world)
+            if evs:
+                evs[1].record(stream)
+            idxs = [router_topk(qb, kf, wq, wk, pb, N, K, causal=True, q_start=st)
+                    for qb, (st, _) in zip(qbs, blocks)]
+            if evs:
+                evs[2].record(stream)
+            outs = [topk_attention(qb, kf, vf, topk_indices=ix, causal=True, q_start=st)
+                    for qb, ix, (st, _) in zip(qbs, idxs, blocks)]
+            if evs:
+                evs[3].record(stream)
+            return outs
+
+        with torch.inference_mode():
+            for _ in range(max(1, warmup)):
+                step()
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize()
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+            for e in evs:
+                step(e)
+            torch.cuda.synchronize()
+            if world > 1:
+                torch.distributed.barrier()
+        ag = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
+        sel = sum(e[1].elapsed_time(e[2]) for e in evs) / steps
+        gat = sum(e[2].elapsed_time(e[3]) for e in evs) / steps
+        tot = sum(e[0].elapsed_time(e[3]) for e in evs) / steps
+        tot, ag, sel, gat = _max_over_ranks([tot, ag, sel, gat], dev, world)
+        rows_local = 2 * blk  # query rows of this rank per head
+        # per-rank algorithmic work of the largest rank (zig-zag ranks are balanced)
+        sflops = (12 * rows_local * 2 * 128 * 64 + 2 * N * 2 * 128 * 64 +
+                  12 * sum(((e - 1) * e - (s - 1) * s) // 2 + (e - s) for s, e in blocks) * 2 * 64)
+        gbytes = gather_bytes(1, 12, rows_local, 128, K)
+        tkey = f"gather_attn_fwd_n{N}_k{K}"
+        entry = {
+            "seq_len": N, "K": K, "n_gpus": world, "ms_per_step": tot, "tokens_s": N / (tot / 1e3),
+            "allgather_ms": ag if world > 1 else 0.0, "select_ms": sel, "gather_ms": gat,
+            "select": {"bound": "tensor", "achieved": sflops / (sel / 1e3) / 1e12, "peak": peaks["bf16_tflops"],
+                       "unit": "TFLOP/s", "algorithmic": f"{sflops} flop per rank per step"},
+            "gather": {"bound": "hbm", "achieved": gbytes / (gat / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
+                       "unit": "GB/s", "algorithmic": f"{gbytes} B per rank per step",
+                       "traffic": traffic.get(tkey) if world == 1 else None},
+            "parallelism": "whole sequence on one GPU" if world == 1 else f"sequence zig-zag x{world}, "
+                           "NCCL all_gather_into_tensor of K and V",
+        }
+        for part in ("select", "gather"):
+            entry[part]["frac"] = entry[part]["achieved"] / entry[part]["peak"]
+        out.append(entry)
+        del ql, kl, vl, qbs
+        torch.cuda.empty_cache()
+    return out
+
+
+def host_link(dev, tensors) -> dict:
+    """Copy-only host->device bandwidth of the e2e step's inputs (pinned, one
+    cudaMemcpyAsync per tensor), CUDA events on the copying stream: the ceiling
+    the e2e figure is held against."""
+    dst = [torch.empty(t.shape, dtype=t.dtype, device=dev) for t in tensors]
+    nbytes = sum(t.numel() * t.element_size() for t in tensors)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(2):
+        for d, t in zip(dst, tensors):
+            d.copy_(t, non_blocking=True)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    a.record(stream)
+    for _ in range(reps):
+        for d, t in zip(dst, tensors):
+            d.copy_(t, non_blocking=True)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    return {"h2d_gbs": nbytes / (ms / 1e3) / 1e9, "bytes": nbytes, "ms": ms}
+
+
 def run_ours(args) -> None:
     world, rank, local = _dist()
+    if args.gpus != world:
+        raise SystemExit(f"bench.py: --gpus {args.gpus} but WORLD_SIZE is {world}; launch N > 1 GPUs with "
+                         f"torchrun --nproc-per-node {args.gpus}")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -249,11 +381,16 @@ def run_ours(args) -> None:
         b.record(stream)
     barrier()
     e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_evs)
+    link = host_link(dev, [qh, kh, vh])
+    del qh, kh, vh, oh
 
     t = torch.tensor([total_ms, e2e_ms, sum(sel_ms), sum(gat_ms)], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     total_ms, e2e_ms, sel_tot, gat_tot = t.tolist()
+    del q, k, v, flush
+    torch.cuda.empty_cache()
+    long_ctx = None if args.no_long_context else run_long_context(dev, world, rank, args.long_steps, 2)
 
     tokens = world * args.steps * B * N
     value = tokens / (total_ms / 1e3)
@@ -288,16 +425,16 @@ def run_ours(args) -> None:
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD_NAME, "global_batch": B * world, "seq_len": N, **w,
-                       "l2": "flushed between steps (256 MB write, outside the timed events)",
-                       "parallelism": f"replicas x{world} (batch-sharded, no data-path collective)"},
+            "config": _config(world),
             "per_gpu_tokens_s": value / world,
             "roofline": roof,
             "kernels": {"select": {"ms": sel_avg_s * 1e3, **select_roof},
                         "gather": {"ms": gat_avg_s * 1e3, **gather_roof}},
             "cpu_baseline": cpu,
             "e2e": {"value": world * args.steps * B * N / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms / args.steps, "host_link_copy_only": link},
+            "long_context": long_ctx,
             "gpu_launches": launches,
             "select_exact_fallback_rows": fb_rows, "select_status": sel_status,
             "clocks": clk.summary(),
@@ -382,7 +519,7 @@ def run_reference(args) -> None:
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD_NAME, **WORKLOAD},
+        "config": _config(world),
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -398,6 +535,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-long-context", action="store_true",
+                    help="skip the long-context (32k-128k) selection and gather figures")
+    ap.add_argument("--long-steps", type=int, default=3, help="timed steps per long-context configuration")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

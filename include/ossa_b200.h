@@ -111,6 +111,20 @@ OSSA_API int ossa_router_topk(const void* q, const void* k, int dtype,
                      ossa_stream_t stream);
 
 /*
+ * ossa_router_topk with each row in the order torch.topk returns.
+ * Replaces ContentRouter.topk (ossa/router.py:202-203), whose result is
+ * torch.topk(score, k).indices: keys by descending score.  Same arguments,
+ * workspace and selected sets as ossa_router_topk; row i lists its keys by
+ * (fp32 score desc, key index asc), -1 padding last.
+ */
+OSSA_API int ossa_router_topk_sorted(const void* q, const void* k, int dtype,
+                                     const float* wq, const float* wk, const float* pos_bias,
+                                     int B, int H, int Hkv, int N, int D, int r, int seq_len_cfg,
+                                     int K, int causal, int32_t* idx_out,
+                                     void* workspace, size_t workspace_bytes,
+                                     ossa_stream_t stream);
+
+/*
  * Diagnostic, no counterpart in the reference: reads (synchronously) the
  * counters block of a router workspace after ossa_router_topk has run on it:
  * the number of rows the tensor-core selector handed to its exact fallback
@@ -167,15 +181,26 @@ OSSA_API int ossa_oracle_topk_ws(const void* q, const void* k, int dtype,
  * array inside the library, held on every GPU that loads the library until the
  * process exits.  Shapes whose ossa_router_workspace_size exceeds 32 MiB are
  * rejected with OSSA_ERR_WORKSPACE.  The first call on each device looks up the
- * array's device address (make it before any stream capture).  All calls share
- * the array: calls whose work overlaps on the GPU race and must be serialised
- * by the caller.  Same arguments and results as ossa_router_topk otherwise.
+ * array's device address (make it before any stream capture); later calls look
+ * it up again unless their stream is capturing.  `stream` must belong to the
+ * current device.  All calls share the array: calls whose work overlaps on the
+ * GPU race and must be serialised by the caller.  Same arguments and results as
+ * ossa_router_topk otherwise.
  */
 OSSA_API int ossa_router_topk_noalloc(const void* q, const void* k, int dtype,
                                       const float* wq, const float* wk, const float* pos_bias,
                                       int B, int H, int Hkv, int N, int D, int r, int seq_len_cfg,
                                       int K, int causal, int32_t* idx_out,
                                       ossa_stream_t stream);
+
+/*
+ * ossa_router_status for ossa_router_topk_noalloc, whose callers never see its
+ * workspace: reads (synchronously) the counters of the last call on the current
+ * device from the library's scratch array: rows handed to the exact fallback and
+ * the status word (0 = ok; nonzero = a bounded device-side wait expired and that
+ * call's indices are not valid).  No counterpart in the reference.
+ */
+OSSA_API int ossa_router_status_noalloc(int* fallback_rows, int* status);
 
 /*
  * Query-row ranges for sequence sharding.  No counterpart in the reference,

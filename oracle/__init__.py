@@ -170,6 +170,20 @@ def router_topk_rows(q, k, wq, wk, pos_bias, seq_len: int, K: int, rows, causal:
     return out
 
 
+def order_by_score(idx: np.ndarray, scores: np.ndarray) -> np.ndarray:
+    """Reorders index rows (as router_topk(..., with_scores=True) returns them)
+    to torch.topk's order: descending score (NaN first, as torch.topk ranks it),
+    ties toward the lower key index, -1 padding last (ossa/router.py:202-203)."""
+    bits = np.ascontiguousarray(scores, dtype=np.float32).view(np.uint32).astype(np.int64)
+    bits = np.where(np.isnan(scores), 0x7FC00000, bits)
+    okey = np.where(bits & 0x80000000, (~bits) & 0xFFFFFFFF, bits | 0x80000000)
+    valid = idx >= 0
+    primary = np.where(valid, -okey, 1)  # padding after every real score
+    secondary = np.where(valid, idx, 0)
+    perm = np.lexsort((secondary, primary), axis=-1)
+    return np.take_along_axis(idx, perm, axis=-1)
+
+
 def torch_index(rows: np.ndarray):
     import torch
     return torch.from_numpy(rows)

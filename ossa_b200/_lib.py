@@ -30,10 +30,12 @@ EXPORTED = (
     "ossa_topk_attention_fwd",
     "ossa_router_workspace_size",
     "ossa_router_topk",
+    "ossa_router_topk_sorted",
     "ossa_router_status",
     "ossa_router_score",
     "ossa_oracle_topk",
     "ossa_router_topk_noalloc",
+    "ossa_router_status_noalloc",
     "ossa_topk_attention_fwd_rows",
     "ossa_router_workspace_size_rows",
     "ossa_router_topk_rows",
@@ -71,6 +73,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ossa_router_workspace_size.restype = sz
     lib.ossa_router_topk.argtypes = [vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, ci, ci, vp, vp, sz, vp]
     lib.ossa_router_topk.restype = ci
+    lib.ossa_router_topk_sorted.argtypes = [vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, ci, ci, vp, vp, sz, vp]
+    lib.ossa_router_topk_sorted.restype = ci
     lib.ossa_router_status.argtypes = [vp, ctypes.POINTER(ci), ctypes.POINTER(ci)]
     lib.ossa_router_status.restype = ci
     lib.ossa_router_score.argtypes = [vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, vp, vp, sz, vp]
@@ -79,6 +83,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ossa_oracle_topk.restype = ci
     lib.ossa_router_topk_noalloc.argtypes = [vp, vp, ci, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, ci, ci, vp, vp]
     lib.ossa_router_topk_noalloc.restype = ci
+    lib.ossa_router_status_noalloc.argtypes = [ctypes.POINTER(ci), ctypes.POINTER(ci)]
+    lib.ossa_router_status_noalloc.restype = ci
     lib.ossa_topk_attention_fwd_rows.argtypes = [vp, vp, vp, vp] + [ci] * 9 + [cf, ci, ci, vp, vp]
     lib.ossa_topk_attention_fwd_rows.restype = ci
     lib.ossa_router_workspace_size_rows.argtypes = [ci] * 7

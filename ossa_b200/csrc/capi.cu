@@ -38,6 +38,19 @@ namespace ossa {
 // Lets other translation units of the library report a message through
 // ossa_last_error_string.
 void set_error_message(const char* msg) { g_last_error = msg; }
+
+int device_sm_count() {
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> cached[kMaxDev];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+        cached[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
 }  // namespace ossa
 
 namespace {
@@ -332,6 +345,26 @@ int ossa_router_topk(const void* q, const void* k, int dtype, const float* wq, c
                      size_t workspace_bytes, ossa_stream_t stream) {
     return ossa_router_topk_rows(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, N, D, r, seq_len_cfg, K, causal, 0,
                                  idx_out, workspace, workspace_bytes, stream);
+}
+
+int ossa_router_topk_sorted(const void* q, const void* k, int dtype, const float* wq, const float* wk,
+                            const float* pos_bias, int B, int H, int Hkv, int N, int D, int r, int seq_len_cfg,
+                            int K, int causal, int32_t* idx_out, void* workspace, size_t workspace_bytes,
+                            ossa_stream_t stream) {
+    int st = ossa_router_topk(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, D, r, seq_len_cfg, K, causal, idx_out,
+                              workspace, workspace_bytes, stream);
+    if (st) return st;
+    if ((long long)B * H * N == 0) return OSSA_OK;
+    if (!ossa::sort_rows_supported(r, K))
+        return fail(OSSA_ERR_UNSUPPORTED, "score-ordered rows support K <= 256 (got K=%d)", K);
+    // the selection left the canonical projections in the workspace
+    const RouterLayout l = router_layout(B, H, Hkv, N, N, r, K);
+    char* base = static_cast<char*>(workspace);
+    ossa::SortRowsArgs a{reinterpret_cast<const float*>(base + l.qp_off),
+                         reinterpret_cast<const float*>(base + l.kp_off),
+                         pos_bias, seq_len_cfg, H, Hkv, N, r, K, (float)(1.0 / sqrt((double)r)),
+                         (long long)B * H * N, idx_out};
+    return cuda_status(ossa::launch_sort_rows(a, static_cast<cudaStream_t>(stream)), "score-order launch");
 }
 
 int ossa_router_score(const void* q, const void* k, int dtype, const float* wq, const float* wk,

@@ -15,6 +15,9 @@ void note_launch(int n = 1);
 // Sets the message ossa_last_error_string returns on this thread.
 void set_error_message(const char* msg);
 
+// Streaming multiprocessors of the current device (queried once per device).
+int device_sm_count();
+
 struct GatherArgs {
     const void* q;
     const void* k;
@@ -93,6 +96,22 @@ cudaError_t launch_rope_heads(const RopeArgs& a, cudaStream_t stream);
 bool split_select_supported(int R, int K);
 size_t split_select_workspace_bytes(long long rows, int N, int K);
 cudaError_t launch_split_select(const SplitSelectArgs& a, cudaStream_t stream);
+
+// Reorders each selected index row (ascending keys, -1 padded) in place to
+// (canonical score desc, key asc), -1 padding last: torch.topk's order.
+// qp (rows, R), kp (B*Hkv*N, R) fp32 projections; rows = B*H*N.
+struct SortRowsArgs {
+    const float* qp;
+    const float* kp;
+    const float* bias;  // nullptr: no position term
+    int L;
+    int H, Hkv, N, R, K;
+    float scale;
+    long long rows;
+    int32_t* idx;       // (rows, K)
+};
+bool sort_rows_supported(int R, int K);
+cudaError_t launch_sort_rows(const SortRowsArgs& a, cudaStream_t stream);
 
 // Dense fp32 scores (B, H, N, N) with the same score definition, no mask.
 struct ScoreDenseArgs {

@@ -11,12 +11,18 @@
 // The array is a file-scope __device__ variable: every GPU that loads the
 // library holds its kNoAllocScratchBytes until the process exits.  Its name is
 // only a host-side stand-in, so the device address is looked up with
-// cudaGetSymbolAddress, once per device, with that device current; the first
-// call on each device does the lookup (make that first call before any stream
-// capture).  All calls share the one array: calls whose work overlaps on the GPU
-// (different streams, or different host threads) race on it and must be
-// serialised by the caller.  The array keeps the previous call's contents;
-// ossa_router_topk clears the parts that must start at zero on every call.
+// cudaGetSymbolAddress, with the device current: the first call on each device
+// does the lookup (make that first call before any stream capture), and every
+// later call made while its stream is not capturing looks it up again, so a
+// context torn down and created again (cudaDeviceReset) cannot leave a stale
+// address behind.  Calls made during a capture use the address of the last
+// lookup.  The stream must belong to the current device.  All calls share the
+// one array: calls whose work overlaps on the GPU (different streams, or
+// different host threads) race on it and must be serialised by the caller.  The
+// array keeps the previous call's contents; ossa_router_topk clears the parts
+// that must start at zero on every call.  Its first 8 bytes are the counters of
+// the last call (rows sent to the exact fallback, status word), which
+// ossa_router_status_noalloc reads.
 #include "../../include/ossa_b200.h"
 #include "kernels.h"
 
@@ -34,14 +40,20 @@ constexpr int kMaxDevices = 64;
 std::mutex g_lock;
 void* g_scratch_ptr[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device (looked up once).
-cudaError_t scratch_address(void** out) {
+// Device address of the scratch array on the current device: looked up on the
+// first call and on every call whose stream is not capturing; a capturing
+// stream reuses the last address (a lookup is not a stream operation, but the
+// capture should record exactly what the caller enqueues).
+cudaError_t scratch_address(cudaStream_t stream, void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> guard(g_lock);
-    if (!g_scratch_ptr[dev]) {
+    if (!g_scratch_ptr[dev] || cap == cudaStreamCaptureStatusNone) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return e;
@@ -70,7 +82,7 @@ int ossa_router_topk_noalloc(const void* q, const void* k, int dtype, const floa
         return OSSA_ERR_WORKSPACE;
     }
     void* ws = nullptr;
-    const cudaError_t e = scratch_address(&ws);
+    const cudaError_t e = scratch_address(static_cast<cudaStream_t>(stream), &ws);
     if (e != cudaSuccess) {
         snprintf(msg, sizeof(msg), "ossa_router_topk_noalloc: scratch address lookup failed: %s",
                  cudaGetErrorString(e));
@@ -79,6 +91,21 @@ int ossa_router_topk_noalloc(const void* q, const void* k, int dtype, const floa
     }
     return ossa_router_topk(q, k, dtype, wq, wk, pos_bias, B, H, Hkv, N, D, r, seq_len_cfg, K, causal, idx_out,
                             ws, kNoAllocScratchBytes, stream);
+}
+
+int ossa_router_status_noalloc(int* fallback_rows, int* status) {
+    int h[2] = {0, 0};
+    // synchronous read of the counters block at the start of this device's array
+    const cudaError_t e = cudaMemcpyFromSymbol(h, g_noalloc_scratch, sizeof(h), 0, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) {
+        char msg[256];
+        snprintf(msg, sizeof(msg), "ossa_router_status_noalloc: counters read failed: %s", cudaGetErrorString(e));
+        ossa::set_error_message(msg);
+        return OSSA_ERR_CUDA;
+    }
+    if (fallback_rows) *fallback_rows = h[0];
+    if (status) *status = h[1];
+    return OSSA_OK;
 }
 
 }  // extern "C"

@@ -1842,11 +1842,12 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.nqb = nqb;
     prm.scale = a.scale;
     const long long nblk = (long long)nqb * a.B * a.H;
+    const int nsm = device_sm_count();
     if (!global_lists) {
         router_tc_kernel<false, kD><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
         // rows sent to the exact selector (K + 32 candidates per warp: 4 entries per lane)
-        exact_rows_kernel<4, kD, kBias><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
+        exact_rows_kernel<4, kD, kBias><<<2 * nsm, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
                                                                      Nq, a.q0, a.K, a.scale, a.causal, counters,
                                                                      fb_list, a.out);
         return record(cudaGetLastError());
@@ -1874,17 +1875,17 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     fp.q0 = a.q0;
     fp.nqb = nqb;
     fp.scale = a.scale;
-    const unsigned fblk = (unsigned)std::min<long long>(((long long)rq + 7) / 8, 148LL * 8);
+    const unsigned fblk = (unsigned)std::min<long long>(((long long)rq + 7) / 8, 8LL * nsm);
     if (wide) final_select_kernel<TcCfg<true, kD>::kCap, kWideMaxK, kD, kBias><<<fblk, 256, 0, stream>>>(fp);
     else final_select_kernel<TcCfg<false, kD>::kCap, kNarrowMaxK, kD, kBias><<<fblk, 256, 0, stream>>>(fp);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     // rows sent to the exact selector (K + 32 candidates per warp: 6 entries per lane for K <= 160)
     if (wide)
-        exact_rows_kernel<6, kD, kBias><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
+        exact_rows_kernel<6, kD, kBias><<<2 * nsm, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
                                                                      Nq, a.q0, a.K, a.scale, a.causal, counters,
                                                                      fb_list, a.out);
     else
-        exact_rows_kernel<4, kD, kBias><<<148 * 2, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
+        exact_rows_kernel<4, kD, kBias><<<2 * nsm, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
                                                                      Nq, a.q0, a.K, a.scale, a.causal, counters,
                                                                      fb_list, a.out);
     return record(cudaGetLastError());

@@ -26,6 +26,17 @@ from .topk_attention import topk_attention
 
 __all__ = ["routed_attention_from_host"]
 
+# The pipeline's three streams, created once per device and reused by every call.
+_streams: dict = {}
+
+
+def _pipeline_streams(dev: torch.device):
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _streams.get(key)
+    if st is None:
+        st = _streams[key] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return st
+
 
 def routed_attention_from_host(q_host, k_host, v_host, wq, wk, pos_bias, seq_len: int, top_k: int,
                                out_host, *, causal: bool = True, chunk: int = 2, device=None):
@@ -52,9 +63,7 @@ def routed_attention_from_host(q_host, k_host, v_host, wq, wk, pos_bias, seq_len
     if dev.type != "cuda":
         raise ValueError("the router weights must live on a CUDA device")
     caller = torch.cuda.current_stream(dev)
-    s_in = torch.cuda.Stream(dev)
-    s_comp = torch.cuda.Stream(dev)
-    s_out = torch.cuda.Stream(dev)
+    s_in, s_comp, s_out = _pipeline_streams(dev)
     # work queued on the caller's stream before this call comes first
     s_in.wait_stream(caller)
     s_comp.wait_stream(caller)

@@ -11,10 +11,12 @@ Additive differences:
 * ``topk(..., causal=True)`` masks keys j > i before selecting (the patched
   forward's behaviour, sparse_forward.py:200-202); the default ``causal=False``
   is the reference's unmasked ``topk`` (ossa/router.py:202-203).
-* ``topk`` returns each row's index set in ascending key order (torch.topk
-  orders by score), padded with -1 where fewer than ``top_k`` keys are
-  eligible under the causal mask.  ``index_dtype`` defaults to int64 like
-  torch.topk; int32 avoids a conversion.
+* ``topk`` returns each row's keys in torch.topk's order (descending fp32
+  score, ties toward the lower key index), padded with -1 where fewer than
+  ``top_k`` keys are eligible under the causal mask.  ``order="index"`` gives
+  ascending key order instead (the selectors' native layout, which the gather
+  consumes).  ``index_dtype`` defaults to int64 like torch.topk; int32 avoids a
+  conversion.
 * Scores are defined by a fixed fp32 evaluation order (fmaf chains) so the
   selected sets are reproducible bit for bit.
 """
@@ -88,11 +90,16 @@ class ContentRouter(nn.Module):
         return self.score(q, k)
 
     def topk(self, q: torch.Tensor, k: torch.Tensor, top_k: int, *, causal: bool = False,
-             index_dtype: torch.dtype = torch.int64) -> torch.Tensor:
-        """Indices (B, H, N, top_k) of the top_k keys per query (see module doc)."""
+             index_dtype: torch.dtype = torch.int64, order: str = "score") -> torch.Tensor:
+        """Indices (B, H, N, top_k) of the top_k keys per query, by descending
+        score like torch.topk (ossa/router.py:202-203); ``order="index"`` lists
+        each row's keys in ascending order instead (see module doc)."""
+        if order not in ("score", "index"):
+            raise ValueError(f"order must be 'score' or 'index', got {order!r}")
         N = q.shape[2]
         if not causal and top_k > N:
             raise RuntimeError(f"selected index k out of range: top_k={top_k} > N={N}")
         wq, wk, pb = self._params()
-        idx = select.router_topk(q, k, wq, wk, pb, self.cfg.seq_len, top_k, causal=causal)
+        fn = select.router_topk_by_score if order == "score" else select.router_topk
+        idx = fn(q, k, wq, wk, pb, self.cfg.seq_len, top_k, causal=causal)
         return idx if index_dtype == torch.int32 else idx.to(index_dtype)

@@ -71,7 +71,17 @@ def router_topk_with_status(q, k, wq, wk, pos_bias, seq_len: int, top_k: int, *,
     return _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, causal=causal, with_status=True)
 
 
-def _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, *, causal=True, with_status=False, q_start=None):
+def router_topk_by_score(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,
+                         pos_bias: torch.Tensor, seq_len: int, top_k: int, *, causal: bool = True) -> torch.Tensor:
+    """router_topk with each row in torch.topk's order: keys by descending fp32
+    score, ties toward the lower key index, -1 padding last (the order of
+    ``torch.topk(score, k).indices`` in ossa/router.py:202-203).  Same sets as
+    router_topk."""
+    return _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, causal=causal, by_score=True)[0]
+
+
+def _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, *, causal=True, with_status=False, q_start=None,
+                 by_score=False):
     B, H, Hkv, N, D = _check_qk(q, k, rows=q_start is not None)
     Nk = k.shape[2]
     q0 = 0 if q_start is None else int(q_start)
@@ -98,7 +108,12 @@ def _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, *, causal=True, with_st
     ws_bytes = L.ossa_router_workspace_size_rows(B, H, Hkv, N, Nk, r, top_k)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        if q_start is None:
+        if by_score:
+            st = L.ossa_router_topk_sorted(qc.data_ptr(), kc.data_ptr(), _lib.dtype_code(qc), wqc.data_ptr(),
+                                           wkc.data_ptr(), pbc.data_ptr(), B, H, Hkv, N, D, r, int(seq_len),
+                                           int(top_k), 1 if causal else 0, out.data_ptr(), ws.data_ptr(),
+                                           ws_bytes, _lib.stream_ptr(dev))
+        elif q_start is None:
             st = L.ossa_router_topk(qc.data_ptr(), kc.data_ptr(), _lib.dtype_code(qc), wqc.data_ptr(),
                                     wkc.data_ptr(), pbc.data_ptr(), B, H, Hkv, N, D, r, int(seq_len),
                                     int(top_k), 1 if causal else 0, out.data_ptr(), ws.data_ptr(),

@@ -1,15 +1,18 @@
 """Generates tests/golden/*.npz by running the reference implementation itself.
 
-Run in a checkout that has the reference source tree (read-only is fine):
+Run in a checkout that has the reference source tree (read-only is fine), giving
+the reference project's root directory (the one holding ``src/ossa`` and
+``checkpoints/``) as the one required argument:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /root/reference
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py <reference-root>
 
 It imports the reference's ``ossa`` package (router.py, sparse_attention.py) and
 its trained router checkpoint (checkpoints/content_router_layer14.pt) and records
 the reference's outputs on seeded inputs (tests/golden/cases.py).  The fixtures
 store the reference's top-K index sets (sorted ascending, entries > i dropped
-and -1 padded, which is the set the causal sparse forward actually uses),
-boundary-score gaps, a few rows of raw logits and sparse-forward outputs.
+and -1 padded, which is the set the causal sparse forward actually uses), the
+same indices in torch.topk's own order (descending score), boundary-score gaps,
+a few rows of raw logits and sparse-forward outputs.
 """
 
 from __future__ import annotations
@@ -93,6 +96,7 @@ def main(ref_root: str) -> None:
         seq_len=np.int64(512), K=np.int64(K),
         checksum=cases.checksum(q, k, v),
         ref_sets=causal_sets(top).astype(np.int16),
+        ref_order=top.numpy().astype(np.int16),
         ref_gap=boundary_gap(logits, K),
         logit_rows=rows,
         ref_logits=logits[:, :, rows, :].numpy(),
@@ -127,6 +131,7 @@ def main(ref_root: str) -> None:
         ref_sets=causal_sets(top_c).astype(np.int16),
         ref_gap=boundary_gap(logits, K),
         ref_full_sets=full_sets(top_full).astype(np.int16),
+        ref_full_order=top_full.numpy().astype(np.int16),
         logit_rows=np.array([0, 1, 15, 16, 127, 128, 199]),
         ref_logits=logits[:, :, [0, 1, 15, 16, 127, 128, 199], :].numpy(),
         ref_out=out.numpy(),
@@ -178,4 +183,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <reference-root>  (the directory holding src/ossa and checkpoints/)")
+    main(sys.argv[1])

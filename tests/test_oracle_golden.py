@@ -35,6 +35,23 @@ def test_checkpoint_router_c1_sets_and_logits(golden_dir):
     np.testing.assert_array_equal(logits[:, :, z["logit_rows"], :], z["ref_logits"])
 
 
+def test_checkpoint_router_c1_score_order(golden_dir):
+    """torch.topk's own order (descending score) on the same workload: the oracle's
+    sets ordered by (score desc, key asc) equal the reference's top-64 indices
+    element for element on every row's first min(64, i + 1) entries (the rest are
+    masked future keys there and -1 here)."""
+    z = _load(golden_dir, "router_ckpt_c1.npz")
+    q, k, v = cases.c1_inputs()
+    idx, sc = oracle.router_topk(q, k, z["wq"], z["wk"], z["pos_bias"], int(z["seq_len"]), int(z["K"]),
+                                 with_scores=True)
+    got = oracle.order_by_score(idx, sc)
+    ref = z["ref_order"].astype(np.int32)
+    N, K = got.shape[2], got.shape[3]
+    prefix = np.arange(K)[None, :] < np.minimum(K, np.arange(N) + 1)[:, None]
+    np.testing.assert_array_equal(np.where(prefix, got, -1), np.where(prefix, ref, -1))
+    assert (got[..., ~prefix] == -1).all()
+
+
 def test_checkpoint_router_c1_output(golden_dir):
     z = _load(golden_dir, "router_ckpt_c1.npz")
     q, k, v = cases.c1_inputs()
@@ -56,8 +73,10 @@ def test_random_router_gqa_causal_and_full(golden_dir):
     assert np.array_equal(cases.checksum(q, k, v, wq, wk, pb), z["checksum"])
     idx = oracle.router_topk(q, k, wq, wk, pb, L, K, causal=True)
     assert np.array_equal(idx, z["ref_sets"].astype(np.int32))
-    idx_full = oracle.router_topk(q, k, wq, wk, pb, L, K, causal=False)
+    idx_full, sc_full = oracle.router_topk(q, k, wq, wk, pb, L, K, causal=False, with_scores=True)
     assert np.array_equal(idx_full, z["ref_full_sets"].astype(np.int32))
+    # ContentRouter.topk's order: torch.topk(score, K).indices, element for element
+    assert np.array_equal(oracle.order_by_score(idx_full, sc_full), z["ref_full_order"].astype(np.int32))
     logits = oracle.router_scores(q, k, wq, wk, pb, L)
     np.testing.assert_array_equal(logits[:, :, z["logit_rows"], :], z["ref_logits"])
     out = rp.masked_index_attention(q, k, v, torch.from_numpy(idx.astype(np.int64)))

@@ -101,10 +101,19 @@ def test_checkpoint_router_matches_reference(golden_dir):
                             "k_proj.0.weight": torch.from_numpy(z["wk"]),
                             "pos_bias.weight": torch.from_numpy(z["pos_bias"])})
     router = router.to(DEV)
-    got = router.topk(q.to(DEV), k.to(DEV), 64, causal=True, index_dtype=torch.int32)
+    got = router.topk(q.to(DEV), k.to(DEV), 64, causal=True, index_dtype=torch.int32, order="index")
     _assert_same(got, z["ref_sets"].astype(np.int32))
     logits = router.score(q.to(DEV), k.to(DEV))
     np.testing.assert_array_equal(logits[:, :, z["logit_rows"]].cpu().numpy(), z["ref_logits"])
+    # torch.topk's order (descending score): row i's first min(64, i + 1) entries are
+    # the reference's, element for element; the rest are -1 here and masked keys there
+    ordered = router.topk(q.to(DEV), k.to(DEV), 64, causal=True).cpu().numpy()
+    ref = z["ref_order"].astype(np.int64)
+    n_valid = np.minimum(64, np.arange(512) + 1)
+    lane = np.arange(64)
+    prefix = lane[None, :] < n_valid[:, None]                 # (N, 64)
+    np.testing.assert_array_equal(np.where(prefix, ordered, -1), np.where(prefix, ref, -1))
+    assert (ordered[..., ~prefix] == -1).all()
 
 
 def test_random_router_matches_reference_unmasked(golden_dir):
@@ -123,9 +132,35 @@ def test_random_router_matches_reference_unmasked(golden_dir):
     router = router.to(DEV)
     full = router.topk(q.to(DEV), k.to(DEV), K)
     assert full.dtype == torch.int64
-    _assert_same(full.int(), z["ref_full_sets"].astype(np.int32))
-    causal = router.topk(q.to(DEV), k.to(DEV), K, causal=True)
+    # element for element: the reference's torch.topk(score, K).indices order
+    np.testing.assert_array_equal(full.cpu().numpy(), z["ref_full_order"].astype(np.int64))
+    full_sets = router.topk(q.to(DEV), k.to(DEV), K, order="index")
+    _assert_same(full_sets.int(), z["ref_full_sets"].astype(np.int32))
+    causal = router.topk(q.to(DEV), k.to(DEV), K, causal=True, order="index")
     _assert_same(causal.int(), z["ref_sets"].astype(np.int32))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,H,Hkv,N,D,r,L,K,causal", [
+    (1, 12, 2, 512, 128, 64, 512, 64, True),     # the small single-layer shape
+    (2, 4, 2, 300, 128, 64, 256, 128, False),    # unmasked, wide K
+    (1, 6, 3, 200, 64, 32, 128, 16, True),       # ragged, clamped pos_bias
+])
+def test_router_topk_score_order(dtype, B, H, Hkv, N, D, r, L, K, causal):
+    """ContentRouter.topk's default order (torch.topk's): every row element for
+    element equal to the oracle's sets ordered by (score desc, key asc)."""
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=7 * N + K, scale=1.0 / math.sqrt(D))
+    q, k = q.to(dtype), k.to(dtype)
+    wq, wk, pb = _weights(D, r, L, seed=K)
+    router = ContentRouter(ContentRouterConfig(head_dim=D, n_heads=H, seq_len=L, proj_dim=r))
+    with torch.no_grad():
+        router.q_proj[0].weight.copy_(wq)
+        router.k_proj[0].weight.copy_(wk)
+        router.pos_bias.weight.copy_(pb)
+    router = router.to(DEV)
+    got = router.topk(q.to(DEV), k.to(DEV), K, causal=causal, index_dtype=torch.int32)
+    idx, sc = oracle.router_topk(q, k, wq, wk, pb, L, K, causal=causal, with_scores=True)
+    _assert_same(got, oracle.order_by_score(idx, sc))
 
 
 def test_all_ties_pick_lowest_indices():

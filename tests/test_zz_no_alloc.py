@@ -13,6 +13,7 @@ The file sorts last so a run that stops at the first failure has already run
 every other test; it also passes when run alone in a fresh process.
 """
 
+import ctypes
 import math
 
 import pytest
@@ -55,6 +56,12 @@ def _no_alloc(q, k, wq, wk, pb, K):
     return out
 
 
+def _status():
+    fb, st = ctypes.c_int(-1), ctypes.c_int(-1)
+    _lib.check(_lib.lib().ossa_router_status_noalloc(ctypes.byref(fb), ctypes.byref(st)))
+    return fb.value, st.value
+
+
 def test_no_alloc_matches_workspace_entry_point_twice():
     K = 64
     first = _inputs(seed=101)
@@ -69,6 +76,50 @@ def test_no_alloc_matches_workspace_entry_point_twice():
     assert torch.equal(a2, b2)
     # and once more on the first inputs after the second call used the scratch
     assert torch.equal(_no_alloc(*first, K), b1)
+    torch.cuda.synchronize()
+    assert _status()[1] == 0  # no bounded device wait expired
+
+
+@pytest.mark.parametrize("K,N,exact", [
+    (128, 512, False),   # 64 < K <= 128: candidate lists and final choice in the scratch
+    (64, 40, False),     # fewer than 128 query rows per head group: CUDA-core selector
+    (64, 700, True),     # the exact CUDA-core selector forced, after tensor-core calls left their data
+])
+def test_no_alloc_other_selector_paths(K, N, exact, monkeypatch):
+    """The other selection paths through the shared scratch, each checked against the
+    workspace entry point on two calls in a row, with the counters read back."""
+    if exact:
+        monkeypatch.setenv("OSSA_ROUTER_SELECT", "exact")
+    x = _inputs(seed=300 + K + N, N=N)
+    ref = _with_workspace(*x, K)
+    for _ in range(2):
+        assert torch.equal(_no_alloc(*x, K), ref)
+        torch.cuda.synchronize()
+        assert _status()[1] == 0
+
+
+def test_no_alloc_allocates_nothing():
+    """Free device memory is unchanged across calls once the output exists (after a
+    warm-up call, which may load kernels)."""
+    K = 64
+    x = _inputs(seed=404, N=2048)
+    out = torch.empty(1, 12, 2048, K, dtype=torch.int32, device=DEV)
+    L = _lib.lib()
+
+    def call():
+        q, k, wq, wk, pb = x
+        _lib.check(L.ossa_router_topk_noalloc(q.data_ptr(), k.data_ptr(), _lib.OSSA_BF16, wq.data_ptr(),
+                                              wk.data_ptr(), pb.data_ptr(), 1, 12, 2, 2048, 128, 64, 2048, K, 1,
+                                              out.data_ptr(), _lib.stream_ptr(q.device)))
+
+    call()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert torch.equal(out, _with_workspace(*x, K))
 
 
 def test_no_alloc_rejects_shapes_beyond_its_scratch():
