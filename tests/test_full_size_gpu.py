@@ -11,7 +11,10 @@
 * The single-layer bf16 workload's gather (B=8, N=4096, K=64): 64 rows of every batch
   element against the fp64 attention oracle.
 
-Indices must be equal; attention outputs within 2e-3 abs/rel (bf16).
+Indices must be equal; attention outputs within 2e-3 abs/rel (bf16) of the fp64
+oracle, plus half a bf16 ulp of the oracle's value: the output is itself a bf16
+number, so at unit-scale values (the oracle workload's V is unit-normal) its own
+rounding is already about 2e-3.
 """
 
 import math
@@ -55,8 +58,13 @@ def _check_gather_rows(out, q, k, v, idx, rows, H, N):
         ref = rp.masked_index_attention(q[b:b + 1, h:h + 1, pos.to(q.device)].float().cpu(),
                                         k[b:b + 1, g:g + 1].float().cpu(), v[b:b + 1, g:g + 1].float().cpu(),
                                         idx[b:b + 1, h:h + 1, pos.to(idx.device)].cpu(), positions=pos)
-        got = out[b:b + 1, h:h + 1, pos.to(out.device)].float().cpu()
-        torch.testing.assert_close(got, ref.float(), **TOL)
+        got = out[b:b + 1, h:h + 1, pos.to(out.device)].double().cpu()
+        mag = ref.abs().clamp(min=2.0 ** -126)
+        half_ulp = torch.exp2(torch.floor(torch.log2(mag)) - 8)  # bf16: 8 significant bits
+        tol = TOL["atol"] + TOL["rtol"] * ref.abs() + half_ulp
+        err = (got - ref).abs()
+        assert bool((err <= tol).all()), (f"(b={b}, h={h}): {int((err > tol).sum())} elements beyond "
+                                         f"2e-3 + half a bf16 ulp; worst excess {float((err - tol).max()):.3g}")
 
 
 @pytest.mark.parametrize("K", [32, 128])
