@@ -166,6 +166,58 @@ gather_attn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k,
 // score, probability and index live in lane 16 * (m & 1) + (m >> 1).
 // Numerics: fp32 dot products of the bf16 inputs, fp32 online softmax, and
 // p rounded to bf16 for the p.v product (as the reference's bf16 einsum does).
+//
+// One (query, head) row, one warp: kb / vb point at this lane's 16-byte column of
+// key / value row 0 of the kv head; irow is the row's K indices.
+template <typename IdxT>
+__device__ __forceinline__ void gather_row_bf16_d128(uint4 qv, const uint4* __restrict__ kb,
+                                                     const uint4* __restrict__ vb, const IdxT* __restrict__ irow,
+                                                     int K, int N, int i, int causal, float scale_log2,
+                                                     __nv_bfloat16* __restrict__ orow, int lane) {
+    constexpr int D = 128;
+    const int half = lane >> 4;
+    const int hl = lane & 15;
+    const int myslot = 2 * hl + half;  // key slot held by this lane
+    float m_run = -INFINITY, l_run = 0.f;
+    float acc[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+
+    for (int kc = 0; kc < K; kc += 32) {
+        const int kk = kc + myslot;
+        const long long jl = kk < K ? (long long)irow[kk] : -1ll;
+        const bool valid = jl >= 0 && jl < N && (!causal || jl <= i);
+        const int jv = valid ? (int)jl : -1;
+        int js[16];
+        float part[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            js[m] = __shfl_sync(kFull, jv, 16 * half + m);
+            const uint4 kr = __ldg(kb + (size_t)max(js[m], 0) * (D / 8));
+            part[m] = dot8_bf16(qv, kr);
+        }
+        // lane l of half h now holds key slot 2 * (l & 15) + h
+        const float dot = transpose_reduce16(part, lane);
+        const float sc = valid ? dot * scale_log2 : -INFINITY;
+        const float m_new = fmaxf(m_run, warp_max(sc));
+        if (m_new == -INFINITY) continue;  // warp-uniform: nothing valid so far
+        const float p = valid ? exp2f(sc - m_new) : 0.f;
+        const float alpha = exp2f(m_run - m_new);
+        l_run = l_run * alpha + warp_sum(p);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc[t] *= alpha;
+        const uint32_t pbits = bf16_pair_bits(p);
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const uint32_t pm = __shfl_sync(kFull, pbits, 16 * half + m);
+            const uint4 vr = __ldg(vb + (size_t)max(js[m], 0) * (D / 8));
+            axpy8_bf16(pm, vr, acc);
+        }
+        m_run = m_new;
+    }
+    store_row_bf16(acc, l_run, orow, lane);
+}
+
 template <typename IdxT>
 __global__ void __launch_bounds__(kGatherThreads)
 gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
@@ -175,8 +227,7 @@ gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
     constexpr int D = 128;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int half = lane >> 4;
-    const int hl = lane & 15;            // 16-byte column slot of this lane
+    const int hl = lane & 15;
     const int G = H / Hkv;
     const int bg = blockIdx.y;
     const int b = bg / Hkv;
@@ -186,84 +237,13 @@ gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
     const int items = nq * G;
     const uint4* kb = reinterpret_cast<const uint4*>(k + (size_t)bg * N * D) + hl;
     const uint4* vb = reinterpret_cast<const uint4*>(v + (size_t)bg * N * D) + hl;
-    // key slot held by this lane: m = 2 * hl + half
-    const int myslot = 2 * hl + half;
-
     for (int w = warp; w < items; w += kGatherWarps) {
         const int il = i0 + w / G;  // query row (local); its key-sequence position is q0 + il
-        const int i = q0 + il;
         const int h = g * G + (w - (w / G) * G);
         const size_t row = ((size_t)b * H + h) * Nq + il;
         const uint4 qv = __ldg(reinterpret_cast<const uint4*>(q + row * D) + hl);
-        const IdxT* irow = idx + row * K;
-        float m_run = -INFINITY, l_run = 0.f;
-        float acc[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) acc[t] = 0.f;
-
-        for (int kc = 0; kc < K; kc += 32) {
-            const int kk = kc + myslot;
-            const long long jl = kk < K ? (long long)irow[kk] : -1ll;
-            const bool valid = jl >= 0 && jl < N && (!causal || jl <= i);
-            const int jv = valid ? (int)jl : -1;
-            int js[16];
-            float part[16];
-#pragma unroll
-            for (int m = 0; m < 16; ++m) {
-                js[m] = __shfl_sync(kFull, jv, 16 * half + m);
-                const uint4 kr = __ldg(kb + (size_t)max(js[m], 0) * (D / 8));
-                float d0 = fma_bf16<false>(qv.x, kr.x, 0.f);
-                float d1 = fma_bf16<true>(qv.x, kr.x, 0.f);
-                d0 = fma_bf16<false>(qv.y, kr.y, d0);
-                d1 = fma_bf16<true>(qv.y, kr.y, d1);
-                d0 = fma_bf16<false>(qv.z, kr.z, d0);
-                d1 = fma_bf16<true>(qv.z, kr.z, d1);
-                d0 = fma_bf16<false>(qv.w, kr.w, d0);
-                d1 = fma_bf16<true>(qv.w, kr.w, d1);
-                part[m] = d0 + d1;
-            }
-            // lane l of half h now holds key slot 2 * (l & 15) + h
-            const float dot = transpose_reduce16(part, lane);
-            const float sc = valid ? dot * scale_log2 : -INFINITY;
-            const float m_new = fmaxf(m_run, warp_max(sc));
-            if (m_new == -INFINITY) continue;  // warp-uniform: nothing valid so far
-            const float p = valid ? exp2f(sc - m_new) : 0.f;
-            const float alpha = exp2f(m_run - m_new);
-            l_run = l_run * alpha + warp_sum(p);
-#pragma unroll
-            for (int t = 0; t < 8; ++t) acc[t] *= alpha;
-            // bf16 p in both halves of a register, as the fma operand
-            const __nv_bfloat16 pb = __float2bfloat16_rn(p);
-            const uint32_t pbits = (uint32_t)__bfloat16_as_ushort(pb) * 0x10001u;
-#pragma unroll
-            for (int m = 0; m < 16; ++m) {
-                const uint32_t pm = __shfl_sync(kFull, pbits, 16 * half + m);
-                const uint4 vr = __ldg(vb + (size_t)max(js[m], 0) * (D / 8));
-                acc[0] = fma_bf16<false>(pm, vr.x, acc[0]);
-                acc[1] = fma_bf16<true>(pm, vr.x, acc[1]);
-                acc[2] = fma_bf16<false>(pm, vr.y, acc[2]);
-                acc[3] = fma_bf16<true>(pm, vr.y, acc[3]);
-                acc[4] = fma_bf16<false>(pm, vr.z, acc[4]);
-                acc[5] = fma_bf16<true>(pm, vr.z, acc[5]);
-                acc[6] = fma_bf16<false>(pm, vr.w, acc[6]);
-                acc[7] = fma_bf16<true>(pm, vr.w, acc[7]);
-            }
-            m_run = m_new;
-        }
-        // the two halves accumulated disjoint keys over the same dims
-#pragma unroll
-        for (int t = 0; t < 8; ++t) acc[t] += __shfl_xor_sync(kFull, acc[t], 16);
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        if (half == 0) {
-            uint4 o;
-            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const __nv_bfloat162 pr = __floats2bfloat162_rn(acc[2 * t] * inv, acc[2 * t + 1] * inv);
-                ow[t] = *reinterpret_cast<const uint32_t*>(&pr);
-            }
-            *(reinterpret_cast<uint4*>(out + row * D) + hl) = o;
-        }
+        gather_row_bf16_d128<IdxT>(qv, kb, vb, idx + row * K, K, N, q0 + il, causal, scale_log2, out + row * D,
+                                   lane);
     }
 }
 
