@@ -246,6 +246,26 @@ OSSA_API int ossa_router_topk_rows_kp(const void* q, int dtype, const float* wq,
                                       void* workspace, size_t workspace_bytes, ossa_stream_t stream);
 
 /*
+ * Router distillation step without the (B, H, N, N) logits.
+ * Replaces distillation_loss(router.score(q, k), dense, k=K) and its backward
+ * (ossa/router.py:80-99 with router.py:171-190, as ossa/bench/content_train.py:141-148
+ * trains the router): the mean over every (i, j) of BCE-with-logits between the
+ * router score (the fp32 score ossa_router_topk selects on) and a 0/1 target that
+ * marks the keys listed in row i of `targets` ((B, H, N, K) int32, -1 padded, any
+ * order; the reference marks the top-K keys of the dense attention).  Writes the
+ * loss (device float) and the gradients of wq, wk ((r, D) fp32) and pos_bias
+ * ((2*seq_len_cfg,) fp32); q and k are inputs, not differentiated (the reference
+ * detaches them).  Memory is linear in N: scores are recomputed tile by tile.
+ */
+OSSA_API size_t ossa_router_distill_workspace_size(int B, int H, int Hkv, int N, int r);
+OSSA_API int ossa_router_distill_grad(const void* q, const void* k, int dtype,
+                                      const float* wq, const float* wk, const float* pos_bias,
+                                      int B, int H, int Hkv, int N, int D, int r, int seq_len_cfg,
+                                      const int32_t* targets, int K, float* loss_out,
+                                      float* dwq, float* dwk, float* dpos_bias,
+                                      void* workspace, size_t workspace_bytes, ossa_stream_t stream);
+
+/*
  * Rotary position embedding fused with the head transpose of the patched
  * layer (ossa/bench/sparse_forward.py:166-178: the q/k/v projections viewed as
  * (B, Hx, N, D), then Qwen2's apply_rotary_pos_emb on q and k).  Additive, for

@@ -29,6 +29,29 @@ def router_score(q, k, wq, wk, pos_bias, seq_len: int) -> torch.Tensor:
     return logits + bias                                   # router.py:189
 
 
+def router_distillation(q, k, wq, wk, pos_bias, seq_len: int, targets, dtype=torch.float64):
+    """ContentRouter training loss and gradients: distillation_loss(router.score(q, k),
+    dense, k) (ossa/router.py:80-99 on router.py:171-190) with the 0/1 target given
+    explicitly as index lists (B, H, N, K), -1 padded, in place of the dense top-k.
+    q (B, H, N, D), k (B, Hkv, N, D) are repeated to H heads as the reference's
+    callers do.  Evaluated in ``dtype`` with autograd; returns (loss, dwq, dwk,
+    dpos_bias)."""
+    H, Hkv = q.shape[1], k.shape[1]
+    wq = wq.detach().to(dtype).requires_grad_(True)
+    wk = wk.detach().to(dtype).requires_grad_(True)
+    pb = pos_bias.detach().to(dtype).requires_grad_(True)
+    logits = router_score(q.to(dtype), repeat_kv(k.to(dtype), H // Hkv), wq, wk, pb, seq_len)
+    idx = targets.long()
+    t = torch.zeros_like(logits)
+    # padding (-1) adds 0 at key 0, so it cannot clear a listed key 0; a key listed
+    # twice is still one target
+    t.scatter_add_(-1, idx.clamp(min=0), (idx >= 0).to(dtype))
+    t = (t > 0).to(dtype)
+    loss = torch.nn.functional.binary_cross_entropy_with_logits(logits, t)
+    loss.backward()
+    return loss.detach(), wq.grad, wk.grad, pb.grad
+
+
 def repeat_kv(x: torch.Tensor, rep: int) -> torch.Tensor:
     """GQA expansion, ossa/bench/sparse_forward.py:175-178."""
     return x.repeat_interleave(rep, dim=1) if rep > 1 else x

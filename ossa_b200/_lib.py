@@ -42,6 +42,8 @@ EXPORTED = (
     "ossa_oracle_workspace_size",
     "ossa_oracle_topk_ws",
     "ossa_rope_to_heads",
+    "ossa_router_distill_workspace_size",
+    "ossa_router_distill_grad",
     "ossa_router_workspace_size_kp",
     "ossa_router_project_keys",
     "ossa_router_topk_rows_kp",
@@ -97,6 +99,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ossa_oracle_topk_ws.restype = ci
     lib.ossa_rope_to_heads.argtypes = [vp, vp, vp, ci, ci, ci, ci, ci, ci, vp, vp]
     lib.ossa_rope_to_heads.restype = ci
+    lib.ossa_router_distill_workspace_size.argtypes = [ci] * 5
+    lib.ossa_router_distill_workspace_size.restype = sz
+    lib.ossa_router_distill_grad.argtypes = [vp, vp, ci, vp, vp, vp] + [ci] * 7 + [vp, ci, vp, vp, vp, vp, vp, sz, vp]
+    lib.ossa_router_distill_grad.restype = ci
     lib.ossa_router_workspace_size_kp.argtypes = [ci] * 7
     lib.ossa_router_workspace_size_kp.restype = sz
     lib.ossa_router_project_keys.argtypes = [vp, ci, vp, ctypes.c_longlong, ci, ci, vp, vp]

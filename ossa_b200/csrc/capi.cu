@@ -404,6 +404,54 @@ int ossa_oracle_topk(const void* q, const void* k, int dtype, int B, int H, int 
                        "oracle top-K launch");
 }
 
+size_t ossa_router_distill_workspace_size(int B, int H, int Hkv, int N, int r) {
+    if (B < 0 || H <= 0 || Hkv <= 0 || N < 0 || !supported_r(r)) return 0;
+    const size_t rq = (size_t)B * H * N * r * sizeof(float), rk = (size_t)B * Hkv * N * r * sizeof(float);
+    return kCountersBytes + 2 * align_up(rq) + 2 * align_up(rk) +
+           align_up(ossa::distill_loss_parts(B, H, N) * sizeof(float));
+}
+
+int ossa_router_distill_grad(const void* q, const void* k, int dtype, const float* wq, const float* wk,
+                             const float* pos_bias, int B, int H, int Hkv, int N, int D, int r, int seq_len_cfg,
+                             const int32_t* targets, int K, float* loss_out, float* dwq, float* dwk,
+                             float* dpos_bias, void* workspace, size_t workspace_bytes, ossa_stream_t stream) {
+    int st = check_heads(B, H, Hkv, N);
+    if (st) return st;
+    if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);
+    if (D <= 0) return fail(OSSA_ERR_INVALID, "bad head_dim D=%d", D);
+    if (!supported_r(r)) return fail(OSSA_ERR_UNSUPPORTED, "proj_dim r=%d not in {16,32,64,128}", r);
+    if (seq_len_cfg <= 0 || seq_len_cfg > (1 << 28)) return fail(OSSA_ERR_INVALID, "bad seq_len_cfg %d", seq_len_cfg);
+    if (K < 0) return fail(OSSA_ERR_INVALID, "bad K=%d", K);
+    if ((long long)B * H * N == 0) return fail(OSSA_ERR_INVALID, "empty input (the mean loss is undefined)");
+    if (!q || !k || !wq || !wk || !pos_bias || !loss_out || !dwq || !dwk || !dpos_bias || (K > 0 && !targets))
+        return fail(OSSA_ERR_INVALID, "null pointer argument");
+    if (!aligned16(q) || !aligned16(k)) return fail(OSSA_ERR_INVALID, "q and k must be 16-byte aligned");
+    const size_t need = ossa_router_distill_workspace_size(B, H, Hkv, N, r);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+        return fail(OSSA_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required, got %zu", need,
+                    workspace ? workspace_bytes : (size_t)0);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    char* w = static_cast<char*>(workspace) + kCountersBytes;
+    const size_t rq = (size_t)B * H * N * r * sizeof(float), rk = (size_t)B * Hkv * N * r * sizeof(float);
+    float* qp = reinterpret_cast<float*>(w);
+    float* kp = reinterpret_cast<float*>(w + align_up(rq));
+    float* dqp = reinterpret_cast<float*>(w + align_up(rq) + align_up(rk));
+    float* dkp = reinterpret_cast<float*>(w + 2 * align_up(rq) + align_up(rk));
+    float* parts = reinterpret_cast<float*>(w + 2 * align_up(rq) + 2 * align_up(rk));
+    ossa::ProjectArgs pa{q, wq, qp, (long long)B * H * N, D, r, dtype};
+    if ((st = cuda_status(ossa::launch_project(pa, s), "q projection launch"))) return st;
+    ossa::ProjectArgs pk{k, wk, kp, (long long)B * Hkv * N, D, r, dtype};
+    if ((st = cuda_status(ossa::launch_project(pk, s), "k projection launch"))) return st;
+    if ((st = cuda_status(cudaMemsetAsync(dwq, 0, (size_t)r * D * sizeof(float), s), "gradient reset"))) return st;
+    if ((st = cuda_status(cudaMemsetAsync(dwk, 0, (size_t)r * D * sizeof(float), s), "gradient reset"))) return st;
+    if ((st = cuda_status(cudaMemsetAsync(dpos_bias, 0, (size_t)2 * seq_len_cfg * sizeof(float), s),
+                          "gradient reset")))
+        return st;
+    ossa::DistillArgs a{q, k, dtype, qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, N, D, r, targets, K,
+                        dqp, dkp, dpos_bias, dwq, dwk, parts, loss_out};
+    return cuda_status(ossa::launch_distill(a, s), "router distillation launch");
+}
+
 int ossa_rope_to_heads(const void* x, const void* cos, const void* sin, int cs_batched, int dtype, int B, int N,
                        int Hx, int D, void* out, ossa_stream_t stream) {
     if (!valid_dtype(dtype)) return fail(OSSA_ERR_INVALID, "bad dtype %d", dtype);

@@ -113,6 +113,30 @@ struct SortRowsArgs {
 bool sort_rows_supported(int R, int K);
 cudaError_t launch_sort_rows(const SortRowsArgs& a, cudaStream_t stream);
 
+// Router distillation loss (BCE over all (i, j) against 0/1 targets) and the
+// gradients of q', k', pos_bias and the projection weights, streamed in tiles.
+struct DistillArgs {
+    const void* q;        // (B*H*N, D) dtype: the rows q' was projected from
+    const void* k;        // (B*Hkv*N, D) dtype
+    int dtype;
+    const float* qp;      // (B*H*N, R) canonical q'
+    const float* kp;      // (B*Hkv*N, R) canonical k'
+    const float* bias;    // (2L,)
+    int L;
+    int B, H, Hkv, N, D, R;
+    const int32_t* tgt;   // (B*H*N, K) target key lists (-1 padded)
+    int K;
+    float* dqp;           // (B*H*N, R) out
+    float* dkp;           // (B*Hkv*N, R) out
+    float* dbias;         // (2L,) accumulated (zero it first)
+    float* dwq;           // (R, D) accumulated (zero it first)
+    float* dwk;           // (R, D) accumulated (zero it first)
+    float* loss_part;     // distill_loss_parts(B, H, N) per-CTA loss sums
+    float* loss_out;      // (1,) mean loss
+};
+size_t distill_loss_parts(int B, int H, int N);
+cudaError_t launch_distill(const DistillArgs& a, cudaStream_t stream);
+
 // Dense fp32 scores (B, H, N, N) with the same score definition, no mask.
 struct ScoreDenseArgs {
     const float* qrows;

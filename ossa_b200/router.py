@@ -89,6 +89,15 @@ class ContentRouter(nn.Module):
             raise TypeError("ContentRouter needs both q and k tensors; call .score(q, k).")
         return self.score(q, k)
 
+    def distillation_loss(self, q: torch.Tensor, k: torch.Tensor, top_k: int, *,
+                          targets: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The reference's training loss, distillation_loss(self.score(q, k), dense,
+        k=top_k) (ossa/router.py:80-99), with autograd into this router's
+        parameters and no N x N tensor (see ossa_b200.train)."""
+        from .train import distillation_loss
+
+        return distillation_loss(self, q, k, top_k, targets=targets)
+
     def topk(self, q: torch.Tensor, k: torch.Tensor, top_k: int, *, causal: bool = False,
              index_dtype: torch.dtype = torch.int64, order: str = "score") -> torch.Tensor:
         """Indices (B, H, N, top_k) of the top_k keys per query, by descending

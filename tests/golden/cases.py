@@ -68,3 +68,8 @@ def oracle_inputs():
 def reference_test_inputs():
     """The reference tests' own shape (tests/test_sparse_attention.py:29-46)."""
     return qkv(1, 4, 4, 64, 16, seed=31)
+
+
+def distill_inputs():
+    """Router training case: B=1, 4 query / 2 kv heads, N=96, D=64, N(0,1)."""
+    return qkv(1, 4, 2, 96, 64, seed=51)

@@ -178,6 +178,37 @@ def main(ref_root: str) -> None:
         out_heads=np.array([0, 3]),
         ref_out=out[:, [0, 3]].numpy(),
     )
+    # --- E: router training step (distillation loss and its gradients) --------
+    from ossa.router import distillation_loss
+
+    q, k, _ = cases.distill_inputs()
+    B, H, N, D = q.shape
+    rep = H // k.shape[1]
+    r, L, K = 32, 64, 16
+    wq, wk, pb = cases.router_weights(D, r, L, seed=41)
+    router = ContentRouter(ContentRouterConfig(head_dim=D, n_heads=H, seq_len=L, proj_dim=r))
+    with torch.no_grad():
+        router.q_proj[0].weight.copy_(wq)
+        router.k_proj[0].weight.copy_(wk)
+        router.pos_bias.weight.copy_(pb)
+    kr = k.repeat_interleave(rep, dim=1)
+    with torch.no_grad():
+        causal = torch.tril(torch.ones(N, N, dtype=torch.bool))
+        dense = torch.softmax((q @ kr.transpose(-2, -1) / math.sqrt(D)).masked_fill(~causal, float("-inf")), dim=-1)
+        target_idx = torch.topk(dense, k=K, dim=-1).indices  # the targets distillation_loss builds
+    logits = router.score(q, kr)
+    loss = distillation_loss(logits, dense, k=K)
+    loss.backward()
+    np.savez_compressed(
+        HERE / "router_distill.npz",
+        r=np.int64(r), seq_len=np.int64(L), K=np.int64(K), weight_seed=np.int64(41),
+        checksum=cases.checksum(q, k, wq, wk, pb),
+        target_idx=target_idx.numpy().astype(np.int16),
+        loss=np.float64(loss.item()),
+        dwq=router.q_proj[0].weight.grad.numpy(),
+        dwk=router.k_proj[0].weight.grad.numpy(),
+        dpos_bias=router.pos_bias.weight.grad.numpy(),
+    )
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

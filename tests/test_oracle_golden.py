@@ -171,3 +171,21 @@ def test_oracle_topk_rows_matches_full_selection(causal):
     full = oracle.oracle_topk(q, k, 16, causal=causal).reshape(-1, 16)
     rows = np.arange(0, 800, 7, dtype=np.int64)
     assert (oracle.oracle_topk_rows(q, k, 16, rows, causal=causal) == full[rows]).all()
+
+
+def test_router_distillation_restatement(golden_dir):
+    """The training loss (ossa/router.py:80-99 on router.py:171-190), restated in
+    fp64 with the target given as index lists: equal to the reference's own loss
+    and gradients (fp32) on its own target indices (torch.topk of the dense
+    attention, masked ties included)."""
+    z = _load(golden_dir, "router_distill.npz")
+    q, k, _ = cases.distill_inputs()
+    D = q.shape[-1]
+    r, L = int(z["r"]), int(z["seq_len"])
+    wq, wk, pb = cases.router_weights(D, r, L, seed=int(z["weight_seed"]))
+    assert np.array_equal(cases.checksum(q, k, wq, wk, pb), z["checksum"])
+    loss, dwq, dwk, dpb = rp.router_distillation(q, k, wq, wk, pb, L, torch.from_numpy(z["target_idx"].astype(np.int64)))
+    np.testing.assert_allclose(float(loss), float(z["loss"]), rtol=1e-6)
+    for got, ref in ((dwq, z["dwq"]), (dwk, z["dwk"]), (dpb, z["dpos_bias"])):
+        np.testing.assert_allclose(got.numpy(), ref, rtol=1e-4, atol=1e-7 * np.abs(ref).max())
+
