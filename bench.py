@@ -365,10 +365,28 @@ def run_ours(args) -> None:
     h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
     d2h = oh.numel() * 2
 
+    chunk = 2
+
     def e2e_step():
         # public host-buffer entry point: chunked H2D / kernels / D2H on three streams
-        routed_attention_from_host(qh, kh, vh, wq, wk, pb, L, K, oh, causal=True, chunk=2)
+        routed_attention_from_host(qh, kh, vh, wq, wk, pb, L, K, oh, causal=True, chunk=chunk)
 
+    # pipeline depth: batch elements per chunk, chosen in the untimed warm-up
+    trial = {}
+    for c in (1, 2, 4):
+        chunk = c
+        e2e_step()
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(2):
+            e2e_step()
+        b_.record(stream)
+        torch.cuda.synchronize()
+        trial[c] = a.elapsed_time(b_)
+    tt = torch.tensor([trial[c] for c in (1, 2, 4)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)  # every rank picks the same
+    chunk = (1, 2, 4)[int(torch.argmin(tt).item())]
     for _ in range(max(1, args.warmup)):
         e2e_step()
     barrier()
@@ -433,7 +451,8 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": world * args.steps * B * N / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms / args.steps, "host_link_copy_only": link},
+                    "ms_per_step": e2e_ms / args.steps, "host_link_copy_only": link,
+                    "pipeline_chunk": chunk},
             "long_context": long_ctx,
             "gpu_launches": launches,
             "select_exact_fallback_rows": fb_rows, "select_status": sel_status,
