@@ -273,13 +273,12 @@ gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
 //     the B operand by ldmatrix.trans from the staged rows; at the end each head's
 //     row is divided by its sum and stored as bf16.
 // Results agree with the per-head form to rounding (tensor-core accumulation order).
-constexpr int kMmaMaxU = 128;     // union keys per query (K <= 128 per head)
-constexpr int kMmaSlotBits = 8;   // hash slots of the union (twice kMmaMaxU)
-constexpr int kMmaSlots = 1 << kMmaSlotBits;
+// The union hash has 2^kSlotBits slots and holds at most half as many keys: 256
+// slots (128 keys) for K <= 64, 512 slots (256 keys) above.
 constexpr int kMmaChunk = 32;     // union keys per chunk: 4 score n-tiles, 2 value k-steps
 constexpr int kMmaWarps = 8;
-constexpr size_t kMmaWarpSmem = (size_t)kMmaChunk * 256 + (size_t)kMmaSlots * 8;
-constexpr size_t kMmaSmem = kMmaWarps * kMmaWarpSmem;
+template <int kSlotBits>
+constexpr size_t mma_smem_bytes() { return kMmaWarps * ((size_t)kMmaChunk * 256 + ((size_t)8 << kSlotBits)); }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -294,13 +293,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <typename IdxT, int G>
+template <typename IdxT, int G, int kSlotBits>
 __global__ void __launch_bounds__(kMmaWarps * 32, 2)
 gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                                  const __nv_bfloat16* __restrict__ v, const IdxT* __restrict__ idx,
                                  __nv_bfloat16* __restrict__ out, int H, int Hkv, int N, int Nq, int q0, int K,
                                  float scale_log2, int causal) {
     constexpr int D = 128;
+    constexpr int kMmaSlots = 1 << kSlotBits;
+    constexpr int kMmaMaxU = kMmaSlots / 2;
+    constexpr size_t kMmaWarpSmem = (size_t)kMmaChunk * 256 + (size_t)kMmaSlots * 8;
     extern __shared__ __align__(128) uint8_t msm[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -356,7 +358,7 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
                 canon = canon && !__any_sync(kFull, xv >= 0 && qi > 0 && !(pv >= 0 && pv < xv));
                 prev31 = __shfl_sync(kFull, xv, 31);
                 if (xv >= 0) {
-                    int slot = (int)(((uint32_t)xv * 2654435761u) >> (32 - kMmaSlotBits));
+                    int slot = (int)(((uint32_t)xv * 2654435761u) >> (32 - kSlotBits));
                     for (int probe = 0; probe < kMmaSlots; ++probe) {
                         const int old = atomicCAS(&ukey[slot], -1, xv);
                         if (old == -1 || old == xv) {
@@ -376,8 +378,9 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
         unsigned mk[kMmaSlots / 32];
 #pragma unroll
         for (int u = 0; u < kMmaSlots / 32; ++u) {
-            kk[u] = ukey[8 * lane + u];  // lane owns slots 8 lane .. 8 lane + 7
-            mk[u] = umask[8 * lane + u];
+            // lane owns slots S lane .. S lane + S - 1, S = kMmaSlots / 32
+            kk[u] = ukey[(kMmaSlots / 32) * lane + u];
+            mk[u] = umask[(kMmaSlots / 32) * lane + u];
         }
         __syncwarp();
         int nmine = 0;
@@ -555,11 +558,15 @@ cudaError_t launch_typed(const GatherArgs& a, cudaStream_t stream) {
     if constexpr (sizeof(T) == 2) {
         const int G = a.H / a.Hkv;
         if (a.D == 128 && a.K <= 128 && (G == 2 || G == 3 || G == 4 || G == 6 || G == 8)) {
-            auto kern = G == 2 ? gather_attn_bf16_d128_mma_kernel<IdxT, 2>
-                      : G == 3 ? gather_attn_bf16_d128_mma_kernel<IdxT, 3>
-                      : G == 4 ? gather_attn_bf16_d128_mma_kernel<IdxT, 4>
-                      : G == 6 ? gather_attn_bf16_d128_mma_kernel<IdxT, 6>
-                               : gather_attn_bf16_d128_mma_kernel<IdxT, 8>;
+            const bool big = a.K > 64;
+#define OSSA_MMA_PICK(GG) (big ? gather_attn_bf16_d128_mma_kernel<IdxT, GG, 9> : gather_attn_bf16_d128_mma_kernel<IdxT, GG, 8>)
+            auto kern = G == 2 ? OSSA_MMA_PICK(2)
+                      : G == 3 ? OSSA_MMA_PICK(3)
+                      : G == 4 ? OSSA_MMA_PICK(4)
+                      : G == 6 ? OSSA_MMA_PICK(6)
+                               : OSSA_MMA_PICK(8);
+#undef OSSA_MMA_PICK
+            const size_t kMmaSmem = big ? mma_smem_bytes<9>() : mma_smem_bytes<8>();
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMmaSmem);
             if (e != cudaSuccess) return e;
             dim3 mgrid((Nq + kMmaWarps - 1) / kMmaWarps, a.B * a.Hkv);
