@@ -247,95 +247,98 @@ __device__ __forceinline__ void fma2(float& acc0, float& acc1, float x, float w0
         : "f"(x), "f"(w0), "f"(w1));
 }
 
-// bf16 rows, D = 128, R = 64 (the ContentRouter shape of the product path): 4 rows x 8
-// output columns per thread (columns cg*4.. and 32 + cg*4..), so a d-step reads one 8-byte
-// x group (4 bf16 rows) and two float4 of W per 32 FMA, and x stays bf16 in shared memory (converted on use, exactly).
-// The next tile's rows are prefetched into registers while the current one is multiplied.
-// Same per-output fmaf chain (d = 0..127 from 0.0f) as project_kernel.
-constexpr int kP2Cols = 8;                        // output columns per thread
-constexpr int kP2Rows = 4;                        // rows per thread
-constexpr int kP2CG = 64 / kP2Cols;               // 8 column groups
-constexpr int kP2RG = kProjThreads / kP2CG;       // 32 row groups
-constexpr int kP2Tile = kP2RG * kP2Rows;          // 128 rows per tile
-constexpr int kP2XS = kP2Tile + 8;                // bf16 stride of a transposed x row (272 B)
-constexpr int kP2Vec = kP2Tile * 128 / 8 / kProjThreads;  // 16-byte row pieces per thread (8)
-constexpr size_t kP2Smem = 128 * 64 * sizeof(float) + 128 * kP2XS * sizeof(__nv_bfloat16);
+// bf16 rows, D = 128, R = 64 (the ContentRouter shape of the product path).  A CTA
+// takes 128-row tiles; warp w owns output columns 8w .. 8w+7 and lane l owns rows
+// l, l+32, l+64, l+96, so a thread holds 4 x 8 accumulators.  For each d the warp
+// reads W[d][8w .. 8w+7] at one address (a broadcast) and each lane unpacks its
+// four x values from 16-byte row pieces it loaded for 8 consecutive d: per 32 FMA
+// of a thread, two broadcast reads of W and half a 16-byte read of x.  The x rows
+// stay bf16 in shared memory (272-byte pitch: the 8 lanes of a quarter warp read
+// 8 consecutive rows from 8 distinct bank groups) and the next tile streams in
+// with cp.async while the current one is multiplied.  Column pairs go through
+// fma.rn.f32x2; every output keeps its fmaf chain d = 0..127 from 0.0f.
+constexpr int kP2Rows = 128;                          // rows per tile
+constexpr int kP2Pitch = 128 * 2 + 16;                // bytes per staged x row
+constexpr int kP2StageBytes = kP2Rows * kP2Pitch;     // 34,816
+constexpr int kP2Pieces = kP2Rows * 16 / kProjThreads;  // 16-byte pieces per thread per tile (8)
+constexpr size_t kP2Smem = 128 * 64 * sizeof(float) + 2 * (size_t)kP2StageBytes;
+
+// Element e (0..7) of 8 packed bf16, widened exactly.  The low half moves up with
+// a byte permute and the high half is masked: both run on the integer pipe, which
+// leaves the FMA pipe to the fma.rn.f32x2 stream.
+__device__ __forceinline__ float bf16_elem(const uint4& u, int e) {
+    const uint32_t wd = e < 2 ? u.x : (e < 4 ? u.y : (e < 6 ? u.z : u.w));
+    return __uint_as_float((e & 1) ? (wd & 0xffff0000u) : __byte_perm(wd, 0u, 0x1054));
+}
 
 __global__ void __launch_bounds__(kProjThreads, 2)
 project_bf16_d128_r64_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
                              float* __restrict__ out, long long rows, long long ntiles) {
     extern __shared__ float4 smem4[];
-    float* Ws = reinterpret_cast<float*>(smem4);                          // [128][64]
-    __nv_bfloat16* Xs = reinterpret_cast<__nv_bfloat16*>(Ws + 128 * 64);  // [128][kP2XS]
+    float* Ws = reinterpret_cast<float*>(smem4);                 // [128 d][64 c]
+    uint8_t* stage = reinterpret_cast<uint8_t*>(Ws + 128 * 64);  // 2 x [128 rows][kP2Pitch]
     const int tid = threadIdx.x;
-    const int cg = tid % kP2CG;
-    const int rg = tid / kP2CG;
+    const int warp = tid >> 5, lane = tid & 31;
     for (int e = tid; e < 64 * 128; e += kProjThreads) {
         const int d = e / 64, c = e - d * 64;
         Ws[d * 64 + c] = __ldg(w + (size_t)c * 128 + d);
     }
-    uint4 pre[kP2Vec];
-    auto fetch = [&](long long tile) {
+    auto issue = [&](long long tile, int buf) {
+        uint8_t* st = stage + (size_t)buf * kP2StageBytes;
 #pragma unroll
-        for (int u = 0; u < kP2Vec; ++u) {
-            // consecutive threads take consecutive rows: conflict-free transposed stores
+        for (int u = 0; u < kP2Pieces; ++u) {
             const int e = tid + u * kProjThreads;
-            const int vcol = e / kP2Tile, r = e - vcol * kP2Tile;
-            const long long gr = tile * kP2Tile + r;
-            pre[u] = gr < rows ? __ldg(reinterpret_cast<const uint4*>(x + gr * 128) + vcol) : make_uint4(0, 0, 0, 0);
+            const int r = e >> 4, v = e & 15;
+            const long long gr = tile * kP2Rows + r;
+            const bool in = gr < rows;
+            cp_async16(st + r * kP2Pitch + v * 16, x + (in ? gr : 0) * 128 + v * 8, in ? 16 : 0);
         }
+        cp_async_commit();
     };
     long long tile = blockIdx.x;
-    if (tile < ntiles) fetch(tile);
-    for (; tile < ntiles; tile += gridDim.x) {
-        __syncthreads();  // the previous tile's products are done with Xs (and Ws is ready)
+    int buf = 0;
+    if (tile < ntiles) issue(tile, 0);
+    const float* wrow = Ws + 8 * warp;
+    for (; tile < ntiles; tile += gridDim.x, buf ^= 1) {
+        cp_async_wait_all();
+        __syncthreads();  // stage[buf] landed for every thread; stage[buf ^ 1] is free (and Ws is ready)
+        if (tile + gridDim.x < ntiles) issue(tile + gridDim.x, buf ^ 1);
+        const uint8_t* st = stage + (size_t)buf * kP2StageBytes + lane * kP2Pitch;
+        float acc[4][8];
 #pragma unroll
-        for (int u = 0; u < kP2Vec; ++u) {
-            const int e = tid + u * kProjThreads;
-            const int vcol = e / kP2Tile, r = e - vcol * kP2Tile;
-            const uint32_t wds[4] = {pre[u].x, pre[u].y, pre[u].z, pre[u].w};
+        for (int a = 0; a < 4; ++a)
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                Xs[(vcol * 8 + 2 * t) * kP2XS + r] = __ushort_as_bfloat16((unsigned short)(wds[t] & 0xffffu));
-                Xs[(vcol * 8 + 2 * t + 1) * kP2XS + r] = __ushort_as_bfloat16((unsigned short)(wds[t] >> 16));
+            for (int c = 0; c < 8; ++c) acc[a][c] = 0.f;
+#pragma unroll 1
+        for (int dc = 0; dc < 16; ++dc) {
+            uint4 xr[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) xr[a] = *reinterpret_cast<const uint4*>(st + a * 32 * kP2Pitch + dc * 16);
+#pragma unroll
+            for (int dd = 0; dd < 8; ++dd) {
+                const int d = dc * 8 + dd;
+                const float4 w0 = *reinterpret_cast<const float4*>(wrow + d * 64);
+                const float4 w1 = *reinterpret_cast<const float4*>(wrow + d * 64 + 4);
+                const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int a = 0; a < 4; ++a) {
+                    const float xa = bf16_elem(xr[a], dd);
+#pragma unroll
+                    for (int c = 0; c < 8; c += 2) fma2(acc[a][c], acc[a][c + 1], xa, wa[c], wa[c + 1]);
+                }
             }
         }
-        __syncthreads();
-        if (tile + gridDim.x < ntiles) fetch(tile + gridDim.x);
-        float acc[kP2Rows][kP2Cols];
 #pragma unroll
-        for (int a = 0; a < kP2Rows; ++a)
-#pragma unroll
-            for (int c = 0; c < kP2Cols; ++c) acc[a][c] = 0.f;
-#pragma unroll 4
-        for (int d = 0; d < 128; ++d) {
-            const uint2 xr = *reinterpret_cast<const uint2*>(Xs + d * kP2XS + rg * kP2Rows);
-            float xa[4];
-            unpack_bf16x2(xr.x, xa[0], xa[1]);
-            unpack_bf16x2(xr.y, xa[2], xa[3]);
-            // columns cg*4 .. +3 and 32 + cg*4 .. +3: each float4 read of the warp spans
-            // 128 consecutive bytes (no bank conflicts)
-            const float4 w0 = *reinterpret_cast<const float4*>(Ws + d * 64 + cg * 4);
-            const float4 w1 = *reinterpret_cast<const float4*>(Ws + d * 64 + 32 + cg * 4);
-            // column pairs (c, c+1) through fma.rn.f32x2: each lane of the pair is
-            // rounded exactly as fmaf, so every output keeps its fmaf chain
-            const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-            for (int a = 0; a < kP2Rows; ++a)
-#pragma unroll
-                for (int c = 0; c < kP2Cols; c += 2) fma2(acc[a][c], acc[a][c + 1], xa[a], wa[c], wa[c + 1]);
-        }
-#pragma unroll
-        for (int a = 0; a < kP2Rows; ++a) {
-            const long long gr = tile * kP2Tile + rg * kP2Rows + a;
+        for (int a = 0; a < 4; ++a) {
+            const long long gr = tile * kP2Rows + lane + 32 * a;
             if (gr < rows) {
-                *reinterpret_cast<float4*>(out + gr * 64 + cg * 4) =
-                    make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
-                *reinterpret_cast<float4*>(out + gr * 64 + 32 + cg * 4) =
-                    make_float4(acc[a][4], acc[a][5], acc[a][6], acc[a][7]);
+                float4* o = reinterpret_cast<float4*>(out + gr * 64 + 8 * warp);
+                o[0] = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+                o[1] = make_float4(acc[a][4], acc[a][5], acc[a][6], acc[a][7]);
             }
         }
     }
+    cp_async_wait_all();
 }
 
 cudaError_t launch_bf16_d128_r64(const ProjectArgs& a, cudaStream_t stream) {
@@ -347,7 +350,7 @@ cudaError_t launch_bf16_d128_r64(const ProjectArgs& a, cudaStream_t stream) {
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
     if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kProjThreads, kP2Smem)) != cudaSuccess)
         return e;
-    const long long ntiles = (a.rows + kP2Tile - 1) / kP2Tile;
+    const long long ntiles = (a.rows + kP2Rows - 1) / kP2Rows;
     if (ntiles == 0) return cudaSuccess;
     const long long grid = std::min<long long>(ntiles, (long long)sms * std::max(1, per_sm));
     kern<<<(unsigned)grid, kProjThreads, kP2Smem, stream>>>(static_cast<const __nv_bfloat16*>(a.x), a.w, a.out,

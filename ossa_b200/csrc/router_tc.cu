@@ -576,11 +576,13 @@ __device__ __forceinline__ float2 score2(uint32_t acc0, uint32_t acc1, uint64_t 
 // The accumulator and the window buffer are released on `tempty` after the last
 // chunk has been scored: the next MMA into this accumulator and the bulk copy of
 // the next window into this buffer start as soon as `tempty` completes.  Every
-// accumulator and window word of the half tile is OR-ed into `dep`, the warp
-// reduces it (each lane waits for its own loads) and the arrive's address depends
-// on the result, so no read of this tile can still be in flight at the release.
-// (A release issued before the last chunk was scored let the next tile's MMA
-// and window copy land under the last chunk's reads on B200.)
+// accumulator load of the half tile has completed at the release (tcgen05.wait::ld
+// precedes each chunk's use, then tcgen05.fence::before_thread_sync); one word of
+// every 16-byte window load is OR-ed into `dep`, the warp reduces it (each lane
+// waits for its own loads) and the arrive's address depends on the result, so no
+// read of this tile can still be in flight at the release.  (A release issued
+// before the last chunk was scored let the next tile's MMA and window copy land
+// under the last chunk's reads on B200.)
 template <typename Fn>
 __device__ __forceinline__ void score_half_tile(uint32_t taddr, uint32_t wsrc, uint64_t* tempty, int lane, Fn&& fn) {
     constexpr int kC = 16, kNC = kHalfCols / kC;
@@ -601,11 +603,7 @@ __device__ __forceinline__ void score_half_tile(uint32_t taddr, uint32_t wsrc, u
         }
         fn(h, v[h & 1], bw[h & 1]);
 #pragma unroll
-        for (int q = 0; q < kC / 4; ++q) {
-            const float4 b = bw[h & 1][q];
-            dep |= ((__float_as_uint(b.x) | __float_as_uint(b.y)) | (__float_as_uint(b.z) | __float_as_uint(b.w))) |
-                   ((v[h & 1][4 * q] | v[h & 1][4 * q + 1]) | (v[h & 1][4 * q + 2] | v[h & 1][4 * q + 3]));
-        }
+        for (int q = 0; q < kC / 4; ++q) dep |= __float_as_uint(bw[h & 1][q].x);
     }
     tc_fence_before();
     dep = __reduce_or_sync(kFull, dep);
