@@ -258,7 +258,8 @@ gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
 //     strictly ascending; else the query goes through gather_row_bf16_d128 per head).
 //     Every valid key goes into an open-addressing hash in shared memory with its
 //     head bit; the occupied slots, compacted in slot order, are the union (at most
-//     kMmaMaxU keys, else per head).
+//     kMmaMaxU keys, else per head).  The q rows are loaded before the union is built,
+//     so their latency overlaps it.
 //  2. the union in chunks of 32 keys: its value rows are copied to shared memory
 //     (cp.async, 16-byte pieces XOR-swizzled by row) while the scores of the chunk
 //     S = Q K_U^T run on mma.sync m16n8k16 (bf16 operands, fp32 accumulation): A =
@@ -274,11 +275,27 @@ gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
 //     row is divided by its sum and stored as bf16.
 // Results agree with the per-head form to rounding (tensor-core accumulation order).
 // The union hash has 2^kSlotBits slots and holds at most half as many keys: 256
-// slots (128 keys) for K <= 64, 512 slots (256 keys) above.
+// slots (128 keys) for K <= 64, 512 slots (256 keys) above.  With N <= 4096 keys and
+// K <= 64 the union is built instead in a per-warp byte array indexed by the key
+// (kDirect): byte j holds the head bits of key j, set by one atomicOr per selected
+// key, so there is no probing and no compare-and-swap; a head bit that is already set
+// marks a repeated key (the per-head form then takes the query).  The entry of the
+// lowest head that selected a key appends it to the union list.
 constexpr int kMmaChunk = 32;     // union keys per chunk: 4 score n-tiles, 2 value k-steps
 constexpr int kMmaWarps = 8;
-template <int kSlotBits>
-constexpr size_t mma_smem_bytes() { return kMmaWarps * ((size_t)kMmaChunk * 256 + ((size_t)8 << kSlotBits)); }
+constexpr int kDirectMaxN = 4096;  // keys covered by the direct head-bit array
+constexpr int kDirectMaxU = 128;   // union entries of the direct form
+// Per warp: the value rows of a chunk (kMmaChunk x 256 B; the direct head-bit array,
+// kDirectMaxN bytes, uses the same space before the first chunk), then the hash
+// slots / union list.
+template <int kSlotBits, bool kDirect>
+constexpr size_t mma_warp_smem() {
+    return (size_t)kMmaChunk * 256 + (kDirect ? (size_t)kDirectMaxU * 8 : ((size_t)8 << kSlotBits));
+}
+static_assert(kDirectMaxN <= kMmaChunk * 256, "the direct head-bit array fits in the value staging area");
+template <int kSlotBits, bool kDirect>
+constexpr size_t mma_smem_bytes() { return kMmaWarps * mma_warp_smem<kSlotBits, kDirect>(); }
+static_assert(mma_warp_smem<8, true>() % 16 == 0 && mma_warp_smem<9, false>() % 16 == 0, "warp areas stay 16-byte aligned");
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -293,16 +310,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <typename IdxT, int G, int kSlotBits>
+template <typename IdxT, int G, int kSlotBits, bool kDirect>
 __global__ void __launch_bounds__(kMmaWarps * 32, 2)
 gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                                  const __nv_bfloat16* __restrict__ v, const IdxT* __restrict__ idx,
                                  __nv_bfloat16* __restrict__ out, int H, int Hkv, int N, int Nq, int q0, int K,
                                  float scale_log2, int causal) {
     constexpr int D = 128;
-    constexpr int kMmaSlots = 1 << kSlotBits;
-    constexpr int kMmaMaxU = kMmaSlots / 2;
-    constexpr size_t kMmaWarpSmem = (size_t)kMmaChunk * 256 + (size_t)kMmaSlots * 8;
+    constexpr int kMmaSlots = kDirect ? kDirectMaxU : 1 << kSlotBits;
+    constexpr int kMmaMaxU = kDirect ? kDirectMaxU : kMmaSlots / 2;
+    constexpr size_t kMmaWarpSmem = mma_warp_smem<kSlotBits, kDirect>();
     extern __shared__ __align__(128) uint8_t msm[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -318,13 +335,15 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
     uint8_t* vs = msm + (size_t)warp * kMmaWarpSmem;  // [kMmaChunk][256 B], pieces swizzled
     int* ukey = reinterpret_cast<int*>(vs + kMmaChunk * 256);       // hash slots, then the union
     unsigned* umask = reinterpret_cast<unsigned*>(ukey + kMmaSlots);
+    uint32_t* dbits = reinterpret_cast<uint32_t*>(vs);  // direct: head bits, 4 keys per word (until chunk 0)
     const __nv_bfloat16* kb = k + (size_t)bg * N * D;
     const __nv_bfloat16* vb = v + (size_t)bg * N * D;
     const size_t row0 = ((size_t)b * H + (size_t)g * G) * Nq + il;  // head t: row0 + t * Nq
 
-    // ---- 1. union of the heads' keys with head bits: open-addressing hash in shared
-    // memory (kMmaSlots slots, linear probing), then compacted by ballot into
-    // ukey / umask (the same arrays) in slot order
+    // ---- 1. union of the heads' keys with head bits into ukey / umask: the direct
+    // head-bit array (kDirect), or an open-addressing hash in shared memory
+    // (kMmaSlots slots, linear probing) compacted by ballot into the same arrays in
+    // slot order
     int x[G][4];
 #pragma unroll
     for (int t = 0; t < G; ++t) {
@@ -336,75 +355,134 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
             x[t][e] = (jl >= 0 && jl < N && (!causal || jl <= i)) ? (int)jl : -1;
         }
     }
+    // q rows of the heads as A fragments (dims 32 c4 .. 32 c4 + 31 of head gq), loaded
+    // now so that their latency overlaps the union build
+    uint32_t qa[16];
+    {
+        const uint4* qp = reinterpret_cast<const uint4*>(q + (row0 + (size_t)gq * Nq) * D + 32 * c4);
 #pragma unroll
-    for (int u = 0; u < kMmaSlots / 32; ++u) {
-        ukey[lane + 32 * u] = -1;
-        umask[lane + 32 * u] = 0u;
+        for (int u = 0; u < 4; ++u) {
+            const uint4 xq = gq < G ? __ldg(qp + u) : make_uint4(0u, 0u, 0u, 0u);
+            qa[4 * u + 0] = xq.x;
+            qa[4 * u + 1] = xq.y;
+            qa[4 * u + 2] = xq.z;
+            qa[4 * u + 3] = xq.w;
+        }
     }
-    __syncwarp();
     bool canon = true;
+    int U = 0;
+    if constexpr (kDirect) {
+        for (int w = lane; w < (N + 15) >> 4; w += 32) reinterpret_cast<uint4*>(dbits)[w] = make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+        bool dup = false;
 #pragma unroll
-    for (int t = 0; t < G; ++t) {
-        int prev31 = -1;
+        for (int t = 0; t < G; ++t) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            if (32 * e < K) {  // warp-uniform
-                const int qi = lane + 32 * e;
+            for (int e = 0; e < 4; ++e) {
                 const int xv = x[t][e];
-                int pv = __shfl_up_sync(kFull, xv, 1);
-                if (lane == 0) pv = prev31;
-                // the selectors' form: valid entries first, strictly ascending (so no
-                // key repeats within a head)
-                canon = canon && !__any_sync(kFull, xv >= 0 && qi > 0 && !(pv >= 0 && pv < xv));
-                prev31 = __shfl_sync(kFull, xv, 31);
-                if (xv >= 0) {
-                    int slot = (int)(((uint32_t)xv * 2654435761u) >> (32 - kSlotBits));
-                    for (int probe = 0; probe < kMmaSlots; ++probe) {
-                        const int old = atomicCAS(&ukey[slot], -1, xv);
-                        if (old == -1 || old == xv) {
-                            atomicOr(&umask[slot], 1u << t);
-                            break;
+                if (32 * e < K && xv >= 0) {
+                    const uint32_t sh = 8u * (uint32_t)(xv & 3) + (uint32_t)t;
+                    const uint32_t old = atomicOr(&dbits[xv >> 2], 1u << sh);
+                    dup = dup || ((old >> sh) & 1u) != 0u;
+                }
+            }
+        }
+        canon = !__any_sync(kFull, dup);
+        __syncwarp();
+#pragma unroll
+        for (int t = 0; t < G; ++t) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (32 * e < K) {  // warp-uniform
+                    const int xv = x[t][e];
+                    unsigned mk = 0u;
+                    bool own = false;
+                    if (xv >= 0) {
+                        mk = (dbits[xv >> 2] >> (8u * (uint32_t)(xv & 3))) & 0xffu;
+                        own = (mk & ((1u << t) - 1u)) == 0u;
+                    }
+                    const unsigned bal = __ballot_sync(kFull, own);
+                    if (own) {
+                        const int pos = U + __popc(bal & lt);
+                        if (pos < kMmaMaxU) {
+                            ukey[pos] = xv;
+                            umask[pos] = mk;
                         }
-                        slot = (slot + 1) & (kMmaSlots - 1);
+                    }
+                    U += __popc(bal);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+#pragma unroll
+        for (int u = 0; u < kMmaSlots / 32; ++u) {
+            ukey[lane + 32 * u] = -1;
+            umask[lane + 32 * u] = 0u;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int t = 0; t < G; ++t) {
+            int prev31 = -1;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (32 * e < K) {  // warp-uniform
+                    const int qi = lane + 32 * e;
+                    const int xv = x[t][e];
+                    int pv = __shfl_up_sync(kFull, xv, 1);
+                    if (lane == 0) pv = prev31;
+                    // the selectors' form: valid entries first, strictly ascending (so no
+                    // key repeats within a head)
+                    canon = canon && !__any_sync(kFull, xv >= 0 && qi > 0 && !(pv >= 0 && pv < xv));
+                    prev31 = __shfl_sync(kFull, xv, 31);
+                    if (xv >= 0) {
+                        int slot = (int)(((uint32_t)xv * 2654435761u) >> (32 - kSlotBits));
+                        for (int probe = 0; probe < kMmaSlots; ++probe) {
+                            const int old = atomicCAS(&ukey[slot], -1, xv);
+                            if (old == -1 || old == xv) {
+                                atomicOr(&umask[slot], 1u << t);
+                                break;
+                            }
+                            slot = (slot + 1) & (kMmaSlots - 1);
+                        }
                     }
                 }
             }
         }
-    }
-    __syncwarp();
-    int U = 0;
-    {
-        int kk[kMmaSlots / 32];
-        unsigned mk[kMmaSlots / 32];
-#pragma unroll
-        for (int u = 0; u < kMmaSlots / 32; ++u) {
-            // lane owns slots S lane .. S lane + S - 1, S = kMmaSlots / 32
-            kk[u] = ukey[(kMmaSlots / 32) * lane + u];
-            mk[u] = umask[(kMmaSlots / 32) * lane + u];
-        }
         __syncwarp();
-        int nmine = 0;
+        {
+            int kk[kMmaSlots / 32];
+            unsigned mk[kMmaSlots / 32];
 #pragma unroll
-        for (int u = 0; u < kMmaSlots / 32; ++u) nmine += kk[u] >= 0 ? 1 : 0;
-        int before = nmine;  // inclusive prefix over lanes
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(kFull, before, o);
-            if (lane >= o) before += y;
-        }
-        U = __shfl_sync(kFull, before, 31);
-        int pos = before - nmine;
-#pragma unroll
-        for (int u = 0; u < kMmaSlots / 32; ++u) {
-            if (kk[u] >= 0) {
-                if (pos < kMmaMaxU) {
-                    ukey[pos] = kk[u];
-                    umask[pos] = mk[u];
-                }
-                ++pos;
+            for (int u = 0; u < kMmaSlots / 32; ++u) {
+                // lane owns slots S lane .. S lane + S - 1, S = kMmaSlots / 32
+                kk[u] = ukey[(kMmaSlots / 32) * lane + u];
+                mk[u] = umask[(kMmaSlots / 32) * lane + u];
             }
+            __syncwarp();
+            int nmine = 0;
+#pragma unroll
+            for (int u = 0; u < kMmaSlots / 32; ++u) nmine += kk[u] >= 0 ? 1 : 0;
+            int before = nmine;  // inclusive prefix over lanes
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(kFull, before, o);
+                if (lane >= o) before += y;
+            }
+            U = __shfl_sync(kFull, before, 31);
+            int pos = before - nmine;
+#pragma unroll
+            for (int u = 0; u < kMmaSlots / 32; ++u) {
+                if (kk[u] >= 0) {
+                    if (pos < kMmaMaxU) {
+                        ukey[pos] = kk[u];
+                        umask[pos] = mk[u];
+                    }
+                    ++pos;
+                }
+            }
+            __syncwarp();
         }
-        __syncwarp();
     }
     if (!canon || U > kMmaMaxU) {
 #pragma unroll 1
@@ -418,19 +496,6 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
         return;
     }
 
-    // ---- q rows of the heads as A fragments (dims 32 c4 .. 32 c4 + 31 of head gq)
-    uint32_t qa[16];
-    {
-        const uint4* qp = reinterpret_cast<const uint4*>(q + (row0 + (size_t)gq * Nq) * D + 32 * c4);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint4 xq = gq < G ? __ldg(qp + u) : make_uint4(0u, 0u, 0u, 0u);
-            qa[4 * u + 0] = xq.x;
-            qa[4 * u + 1] = xq.y;
-            qa[4 * u + 2] = xq.z;
-            qa[4 * u + 3] = xq.w;
-        }
-    }
     const uint32_t vs_s = (uint32_t)__cvta_generic_to_shared(vs);
     // ldmatrix.x4.trans: lanes 0-7 / 8-15 / 16-23 / 24-31 address rows of keys
     // +0..7 / +8..15 / +0..7 / +8..15 at dims 16 np (first two) and 16 np + 8 (last two)
@@ -559,14 +624,19 @@ cudaError_t launch_typed(const GatherArgs& a, cudaStream_t stream) {
         const int G = a.H / a.Hkv;
         if (a.D == 128 && a.K <= 128 && (G == 2 || G == 3 || G == 4 || G == 6 || G == 8)) {
             const bool big = a.K > 64;
-#define OSSA_MMA_PICK(GG) (big ? gather_attn_bf16_d128_mma_kernel<IdxT, GG, 9> : gather_attn_bf16_d128_mma_kernel<IdxT, GG, 8>)
+            const bool direct = a.N <= kDirectMaxN && a.K <= 64;
+#define OSSA_MMA_PICK(GG)                                                                      \
+    (direct ? gather_attn_bf16_d128_mma_kernel<IdxT, GG, 8, true>                              \
+            : (big ? gather_attn_bf16_d128_mma_kernel<IdxT, GG, 9, false>                      \
+                   : gather_attn_bf16_d128_mma_kernel<IdxT, GG, 8, false>))
             auto kern = G == 2 ? OSSA_MMA_PICK(2)
                       : G == 3 ? OSSA_MMA_PICK(3)
                       : G == 4 ? OSSA_MMA_PICK(4)
                       : G == 6 ? OSSA_MMA_PICK(6)
                                : OSSA_MMA_PICK(8);
 #undef OSSA_MMA_PICK
-            const size_t kMmaSmem = big ? mma_smem_bytes<9>() : mma_smem_bytes<8>();
+            const size_t kMmaSmem =
+                direct ? mma_smem_bytes<8, true>() : (big ? mma_smem_bytes<9, false>() : mma_smem_bytes<8, false>());
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMmaSmem);
             if (e != cudaSuccess) return e;
             dim3 mgrid((Nq + kMmaWarps - 1) / kMmaWarps, a.B * a.Hkv);

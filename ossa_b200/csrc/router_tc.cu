@@ -1323,8 +1323,11 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     const int rbase = r0 + 16 * hf;
                     if ((K & 3) == 0) {
                         const int per_row = K >> 2;
+                        // f / per_row by a reciprocal: (f + 0.5) / per_row stays at least
+                        // 1/32 away from an integer for f < 256, per_row <= 16
+                        const float inv_pr = 1.f / (float)per_row;
                         for (int f = lane; f < 16 * per_row; f += 32) {
-                            const int rin = f / per_row, v = f - rin * per_row;
+                            const int rin = (int)(((float)f + 0.5f) * inv_pr), v = f - rin * per_row;
                             if ((workmask >> (2 * rin)) & 1u) {
                                 const int rrow = rbase + rin;
                                 const uint4 val = lds_u4(stage_s + 256u * rrow + 16u * (uint32_t)(v ^ (rrow & 7)));
