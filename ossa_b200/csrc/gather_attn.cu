@@ -254,48 +254,46 @@ gather_attn_bf16_d128_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
 // ------------------------------------------- GQA heads on the tensor cores (bf16, D = 128)
 //
 // One warp per query and kv head, all G (2, 3, 4, 6 or 8) query heads of the group at once:
-//  1. union: the G index rows must be in the selectors' form (valid entries first,
-//     strictly ascending; else the query goes through gather_row_bf16_d128 per head).
-//     Every valid key goes into an open-addressing hash in shared memory with its
-//     head bit; the occupied slots, compacted in slot order, are the union (at most
-//     kMmaMaxU keys, else per head).  The q rows are loaded before the union is built,
-//     so their latency overlaps it.
-//  2. the union in chunks of 32 keys: its value rows are copied to shared memory
-//     (cp.async, 16-byte pieces XOR-swizzled by row) while the scores of the chunk
-//     S = Q K_U^T run on mma.sync m16n8k16 (bf16 operands, fp32 accumulation): A =
-//     the G heads' q rows (rows G..15 zero), B = 8 union keys per n-tile.  The
-//     contraction runs over the head dims in a permuted order, the same for A and B
-//     (lane c = lane % 4 of a quad supplies dims 32c .. 32c + 31, four per k-step),
-//     so each lane loads one contiguous 64-byte piece of a key row per n-tile;
-//  3. online softmax per head over its selected keys (head bit set; others masked):
-//     a head's scores sit in the four lanes of one quad, reduced by two shuffles;
-//     p is rounded to bf16 for p.v, as in the per-head form;
-//  4. O += P V_chunk with mma.sync: P from the score fragments (no shuffles), V as
-//     the B operand by ldmatrix.trans from the staged rows; at the end each head's
-//     row is divided by its sum and stored as bf16.
+//  1. q: the G heads' rows as mma A fragments, loaded first so that their latency
+//     overlaps the union build.
+//  2. union of the heads' keys with head bits.  Direct form (N <= 4096, K <= 64): a
+//     per-warp byte array indexed by the key holds the head bits, set by one atomicOr
+//     per selected key (no probing, no compare-and-swap); a head bit that is already set
+//     marks a repeated key.  Hash form: the G index rows must be in the selectors' form
+//     (valid entries first, strictly ascending); every valid key goes into an
+//     open-addressing hash with its head bit.  The union list (at most kMaxU keys) holds
+//     each key once with its head bits.  A repeated key, a row out of form (hash form)
+//     or a larger union sends the query through gather_row_bf16_d128 per head.
+//  3. the union in chunks of 16 keys.  Key and value rows are copied to shared memory
+//     with cp.async (16-byte pieces XOR-swizzled by row): the key rows of chunk c + 1
+//     are in flight while chunk c is scored, the value rows of chunk c while its scores
+//     and softmax run.  S = Q K^T on mma.sync m16n8k16 (bf16 operands, fp32
+//     accumulation): A = the heads' q rows (rows G..15 zero), B = 8 keys per n-tile by
+//     ldmatrix from the staged key rows.
+//  4. online softmax per head over its selected keys (head bit set; others masked): a
+//     head's scores sit in the four lanes of one quad, reduced by two shuffles; p is
+//     rounded to bf16 for p.v, as in the per-head form.
+//  5. O += P V with mma.sync: P from the score fragments (no shuffles), V as the B
+//     operand by ldmatrix.trans from the staged value rows; at the end each head's row
+//     is divided by its sum and stored as bf16.
 // Results agree with the per-head form to rounding (tensor-core accumulation order).
-// The union hash has 2^kSlotBits slots and holds at most half as many keys: 256
-// slots (128 keys) for K <= 64, 512 slots (256 keys) above.  With N <= 4096 keys and
-// K <= 64 the union is built instead in a per-warp byte array indexed by the key
-// (kDirect): byte j holds the head bits of key j, set by one atomicOr per selected
-// key, so there is no probing and no compare-and-swap; a head bit that is already set
-// marks a repeated key (the per-head form then takes the query).  The entry of the
-// lowest head that selected a key appends it to the union list.
-constexpr int kMmaChunk = 32;     // union keys per chunk: 4 score n-tiles, 2 value k-steps
+constexpr int kMmaChunk = 16;                    // union keys per chunk: 2 score n-tiles, 1 value k-step
 constexpr int kMmaWarps = 8;
-constexpr int kDirectMaxN = 4096;  // keys covered by the direct head-bit array
-constexpr int kDirectMaxU = 128;   // union entries of the direct form
-// Per warp: the value rows of a chunk (kMmaChunk x 256 B; the direct head-bit array,
-// kDirectMaxN bytes, uses the same space before the first chunk), then the hash
-// slots / union list.
+constexpr int kRowBytes = 256;                   // one bf16 key or value row (D = 128)
+constexpr int kChunkBytes = kMmaChunk * kRowBytes;
+constexpr int kStageBytes = 3 * kChunkBytes;     // key rows of two chunks, value rows of one
+constexpr int kDirectMaxN = 4096;                // keys covered by the direct head-bit array
 template <int kSlotBits, bool kDirect>
-constexpr size_t mma_warp_smem() {
-    return (size_t)kMmaChunk * 256 + (kDirect ? (size_t)kDirectMaxU * 8 : ((size_t)8 << kSlotBits));
-}
-static_assert(kDirectMaxN <= kMmaChunk * 256, "the direct head-bit array fits in the value staging area");
+constexpr int mma_max_union() { return kDirect ? 128 : (1 << kSlotBits) / 2; }
+// Per warp: the staging area (the hash slots or the direct head-bit array use it while
+// the union is built), then the union list (keys, head bits).
+template <int kSlotBits, bool kDirect>
+constexpr size_t mma_warp_smem() { return (size_t)kStageBytes + (size_t)8 * mma_max_union<kSlotBits, kDirect>(); }
 template <int kSlotBits, bool kDirect>
 constexpr size_t mma_smem_bytes() { return kMmaWarps * mma_warp_smem<kSlotBits, kDirect>(); }
+static_assert(kDirectMaxN <= kStageBytes && ((size_t)8 << 9) <= (size_t)kStageBytes, "the union build fits in the staging area");
 static_assert(mma_warp_smem<8, true>() % 16 == 0 && mma_warp_smem<9, false>() % 16 == 0, "warp areas stay 16-byte aligned");
+static_assert(2 * (mma_smem_bytes<9, false>() + 1024) <= 233472, "two CTAs per SM");
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -310,6 +308,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait_pending() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
+
 template <typename IdxT, int G, int kSlotBits, bool kDirect>
 __global__ void __launch_bounds__(kMmaWarps * 32, 2)
 gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
@@ -317,9 +320,8 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
                                  __nv_bfloat16* __restrict__ out, int H, int Hkv, int N, int Nq, int q0, int K,
                                  float scale_log2, int causal) {
     constexpr int D = 128;
-    constexpr int kMmaSlots = kDirect ? kDirectMaxU : 1 << kSlotBits;
-    constexpr int kMmaMaxU = kDirect ? kDirectMaxU : kMmaSlots / 2;
-    constexpr size_t kMmaWarpSmem = mma_warp_smem<kSlotBits, kDirect>();
+    constexpr int kMaxU = mma_max_union<kSlotBits, kDirect>();
+    constexpr int kSlots = 1 << kSlotBits;
     extern __shared__ __align__(128) uint8_t msm[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -332,18 +334,26 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
     const int il = blockIdx.x * kMmaWarps + warp;
     if (il >= Nq) return;  // warp-uniform; no CTA-wide barrier follows
     const int i = q0 + il;
-    uint8_t* vs = msm + (size_t)warp * kMmaWarpSmem;  // [kMmaChunk][256 B], pieces swizzled
-    int* ukey = reinterpret_cast<int*>(vs + kMmaChunk * 256);       // hash slots, then the union
-    unsigned* umask = reinterpret_cast<unsigned*>(ukey + kMmaSlots);
-    uint32_t* dbits = reinterpret_cast<uint32_t*>(vs);  // direct: head bits, 4 keys per word (until chunk 0)
+    uint8_t* stage = msm + (size_t)warp * mma_warp_smem<kSlotBits, kDirect>();
+    int* ukey = reinterpret_cast<int*>(stage + kStageBytes);  // the union list
+    unsigned* umask = reinterpret_cast<unsigned*>(ukey + kMaxU);
     const __nv_bfloat16* kb = k + (size_t)bg * N * D;
     const __nv_bfloat16* vb = v + (size_t)bg * N * D;
     const size_t row0 = ((size_t)b * H + (size_t)g * G) * Nq + il;  // head t: row0 + t * Nq
 
-    // ---- 1. union of the heads' keys with head bits into ukey / umask: the direct
-    // head-bit array (kDirect), or an open-addressing hash in shared memory
-    // (kMmaSlots slots, linear probing) compacted by ballot into the same arrays in
-    // slot order
+    // ---- 1. q rows as A fragments: k-step s takes dims 16 s + 2 c4, +1 (a0) and
+    // 16 s + 8 + 2 c4, +1 (a2) of head gq (rows G..15 zero)
+    uint32_t qa[16];
+    {
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(q + (row0 + (size_t)(gq < G ? gq : 0) * Nq) * D);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            qa[2 * s] = gq < G ? __ldg(qw + 8 * s + c4) : 0u;
+            qa[2 * s + 1] = gq < G ? __ldg(qw + 8 * s + 4 + c4) : 0u;
+        }
+    }
+
+    // ---- 2. union of the heads' keys with head bits into ukey / umask
     int x[G][4];
 #pragma unroll
     for (int t = 0; t < G; ++t) {
@@ -355,23 +365,10 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
             x[t][e] = (jl >= 0 && jl < N && (!causal || jl <= i)) ? (int)jl : -1;
         }
     }
-    // q rows of the heads as A fragments (dims 32 c4 .. 32 c4 + 31 of head gq), loaded
-    // now so that their latency overlaps the union build
-    uint32_t qa[16];
-    {
-        const uint4* qp = reinterpret_cast<const uint4*>(q + (row0 + (size_t)gq * Nq) * D + 32 * c4);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint4 xq = gq < G ? __ldg(qp + u) : make_uint4(0u, 0u, 0u, 0u);
-            qa[4 * u + 0] = xq.x;
-            qa[4 * u + 1] = xq.y;
-            qa[4 * u + 2] = xq.z;
-            qa[4 * u + 3] = xq.w;
-        }
-    }
     bool canon = true;
     int U = 0;
     if constexpr (kDirect) {
+        uint32_t* dbits = reinterpret_cast<uint32_t*>(stage);  // byte j: head bits of key j
         for (int w = lane; w < (N + 15) >> 4; w += 32) reinterpret_cast<uint4*>(dbits)[w] = make_uint4(0u, 0u, 0u, 0u);
         __syncwarp();
         bool dup = false;
@@ -389,6 +386,7 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
         }
         canon = !__any_sync(kFull, dup);
         __syncwarp();
+        // the entry of the lowest head that selected a key appends it
 #pragma unroll
         for (int t = 0; t < G; ++t) {
 #pragma unroll
@@ -404,7 +402,7 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
                     const unsigned bal = __ballot_sync(kFull, own);
                     if (own) {
                         const int pos = U + __popc(bal & lt);
-                        if (pos < kMmaMaxU) {
+                        if (pos < kMaxU) {
                             ukey[pos] = xv;
                             umask[pos] = mk;
                         }
@@ -413,12 +411,13 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
                 }
             }
         }
-        __syncwarp();
     } else {
+        int* skey = reinterpret_cast<int*>(stage);  // hash slots (linear probing)
+        unsigned* smask = reinterpret_cast<unsigned*>(skey + kSlots);
 #pragma unroll
-        for (int u = 0; u < kMmaSlots / 32; ++u) {
-            ukey[lane + 32 * u] = -1;
-            umask[lane + 32 * u] = 0u;
+        for (int u = 0; u < kSlots / 32; ++u) {
+            skey[lane + 32 * u] = -1;
+            smask[lane + 32 * u] = 0u;
         }
         __syncwarp();
 #pragma unroll
@@ -437,54 +436,51 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
                     prev31 = __shfl_sync(kFull, xv, 31);
                     if (xv >= 0) {
                         int slot = (int)(((uint32_t)xv * 2654435761u) >> (32 - kSlotBits));
-                        for (int probe = 0; probe < kMmaSlots; ++probe) {
-                            const int old = atomicCAS(&ukey[slot], -1, xv);
+                        for (int probe = 0; probe < kSlots; ++probe) {
+                            const int old = atomicCAS(&skey[slot], -1, xv);
                             if (old == -1 || old == xv) {
-                                atomicOr(&umask[slot], 1u << t);
+                                atomicOr(&smask[slot], 1u << t);
                                 break;
                             }
-                            slot = (slot + 1) & (kMmaSlots - 1);
+                            slot = (slot + 1) & (kSlots - 1);
                         }
                     }
                 }
             }
         }
         __syncwarp();
-        {
-            int kk[kMmaSlots / 32];
-            unsigned mk[kMmaSlots / 32];
+        // occupied slots in slot order: lane owns slots S lane .. S lane + S - 1, S = kSlots / 32
+        int kk[kSlots / 32];
+        unsigned mk[kSlots / 32];
 #pragma unroll
-            for (int u = 0; u < kMmaSlots / 32; ++u) {
-                // lane owns slots S lane .. S lane + S - 1, S = kMmaSlots / 32
-                kk[u] = ukey[(kMmaSlots / 32) * lane + u];
-                mk[u] = umask[(kMmaSlots / 32) * lane + u];
-            }
-            __syncwarp();
-            int nmine = 0;
+        for (int u = 0; u < kSlots / 32; ++u) {
+            kk[u] = skey[(kSlots / 32) * lane + u];
+            mk[u] = smask[(kSlots / 32) * lane + u];
+        }
+        int nmine = 0;
 #pragma unroll
-            for (int u = 0; u < kMmaSlots / 32; ++u) nmine += kk[u] >= 0 ? 1 : 0;
-            int before = nmine;  // inclusive prefix over lanes
+        for (int u = 0; u < kSlots / 32; ++u) nmine += kk[u] >= 0 ? 1 : 0;
+        int before = nmine;  // inclusive prefix over lanes
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(kFull, before, o);
-                if (lane >= o) before += y;
-            }
-            U = __shfl_sync(kFull, before, 31);
-            int pos = before - nmine;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(kFull, before, o);
+            if (lane >= o) before += y;
+        }
+        U = __shfl_sync(kFull, before, 31);
+        int pos = before - nmine;
 #pragma unroll
-            for (int u = 0; u < kMmaSlots / 32; ++u) {
-                if (kk[u] >= 0) {
-                    if (pos < kMmaMaxU) {
-                        ukey[pos] = kk[u];
-                        umask[pos] = mk[u];
-                    }
-                    ++pos;
+        for (int u = 0; u < kSlots / 32; ++u) {
+            if (kk[u] >= 0) {
+                if (pos < kMaxU) {
+                    ukey[pos] = kk[u];
+                    umask[pos] = mk[u];
                 }
+                ++pos;
             }
-            __syncwarp();
         }
     }
-    if (!canon || U > kMmaMaxU) {
+    __syncwarp();  // the union list is complete; the staging area is free
+    if (!canon || U > kMaxU) {
 #pragma unroll 1
         for (int t = 0; t < G; ++t) {
             const size_t row = row0 + (size_t)t * Nq;
@@ -496,63 +492,80 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
         return;
     }
 
-    const uint32_t vs_s = (uint32_t)__cvta_generic_to_shared(vs);
-    // ldmatrix.x4.trans: lanes 0-7 / 8-15 / 16-23 / 24-31 address rows of keys
-    // +0..7 / +8..15 / +0..7 / +8..15 at dims 16 np (first two) and 16 np + 8 (last two)
+    // ---- 3.-5. the union in chunks of kMmaChunk keys
+    const uint32_t st_s = (uint32_t)__cvta_generic_to_shared(stage);  // key rows: two chunk buffers
+    const uint32_t vst_s = st_s + 2u * kChunkBytes;                    // value rows of one chunk
+    // Staging: lane copies the 16-byte piece pc = lane % 16 of rows lane / 16 + 2 r of a
+    // chunk; rows past the chunk's keys are zero-filled (source size 0).
+    auto stage_rows = [&](uint32_t dst_base, const __nv_bfloat16* base, int c0) {
+        const int nk = min(kMmaChunk, U - c0);
+        const int pc = lane & 15;
+#pragma unroll
+        for (int r = 0; r < kMmaChunk / 2; ++r) {
+            const int row = 2 * r + (lane >> 4);
+            const bool valid = row < nk;
+            const int key = valid ? ukey[c0 + row] : 0;
+            const uint32_t dst = dst_base + (uint32_t)(row * kRowBytes + ((pc ^ (row & 7)) << 4));
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
+                         "l"(base + (size_t)key * D + pc * 8), "r"(valid ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // ldmatrix row addresses.  Key rows (B of S, no transpose): lanes 8 j .. 8 j + 7 give
+    // rows 0..7 of an n-tile at piece 4 m + j, so one x4 load holds (b0, b1) of k-steps
+    // 2 m and 2 m + 1.  Value rows (B of P V, transposed): lanes 0-7 / 8-15 / 16-23 /
+    // 24-31 give key rows 0..7 / 8..15 / 0..7 / 8..15 at dims 16 np (first two) and
+    // 16 np + 8 (last two).
+    const int krow = lane & 7, kpiece = lane >> 3;
     const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8;
     const int lcol = lane >> 4;
     float oacc[16][4];
 #pragma unroll
     for (int n = 0; n < 16; ++n) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
-
-    for (int c0 = 0; c0 < U; c0 += kMmaChunk) {
+    const int nch = (U + kMmaChunk - 1) / kMmaChunk;
+    if (nch > 0) stage_rows(st_s, kb, 0);
+    for (int c = 0; c < nch; ++c) {
+        const int c0 = c * kMmaChunk;
         const int nk = min(kMmaChunk, U - c0);
-        const int nt = (nk + 7) >> 3;      // score n-tiles of this chunk
-        const int nks = (nk + 15) >> 4;    // value k-steps of this chunk
-        // value rows of the chunk to shared memory (zero rows up to a multiple of 16)
-        __syncwarp();  // the previous chunk's ldmatrix reads are done
-        for (int e = lane; e < nks * 16 * 16; e += 32) {
-            const int row = e >> 4, pc = e & 15;
-            const uint32_t dst = vs_s + (uint32_t)(row * 256 + ((pc ^ (row & 7)) << 4));
-            if (row < nk) {
-                const void* src = vb + (size_t)ukey[c0 + row] * D + pc * 8;
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-            } else {
-                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0u) : "memory");
-            }
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
+        const bool more = c + 1 < nch;  // warp-uniform
+        __syncwarp();  // chunk c - 1 is done with the value rows and with key buffer (c + 1) & 1
+        stage_rows(vst_s, vb, c0);
+        if (more) stage_rows(st_s + (uint32_t)(((c + 1) & 1) * kChunkBytes), kb, c0 + kMmaChunk);
+        // groups in flight: key rows of c, value rows of c, key rows of c + 1 (if any)
+        if (more) cp_async_wait_pending<2>();
+        else cp_async_wait_pending<1>();
+        __syncwarp();
         // scores of the chunk
-        float sacc[kMmaChunk / 8][4];
+        const uint32_t kst = st_s + (uint32_t)((c & 1) * kChunkBytes);
+        float sacc[2][4];
 #pragma unroll
-        for (int t = 0; t < kMmaChunk / 8; ++t) {
+        for (int t = 0; t < 2; ++t) {
             sacc[t][0] = sacc[t][1] = sacc[t][2] = sacc[t][3] = 0.f;
-            if (t < nt) {
-                const int u = c0 + 8 * t + gq;
-                const int j = 8 * t + gq < nk ? ukey[u] : 0;
-                const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)j * D + 32 * c4);
-                uint32_t kw[16];
+            if (8 * t < nk) {
+                const int row = 8 * t + krow;
 #pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    const uint4 xk = __ldg(kp + w);
-                    kw[4 * w + 0] = xk.x;
-                    kw[4 * w + 1] = xk.y;
-                    kw[4 * w + 2] = xk.z;
-                    kw[4 * w + 3] = xk.w;
+                for (int m = 0; m < 4; ++m) {
+                    const int piece = 4 * m + kpiece;
+                    uint32_t r0, r1, r2, r3;
+                    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                                 : "r"(kst + (uint32_t)(row * kRowBytes + ((piece ^ (row & 7)) << 4))));
+                    mma_bf16_16816(sacc[t], qa[4 * m], qa[4 * m + 1], r0, r1);
+                    mma_bf16_16816(sacc[t], qa[4 * m + 2], qa[4 * m + 3], r2, r3);
                 }
-#pragma unroll
-                for (int s = 0; s < 8; ++s) mma_bf16_16816(sacc[t], qa[2 * s], qa[2 * s + 1], kw[2 * s], kw[2 * s + 1]);
             }
         }
         // online softmax of head gq over its selected keys c0 + 8 t + 2 c4 + e
         float mx = -INFINITY;
 #pragma unroll
-        for (int t = 0; t < kMmaChunk / 8; ++t) {
+        for (int t = 0; t < 2; ++t) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int ul = 8 * t + 2 * c4 + e;
-                const bool sel = ul < nk && gq < G && ((umask[c0 + ul] >> gq) & 1u);
+                const unsigned hb = ul < nk ? umask[c0 + ul] : 0u;
+                const bool sel = gq < G && ((hb >> gq) & 1u);
                 sacc[t][e] = sel ? sacc[t][e] * scale_log2 : -INFINITY;
                 mx = fmaxf(mx, sacc[t][e]);
             }
@@ -562,9 +575,9 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
         const float m_new = fmaxf(m_run, mx);
         const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);
         float sum = 0.f;
-        uint32_t pa[kMmaChunk / 8];
+        uint32_t pa[2];
 #pragma unroll
-        for (int t = 0; t < kMmaChunk / 8; ++t) {
+        for (int t = 0; t < 2; ++t) {
             const float p0 = m_new == -INFINITY ? 0.f : exp2f(sacc[t][0] - m_new);
             const float p1 = m_new == -INFINITY ? 0.f : exp2f(sacc[t][1] - m_new);
             sum += p0 + p1;
@@ -580,23 +593,18 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
             oacc[n][1] *= alpha;
         }
         // O += P V of the chunk
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        if (more) cp_async_wait_pending<1>();
+        else cp_async_wait_pending<0>();
         __syncwarp();
 #pragma unroll
-        for (int ks = 0; ks < kMmaChunk / 16; ++ks) {
-            if (ks < nks) {
-                const int row = 16 * ks + lrow;
-#pragma unroll
-                for (int np = 0; np < 8; ++np) {
-                    const int pc = 2 * np + lcol;
-                    uint32_t r0, r1, r2, r3;
-                    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                                 : "r"(vs_s + (uint32_t)(row * 256 + ((pc ^ (row & 7)) << 4))));
-                    mma_bf16_16816(oacc[2 * np], pa[2 * ks], pa[2 * ks + 1], r0, r1);
-                    mma_bf16_16816(oacc[2 * np + 1], pa[2 * ks], pa[2 * ks + 1], r2, r3);
-                }
-            }
+        for (int np = 0; np < 8; ++np) {
+            const int pc = 2 * np + lcol;
+            uint32_t r0, r1, r2, r3;
+            asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                         : "r"(vst_s + (uint32_t)(lrow * kRowBytes + ((pc ^ (lrow & 7)) << 4))));
+            mma_bf16_16816(oacc[2 * np], pa[0], pa[1], r0, r1);
+            mma_bf16_16816(oacc[2 * np + 1], pa[0], pa[1], r2, r3);
         }
     }
     if (gq < G) {
