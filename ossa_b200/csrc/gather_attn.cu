@@ -303,6 +303,24 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
         : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
+// mma.sync m16n8k16 with all four A registers (rows 0..15).
+__device__ __forceinline__ void mma_bf16_16816_a4(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                  uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Transpose of an 8 x 8 bf16 matrix held one 32-bit pair per lane (lane 4 r + c holds
+// row r, columns 2 c, 2 c + 1; afterwards the same for the transpose).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&v);
@@ -512,18 +530,18 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    // ldmatrix row addresses.  Key rows (B of S, no transpose): lanes 8 j .. 8 j + 7 give
-    // rows 0..7 of an n-tile at piece 4 m + j, so one x4 load holds (b0, b1) of k-steps
-    // 2 m and 2 m + 1.  Value rows (B of P V, transposed): lanes 0-7 / 8-15 / 16-23 /
-    // 24-31 give key rows 0..7 / 8..15 / 0..7 / 8..15 at dims 16 np (first two) and
-    // 16 np + 8 (last two).
-    const int krow = lane & 7, kpiece = lane >> 3;
-    const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8;
-    const int lcol = lane >> 4;
-    float oacc[16][4];
+    // ldmatrix row addresses (16 rows of a chunk, 16-byte pieces).  Key rows, the A
+    // operand of S^T (no transpose): lanes 0-7 / 8-15 / 16-23 / 24-31 give key rows
+    // 0..7 / 8..15 / 0..7 / 8..15 at piece 2 s / 2 s / 2 s + 1 / 2 s + 1 (k-step s).
+    // Value rows, the A operand of O^T (transposed): key rows 0..7 / 0..7 / 8..15 /
+    // 8..15 at piece 2 mt / 2 mt + 1 / 2 mt / 2 mt + 1 (dims 16 mt .. 16 mt + 15).
+    const int krow = (lane & 7) + ((lane >> 3) & 1) * 8, kpc = lane >> 4;
+    const int vrow = (lane & 7) + (lane >> 4) * 8, vpc = (lane >> 3) & 1;
+    // O^T accumulators: dims 16 mt + gq (+8) of heads 2 c4, 2 c4 + 1
+    float oacc[8][4];
 #pragma unroll
-    for (int n = 0; n < 16; ++n) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
+    for (int n = 0; n < 8; ++n) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // heads 2 c4, 2 c4 + 1
     const int nch = (U + kMmaChunk - 1) / kMmaChunk;
     if (nch > 0) stage_rows(st_s, kb, 0);
     for (int c = 0; c < nch; ++c) {
@@ -537,82 +555,86 @@ gather_attn_bf16_d128_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv
         if (more) cp_async_wait_pending<2>();
         else cp_async_wait_pending<1>();
         __syncwarp();
-        // scores of the chunk
+        // S^T = K Q^T of the chunk: keys gq, gq + 8 x heads 2 c4, 2 c4 + 1
         const uint32_t kst = st_s + (uint32_t)((c & 1) * kChunkBytes);
-        float sacc[2][4];
+        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            sacc[t][0] = sacc[t][1] = sacc[t][2] = sacc[t][3] = 0.f;
-            if (8 * t < nk) {
-                const int row = 8 * t + krow;
-#pragma unroll
-                for (int m = 0; m < 4; ++m) {
-                    const int piece = 4 * m + kpiece;
-                    uint32_t r0, r1, r2, r3;
-                    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                                 : "r"(kst + (uint32_t)(row * kRowBytes + ((piece ^ (row & 7)) << 4))));
-                    mma_bf16_16816(sacc[t], qa[4 * m], qa[4 * m + 1], r0, r1);
-                    mma_bf16_16816(sacc[t], qa[4 * m + 2], qa[4 * m + 3], r2, r3);
-                }
-            }
+        for (int s = 0; s < 8; ++s) {
+            const int piece = 2 * s + kpc;
+            uint32_t a0, a1, a2, a3;
+            asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+                         : "r"(kst + (uint32_t)(krow * kRowBytes + ((piece ^ (krow & 7)) << 4))));
+            mma_bf16_16816_a4(sacc, a0, a1, a2, a3, qa[2 * s], qa[2 * s + 1]);
         }
-        // online softmax of head gq over its selected keys c0 + 8 t + 2 c4 + e
-        float mx = -INFINITY;
+        // online softmax per head over its selected keys c0 + gq, c0 + gq + 8; a head's
+        // scores sit in the eight lanes of equal c4
+        bool sel[2][2];
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
+        for (int h = 0; h < 2; ++h) {
+            const int ul = gq + 8 * h;
+            const unsigned hb = ul < nk ? umask[c0 + ul] : 0u;
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int ul = 8 * t + 2 * c4 + e;
-                const unsigned hb = ul < nk ? umask[c0 + ul] : 0u;
-                const bool sel = gq < G && ((hb >> gq) & 1u);
-                sacc[t][e] = sel ? sacc[t][e] * scale_log2 : -INFINITY;
-                mx = fmaxf(mx, sacc[t][e]);
-            }
+            for (int e = 0; e < 2; ++e) sel[h][e] = 2 * c4 + e < G && ((hb >> (2 * c4 + e)) & 1u);
         }
-        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);
-        float sum = 0.f;
-        uint32_t pa[2];
+        float mx[2], alpha[2], pr[2][2];
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            const float p0 = m_new == -INFINITY ? 0.f : exp2f(sacc[t][0] - m_new);
-            const float p1 = m_new == -INFINITY ? 0.f : exp2f(sacc[t][1] - m_new);
-            sum += p0 + p1;
-            pa[t] = pack_bf16x2(p0, p1);
+        for (int e = 0; e < 2; ++e) {
+            const float s0 = sel[0][e] ? sacc[e] * scale_log2 : -INFINITY;
+            const float s1 = sel[1][e] ? sacc[2 + e] * scale_log2 : -INFINITY;
+            float m = fmaxf(s0, s1);
+            m = fmaxf(m, __shfl_xor_sync(kFull, m, 4));
+            m = fmaxf(m, __shfl_xor_sync(kFull, m, 8));
+            m = fmaxf(m, __shfl_xor_sync(kFull, m, 16));
+            mx[e] = fmaxf(m_run[e], m);
+            alpha[e] = mx[e] == -INFINITY ? 1.f : exp2f(m_run[e] - mx[e]);
+            pr[0][e] = mx[e] == -INFINITY ? 0.f : exp2f(s0 - mx[e]);
+            pr[1][e] = mx[e] == -INFINITY ? 0.f : exp2f(s1 - mx[e]);
+            float sum = pr[0][e] + pr[1][e];
+            sum += __shfl_xor_sync(kFull, sum, 4);
+            sum += __shfl_xor_sync(kFull, sum, 8);
+            sum += __shfl_xor_sync(kFull, sum, 16);
+            l_run[e] = l_run[e] * alpha[e] + sum;
+            m_run[e] = mx[e];
         }
-        sum += __shfl_xor_sync(kFull, sum, 1);
-        sum += __shfl_xor_sync(kFull, sum, 2);
-        l_run = l_run * alpha + sum;
-        m_run = m_new;
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
-            oacc[n][0] *= alpha;
-            oacc[n][1] *= alpha;
+        for (int n = 0; n < 8; ++n) {
+            oacc[n][0] *= alpha[0];
+            oacc[n][1] *= alpha[1];
+            oacc[n][2] *= alpha[0];
+            oacc[n][3] *= alpha[1];
         }
-        // O += P V of the chunk
+        // P^T as the B operand: each 8 x 8 (keys x heads) half of the score tile,
+        // rounded to bf16, transposed across the warp
+        const uint32_t pb0 = movmatrix_trans(pack_bf16x2(pr[0][0], pr[0][1]));
+        const uint32_t pb1 = movmatrix_trans(pack_bf16x2(pr[1][0], pr[1][1]));
+        // O^T += V^T P^T of the chunk
         if (more) cp_async_wait_pending<1>();
         else cp_async_wait_pending<0>();
         __syncwarp();
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
-            const int pc = 2 * np + lcol;
-            uint32_t r0, r1, r2, r3;
+        for (int mt = 0; mt < 8; ++mt) {
+            const int pc = 2 * mt + vpc;
+            uint32_t a0, a1, a2, a3;
             asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                         : "r"(vst_s + (uint32_t)(lrow * kRowBytes + ((pc ^ (lrow & 7)) << 4))));
-            mma_bf16_16816(oacc[2 * np], pa[0], pa[1], r0, r1);
-            mma_bf16_16816(oacc[2 * np + 1], pa[0], pa[1], r2, r3);
+                         : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+                         : "r"(vst_s + (uint32_t)(vrow * kRowBytes + ((pc ^ (vrow & 7)) << 4))));
+            mma_bf16_16816_a4(oacc[mt], a0, a1, a2, a3, pb0, pb1);
         }
     }
-    if (gq < G) {
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        __nv_bfloat16* orow = out + (row0 + (size_t)gq * Nq) * D + 2 * c4;
+    // each head's row divided by its sum; the 8 x 8 (dims x heads) halves of every O^T
+    // tile transposed back, so lane (gq, c4) stores dims 2 c4, 2 c4 + 1 of head gq
+    const float inv0 = l_run[0] > 0.f ? 1.f / l_run[0] : 0.f;
+    const float inv1 = l_run[1] > 0.f ? 1.f / l_run[1] : 0.f;
+    __nv_bfloat16* orow = out + (row0 + (size_t)(gq < G ? gq : 0) * Nq) * D + 2 * c4;
 #pragma unroll
-        for (int n = 0; n < 16; ++n)
-            *reinterpret_cast<uint32_t*>(orow + 8 * n) = pack_bf16x2(oacc[n][0] * inv, oacc[n][1] * inv);
+    for (int mt = 0; mt < 8; ++mt) {
+        const uint32_t lo = movmatrix_trans(pack_bf16x2(oacc[mt][0] * inv0, oacc[mt][1] * inv1));
+        const uint32_t hi = movmatrix_trans(pack_bf16x2(oacc[mt][2] * inv0, oacc[mt][3] * inv1));
+        if (gq < G) {
+            *reinterpret_cast<uint32_t*>(orow + 16 * mt) = lo;
+            *reinterpret_cast<uint32_t*>(orow + 16 * mt + 8) = hi;
+        }
     }
 }
 
