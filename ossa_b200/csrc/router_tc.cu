@@ -1287,30 +1287,40 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 {
                     const uint32_t LA = smem_u32(frowbuf) + 4u;             // .y fields
                     const uint32_t LB = LA + 8u * Cfg::kCap;
+                    // Lane 2r merges from the front (smaller key first), lane 2r+1 from the
+                    // back (larger key first).  Keys are compared as u = j (front) or
+                    // u = 0x7fffffff - j (back) unsigned, so one compare serves both lanes
+                    // and an exhausted list (j = -1) sorts last.  Each list keeps its
+                    // current and next key in registers; the shared-memory read that
+                    // refills the taken list's next key is issued a step before it is
+                    // compared, and no step branches.
                     const int dir = fh ? -1 : 1;
+                    const uint32_t ubase = fh ? 0x7fffffffu : 0u;
+                    auto key_u = [&](uint32_t base, int idx, int n) -> uint32_t {
+                        const uint32_t j = lds_u32_or(base + 8u * (uint32_t)idx, work && idx >= 0 && idx < n, 0xffffffffu);
+                        return fh ? ubase - j : j;  // j = -1 maps to 0x80000000 (back) or 0xffffffff (front)
+                    };
                     int ia = fh ? nA - 1 : 0, ib = fh ? nB - 1 : 0;
-                    // lane 2r takes the smaller key each step, lane 2r+1 the larger:
-                    // compare on j for the front and on -j for the back
-                    const int sgn = fh ? -1 : 1;
-                    int ja = (work && ia >= 0 && ia < nA) ? (int)lds_u32(LA + 8u * ia) : -1;
-                    int jb = (work && ib >= 0 && ib < nB) ? (int)lds_u32(LB + 8u * ib) : -1;
+                    uint32_t ua = key_u(LA, ia, nA), ua2 = key_u(LA, ia + dir, nA);
+                    uint32_t ub = key_u(LB, ib, nB), ub2 = key_u(LB, ib + dir, nB);
                     const uint32_t srow = stage_s + 256u * frow;
                     const int swz = (frow & 7) << 2;
+                    const int col0 = fh ? ntot - 1 : 0;
                     for (int st = 0; st < steps; ++st) {
-                        if (work && st < mcount) {
-                            const int ka = ja < 0 ? INT_MAX : sgn * ja;
-                            const int kb = jb < 0 ? INT_MAX : sgn * jb;
-                            const bool ta = ka < kb;
-                            const int col = fh ? ntot - 1 - st : st;
-                            sts_f32(srow + 4u * (uint32_t)(col ^ swz), __int_as_float(ta ? ja : jb));
-                            if (ta) {
-                                ia += dir;
-                                ja = (ia >= 0 && ia < nA) ? (int)lds_u32(LA + 8u * ia) : -1;
-                            } else {
-                                ib += dir;
-                                jb = (ib >= 0 && ib < nB) ? (int)lds_u32(LB + 8u * ib) : -1;
-                            }
-                        }
+                        const bool ta = ua < ub;
+                        const uint32_t u = ta ? ua : ub;
+                        const int col = col0 + dir * st;
+                        sts_u32_if(srow + 4u * (uint32_t)(col ^ swz), fh ? ubase - u : u, work && st < mcount);
+                        // the taken list advances: its next key becomes current, and the key
+                        // after that is read
+                        const int nidx = (ta ? ia : ib) + 2 * dir;
+                        const uint32_t fetched = key_u(ta ? LA : LB, nidx, ta ? nA : nB);
+                        ia += ta ? dir : 0;
+                        ib += ta ? 0 : dir;
+                        ua = ta ? ua2 : ua;
+                        ub = ta ? ub : ub2;
+                        ua2 = ta ? fetched : ua2;
+                        ub2 = ta ? ub2 : fetched;
                     }
                     if (work && fh) {
                         for (int q = ntot; q < K; ++q) sts_f32(srow + 4u * (uint32_t)(q ^ swz), __int_as_float(-1));
