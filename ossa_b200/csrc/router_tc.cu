@@ -417,16 +417,16 @@ __device__ __forceinline__ float canonical_score(const float* __restrict__ qrow,
     else return __fmul_rn(acc, scale);
 }
 
-// count_ge over the first nch 8-entry chunks of x only (nch uniform across the warp).
+// count_ge over every 8-entry chunk of x: slots past a list's end hold -inf and count
+// for no finite v.  (Skipping the chunks past the warp's longest list costs a branch
+// per chunk, which measured slower than counting them.)
 template <int NX>
-__device__ __forceinline__ int count_ge_chunks(const float (&x)[NX], float v, int nch) {
+__device__ __forceinline__ int count_ge_chunks(const float (&x)[NX], float v) {
     int c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
     for (int ch = 0; ch < NX / 8; ++ch) {
-        if (ch < nch) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) c[u] += x[8 * ch + u] >= v ? 1 : 0;
-        }
+        for (int u = 0; u < 8; ++u) c[u] += x[8 * ch + u] >= v ? 1 : 0;
     }
     return ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
 }
@@ -1057,8 +1057,12 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     lo = __uint_as_float(frowbuf[Cfg::kRowStride - 1].x);
                 }
                 const uint32_t own_s = smem_u32(own);
-                // Slots past the warp's longest sub-list hold -inf in every lane and
-                // change no count or extremum below: loops stop after nch 8-slot chunks.
+                // Slots past a sub-list's end hold -inf and change no count or extremum
+                // below (lo, U and W are finite whenever the row has more than K
+                // candidates).  The loads and the longer loops stop after the warp's
+                // longest list (nch 8-slot chunks, a branch per chunk); the bisection
+                // counts and the maximum take every slot, which measured faster than the
+                // branches.
                 const int nch = (int)((__reduce_max_sync(kFull, work ? (unsigned)nown : 0u) + 7u) >> 3);
                 float x[Cfg::kCap];
     #pragma unroll
@@ -1080,15 +1084,13 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 for (int u = 0; u < 8; ++u) hi8[u] = -INFINITY;
     #pragma unroll
                 for (int ch = 0; ch < Cfg::kCap / 8; ++ch) {
-                    if (ch < nch) {
     #pragma unroll
-                        for (int u = 0; u < 8; ++u) hi8[u] = fmaxf(hi8[u], x[8 * ch + u]);
-                    }
+                    for (int u = 0; u < 8; ++u) hi8[u] = fmaxf(hi8[u], x[8 * ch + u]);
                 }
                 float hi = fmaxf(fmaxf(fmaxf(hi8[0], hi8[1]), fmaxf(hi8[2], hi8[3])),
                                  fmaxf(fmaxf(hi8[4], hi8[5]), fmaxf(hi8[6], hi8[7])));
                 hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, 1));
-                int cnt_lo = count_ge_chunks<Cfg::kCap>(x, lo, nch);
+                int cnt_lo = count_ge_chunks<Cfg::kCap>(x, lo);
                 cnt_lo += __shfl_xor_sync(kFull, cnt_lo, 1);
                 if (work && !all_in && cnt_lo < K) {
                     to_fallback = true;  // cannot happen: lb is reached by K candidates
@@ -1103,7 +1105,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 for (int it = 0; it < 40; ++it) {
                     if (__all_sync(kFull, done)) break;
                     const float mid = lo + 0.5f * (hi - lo);
-                    int c = count_ge_chunks<Cfg::kCap>(x, mid, nch);
+                    int c = count_ge_chunks<Cfg::kCap>(x, mid);
                     c += __shfl_xor_sync(kFull, c, 1);
                     if (!done) {
                         if (!(mid > lo && mid < hi)) {
