@@ -147,6 +147,7 @@ constexpr int kWideMaxK = TcCfg<true>::kMaxK;
 constexpr int kNarrowMaxK = TcCfg<false>::kMaxK;
 
 constexpr float kTwoPowM22 = 2.384185791015625e-07f;  // 2^-22
+constexpr int kSkipMinTiles = 40;  // key tiles from which pass 2 tests the half-tile skip
 
 // ---------------------------------------------------------------- prep kernels
 
@@ -224,6 +225,27 @@ __global__ void window_table_kernel(const float* __restrict__ bias, int L, int c
 // Tile diagonals of a call: tile (qb, key tile) uses window nqb - 1 - qb + key tile.
 __host__ __device__ constexpr int window_count(int nqb, int tiles_n) { return nqb + tiles_n - 1; }
 
+// Largest bias term of each (tile diagonal d, column half hf, tile row r): the maximum
+// over the 64 columns c of that half of the window value of (r, c), u_d[c - r + 127]
+// (-inf where every column is causally masked).  Read from the window images: u_d[z]
+// is copy 0 at position z for z < kWinLen, copy 3 at z - 3 above.  Pass 2 of the
+// selector skips a warp's half tile when no row can reach its threshold there.
+__global__ void window_max_kernel(const float* __restrict__ wtab, int ndiag, float* __restrict__ out) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (long long)ndiag * 2 * kTileM) return;
+    const int d = (int)(t / (2 * kTileM));
+    const int rem = (int)(t - (long long)d * 2 * kTileM);
+    const int hf = rem / kTileM, r = rem - hf * kTileM;
+    const float* w = wtab + (size_t)d * (4 * kWinCopy);
+    float mx = -INFINITY;
+    for (int c = 64 * hf; c < 64 * hf + 64; ++c) {
+        const int z = c - r + (kTileN - 1);
+        const float v = z < kWinLen ? __ldg(w + z) : __ldg(w + 3 * kWinCopy + (z - 3));
+        mx = fmaxf(mx, v);
+    }
+    out[t] = mx;
+}
+
 // Power-of-two exponent e with max_abs * 2^e in [2^12, 2^13).
 __device__ __forceinline__ int scale_exponent(float max_abs) {
     int ex = 0;
@@ -287,9 +309,12 @@ __global__ void kconvert_kernel(const float* __restrict__ kp, __half* __restrict
 // Eight threads per query row (kD / 8 values each, coalesced loads and
 // stores): scaled fp16 row, epilogue multiplier and error bound.
 template <int kD>
+// Also rowub[row]: a bound on (approximate score - position bias term) for every key of
+// the row: scale |q'| max|k'| + delta with margins for the roundings.
 __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp, __half* __restrict__ q16,
-                                                    float2* __restrict__ rowinfo, long long rows, int H, int Hkv,
-                                                    int Nq, float scale, const uint32_t* __restrict__ stats,
+                                                    float2* __restrict__ rowinfo, float* __restrict__ rowub,
+                                                    long long rows, int H, int Hkv, int Nq, float scale,
+                                                    const uint32_t* __restrict__ stats,
                                                     const uint32_t* __restrict__ gstats) {
     constexpr int kV4 = kD / 32;  // float4 per thread
     const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
@@ -360,8 +385,11 @@ __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp
                         kTwoPowM22 * (bmax + cross) + 1e-30f;
     if (nonfinite || !isfinite(delta) || !(m >= 1.1754944e-38f) || !isfinite(m)) {
         rowinfo[rr] = make_float2(__int_as_float(0x7fc00000), 0.f);  // NaN multiplier: exact fallback
+        rowub[rr] = INFINITY;
     } else {
         rowinfo[rr] = make_float2(m, delta);
+        // + max|bias| 2^-20: the final rounding of score + bias term, whatever the sign
+        rowub[rr] = (cross * 1.0001f + delta) * 1.0001f + bmax * 9.5367431640625e-07f;
     }
 }
 
@@ -377,6 +405,8 @@ struct TcParams {
     int32_t* fb_list;
     int* status;
     const float* wtab;  // pos_bias window images, one per tile diagonal (kWinBytes each)
+    const float* wmax;  // per diagonal, column half and tile row: the largest window value
+    const float* rowub; // per row: bound on |approximate score - bias term|
     uint2* lists;  // wide: (score, key) sub-lists, TcCfg::kCap per row and column half
     int* counts;   // wide: sub-list lengths, -1 sends the row to the exact fallback
     int L, H, Hkv, N, K, causal, nqb;
@@ -610,7 +640,7 @@ __device__ __forceinline__ void score_half_tile(uint32_t taddr, uint32_t wsrc, u
     if (lane == 0) mbar_arrive_after(tempty, dep);
 }
 
-template <bool kWide, int kD = 64>
+template <bool kWide, int kD = 64, bool kSkip = false>
 __global__ void __launch_bounds__(kThreads, 1)
 router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const TcParams p) {
@@ -952,12 +982,36 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         else
             list_base = smem_u32(sub);
         int cnt = 0;
+        // Exact skip: every approximate score of this row in a half tile is at most
+        // cub + (the half tile's largest bias term for this row); when that is below
+        // theta for every row of the warp, the half tile holds no candidate and is
+        // released without being read.  (Rows without a finite theta append nothing.)
+        // Only query blocks with kSkipMinTiles key tiles or more test it (and only the
+        // kSkip build of the kernel, launched when the keys reach that many tiles): the
+        // K-th best score of a shorter row sits lower among its scores and the test
+        // rarely pays (measured at N = 4096: ~90 cycles per tile, almost no skips).
+        const bool try_skip = kSkip && T >= kSkipMinTiles;  // CTA-uniform
+        const float cub = (i < Nq && try_skip) ? p.rowub[(size_t)bh * Nq + i] : INFINITY;
+        const float* wmax_row = p.wmax + ((size_t)(p.nqb - 1 - qb) * 2 + hf) * kTileM + row;
+        float wm_next = try_skip ? __ldg(wmax_row) : 0.f;
         for (int t = T; t < T2 && ok; ++t) {
             const int j0 = (t - T) * kTileN;
             const int ab = t % kAccBufs;
+            const float wm = wm_next;
+            if (try_skip && t + 1 < T2) wm_next = __ldg(wmax_row + (size_t)(t + 1 - T) * (2 * kTileM));
             if (!tile_prologue(t)) {
                 ok = false;
                 break;
+            }
+            if (try_skip) {
+                float ub = cub + wm;
+                ub += fabsf(ub) * kTwoPowM22;  // the rounding of the sum
+                const bool need = theta == theta && !(ub < theta);
+                if (!__any_sync(kFull, need)) {
+                    tc_fence_before();
+                    if (lane == 0) mbar_arrive(tempty + ab);
+                    continue;
+                }
             }
             const uint32_t taddr = tmem + ((uint32_t)r0 << 16) + (uint32_t)(ab * kTileN + cbase);
             const uint32_t mycopy_s = wrd_s + (uint32_t)(ab * kWinBytes);
@@ -1752,7 +1806,10 @@ size_t tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K, int kD) {
     const int nqb = (Nq + kTileM - 1) / kTileM, tiles_n = (N + kTileN - 1) / kTileN;
     size_t total = al(rq * kD * 2) + al(rk * kD * 2) + al(rq * sizeof(float2)) +
                    al((kStatWords * (size_t)B * Hkv + 2) * 4) + al(rq * 4) +
-                   (nqb > 0 && tiles_n > 0 ? al((size_t)window_count(nqb, tiles_n) * kWinBytes) : 0);
+                   (nqb > 0 && tiles_n > 0 ? al((size_t)window_count(nqb, tiles_n) * kWinBytes) +
+                                                  al((size_t)window_count(nqb, tiles_n) * 2 * kTileM * 4)
+                                            : 0) +
+                   al(rq * 4);
     const bool wide = K > kNarrowMaxK;
     if (wide || kD > 64) {
         const size_t lrows = (size_t)B * H * nqb * kTileM;
@@ -1787,6 +1844,10 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     const int ndiag = window_count(nqb, tiles_n);
     float* wtab = reinterpret_cast<float*>(w);
     w += al((size_t)ndiag * kWinBytes);
+    float* wmax = reinterpret_cast<float*>(w);
+    w += al((size_t)ndiag * 2 * kTileM * 4);
+    float* rowub = reinterpret_cast<float*>(w);
+    w += al(rq * 4);
     const bool wide = a.K > kNarrowMaxK;
     const bool global_lists = wide || kD > 64;
     const int cap = wide ? TcCfg<true, kD>::kCap : TcCfg<false, kD>::kCap;
@@ -1814,8 +1875,9 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
         dim3 g2((unsigned)(((long long)a.N * (kD / 4) + 255) / 256), BG);
         kconvert_kernel<kD><<<g2, 256, 0, stream>>>(a.kp32, k16, a.N, stats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-        qprep_kernel<kD><<<(unsigned)((rq * 8 + 255) / 256), 256, 0, stream>>>(a.qp32, q16, rowinfo, (long long)rq,
-                                                                           a.H, a.Hkv, Nq, a.scale, stats, gstats);
+        qprep_kernel<kD><<<(unsigned)((rq * 8 + 255) / 256), 256, 0, stream>>>(a.qp32, q16, rowinfo, rowub,
+                                                                           (long long)rq, a.H, a.Hkv, Nq, a.scale,
+                                                                           stats, gstats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
         // offset of bias-line index 0: the window of tile (qb, key tile) starts at
         // i - j + L = q0 + kTileN * (qb - key tile) + 127 + L (its first column
@@ -1825,12 +1887,20 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
         window_table_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, stream>>>(kBias ? a.bias : nullptr, a.L,
                                                                              a.causal, o_max, ndiag, wtab);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        if (tiles_n >= kSkipMinTiles) {  // read only by the build with the half-tile skip
+            const long long nm = (long long)ndiag * 2 * kTileM;
+            window_max_kernel<<<(unsigned)((nm + 255) / 256), 256, 0, stream>>>(wtab, ndiag, wmax);
+            if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        }
     }
     CUtensorMap tmA, tmB;
     if (!make_row_map(&tmA, q16, rq, kD) || !make_row_map(&tmB, k16, rk, kD)) return cudaErrorInvalidValue;
     const int smem_bytes = (int)(wide ? TcCfg<true, kD>::kSmemBytes : TcCfg<false, kD>::kSmemBytes);
-    e = cudaFuncSetAttribute(wide ? router_tc_kernel<true, kD> : router_tc_kernel<false, kD>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    // the build with the half-tile skip when some query block reaches kSkipMinTiles key tiles
+    const bool skip = tiles_n >= kSkipMinTiles;
+    auto kern = wide ? (skip ? router_tc_kernel<true, kD, true> : router_tc_kernel<true, kD, false>)
+                     : (skip ? router_tc_kernel<false, kD, true> : router_tc_kernel<false, kD, false>);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     TcParams prm;
     prm.rowinfo = rowinfo;
@@ -1844,6 +1914,8 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.lists = lists;
     prm.counts = counts;
     prm.wtab = wtab;
+    prm.wmax = wmax;
+    prm.rowub = rowub;
     prm.L = a.L;
     prm.H = a.H;
     prm.Hkv = a.Hkv;
@@ -1857,7 +1929,7 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     const long long nblk = (long long)nqb * a.B * a.H;
     const int nsm = device_sm_count();
     if (!global_lists) {
-        router_tc_kernel<false, kD><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
+        kern<<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
         // rows sent to the exact selector (K + 32 candidates per warp: 4 entries per lane)
         exact_rows_kernel<4, kD, kBias><<<2 * nsm, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
@@ -1865,8 +1937,7 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
                                                                      fb_list, a.out);
         return record(cudaGetLastError());
     }
-    if (wide) router_tc_kernel<true, kD><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
-    else router_tc_kernel<false, kD><<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
+    kern<<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     FinalParams fp;
     fp.lists = lists;

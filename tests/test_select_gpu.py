@@ -355,6 +355,30 @@ def test_tensor_core_selector_wide_error_band(K):
     _assert_same(tc.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
 
 
+@pytest.mark.parametrize("K", [64, 128])
+@pytest.mark.parametrize("qscale,bias_scale", [
+    (1.0 / math.sqrt(128), 1.0),  # position bias dominates: many half tiles are skipped
+    (0.6, 1.0),                   # model-like content magnitudes: the content bound is loose
+    (1.0 / math.sqrt(128), 0.0),  # no bias at all: only the content bound
+])
+def test_tensor_core_selector_half_tile_skip(K, qscale, bias_scale):
+    """Query blocks with 40 or more key tiles skip, in pass 2, the half tiles whose
+    score bound (content bound of the row + largest bias term of the half tile) is
+    below the row's candidate threshold for every row of a warp.  N = 6144 puts the
+    last nine query blocks of each head on that path; every row must equal the exact
+    CUDA-core selector, whatever dominates the scores."""
+    B, H, Hkv, N, D, r = 1, 6, 2, 6144, 128, 64
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=60 + K, scale=qscale)
+    q, k = q.bfloat16(), k.bfloat16()
+    wq, wk, pb = _weights(D, r, N, seed=61 + K, bias_scale=bias_scale)
+    tc, ex, fb, status = _run_both(q, k, wq, wk, pb, N, K, True)
+    assert status == 0
+    assert torch.equal(tc, ex), f"{(tc != ex).any(-1).sum().item()} rows differ"
+    rows = np.array([0, 5000, N - 1, 3 * N - 1, B * H * N - 1], dtype=np.int64)
+    ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows, causal=True)
+    _assert_same(tc.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
+
+
 @pytest.mark.parametrize("K,causal", [(128, True), (128, False), (64, True)])
 def test_tensor_core_selector_repeated_calls_identical(K, causal):
     """Hundreds of back-to-back calls on the same inputs return the same indices
