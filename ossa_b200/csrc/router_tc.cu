@@ -1431,8 +1431,95 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
 // --------------------------------------------------- exact fallback for listed rows
 
-// One warp per listed row: canonical scores on CUDA cores, streaming selection
-// with a per-warp candidate list (the same rule as the exact CTA selector).
+// Streaming exact selection by one warp (the same rule as the exact CTA selector):
+// items arrive 32 at a time in ascending key order; an item is admitted when its
+// order key beats theta, the K-th best kept so far, and the buffer wb (32 EPL
+// entries) is cut back to the K best whenever it could overflow.  Ties keep the
+// earlier slot, that is the lower key index.
+template <int EPL>
+__device__ __forceinline__ void stream_chunk(bool valid, uint32_t key, uint32_t j, int K, uint2* wb, int& cnt,
+                                             uint32_t& theta, int lane, unsigned lt) {
+    constexpr int CAP = 32 * EPL;
+    const bool adm = valid && key > theta;
+    const unsigned bal = __ballot_sync(kFull, adm);
+    if (adm) wb[cnt + __popc(bal & lt)] = make_uint2(key, j);
+    cnt += __popc(bal);
+    __syncwarp();
+    if (cnt > CAP - 32) {
+        uint32_t u[EPL], jv[EPL];
+        bool val[EPL], keep[EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+            const int q = lane + 32 * e;
+            val[e] = q < cnt;
+            const uint2 t = val[e] ? wb[q] : make_uint2(0u, 0u);
+            u[e] = t.x;
+            jv[e] = t.y;
+        }
+        uint32_t Tk;
+        warp_topk_mask<EPL>(u, val, K, keep, &Tk);
+        __syncwarp();
+        int outpos = 0;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+            const unsigned kb = __ballot_sync(kFull, keep[e]);
+            if (keep[e]) wb[outpos + __popc(kb & lt)] = make_uint2(u[e], jv[e]);
+            outpos += __popc(kb);
+        }
+        __syncwarp();
+        cnt = outpos;
+        theta = Tk;
+    }
+}
+
+// The K best of the warp's buffer in slot order (ascending key index): emit(pos,
+// entry) for each; returns how many.
+template <int EPL, typename Emit>
+__device__ __forceinline__ int stream_finish(int cnt, int K, const uint2* wb, int lane, unsigned lt, Emit&& emit) {
+    uint32_t u[EPL], jv[EPL];
+    bool val[EPL], keep[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        const int q = lane + 32 * e;
+        val[e] = q < cnt;
+        const uint2 t = val[e] ? wb[q] : make_uint2(0u, 0u);
+        u[e] = t.x;
+        jv[e] = t.y;
+    }
+    if (cnt > K) {
+        warp_topk_mask<EPL>(u, val, K, keep);
+    } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) keep[e] = val[e];
+    }
+    int outpos = 0;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        const unsigned kb = __ballot_sync(kFull, keep[e]);
+        if (keep[e]) emit(outpos + __popc(kb & lt), make_uint2(u[e], jv[e]));
+        outpos += __popc(kb);
+    }
+    return outpos;
+}
+
+// Position, key range and rows of listed row `row` (global query-row index).
+struct FbRow {
+    const float* qrow;
+    const float* kbase;
+    int i, n;
+};
+template <int kD>
+__device__ __forceinline__ FbRow fb_row(const float* qp, const float* kp, long long row, int H, int Hkv, int N,
+                                        int Nq, int q0, int causal) {
+    const long long bh = row / Nq;
+    const int i = q0 + (int)(row - bh * Nq);  // position in the key sequence
+    const int b = (int)(bh / H);
+    const int h = (int)(bh - (long long)b * H);
+    const int g = h / (H / Hkv);
+    return FbRow{qp + row * kD, kp + (size_t)(b * Hkv + g) * N * kD, i, causal ? min(i + 1, N) : N};
+}
+
+// One warp per listed row: canonical scores on CUDA cores, streaming selection.
 template <int EPL, int kD = kR, bool kBias = true>
 __global__ void __launch_bounds__(256)
 exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, const float* __restrict__ bias,
@@ -1448,78 +1535,78 @@ exact_rows_kernel(const float* __restrict__ qp, const float* __restrict__ kp, co
     uint2* wb = sbuf[warp];
     for (int idx = blockIdx.x * 8 + warp; idx < total; idx += gridDim.x * 8) {
         const long long row = fb_list[idx];
-        const long long bh = row / Nq;
-        const int i = q0 + (int)(row - bh * Nq);  // position in the key sequence
-        const int b = (int)(bh / H);
-        const int h = (int)(bh - (long long)b * H);
-        const int g = h / (H / Hkv);
-        const float* qrow = qp + row * kD;
-        const float* kbase = kp + (size_t)(b * Hkv + g) * N * kD;
-        const int n = causal ? min(i + 1, N) : N;
+        const FbRow r = fb_row<kD>(qp, kp, row, H, Hkv, N, Nq, q0, causal);
         uint32_t theta = 0u;
         int cnt = 0;
-        for (int j0 = 0; j0 < n; j0 += 32) {
+        for (int j0 = 0; j0 < r.n; j0 += 32) {
             const int j = j0 + lane;
+            const bool valid = j < r.n;
             uint32_t key = 0u;
-            const bool valid = j < n;
-            if (valid) key = order_key(canonical_score<kD, kBias>(qrow, kbase + (size_t)j * kD, bias, L, i, j, scale));
-            const bool adm = valid && key > theta;
-            const unsigned bal = __ballot_sync(kFull, adm);
-            if (adm) wb[cnt + __popc(bal & lt)] = make_uint2(key, (uint32_t)j);
-            cnt += __popc(bal);
-            __syncwarp();
-            if (cnt > CAP - 32) {
-                uint32_t u[EPL], jv[EPL];
-                bool val[EPL], keep[EPL];
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) {
-                    const int q = lane + 32 * e;
-                    val[e] = q < cnt;
-                    const uint2 t = val[e] ? wb[q] : make_uint2(0u, 0u);
-                    u[e] = t.x;
-                    jv[e] = t.y;
-                }
-                uint32_t Tk;
-                warp_topk_mask<EPL>(u, val, K, keep, &Tk);
-                __syncwarp();
-                int outpos = 0;
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) {
-                    const unsigned kb = __ballot_sync(kFull, keep[e]);
-                    if (keep[e]) wb[outpos + __popc(kb & lt)] = make_uint2(u[e], jv[e]);
-                    outpos += __popc(kb);
-                }
-                __syncwarp();
-                cnt = outpos;
-                theta = Tk;
-            }
-        }
-        uint32_t u[EPL], jv[EPL];
-        bool val[EPL], keep[EPL];
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-            const int q = lane + 32 * e;
-            val[e] = q < cnt;
-            const uint2 t = val[e] ? wb[q] : make_uint2(0u, 0u);
-            u[e] = t.x;
-            jv[e] = t.y;
-        }
-        if (cnt > K) {
-            warp_topk_mask<EPL>(u, val, K, keep);
-        } else {
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) keep[e] = val[e];
+            if (valid) key = order_key(canonical_score<kD, kBias>(r.qrow, r.kbase + (size_t)j * kD, bias, L, r.i, j, scale));
+            stream_chunk<EPL>(valid, key, (uint32_t)j, K, wb, cnt, theta, lane, lt);
         }
         int32_t* orow = out + row * K;
-        int outpos = 0;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-            const unsigned kb = __ballot_sync(kFull, keep[e]);
-            if (keep[e]) orow[outpos + __popc(kb & lt)] = (int32_t)jv[e];
-            outpos += __popc(kb);
-        }
-        for (int q = outpos + lane; q < K; q += 32) orow[q] = -1;
+        const int nout = stream_finish<EPL>(cnt, K, wb, lane, lt, [&](int pos, uint2 e) { orow[pos] = (int32_t)e.y; });
+        for (int q = nout + lane; q < K; q += 32) orow[q] = -1;
         __syncwarp();
+    }
+}
+
+// Long rows: one CTA per listed row.  Each of its 8 warps streams one eighth of the
+// row's keys (in key order) to its own K best, and warp 0 streams the 8 lists, in
+// segment order, to the row's K best.  The K best of the row are among the union of
+// the segments' K best, and that stream is still in ascending key order, so the
+// result is the single-warp one.
+template <int EPL, int kD = kR, bool kBias = true>
+__global__ void __launch_bounds__(256)
+exact_rows_split_kernel(const float* __restrict__ qp, const float* __restrict__ kp, const float* __restrict__ bias,
+                        int L, int H, int Hkv, int N, int Nq, int q0, int K, float scale, int causal,
+                        const int* __restrict__ fb_count, const int32_t* __restrict__ fb_list,
+                        int32_t* __restrict__ out) {
+    constexpr int CAP = 32 * EPL;
+    __shared__ uint2 sbuf[8][CAP];
+    __shared__ uint2 sres[8][CAP];
+    __shared__ int scnt[8];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = lanemask_lt();
+    const int total = *reinterpret_cast<const volatile int*>(fb_count);
+    uint2* wb = sbuf[warp];
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+        const long long row = fb_list[idx];
+        const FbRow r = fb_row<kD>(qp, kp, row, H, Hkv, N, Nq, q0, causal);
+        const int seg = ((r.n + 8 * 32 - 1) / (8 * 32)) * 32;  // a multiple of 32 keys per warp
+        const int s0 = min(r.n, warp * seg), s1 = min(r.n, s0 + seg);
+        uint32_t theta = 0u;
+        int cnt = 0;
+        for (int j0 = s0; j0 < s1; j0 += 32) {
+            const int j = j0 + lane;
+            const bool valid = j < s1;
+            uint32_t key = 0u;
+            if (valid) key = order_key(canonical_score<kD, kBias>(r.qrow, r.kbase + (size_t)j * kD, bias, L, r.i, j, scale));
+            stream_chunk<EPL>(valid, key, (uint32_t)j, K, wb, cnt, theta, lane, lt);
+        }
+        uint2* res = sres[warp];
+        const int nres = stream_finish<EPL>(cnt, K, wb, lane, lt, [&](int pos, uint2 e) { res[pos] = e; });
+        if (lane == 0) scnt[warp] = nres;
+        __syncthreads();
+        if (warp == 0) {
+            theta = 0u;
+            cnt = 0;
+            for (int w = 0; w < 8; ++w) {
+                const int m = scnt[w];
+                for (int p0 = 0; p0 < m; p0 += 32) {
+                    const int p = p0 + lane;
+                    const bool valid = p < m;
+                    const uint2 e = valid ? sres[w][p] : make_uint2(0u, 0u);
+                    stream_chunk<EPL>(valid, e.x, e.y, K, wb, cnt, theta, lane, lt);
+                }
+            }
+            int32_t* orow = out + row * K;
+            const int nout = stream_finish<EPL>(cnt, K, wb, lane, lt, [&](int pos, uint2 e) { orow[pos] = (int32_t)e.y; });
+            for (int q = nout + lane; q < K; q += 32) orow[q] = -1;
+        }
+        __syncthreads();  // sres and scnt are reused by the next row
     }
 }
 
@@ -1819,6 +1906,24 @@ size_t tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K, int kD) {
     return total;
 }
 
+// The exact selector for the rows listed in fb_list (their count is on the device):
+// a warp per row, or for long rows (N >= kSplitRowsMinN) a CTA per row.
+constexpr int kSplitRowsMinN = 8192;
+template <int EPL, int kD, bool kBias>
+cudaError_t launch_exact_rows(const RouterTcArgs& a, int Nq, const int* counters, const int32_t* fb_list,
+                              cudaStream_t stream) {
+    const int nsm = device_sm_count();
+    if (a.N >= kSplitRowsMinN)
+        exact_rows_split_kernel<EPL, kD, kBias><<<nsm, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv,
+                                                                          a.N, Nq, a.q0, a.K, a.scale, a.causal,
+                                                                          counters, fb_list, a.out);
+    else
+        exact_rows_kernel<EPL, kD, kBias><<<2 * nsm, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
+                                                                        Nq, a.q0, a.K, a.scale, a.causal, counters,
+                                                                        fb_list, a.out);
+    return record(cudaGetLastError());
+}
+
 // One selection: prep kernels, the tensor-core kernel, then (lists in global
 // memory) the warp-per-row final choice, then the exact fallback rows.
 // kBias: router scores (pos_bias added); without it the oracle's scaled dot
@@ -1932,10 +2037,7 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
         kern<<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
         // rows sent to the exact selector (K + 32 candidates per warp: 4 entries per lane)
-        exact_rows_kernel<4, kD, kBias><<<2 * nsm, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
-                                                                     Nq, a.q0, a.K, a.scale, a.causal, counters,
-                                                                     fb_list, a.out);
-        return record(cudaGetLastError());
+        return launch_exact_rows<4, kD, kBias>(a, Nq, counters, fb_list, stream);
     }
     kern<<<(unsigned)nblk, kThreads, smem_bytes, stream>>>(tmA, tmB, prm);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
@@ -1964,15 +2066,8 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     else final_select_kernel<TcCfg<false, kD>::kCap, kNarrowMaxK, kD, kBias><<<fblk, 256, 0, stream>>>(fp);
     if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
     // rows sent to the exact selector (K + 32 candidates per warp: 6 entries per lane for K <= 160)
-    if (wide)
-        exact_rows_kernel<6, kD, kBias><<<2 * nsm, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
-                                                                     Nq, a.q0, a.K, a.scale, a.causal, counters,
-                                                                     fb_list, a.out);
-    else
-        exact_rows_kernel<4, kD, kBias><<<2 * nsm, 256, 0, stream>>>(a.qp32, a.kp32, a.bias, a.L, a.H, a.Hkv, a.N,
-                                                                     Nq, a.q0, a.K, a.scale, a.causal, counters,
-                                                                     fb_list, a.out);
-    return record(cudaGetLastError());
+    if (wide) return launch_exact_rows<6, kD, kBias>(a, Nq, counters, fb_list, stream);
+    return launch_exact_rows<4, kD, kBias>(a, Nq, counters, fb_list, stream);
 }
 
 // bf16 rows -> fp32 rows (the oracle's canonical scores read fp32), 8 values per thread.

@@ -289,6 +289,29 @@ def test_tensor_core_selector_ties_go_to_exact_fallback(N, K):
     _assert_same(got, oracle.router_topk(q, k, wq, wk, pb, L, K))
 
 
+@pytest.mark.parametrize("K", [64, 128])
+def test_long_rows_exact_fallback_split(K):
+    """Rows of 8192 keys or more that go to the exact selector are split over the 8
+    warps of a CTA and merged: with every score tied, each row still lists its
+    lowest K key indices (all but the first few hundred rows of a head take that
+    path: shorter rows fit their candidate lists)."""
+    B, H, Hkv, N, D, r = 1, 2, 1, 8192, 64, 64
+    q = torch.randn(B, H, N, D)
+    k = torch.randn(B, Hkv, N, D)
+    wq = torch.zeros(r, D)
+    wk = torch.zeros(r, D)
+    pb = torch.full((2 * N, 1), 0.25)
+    got, fb, status = router_topk_with_status(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
+    assert status == 0 and fb >= B * H * (N - 640)
+    i = torch.arange(N).view(N, 1)
+    j = torch.arange(K).view(1, K)
+    expect = torch.where(j <= i, j, torch.full_like(j, -1)).to(torch.int32)
+    assert torch.equal(got.cpu(), expect.expand(B, H, N, K))
+    rows = np.array([0, K - 1, K, 5000, N - 1, 2 * N - 1], dtype=np.int64)
+    _assert_same(got.reshape(-1, K)[torch.from_numpy(rows).to(DEV)],
+                 oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows, causal=True))
+
+
 @pytest.mark.parametrize("K", [16, 128])
 def test_tensor_core_selector_non_finite_rows(K):
     """A key with an infinite component makes every score of that (b, kv head)
