@@ -10,6 +10,11 @@
   equal the CPU oracle; the gather on sampled rows matches the fp64 attention oracle.
 * The single-layer bf16 workload's gather (B=8, N=4096, K=64): 64 rows of every batch
   element against the fp64 attention oracle.
+* The full model's patched attention (ossa/bench/sparse_forward.py:166-225) at the
+  Qwen2.5-1.5B layer shape (hidden 1536, 12/2 heads, head_dim 128), bf16, N=4096, K=64,
+  inside a Qwen2 decoder layer: the layer's own selected keys equal the CPU oracle on
+  sampled rows and its attention output (the input of o_proj) matches the fp64
+  attention oracle on them.
 
 Indices must be equal; attention outputs within 2e-3 abs/rel (bf16) of the fp64
 oracle, plus half a bf16 ulp of the oracle's value: the output is itself a bf16
@@ -130,4 +135,55 @@ def test_single_layer_gather_64_rows_per_batch_element():
         rows.append((b * H + heads) * N + pos)
     rows = np.concatenate(rows).astype(np.int64)
     assert len(rows) == 64 * B
+    _check_gather_rows(out, q, k, v, idx, rows, H, N)
+
+
+def test_full_model_layer_patched_attention_full_size():
+    """One decoder layer of the full-model workload with random bf16 weights and a
+    random-init router: the patched forward's q, k, v are recomputed from the layer's
+    captured input with the same operations, its selection is checked row by row
+    against the CPU oracle, and its attention output (captured where it enters o_proj)
+    against the fp64 attention oracle over those indices."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from ossa_b200 import ContentRouter, ContentRouterConfig
+    from ossa_b200.bench.sparse_forward import patch_all_layers
+    from ossa_b200.rope import rope_to_heads
+
+    B, N, K, H, Hkv, D = 1, 4096, 64, 12, 2, 128
+    cfg = Qwen2Config(hidden_size=1536, intermediate_size=8960, num_hidden_layers=1, num_attention_heads=H,
+                      num_key_value_heads=Hkv, vocab_size=1024, max_position_embeddings=N, rope_theta=1e6)
+    torch.manual_seed(21)
+    model = Qwen2ForCausalLM(cfg).to(DEV).bfloat16().eval()
+    router = ContentRouter(ContentRouterConfig(head_dim=D, n_heads=H, seq_len=N, proj_dim=64))
+    torch.nn.init.xavier_uniform_(router.q_proj[0].weight)
+    torch.nn.init.xavier_uniform_(router.k_proj[0].weight)
+    router = router.to(DEV)
+    restore = patch_all_layers(model, "router", K, routers={0: router})
+    attn = model.model.layers[0].self_attn
+    seen = {}
+    h1 = attn.register_forward_pre_hook(lambda m, a, kw: seen.update(inp=kw), with_kwargs=True)
+    h2 = attn.o_proj.register_forward_pre_hook(lambda m, a: seen.update(out=a[0].detach().clone()))
+    ids = torch.randint(0, 1024, (B, N), generator=torch.Generator().manual_seed(22)).to(DEV)
+    try:
+        with torch.no_grad():
+            model(input_ids=ids, use_cache=False)
+    finally:
+        h1.remove()
+        h2.remove()
+        restore()
+    hs = seen["inp"]["hidden_states"]
+    cos, sin = seen["inp"]["position_embeddings"]
+    with torch.no_grad():
+        q = rope_to_heads(attn.q_proj(hs), H, cos, sin)
+        k = rope_to_heads(attn.k_proj(hs), Hkv, cos, sin)
+        v = rope_to_heads(attn.v_proj(hs), Hkv)
+        wq, wk, pb = router.q_proj[0].weight, router.k_proj[0].weight, router.pos_bias.weight
+        idx = router_topk(q, k, wq, wk, pb, N, K)
+    out = seen["out"].view(B, N, H, D).transpose(1, 2)
+    rows = _sample_rows(B, H, N, 256, seed=23)
+    ref = oracle.router_topk_rows(q.cpu(), k.cpu(), wq.detach().cpu(), wk.detach().cpu(), pb.detach().cpu(), N, K,
+                                  rows)
+    got = idx.reshape(-1, K)[torch.from_numpy(rows).to(DEV)].cpu().numpy()
+    assert (got == ref).all(), f"{int((got != ref).any(-1).sum())} of {len(rows)} sampled rows differ"
     _check_gather_rows(out, q, k, v, idx, rows, H, N)
