@@ -170,6 +170,16 @@ int check_router(const void* q, const void* k, int dtype, const float* wq, const
     return OSSA_OK;
 }
 
+// Whether the tensor-core selector takes this call with its query operand made
+// straight from the bf16 q rows (router_qtc.cu) and canonical q' only for the rows
+// that need it.  OSSA_QPROJ=canonical projects every row first (the same indices;
+// the switch exists to cross-check the two).
+bool lazy_qproj(const ossa::ProjectArgs& pa, int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
+    const char* env = getenv("OSSA_QPROJ");
+    if (env && env[0] == 'c') return false;
+    return use_tensor_core_select(B, H, Hkv, Nq, Nk, r, K) && ossa::qproj_tc_supported(pa);
+}
+
 int project_both(const void* q, const void* k, int dtype, const float* wq, const float* wk,
                  int B, int H, int Hkv, int Nq, int Nk, int D, int r, void* ws, cudaStream_t stream,
                  float** qp_out, float** kp_out) {
@@ -191,9 +201,11 @@ int project_both(const void* q, const void* k, int dtype, const float* wq, const
 // Selection of Nq query rows from projected q' (B*H*Nq, r) and k' (B*Hkv*Nk, r):
 // the tensor-core selector, the split selector (few rows, many keys) or the
 // CTA selector; `l` is the workspace layout of the call.
+// qproj: the q projection, not launched yet, when the caller leaves q' to the
+// tensor-core selector (lazy_qproj); any other selector projects it first.
 int select_rows(const float* qp, const float* kp, const float* pos_bias, int B, int H, int Hkv, int Nq, int Nk,
                 int r, int seq_len_cfg, int K, int causal, int q_start, int32_t* idx_out, void* workspace,
-                const RouterLayout& l, cudaStream_t s) {
+                const RouterLayout& l, cudaStream_t s, const ossa::ProjectArgs* qproj = nullptr) {
     const float scale = (float)(1.0 / sqrt((double)r));
     if (use_tensor_core_select(B, H, Hkv, Nq, Nk, r, K)) {
         ossa::RouterTcArgs a{qp, kp, pos_bias, seq_len_cfg, B, H, Hkv, Nk, K, causal ? 1 : 0, scale,
@@ -201,7 +213,12 @@ int select_rows(const float* qp, const float* kp, const float* pos_bias, int B, 
                              reinterpret_cast<int*>(workspace)};
         a.Nq = Nq;
         a.q0 = q_start;
+        a.qproj = qproj;
         return cuda_status(ossa::launch_router_tc(a, s), "tensor-core router top-K launch");
+    }
+    if (qproj) {
+        int st = cuda_status(ossa::launch_project(*qproj, s), "q projection launch");
+        if (st) return st;
     }
     const char* env = getenv("OSSA_ROUTER_SELECT");
     if (split_shape(B, H, Nq, Nk) && !(env && env[0] == 'e')) {
@@ -292,11 +309,20 @@ int ossa_router_topk_rows(const void* q, const void* k, int dtype, const float* 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     st = cuda_status(cudaMemsetAsync(workspace, 0, kCountersBytes, s), "workspace counters reset");
     if (st) return st;
-    float *qp = nullptr, *kp = nullptr;
+    const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K);
+    float* qp = reinterpret_cast<float*>(static_cast<char*>(workspace) + l.qp_off);
+    float* kp = reinterpret_cast<float*>(static_cast<char*>(workspace) + l.kp_off);
+    const ossa::ProjectArgs pa{q, wq, qp, (long long)B * H * Nq, D, r, dtype};
+    if (lazy_qproj(pa, B, H, Hkv, Nq, Nk, r, K)) {
+        const ossa::ProjectArgs pk{k, wk, kp, (long long)B * Hkv * Nk, D, r, dtype};
+        if ((st = cuda_status(ossa::launch_project(pk, s), "k projection launch"))) return st;
+        return select_rows(qp, kp, pos_bias, B, H, Hkv, Nq, Nk, r, seq_len_cfg, K, causal, q_start, idx_out,
+                           workspace, l, s, &pa);
+    }
     st = project_both(q, k, dtype, wq, wk, B, H, Hkv, Nq, Nk, D, r, workspace, s, &qp, &kp);
     if (st) return st;
     return select_rows(qp, kp, pos_bias, B, H, Hkv, Nq, Nk, r, seq_len_cfg, K, causal, q_start, idx_out, workspace,
-                       router_layout(B, H, Hkv, Nq, Nk, r, K), s);
+                       l, s);
 }
 
 size_t ossa_router_workspace_size_kp(int B, int H, int Hkv, int Nq, int Nk, int r, int K) {
@@ -332,7 +358,10 @@ int ossa_router_topk_rows_kp(const void* q, int dtype, const float* wq, const fl
     if (st) return st;
     const RouterLayout l = router_layout(B, H, Hkv, Nq, Nk, r, K, false);
     float* qp = reinterpret_cast<float*>(static_cast<char*>(workspace) + l.qp_off);
-    ossa::ProjectArgs pa{q, wq, qp, (long long)B * H * Nq, D, r, dtype};
+    const ossa::ProjectArgs pa{q, wq, qp, (long long)B * H * Nq, D, r, dtype};
+    if (lazy_qproj(pa, B, H, Hkv, Nq, Nk, r, K))
+        return select_rows(qp, kp, pos_bias, B, H, Hkv, Nq, Nk, r, seq_len_cfg, K, causal, q_start, idx_out,
+                           workspace, l, s, &pa);
     st = cuda_status(ossa::launch_project(pa, s), "q projection launch");
     if (st) return st;
     return select_rows(qp, kp, pos_bias, B, H, Hkv, Nq, Nk, r, seq_len_cfg, K, causal, q_start, idx_out, workspace,
@@ -357,9 +386,14 @@ int ossa_router_topk_sorted(const void* q, const void* k, int dtype, const float
     if ((long long)B * H * N == 0) return OSSA_OK;
     if (!ossa::sort_rows_supported(r, K))
         return fail(OSSA_ERR_UNSUPPORTED, "score-ordered rows support K <= 256 (got K=%d)", K);
-    // the selection left the canonical projections in the workspace
+    // the selection left the canonical k' in the workspace, and q' too unless the
+    // tensor-core selector made only the rows it needed: then q' is projected here
     const RouterLayout l = router_layout(B, H, Hkv, N, N, r, K);
     char* base = static_cast<char*>(workspace);
+    const ossa::ProjectArgs pa{q, wq, reinterpret_cast<float*>(base + l.qp_off), (long long)B * H * N, D, r, dtype};
+    if (lazy_qproj(pa, B, H, Hkv, N, N, r, K) &&
+        (st = cuda_status(ossa::launch_project(pa, static_cast<cudaStream_t>(stream)), "q projection launch")))
+        return st;
     ossa::SortRowsArgs a{reinterpret_cast<const float*>(base + l.qp_off),
                          reinterpret_cast<const float*>(base + l.kp_off),
                          pos_bias, seq_len_cfg, H, Hkv, N, r, K, (float)(1.0 / sqrt((double)r)),

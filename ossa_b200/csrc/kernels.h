@@ -44,6 +44,26 @@ struct ProjectArgs {
 };
 cudaError_t launch_project(const ProjectArgs& a, cudaStream_t stream);
 
+// The tensor-core selector's query operand straight from bf16 q rows (D = 128,
+// r = 64; router_qtc.cu): q16 (fp16, scaled per row), rowinfo (multiplier, error
+// bound covering the canonical q') and rowub, from the per-(b, kv head) key
+// statistics.  The canonical q' itself is not written.
+struct QPrepArgs {
+    const void* x;   // bf16 q rows [rows][128]
+    const float* w;  // Wq [64][128]
+    float* wt;       // written: Wq transposed, [128][64] (read by the selector's on-demand q' rows)
+    long long rows;
+    void* q16;
+    float2* rowinfo;
+    float* rowub;
+    const uint32_t* stats;
+    const uint32_t* gstats;
+    int H, Hkv, Nq;
+    float scale;
+};
+bool qproj_tc_supported(const ProjectArgs& a);
+cudaError_t launch_qproj_tc(const QPrepArgs& a, cudaStream_t stream);
+
 // Exact fp32 causal/full top-K over score(i,j) = dot(qrows_i, krows_j) * scale
 // (+ pos_bias[clamp(i - j + L, 0, 2L - 1)] when bias != nullptr).
 // qrows: (B*H*N, R), krows: (B*Hkv*N, R), both `dtype`.
@@ -169,6 +189,10 @@ struct RouterTcArgs {
     int* counters;
     int Nq = 0;  // query rows per (b, h); 0 means N (queries are the keys' positions)
     int q0 = 0;  // position of query row 0 in the key sequence
+    // When set (qproj_tc_supported), q' is not projected up front: the selector's
+    // query operand comes from launch_qproj_tc and the canonical q' rows are computed
+    // into qp32 (qproj->out) only for the rows that need them.
+    const ProjectArgs* qproj = nullptr;
 };
 bool router_tc_supported(int r, int K);
 size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K);

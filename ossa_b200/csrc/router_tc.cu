@@ -62,6 +62,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "router_prep.cuh"
 #include "select_warp.cuh"
 #include "sm100.cuh"
 
@@ -135,7 +136,7 @@ struct TcCfg {
     static constexpr size_t kBufBytes =
         kGlobal ? (kOffLb - kOffBuf) + (size_t)kTileM * 4 : (size_t)kTileM * kRowStride * sizeof(uint2);
     static constexpr size_t kOffBar = (kOffBuf + kBufBytes + 7) / 8 * 8;
-    static constexpr int kNumBars = 2 * kStages + 1 + 2 * kAccBufs + 1;
+    static constexpr int kNumBars = 2 * kStages + 1 + 2 * kAccBufs + 2;
     static constexpr size_t kOffSlot = kOffBar + (size_t)kNumBars * 8;
     static constexpr size_t kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
     static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -146,15 +147,11 @@ struct TcCfg {
 constexpr int kWideMaxK = TcCfg<true>::kMaxK;
 constexpr int kNarrowMaxK = TcCfg<false>::kMaxK;
 
-constexpr float kTwoPowM22 = 2.384185791015625e-07f;  // 2^-22
 constexpr int kSkipMinTiles = 40;  // key tiles from which pass 2 tests the half-tile skip
 
 // ---------------------------------------------------------------- prep kernels
 
-// Per (b, kv head) statistics, kStatWords words each: [0] max |k'| bits,
-// [1] max_j |k'_j|_2 bits, [2] non-finite flag, [3] max_j |fp16(k'_j) - k'_j|_2 bits
-// (the largest conversion error of a key row, written by kconvert_kernel).
-constexpr int kStatWords = 4;
+// Per (b, kv head) statistics: the kStatWords words described in router_prep.cuh.
 template <int kD>
 __global__ void kstats_kernel(const float* __restrict__ kp, int N, uint32_t* __restrict__ stats) {
     const int bg = blockIdx.y;
@@ -245,21 +242,6 @@ __global__ void window_max_kernel(const float* __restrict__ wtab, int ndiag, flo
     }
     out[t] = mx;
 }
-
-// Power-of-two exponent e with max_abs * 2^e in [2^12, 2^13).
-__device__ __forceinline__ int scale_exponent(float max_abs) {
-    int ex = 0;
-    frexpf(max_abs, &ex);
-    return max_abs > 0.f ? 13 - ex : 0;
-}
-
-// x * 2^e for the scalings above, with f = 2^e from pow2f: a multiply by the
-// exact power of two when 2^e and 2^-e are normal floats (then the product equals
-// ldexpf(x, e)), ldexpf otherwise.
-__device__ __forceinline__ float pow2f(int e) {
-    return (e > -126 && e < 127) ? __int_as_float((e + 127) << 23) : 0.f;
-}
-__device__ __forceinline__ float scale2(float x, int e, float f) { return f != 0.f ? x * f : ldexpf(x, e); }
 
 // fp16 copy of k' scaled by the (b, kv head) power of two, one float4 per thread
 // (kD / 4 threads per key row), and the norm of each row's conversion error,
@@ -367,30 +349,7 @@ __global__ void __launch_bounds__(256) qprep_kernel(const float* __restrict__ qp
 #pragma unroll
     for (int o2 = 1; o2 < 8; o2 <<= 1) dd += __shfl_xor_sync(0xffu << (threadIdx.x & 24), dd, o2);
     if (part != 0) return;
-    const int ek = scale_exponent(__uint_as_float(stats[kStatWords * bg + 0]));
-    const float kmax = __uint_as_float(stats[kStatWords * bg + 1]);
-    const float dkmax = __uint_as_float(stats[kStatWords * bg + 3]);
-    const float bmax = __uint_as_float(gstats[0]);
-    const bool nonfinite = bad != 0u || stats[kStatWords * bg + 2] != 0u || gstats[1] != 0u;
-    const float m = ldexpf(scale, -(eq + ek));
-    const float qn = sqrtf(ss) * 1.0001f;
-    const float dq = sqrtf(dd) * 1.0001f;
-    const float cross = scale * qn * kmax;
-    // |approx - canonical| <= scale * |q'.dk + dq.k' + dq.dk| (fp16 conversion,
-    // Cauchy-Schwarz with the measured errors) + scale * 2^-13 |q'| max|k'| (fp32
-    // accumulation in the tensor core and in the canonical chain: 64 terms at a few
-    // ulp each, twice that for 128) + 2^-22 (max|bias| + cross) (the final roundings)
-    constexpr float kAcc = 1.220703125e-4f * (kD / 64);
-    const float delta = scale * (qn * dkmax + dq * kmax + dq * dkmax) * 1.0001f + scale * kAcc * qn * kmax +
-                        kTwoPowM22 * (bmax + cross) + 1e-30f;
-    if (nonfinite || !isfinite(delta) || !(m >= 1.1754944e-38f) || !isfinite(m)) {
-        rowinfo[rr] = make_float2(__int_as_float(0x7fc00000), 0.f);  // NaN multiplier: exact fallback
-        rowub[rr] = INFINITY;
-    } else {
-        rowinfo[rr] = make_float2(m, delta);
-        // + max|bias| 2^-20: the final rounding of score + bias term, whatever the sign
-        rowub[rr] = (cross * 1.0001f + delta) * 1.0001f + bmax * 9.5367431640625e-07f;
-    }
+    row_finish<kD>(rr, eq, ss, dd, bad != 0u, bg, scale, stats, gstats, rowinfo, rowub);
 }
 
 // ------------------------------------------------------------ selection kernel
@@ -407,6 +366,10 @@ struct TcParams {
     const float* wtab;  // pos_bias window images, one per tile diagonal (kWinBytes each)
     const float* wmax;  // per diagonal, column half and tile row: the largest window value
     const float* rowub; // per row: bound on |approximate score - bias term|
+    // non-null: qp32 holds only the rows computed on demand (warp_canon_q) from the
+    // bf16 query rows q_in and the transposed Wq
+    const __nv_bfloat16* q_in;
+    const float* wt;
     uint2* lists;  // wide: (score, key) sub-lists, TcCfg::kCap per row and column half
     int* counts;   // wide: sub-list lengths, -1 sends the row to the exact fallback
     int L, H, Hkv, N, K, causal, nqb;
@@ -417,8 +380,9 @@ struct TcParams {
 // Canonical fp32 score of (query row qrow, key row krow): the fmaf chain over
 // d = 0..kD-1 in order, times scale, plus (router) the position-bias term at
 // offset i - j.  Key-row loads go out 64 values at a time (one memory round
-// trip for kD = 64; the query row is reused and cached).
-template <int kD = kR, bool kBias = true>
+// trip for kD = 64; the query row is reused and cached).  kQcg: the query row may
+// have been written by this kernel (warp_canon_q), so it is read through L2.
+template <int kD = kR, bool kBias = true, bool kQcg = false>
 __device__ __forceinline__ float canonical_score(const float* __restrict__ qrow, const float* __restrict__ krow,
                                                  const float* __restrict__ bias, int L, int i, int j,
                                                  float scale) {
@@ -436,7 +400,8 @@ __device__ __forceinline__ float canonical_score(const float* __restrict__ qrow,
         for (int u = 0; u < 16; ++u) bk[u] = __ldg(reinterpret_cast<const float4*>(krow) + c0 + u);
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(qrow) + c0 + u);
+            const float4 a = kQcg ? __ldcg(reinterpret_cast<const float4*>(qrow) + c0 + u)
+                                  : __ldg(reinterpret_cast<const float4*>(qrow) + c0 + u);
             acc = fmaf(a.x, bk[u].x, acc);
             acc = fmaf(a.y, bk[u].y, acc);
             acc = fmaf(a.z, bk[u].z, acc);
@@ -666,6 +631,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint64_t* tfull = afull + 1;
     uint64_t* tempty = tfull + kAccBufs;
     uint64_t* mdone = tempty + kAccBufs;
+    uint64_t* wtbar = mdone + 1;  // narrow, on-demand q' rows: transposed Wq in shared memory
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffSlot);
 
     const int N = p.N, H = p.H, Hkv = p.Hkv, Nq = p.Nq;
@@ -704,6 +670,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             mbar_init(tempty + s, kEpiWarps);
         }
         mbar_init(mdone, 1);
+        mbar_init(wtbar, 1);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -1090,6 +1057,19 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             // the bound), 16 bits per column half.
             reinterpret_cast<int16_t*>(&rowbuf[Cfg::kRowStride - 1].y)[hf] = (int16_t)(fb ? -1 : cnt);
             named_bar_sync(pair_bar, 64);
+            if (p.q_in != nullptr) {
+                // Wq transposed into shared memory for the on-demand canonical q' rows:
+                // d = 0..63 into the query tile (idle: every MMA has completed) and
+                // d = 64..127 into the window buffers (idle once all eight epilogue
+                // warps are past pass 2), two bulk copies completing on wtbar
+                named_bar_sync(5, 32 * kEpiWarps);
+                if (ew == 0 && lane == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive_expect_tx(wtbar, 2 * 16384);
+                    bulk_load(sA, p.wt, 16384, wtbar);
+                    bulk_load(win, p.wt + 4096, 16384, wtbar);
+                }
+            }
             {
                 const int frow = r0 + 16 * hf + (lane >> 1);
                 const int fh = lane & 1;
@@ -1234,6 +1214,27 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 const int oth_nb = __shfl_xor_sync(kFull, own_nb, 1);
                 const int need = K - n_in;
                 const bool rescore = work && !all_in && own_nb + oth_nb != need;
+                if (p.q_in != nullptr) {
+                    // canonical q' of the rows that rescore or go to the exact selector,
+                    // one row at a time by the whole warp
+                    unsigned pend = __ballot_sync(kFull, (rescore || to_fallback) && fh == 0);
+                    if (pend != 0u && !__all_sync(kFull, mbar_wait(wtbar, 0u))) {
+                        if (lane == 0) atomicOr(p.status, 16);
+                        pend = 0u;
+                    }
+                    while (pend != 0u) {  // two rows per pass over the weights
+                        const int s0 = __ffs(pend) - 1;
+                        pend &= pend - 1u;
+                        const int s1 = pend != 0u ? __ffs(pend) - 1 : s0;
+                        pend &= pend - 1u;
+                        const unsigned long long r0 = __shfl_sync(kFull, (unsigned long long)orow_id, s0);
+                        const unsigned long long r1 = __shfl_sync(kFull, (unsigned long long)orow_id, s1);
+                        float* qp = const_cast<float*>(p.qp32);
+                        warp_canon_q2_smem(p.q_in + r0 * 128, p.q_in + r1 * 128, reinterpret_cast<const float*>(sA),
+                                           win, qp + r0 * kR, s1 != s0 ? qp + r1 * kR : nullptr, lane);
+                    }
+                    __syncwarp();
+                }
 
                 // 2. canonical rescoring of the boundary band, in place: a band entry's
                 // score word becomes the order key of its canonical score; bm marks the
@@ -1263,8 +1264,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         for (uint32_t m = bm[w]; m != 0u; m &= m - 1u) {
                             const int q = 32 * w + __ffs(m) - 1;
                             const int jj = (int)lds_u32(own_s + 8u * q + 4u);
-                            const float ex = canonical_score(qrow, kbase + (size_t)jj * kR, p.bias, p.L, p.q0 + fi,
-                                                             jj, p.scale);
+                            const float ex = canonical_score<kR, true, true>(qrow, kbase + (size_t)jj * kR, p.bias,
+                                                                             p.L, p.q0 + fi, jj, p.scale);
                             sts_f32(own_s + 8u * q, __uint_as_float(order_key(ex)));
                         }
                     }
@@ -1418,6 +1419,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     p.fb_list[pos] = (int32_t)orow_id;
                 }
             }
+            // the bulk copies of Wq land before the CTA retires
+            if (p.q_in != nullptr && ew == 0 && lane == 0 && !mbar_wait(wtbar, 0u)) atomicOr(p.status, 16);
         }
     }
 
@@ -1619,6 +1622,8 @@ struct FinalParams {
     const float* bias;
     const float* qp32;
     const float* kp32;
+    const __nv_bfloat16* q_in;  // as in TcParams
+    const float* wt;
     int32_t* out;
     int* fb_count;
     int32_t* fb_list;
@@ -1646,10 +1651,16 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
     static_assert(kEPL * 32 == 2 * kCap && kMaxBand <= 32, "list and band layout");
     __shared__ int skept[8][2][kMaxOut];
     __shared__ int sband[8][32];
+    __shared__ __align__(16) float swt[128 * 64];  // on-demand q' rows: Wq transposed, [d][c]
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const unsigned lt = lanemask_lt();
     const int K = p.K;
+    if (p.q_in != nullptr) {
+        for (int e = threadIdx.x; e < 128 * 64 / 4; e += blockDim.x)
+            reinterpret_cast<float4*>(swt)[e] = __ldg(reinterpret_cast<const float4*>(p.wt) + e);
+        __syncthreads();
+    }
     for (long long row = (long long)blockIdx.x * 8 + warp; row < p.rows; row += (long long)gridDim.x * 8) {
         const int ca = p.counts[2 * row], cb = p.counts[2 * row + 1];
         bool fallback = ca < 0 || cb < 0 || ca > kCap || cb > kCap;
@@ -1721,11 +1732,15 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                     const int g = (int)(bh - (long long)b * p.H) / (p.H / p.Hkv);
                     const float* qrow = p.qp32 + (size_t)row * kD;
                     const float* kbase = p.kp32 + (size_t)(b * p.Hkv + g) * p.N * kD;
+                    if (p.q_in != nullptr) {
+                        warp_canon_q2_smem(p.q_in + row * 128, p.q_in + row * 128, swt, swt + 4096, const_cast<float*>(qrow), nullptr, lane);
+                        __syncwarp();
+                    }
                     uint32_t ek[kEPL];
 #pragma unroll
                     for (int e = 0; e < kEPL; ++e)
-                        ek[e] = val[e] ? order_key(canonical_score<kD, kBias>(qrow, kbase + (size_t)jv[e] * kD, p.bias,
-                                                                              p.L, ipos, (int)jv[e], p.scale))
+                        ek[e] = val[e] ? order_key(canonical_score<kD, kBias, true>(
+                                             qrow, kbase + (size_t)jv[e] * kD, p.bias, p.L, ipos, (int)jv[e], p.scale))
                                        : 0u;
                     uint32_t Te;
                     int ties;
@@ -1761,12 +1776,15 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                         if (band[e]) sband[warp][slot[e]] = (int)jv[e];
                         base += __popc(bal);
                     }
+                    if (p.q_in != nullptr)
+                        warp_canon_q2_smem(p.q_in + row * 128, p.q_in + row * 128, swt, swt + 4096,
+                                           const_cast<float*>(p.qp32) + row * kD, nullptr, lane);
                     __syncwarp();
                     uint32_t ek = 0u;
                     int jj = INT_MAX;
                     if (lane < (int)nb) {
                         jj = sband[warp][lane];
-                        const float ex = canonical_score<kD, kBias>(
+                        const float ex = canonical_score<kD, kBias, true>(
                             p.qp32 + (size_t)row * kD, p.kp32 + ((size_t)(b * p.Hkv + g) * p.N + jj) * kD, p.bias,
                             p.L, ipos, jj, p.scale);
                         ek = order_key(ex);
@@ -1838,6 +1856,9 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                 __syncwarp();  // skept is rewritten for the next row
             }
         }
+        if (fallback && p.q_in != nullptr)
+            warp_canon_q2_smem(p.q_in + row * 128, p.q_in + row * 128, swt, swt + 4096,
+                               const_cast<float*>(p.qp32) + row * kD, nullptr, lane);
         if (fallback && lane == 0) {
             const int pos = atomicAdd(p.fb_count, 1);
             p.fb_list[pos] = (int32_t)row;
@@ -1896,7 +1917,7 @@ size_t tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K, int kD) {
                    (nqb > 0 && tiles_n > 0 ? al((size_t)window_count(nqb, tiles_n) * kWinBytes) +
                                                   al((size_t)window_count(nqb, tiles_n) * 2 * kTileM * 4)
                                             : 0) +
-                   al(rq * 4);
+                   al(rq * 4) + al(64 * 128 * 4);
     const bool wide = K > kNarrowMaxK;
     if (wide || kD > 64) {
         const size_t lrows = (size_t)B * H * nqb * kTileM;
@@ -1953,6 +1974,8 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     w += al((size_t)ndiag * 2 * kTileM * 4);
     float* rowub = reinterpret_cast<float*>(w);
     w += al(rq * 4);
+    float* wt = reinterpret_cast<float*>(w);  // Wq transposed (on-demand canonical q' rows)
+    w += al(64 * 128 * 4);
     const bool wide = a.K > kNarrowMaxK;
     const bool global_lists = wide || kD > 64;
     const int cap = wide ? TcCfg<true, kD>::kCap : TcCfg<false, kD>::kCap;
@@ -1980,10 +2003,15 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
         dim3 g2((unsigned)(((long long)a.N * (kD / 4) + 255) / 256), BG);
         kconvert_kernel<kD><<<g2, 256, 0, stream>>>(a.kp32, k16, a.N, stats);
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
-        qprep_kernel<kD><<<(unsigned)((rq * 8 + 255) / 256), 256, 0, stream>>>(a.qp32, q16, rowinfo, rowub,
-                                                                           (long long)rq, a.H, a.Hkv, Nq, a.scale,
-                                                                           stats, gstats);
-        if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        if (a.qproj != nullptr) {
+            const QPrepArgs qa{a.qproj->x, a.qproj->w, wt, (long long)rq, q16, rowinfo, rowub, stats, gstats,
+                               a.H, a.Hkv, Nq, a.scale};
+            if ((e = launch_qproj_tc(qa, stream)) != cudaSuccess) return e;
+        } else {
+            qprep_kernel<kD><<<(unsigned)((rq * 8 + 255) / 256), 256, 0, stream>>>(
+                a.qp32, q16, rowinfo, rowub, (long long)rq, a.H, a.Hkv, Nq, a.scale, stats, gstats);
+            if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
+        }
         // offset of bias-line index 0: the window of tile (qb, key tile) starts at
         // i - j + L = q0 + kTileN * (qb - key tile) + 127 + L (its first column
         // against its last row)
@@ -2011,6 +2039,8 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     prm.rowinfo = rowinfo;
     prm.bias = a.bias;
     prm.qp32 = a.qp32;
+    prm.q_in = a.qproj ? static_cast<const __nv_bfloat16*>(a.qproj->x) : nullptr;
+    prm.wt = a.qproj ? wt : nullptr;
     prm.kp32 = a.kp32;
     prm.out = a.out;
     prm.fb_count = counters;
@@ -2047,6 +2077,8 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
     fp.rowinfo = rowinfo;
     fp.bias = a.bias;
     fp.qp32 = a.qp32;
+    fp.q_in = prm.q_in;
+    fp.wt = prm.wt;
     fp.kp32 = a.kp32;
     fp.out = a.out;
     fp.fb_count = counters;
@@ -2095,7 +2127,11 @@ size_t router_tc_workspace_bytes(int B, int H, int Hkv, int Nq, int N, int K) {
     return tc_workspace_bytes(B, H, Hkv, Nq, N, K, kR);
 }
 
-cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) { return launch_tc<kR, true>(a, stream); }
+cudaError_t launch_router_tc(const RouterTcArgs& a, cudaStream_t stream) {
+    if (a.qproj != nullptr && (a.qproj->out != a.qp32 || a.qproj->R != kR || !qproj_tc_supported(*a.qproj)))
+        return cudaErrorInvalidValue;
+    return launch_tc<kR, true>(a, stream);
+}
 
 bool oracle_tc_supported(int D, int K) { return D == kOracleD && K >= 1 && K <= kWideMaxK; }
 

@@ -419,3 +419,71 @@ def test_tensor_core_selector_repeated_calls_identical(K, causal):
     for _ in range(400):
         bad += int(not torch.equal(router_topk(*args, causal=causal), ex))
     assert bad == 0, f"{bad} of 400 calls differ"
+
+
+def _both_projections(q, k, wq, wk, pb, L, K, causal=True):
+    """router_topk with the query operand made from q on the tensor cores (canonical
+    q' rows computed only where the selection needs them), and with every q' row
+    projected canonically first (OSSA_QPROJ=canonical)."""
+    import os
+    args = (q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), L, K)
+    lazy, fb, status = router_topk_with_status(*args, causal=causal)
+    os.environ["OSSA_QPROJ"] = "canonical"
+    try:
+        canon = router_topk(*args, causal=causal)
+    finally:
+        del os.environ["OSSA_QPROJ"]
+    return lazy, canon, fb, status
+
+
+@pytest.mark.parametrize("case", ["ties", "nonfinite_query", "large_rows", "rows_block"])
+@pytest.mark.parametrize("K", [64, 128])
+def test_tensor_core_query_operand_on_demand_rows(case, K):
+    """bf16 q, head_dim 128, proj_dim 64: the selector's fp16 query operand comes
+    from a tensor-core projection of q, and the canonical fp32 q' (fmaf chain) is
+    computed only for the rows that rescore their boundary band or go to the exact
+    selector.  Rows on both of those paths give the indices of the canonical
+    projection and of the oracle: all-tied scores (every row to the exact
+    selector), a query row with an infinite entry, rows of large magnitude (wide
+    error bands), and a block of query rows at an offset."""
+    B, H, Hkv, N, D, r = 1, 12, 2, 768, 128, 64
+    q, k, _ = cases.qkv(B, H, Hkv, N, D, seed=90 + K, scale=1.0 / math.sqrt(D))
+    wq, wk, pb = _weights(D, r, N, seed=91 + K)
+    q0 = 0
+    if case == "ties":
+        wk = torch.zeros_like(wk)
+        pb = torch.full_like(pb, 0.25)
+    elif case == "nonfinite_query":
+        q[0, 3, 400, 17] = float("inf")
+        q[0, 7, 10, 0] = float("-inf")
+    elif case == "large_rows":
+        q[0, :4] *= 40.0
+    q, k = q.bfloat16(), k.bfloat16()
+    if case == "rows_block":
+        q0 = 256
+        qb = q[:, :, q0:q0 + 384].contiguous()
+        args = (qb.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), pb.to(DEV), N, K)
+        lazy = router_topk(*args, q_start=q0)
+        import os
+        os.environ["OSSA_QPROJ"] = "canonical"
+        try:
+            canon = router_topk(*args, q_start=q0)
+        finally:
+            del os.environ["OSSA_QPROJ"]
+        assert torch.equal(lazy, canon), f"{(lazy != canon).any(-1).sum().item()} rows differ"
+        rows = np.array([0, 1, 200, 383, 384, 3 * 384 - 1, 12 * 384 - 1], dtype=np.int64)
+        full = oracle.router_topk_rows(q, k, wq, wk, pb, N, K,
+                                       (rows // 384) * N + q0 + rows % 384, causal=True)
+        _assert_same(lazy.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], full)
+        return
+    lazy, canon, fb, status = _both_projections(q, k, wq, wk, pb, N, K)
+    assert status == 0
+    assert torch.equal(lazy, canon), f"{(lazy != canon).any(-1).sum().item()} rows differ"
+    if case == "ties":
+        assert fb > 0
+        _assert_same(lazy, oracle.router_topk(q, k, wq, wk, pb, N, K))
+    else:
+        rows = np.concatenate([np.arange(0, B * H * N, 97),
+                               np.array([3 * N + 400, 7 * N + 10, 7 * N + 11, N - 1])]).astype(np.int64)
+        ref = oracle.router_topk_rows(q, k, wq, wk, pb, N, K, rows, causal=True)
+        _assert_same(lazy.reshape(-1, K)[torch.from_numpy(rows).to(DEV)], ref)
