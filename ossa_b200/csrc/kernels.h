@@ -1,6 +1,7 @@
 // Internal launcher interface between the C ABI (capi.cu) and the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -17,6 +18,12 @@ void set_error_message(const char* msg);
 
 // Streaming multiprocessors of the current device (queried once per device).
 int device_sm_count();
+
+// Tensor map of a (rows x cols) row-major matrix of 16-bit values (bf16, else fp16)
+// in box_rows x 64-column boxes with the 128-byte swizzle (a row of cols > 64 takes
+// cols / 64 boxes).
+bool make_row_map_16(CUtensorMap* map, const void* base, bool bf16, unsigned long long rows, int cols,
+                     int box_rows);
 
 struct GatherArgs {
     const void* q;
@@ -58,6 +65,7 @@ struct QPrepArgs {
     float* rowub;
     const uint32_t* stats;
     const uint32_t* gstats;
+    int* status;  // bit 32: a bounded wait of the kernel expired
     int H, Hkv, Nq;
     float scale;
 };

@@ -2005,7 +2005,7 @@ cudaError_t launch_tc(const RouterTcArgs& a, cudaStream_t stream) {
         if ((e = record(cudaGetLastError())) != cudaSuccess) return e;
         if (a.qproj != nullptr) {
             const QPrepArgs qa{a.qproj->x, a.qproj->w, wt, (long long)rq, q16, rowinfo, rowub, stats, gstats,
-                               a.H, a.Hkv, Nq, a.scale};
+                               counters + 1, a.H, a.Hkv, Nq, a.scale};
             if ((e = launch_qproj_tc(qa, stream)) != cudaSuccess) return e;
         } else {
             qprep_kernel<kD><<<(unsigned)((rq * 8 + 255) / 256), 256, 0, stream>>>(
@@ -2120,6 +2120,20 @@ __global__ void widen_bf16_kernel(const __nv_bfloat16* __restrict__ in, float* _
 }
 
 }  // namespace
+
+bool make_row_map_16(CUtensorMap* map, const void* base, bool bf16, unsigned long long rows, int cols,
+                     int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 bool router_tc_supported(int r, int K) { return r == kR && K >= 1 && K <= kWideMaxK; }
 
