@@ -15,10 +15,10 @@
 //    with eps >= |q'_tc - q'| from |x| |W|_F (Cauchy-Schwarz per output).
 //
 // One persistent CTA per SM walks 128-row tiles: warp 0 streams x tiles (two
-// 128 x 64 boxes, 128-byte swizzle) through a 4-stage ring with TMA, warp 1 issues
-// 2 x 8 MMAs of 128 x 64 x 16 per tile (W hi, then W lo) into one of four 64-column
-// TMEM accumulators, and eight epilogue warps give every row to one thread: warps
-// 2..5 take the even tiles, warps 6..9 the odd ones, each warp the 32 rows of its
+// 128 x 64 boxes, 128-byte swizzle) through a 6-stage ring with TMA, warp 1 issues
+// 2 x 8 MMAs of 128 x 64 x 16 per tile (W hi, then W lo) into one of eight 64-column
+// TMEM accumulators, and four groups of four epilogue warps give every row to one
+// thread: group g takes the tiles t with t % 4 == g, each warp the 32 rows of its
 // TMEM lane quadrant.  A thread reads |x|^2 from the staged tile and its row's 64
 // outputs with tcgen05.ld in 16-column chunks, twice (the row maximum sets the fp16
 // scaling before any value is converted; a compact loop keeps the code in the
@@ -43,12 +43,13 @@ namespace {
 using namespace sm100;
 
 constexpr int kQtRows = 128;                 // rows per tile (MMA M)
-constexpr int kQtStages = 4;                 // x tile ring
+constexpr int kQtStages = 6;                 // x tile ring
 constexpr int kQtTileB = kQtRows * 128 * 2;  // one x tile: two 128 x 64 boxes (32 KB)
 constexpr int kQtWB = 64 * 128 * 2;          // one W part: two 64 x 64 sub-tiles (16 KB)
-constexpr int kQtEpiWarps = 8;                       // 4 per accumulator
-constexpr int kQtThreads = 32 * (2 + kQtEpiWarps);  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr int kQtAcc = 4;                    // 64-column TMEM accumulators
+constexpr int kQtGroups = 4;                         // epilogue groups of 4 warps, one tile each in turn
+constexpr int kQtEpiWarps = 4 * kQtGroups;
+constexpr int kQtThreads = 32 * (2 + kQtEpiWarps);  // warp 0 TMA, warp 1 MMA, then the epilogue warps
+constexpr int kQtAcc = 2 * kQtGroups;        // 64-column TMEM accumulators
 constexpr uint32_t kQtTmemCols = 64 * kQtAcc;
 constexpr int kQtOffWhi = kQtStages * kQtTileB;
 constexpr int kQtOffWlo = kQtOffWhi + kQtWB;
@@ -117,11 +118,11 @@ qproj_umma_kernel(const __grid_constant__ CUtensorMap tmX, const QPrepArgs p) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < kQtStages; ++s) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, 1 + kQtEpiWarps / 2);  // MMA commit + the tile's 4 epilogue warps (|x| read)
+            mbar_init(empty + s, 1 + 4);  // MMA commit + the tile's 4 epilogue warps (|x| read)
         }
         for (int a = 0; a < kQtAcc; ++a) {
             mbar_init(afull + a, 1);
-            mbar_init(aempty + a, kQtEpiWarps / 2);
+            mbar_init(aempty + a, 4);
         }
         mbar_init(mdone, 1);
         fence_mbar_init();
@@ -195,11 +196,11 @@ qproj_umma_kernel(const __grid_constant__ CUtensorMap tmX, const QPrepArgs p) {
         for (int u = 0; u < kQtThreads / 32; ++u) wf += wred[u];
         wf = sqrtf(wf) * 1.001f;  // >= |W|_F
         const int qd = warp & 3;                // TMEM lane quadrant this warp may access
-        const int par = (warp - 2) / 4;         // tiles t with t % 2 == par (accumulator par)
+        const int par = (warp - 2) / 4;         // tiles t with t % kQtGroups == par
         const int r = qd * 32 + lane;
         __half* q16 = static_cast<__half*>(p.q16);
         bool ok = true;
-        for (int t = par; t < my_tiles; t += 2) {
+        for (int t = par; t < my_tiles; t += kQtGroups) {
             const int s = t % kQtStages, ab = t % kQtAcc;
             const bool got = mbar_wait(afull + ab, (t / kQtAcc) & 1) && mbar_wait(full + s, (t / kQtStages) & 1);
             if (!__all_sync(kFull, got)) {
