@@ -365,16 +365,18 @@ def run_ours(args) -> None:
     h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
     d2h = oh.numel() * 2
 
-    chunk = 2
+    chunk, groups = 2, 1
 
     def e2e_step():
         # public host-buffer entry point: chunked H2D / kernels / D2H on three streams
-        routed_attention_from_host(qh, kh, vh, wq, wk, pb, L, K, oh, causal=True, chunk=chunk)
+        routed_attention_from_host(qh, kh, vh, wq, wk, pb, L, K, oh, causal=True, chunk=chunk, groups=groups)
 
-    # pipeline depth: batch elements per chunk, chosen in the untimed warm-up
+    # pipeline depth: batch elements per chunk (or GQA groups of one element),
+    # chosen in the untimed warm-up
+    options = [(1, w["Hkv"]), (1, 1), (2, 1), (4, 1)] if w["Hkv"] > 1 else [(1, 1), (2, 1), (4, 1)]
     trial = {}
-    for c in (1, 2, 4):
-        chunk = c
+    for c in options:
+        chunk, groups = c
         e2e_step()
         a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -383,10 +385,10 @@ def run_ours(args) -> None:
         b_.record(stream)
         torch.cuda.synchronize()
         trial[c] = a.elapsed_time(b_)
-    tt = torch.tensor([trial[c] for c in (1, 2, 4)], dtype=torch.float64, device=dev)
+    tt = torch.tensor([trial[c] for c in options], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)  # every rank picks the same
-    chunk = (1, 2, 4)[int(torch.argmin(tt).item())]
+    chunk, groups = options[int(torch.argmin(tt).item())]
     for _ in range(max(1, args.warmup)):
         e2e_step()
     barrier()
@@ -452,7 +454,7 @@ def run_ours(args) -> None:
             "e2e": {"value": world * args.steps * B * N / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms / args.steps, "host_link_copy_only": link,
-                    "pipeline_chunk": chunk},
+                    "pipeline_chunk": chunk, "pipeline_groups": groups},
             "long_context": long_ctx,
             "gpu_launches": launches,
             "select_exact_fallback_rows": fb_rows, "select_status": sel_status,
