@@ -670,7 +670,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             mbar_init(tempty + s, kEpiWarps);
         }
         mbar_init(mdone, 1);
-        mbar_init(wtbar, 1);
+        mbar_init(wtbar, 2);  // the two halves of Wq transposed (MMA warp, window warp)
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -733,6 +733,14 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             }
             mma_commit(mdone);  // completes once every MMA issued above has finished
             mbar_wait(mdone, 0);
+            if constexpr (!kGlobal) {
+                // on-demand q' rows: d = 0..63 of Wq transposed into the query tile, idle
+                // now that every MMA has completed
+                if (ok && p.q_in != nullptr) {
+                    mbar_arrive_expect_tx(wtbar, 16384);
+                    bulk_load(sA, p.wt, 16384, wtbar);
+                }
+            }
             if (!ok) atomicOr(p.status, 2);
         }
     } else if (warp == 2) {
@@ -760,6 +768,19 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             if (!ok)
                 for (int t = max(0, issued - kAccBufs); t < issued; ++t)
                     mbar_wait(tfull + t % kAccBufs, (t / kAccBufs) & 1);
+            if constexpr (!kGlobal) {
+                // on-demand q' rows: d = 64..127 of Wq transposed into the window
+                // buffers once every epilogue warp has released the last of them
+                if (ok && p.q_in != nullptr) {
+                    for (int t = max(0, T2 - kAccBufs); t < T2 && ok; ++t)
+                        ok = mbar_wait(tempty + t % kAccBufs, (t / kAccBufs) & 1);
+                    if (ok) {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        mbar_arrive_expect_tx(wtbar, 16384);
+                        bulk_load(win, p.wt + 4096, 16384, wtbar);
+                    }
+                }
+            }
             if (!ok) atomicOr(p.status, 8);
         }
     } else {
@@ -1057,19 +1078,6 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             // the bound), 16 bits per column half.
             reinterpret_cast<int16_t*>(&rowbuf[Cfg::kRowStride - 1].y)[hf] = (int16_t)(fb ? -1 : cnt);
             named_bar_sync(pair_bar, 64);
-            if (p.q_in != nullptr) {
-                // Wq transposed into shared memory for the on-demand canonical q' rows:
-                // d = 0..63 into the query tile (idle: every MMA has completed) and
-                // d = 64..127 into the window buffers (idle once all eight epilogue
-                // warps are past pass 2), two bulk copies completing on wtbar
-                named_bar_sync(5, 32 * kEpiWarps);
-                if (ew == 0 && lane == 0) {
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mbar_arrive_expect_tx(wtbar, 2 * 16384);
-                    bulk_load(sA, p.wt, 16384, wtbar);
-                    bulk_load(win, p.wt + 4096, 16384, wtbar);
-                }
-            }
             {
                 const int frow = r0 + 16 * hf + (lane >> 1);
                 const int fh = lane & 1;
