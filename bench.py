@@ -429,7 +429,8 @@ def run_ours(args) -> None:
     dominant = gather_roof if gat_tot >= sel_tot else select_roof
     roof = dict(dominant)
     roof["kernel"] = ("gather_attn_fwd" if dominant is gather_roof else
-                      "router selection step (router_topk: projections, prep, router_tc_kernel, fallback), "
+                      "router selection step (router_topk: k projection, key statistics, query operand "
+                      "(qproj_umma_kernel), router_tc_kernel, fallback), "
                       "timed with events around the call")
     roof["peak_source"] = f"{peaks['source']} (MEASURED_PEAKS.json burst)" if peaks["source"] == "measured" \
         else "fallback"
