@@ -3,7 +3,7 @@
 // projection that produces the operand straight from q (router_qtc.cu): the
 // power-of-two scaling of the fp16 copy, the epilogue multiplier, the bound on
 // |approximate score - canonical score| and the bound on (approximate score - bias
-// term); and the canonical q' row of a single query, for the rows that need it
+// term); and the canonical q' rows of single queries, for the rows that need them
 // when only the tensor-core projection ran.
 #pragma once
 
@@ -82,58 +82,15 @@ __device__ __forceinline__ void row_finish(long long row, int eq, float ss, floa
                           rowub);
 }
 
-// Canonical q' of two query rows (bf16 x0, x1, 128 values each; x1 may repeat
-// x0), the fmaf chain over d = 0..127 from 0.0f per output as in the projection
-// kernels, computed by the 32 lanes of a warp (outputs 2 lane and 2 lane + 1) from
-// the transposed weights wt [128 d][64 c] (one coalesced 256-byte load per d,
-// shared by the two rows) and stored to q0 and q1 (q1 null: one row).  The caller
-// orders the stores before any read of the rows (__syncwarp, or the end of the
-// kernel).
-__device__ __forceinline__ void warp_canon_q2(const __nv_bfloat16* __restrict__ x0,
-                                              const __nv_bfloat16* __restrict__ x1, const float* __restrict__ wt,
-                                              float* q0, float* q1, int lane) {
-    const uint4* xr0 = reinterpret_cast<const uint4*>(x0);
-    const uint4* xr1 = reinterpret_cast<const uint4*>(x1);
-    const float2* w2 = reinterpret_cast<const float2*>(wt) + lane;
-    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-#pragma unroll 2
-    for (int c = 0; c < 16; ++c) {
-        const uint4 xv0 = __ldg(xr0 + c), xv1 = __ldg(xr1 + c);
-        float2 wv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) wv[u] = __ldg(w2 + (8 * c + u) * 32);
-        float xf[8], yf[8];
-        unpack_bf16x2(xv0.x, xf[0], xf[1]);
-        unpack_bf16x2(xv0.y, xf[2], xf[3]);
-        unpack_bf16x2(xv0.z, xf[4], xf[5]);
-        unpack_bf16x2(xv0.w, xf[6], xf[7]);
-        unpack_bf16x2(xv1.x, yf[0], yf[1]);
-        unpack_bf16x2(xv1.y, yf[2], yf[3]);
-        unpack_bf16x2(xv1.z, yf[4], yf[5]);
-        unpack_bf16x2(xv1.w, yf[6], yf[7]);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            a0 = fmaf(xf[u], wv[u].x, a0);
-            a1 = fmaf(xf[u], wv[u].y, a1);
-            b0 = fmaf(yf[u], wv[u].x, b0);
-            b1 = fmaf(yf[u], wv[u].y, b1);
-        }
-    }
-    reinterpret_cast<float2*>(q0)[lane] = make_float2(a0, a1);
-    if (q1 != nullptr) reinterpret_cast<float2*>(q1)[lane] = make_float2(b0, b1);
-}
-
-// One row: warp_canon_q2 with the row twice.
-__device__ __forceinline__ void warp_canon_q(const __nv_bfloat16* __restrict__ x, const float* __restrict__ wt,
-                                             float* qrow, int lane) {
-    warp_canon_q2(x, x, wt, qrow, nullptr, lane);
-}
-
-// The same two rows from the transposed weights in shared memory: wt_lo holds
-// d = 0..63 and wt_hi d = 64..127, [d][64 c] each (256 bytes per d: one
+// Canonical q' of two query rows (bf16 x0, x1, 128 values each; x1 may repeat x0),
+// the fmaf chain over d = 0..127 from 0.0f per output as in the projection kernels,
+// computed by the 32 lanes of a warp (outputs 2 lane and 2 lane + 1) and stored to
+// q0 and q1 (q1 null: one row).  The weights are Wq transposed in shared memory:
+// wt_lo holds d = 0..63 and wt_hi d = 64..127, [d][64 c] each (256 bytes per d: one
 // conflict-free 8-byte load per lane).  Lanes 0..15 load row x0 and lanes 16..31 row
-// x1, 16 bytes each, and pass them around with shuffles.
-__device__ __forceinline__ void warp_canon_q2_smem(const __nv_bfloat16* __restrict__ x0,
+// x1, 16 bytes each, and pass them around with shuffles.  The caller orders the
+// stores before any read of the rows (__syncwarp, or the end of the kernel).
+__device__ __forceinline__ void warp_canon_q2(const __nv_bfloat16* __restrict__ x0,
                                                    const __nv_bfloat16* __restrict__ x1, const float* wt_lo,
                                                    const float* wt_hi, float* q0, float* q1, int lane) {
     const uint4 xv = __ldg(reinterpret_cast<const uint4*>(lane < 16 ? x0 : x1) + (lane & 15));

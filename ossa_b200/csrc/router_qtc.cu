@@ -3,7 +3,7 @@
 // q_proj(q)).  The selector scores with fp16 copies of q' and needs the canonical
 // fp32 q' (the fmaf chain over d = 0..127) only for the rows whose top-K boundary is
 // rescored or that go to the exact selector, about a tenth of the rows; those rows
-// compute it themselves (warp_canon_q2_smem).  So this kernel reads q once and
+// compute it themselves (warp_canon_q2).  So this kernel reads q once and
 // writes only what the selector reads for every row:
 //
 //  * q' = x W^T on the 5th-generation tensor cores (tcgen05.mma kind::f16, bf16

@@ -366,7 +366,7 @@ struct TcParams {
     const float* wtab;  // pos_bias window images, one per tile diagonal (kWinBytes each)
     const float* wmax;  // per diagonal, column half and tile row: the largest window value
     const float* rowub; // per row: bound on |approximate score - bias term|
-    // non-null: qp32 holds only the rows computed on demand (warp_canon_q) from the
+    // non-null: qp32 holds only the rows computed on demand (warp_canon_q2) from the
     // bf16 query rows q_in and the transposed Wq
     const __nv_bfloat16* q_in;
     const float* wt;
@@ -381,7 +381,7 @@ struct TcParams {
 // d = 0..kD-1 in order, times scale, plus (router) the position-bias term at
 // offset i - j.  Key-row loads go out 64 values at a time (one memory round
 // trip for kD = 64; the query row is reused and cached).  kQcg: the query row may
-// have been written by this kernel (warp_canon_q), so it is read through L2.
+// have been written by this kernel (warp_canon_q2), so it is read through L2.
 template <int kD = kR, bool kBias = true, bool kQcg = false>
 __device__ __forceinline__ float canonical_score(const float* __restrict__ qrow, const float* __restrict__ krow,
                                                  const float* __restrict__ bias, int L, int i, int j,
@@ -1238,7 +1238,7 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         const unsigned long long r0 = __shfl_sync(kFull, (unsigned long long)orow_id, s0);
                         const unsigned long long r1 = __shfl_sync(kFull, (unsigned long long)orow_id, s1);
                         float* qp = const_cast<float*>(p.qp32);
-                        warp_canon_q2_smem(p.q_in + r0 * 128, p.q_in + r1 * 128, reinterpret_cast<const float*>(sA),
+                        warp_canon_q2(p.q_in + r0 * 128, p.q_in + r1 * 128, reinterpret_cast<const float*>(sA),
                                            win, qp + r0 * kR, s1 != s0 ? qp + r1 * kR : nullptr, lane);
                     }
                     __syncwarp();
@@ -1741,7 +1741,8 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                     const float* qrow = p.qp32 + (size_t)row * kD;
                     const float* kbase = p.kp32 + (size_t)(b * p.Hkv + g) * p.N * kD;
                     if (p.q_in != nullptr) {
-                        warp_canon_q2_smem(p.q_in + row * 128, p.q_in + row * 128, swt, swt + 4096, const_cast<float*>(qrow), nullptr, lane);
+                        warp_canon_q2(p.q_in + row * 128, p.q_in + row * 128, swt, swt + 4096,
+                                      const_cast<float*>(qrow), nullptr, lane);
                         __syncwarp();
                     }
                     uint32_t ek[kEPL];
@@ -1785,7 +1786,7 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
                         base += __popc(bal);
                     }
                     if (p.q_in != nullptr)
-                        warp_canon_q2_smem(p.q_in + row * 128, p.q_in + row * 128, swt, swt + 4096,
+                        warp_canon_q2(p.q_in + row * 128, p.q_in + row * 128, swt, swt + 4096,
                                            const_cast<float*>(p.qp32) + row * kD, nullptr, lane);
                     __syncwarp();
                     uint32_t ek = 0u;
@@ -1865,7 +1866,7 @@ __global__ void __launch_bounds__(256) final_select_kernel(const FinalParams p) 
             }
         }
         if (fallback && p.q_in != nullptr)
-            warp_canon_q2_smem(p.q_in + row * 128, p.q_in + row * 128, swt, swt + 4096,
+            warp_canon_q2(p.q_in + row * 128, p.q_in + row * 128, swt, swt + 4096,
                                const_cast<float*>(p.qp32) + row * kD, nullptr, lane);
         if (fallback && lane == 0) {
             const int pos = atomicAdd(p.fb_count, 1);
