@@ -365,18 +365,21 @@ def run_ours(args) -> None:
     h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
     d2h = oh.numel() * 2
 
-    chunk, groups = 2, 1
+    chunk, groups, edge = 2, 1, 1
 
     def e2e_step():
         # public host-buffer entry point: chunked H2D / kernels / D2H on three streams
-        routed_attention_from_host(qh, kh, vh, wq, wk, pb, L, K, oh, causal=True, chunk=chunk, groups=groups)
+        routed_attention_from_host(qh, kh, vh, wq, wk, pb, L, K, oh, causal=True, chunk=chunk, groups=groups,
+                                   edge_groups=edge)
 
     # pipeline depth: batch elements per chunk (or GQA groups of one element),
     # chosen in the untimed warm-up
-    options = [(1, w["Hkv"]), (1, 1), (2, 1), (4, 1)] if w["Hkv"] > 1 else [(1, 1), (2, 1), (4, 1)]
+    options = [(1, 1, 1), (2, 1, 1), (4, 1, 1)]
+    if w["Hkv"] > 1:
+        options += [(1, 1, w["Hkv"]), (1, w["Hkv"], 1)]
     trial = {}
     for c in options:
-        chunk, groups = c
+        chunk, groups, edge = c
         e2e_step()
         a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -388,7 +391,7 @@ def run_ours(args) -> None:
     tt = torch.tensor([trial[c] for c in options], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)  # every rank picks the same
-    chunk, groups = options[int(torch.argmin(tt).item())]
+    chunk, groups, edge = options[int(torch.argmin(tt).item())]
     for _ in range(max(1, args.warmup)):
         e2e_step()
     barrier()
@@ -455,7 +458,7 @@ def run_ours(args) -> None:
             "e2e": {"value": world * args.steps * B * N / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms / args.steps, "host_link_copy_only": link,
-                    "pipeline_chunk": chunk, "pipeline_groups": groups},
+                    "pipeline_chunk": chunk, "pipeline_groups": groups, "pipeline_edge_groups": edge},
             "long_context": long_ctx,
             "gpu_launches": launches,
             "select_exact_fallback_rows": fb_rows, "select_status": sel_status,

@@ -77,7 +77,8 @@ def release_pipeline_buffers() -> None:
 
 
 def routed_attention_from_host(q_host, k_host, v_host, wq, wk, pos_bias, seq_len: int, top_k: int,
-                               out_host, *, causal: bool = True, chunk: int = 2, groups: int = 1, device=None):
+                               out_host, *, causal: bool = True, chunk: int = 2, groups: int = 1,
+                               edge_groups: int = 1, device=None):
     """ContentRouter selection + gathered sparse attention for host tensors.
 
     ``q_host`` (B, H, N, D), ``k_host``/``v_host`` (B, Hkv, N, D) and ``out_host``
@@ -89,7 +90,9 @@ def routed_attention_from_host(q_host, k_host, v_host, wq, wk, pos_bias, seq_len
     element into that many slices of whole GQA groups (``groups`` divides the kv
     head count; a slice is contiguous in the (B, heads, N, D) layouts), which halves
     or better the copy-in before the first kernels and the copy-out after the last
-    ones.  The device buffers of a shape are allocated on its first call and kept for
+    ones; ``edge_groups`` > 1 slices only the first and the last batch element that
+    way (the chunks between keep whole elements, whose kernels use the GPU better).
+    The device buffers of a shape are allocated on its first call and kept for
     the next ones (``release_pipeline_buffers`` drops them).
     """
     for name, t in (("q_host", q_host), ("k_host", k_host), ("v_host", v_host), ("out_host", out_host)):
@@ -113,6 +116,10 @@ def routed_attention_from_host(q_host, k_host, v_host, wq, wk, pos_bias, seq_len
         raise ValueError(f"groups must divide the kv head count {Hkv}, got {groups}")
     if groups > 1 and chunk != 1:
         raise ValueError("groups > 1 needs chunk=1 (a slice of one batch element)")
+    if edge_groups < 1 or Hkv % edge_groups != 0:
+        raise ValueError(f"edge_groups must divide the kv head count {Hkv}, got {edge_groups}")
+    if edge_groups > 1 and chunk != 1:
+        raise ValueError("edge_groups > 1 needs chunk=1 (a slice of one batch element)")
     dev = torch.device(device) if device is not None else wq.device
     if dev.type != "cuda":
         raise ValueError("the router weights must live on a CUDA device")
@@ -131,7 +138,7 @@ def routed_attention_from_host(q_host, k_host, v_host, wq, wk, pos_bias, seq_len
     pbc = pos_bias.detach().to(dev, torch.float32).contiguous()
     L = _lib.lib()
     c = min(chunk, B)
-    Hs, Hkvs = H // groups, Hkv // groups  # query and kv heads of a chunk
+    Hs, Hkvs = H // groups, Hkv // groups  # query and kv heads of the largest chunk (buffer shapes)
     key = (dev.index if dev.index is not None else torch.cuda.current_device(), tuple(q_host.shape),
            tuple(k_host.shape), q_host.dtype, c, groups, int(top_k), r)
     buf = _buffers.get(key)
@@ -149,14 +156,20 @@ def routed_attention_from_host(q_host, k_host, v_host, wq, wk, pos_bias, seq_len
             t.record_stream(sc)
     s_out.wait_stream(caller)
     scale = float(1.0 / math.sqrt(D))
-    units = [(b0, gi) for b0 in range(0, B, c) for gi in range(groups)]
-    for i, (b0, gi) in enumerate(units):
+    # chunks: (first batch element, slices of it, slice index)
+    units = []
+    for b0 in range(0, B, c):
+        ng = max(groups, edge_groups) if (b0 == 0 or b0 + c >= B) else groups
+        units += [(b0, ng, gi) for gi in range(ng)]
+    for i, (b0, ng, gi) in enumerate(units):
         b1 = min(B, b0 + c)
         n, par = b1 - b0, i % _NBUF
-        hq = slice(gi * Hs, (gi + 1) * Hs)      # the chunk's query heads
-        hk = slice(gi * Hkvs, (gi + 1) * Hkvs)  # and their kv heads
-        qd, kd, vd = buf.q[par][:n], buf.k[par][:n], buf.v[par][:n]
-        idx, out = buf.idx[par][:n], buf.out[par][:n]
+        hs, hks = H // ng, Hkv // ng
+        hq = slice(gi * hs, (gi + 1) * hs)      # the chunk's query heads
+        hk = slice(gi * hks, (gi + 1) * hks)    # and their kv heads
+        # a slice uses the leading heads of the buffers (contiguous: n = 1 when ng > 1)
+        qd, kd, vd = buf.q[par][:n, :hs], buf.k[par][:n, :hks], buf.v[par][:n, :hks]
+        idx, out = buf.idx[par][:n, :hs], buf.out[par][:n, :hs]
         s_in.wait_event(buf.comp_done[par])  # chunk i - _NBUF no longer reads these inputs
         with torch.cuda.stream(s_in):
             qd.copy_(q_host[b0:b1, hq], non_blocking=True)
@@ -168,11 +181,11 @@ def routed_attention_from_host(q_host, k_host, v_host, wq, wk, pos_bias, seq_len
         s_comp.wait_event(buf.out_done[par])  # chunk i - _NBUF's output has been copied out
         with torch.cuda.device(dev):
             _lib.check(L.ossa_router_topk(qd.data_ptr(), kd.data_ptr(), code, wqc.data_ptr(), wkc.data_ptr(),
-                                          pbc.data_ptr(), n, Hs, Hkvs, N, D, r, int(seq_len), int(top_k),
+                                          pbc.data_ptr(), n, hs, hks, N, D, r, int(seq_len), int(top_k),
                                           1 if causal else 0, idx.data_ptr(), buf.ws[par].data_ptr(),
                                           buf.ws_bytes, s_comp.cuda_stream))
             _lib.check(L.ossa_topk_attention_fwd(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), idx.data_ptr(), 0,
-                                                 code, n, Hs, Hkvs, N, D, int(top_k), scale,
+                                                 code, n, hs, hks, N, D, int(top_k), scale,
                                                  1 if causal else 0, out.data_ptr(), s_comp.cuda_stream))
         buf.comp_done[par].record(s_comp)
         s_out.wait_event(buf.comp_done[par])

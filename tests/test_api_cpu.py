@@ -123,6 +123,8 @@ def test_host_pipeline_argument_checks():
         routed_attention_from_host(q, k, k, w, w, pb, 8, 4, torch.zeros_like(q), chunk=1, groups=3)
     with pytest.raises(ValueError, match="chunk=1"):
         routed_attention_from_host(q, k, k, w, w, pb, 8, 4, torch.zeros_like(q), chunk=2, groups=2)
+    with pytest.raises(ValueError, match="edge_groups must divide"):
+        routed_attention_from_host(q, k, k, w, w, pb, 8, 4, torch.zeros_like(q), chunk=1, edge_groups=3)
     with pytest.raises(ValueError, match="CUDA"):
         routed_attention_from_host(q, k, k, w, w, pb, 8, 4, torch.zeros_like(q))
 

@@ -12,11 +12,13 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 
 
-@pytest.mark.parametrize("B,chunk,groups", [(3, 2, 1), (4, 1, 1), (2, 5, 1), (3, 1, 2)])
-def test_host_pipeline_matches_device_path(B, chunk, groups):
-    """groups = 2: each batch element moves as two slices of one GQA group each."""
+@pytest.mark.parametrize("B,chunk,groups,edge", [(3, 2, 1, 1), (4, 1, 1, 1), (2, 5, 1, 1), (3, 1, 2, 1),
+                                               (4, 1, 1, 2), (1, 1, 1, 2)])
+def test_host_pipeline_matches_device_path(B, chunk, groups, edge):
+    """groups = 2: each batch element moves as two slices of one GQA group each;
+    edge = 2: only the first and the last batch element do."""
     H, Hkv, N, D, r, K, L = 4, 2, 384, 128, 64, 32, 512
-    g = torch.Generator().manual_seed(B * 10 + chunk + groups)
+    g = torch.Generator().manual_seed(B * 10 + chunk + groups + 5 * edge)
     s = D ** -0.5
     q = (torch.randn(B, H, N, D, generator=g) * s).bfloat16().pin_memory()
     k = (torch.randn(B, Hkv, N, D, generator=g) * s).bfloat16().pin_memory()
@@ -25,7 +27,7 @@ def test_host_pipeline_matches_device_path(B, chunk, groups):
     wk = (torch.randn(r, D, generator=g) * 0.1).to(DEV)
     pb = torch.randn(2 * L, 1, generator=g).to(DEV)
     out_h = torch.empty_like(q).pin_memory()
-    routed_attention_from_host(q, k, v, wq, wk, pb, L, K, out_h, chunk=chunk, groups=groups)
+    routed_attention_from_host(q, k, v, wq, wk, pb, L, K, out_h, chunk=chunk, groups=groups, edge_groups=edge)
     torch.cuda.current_stream().synchronize()
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
     idx = router_topk(qd, kd, wq, wk, pb, L, K)
