@@ -17,9 +17,9 @@
 // One persistent CTA per SM walks 128-row tiles: warp 0 streams x tiles (two
 // 128 x 64 boxes, 128-byte swizzle) through a 6-stage ring with TMA, warp 1 issues
 // 2 x 8 MMAs of 128 x 64 x 16 per tile (W hi, then W lo) into one of eight 64-column
-// TMEM accumulators, and four groups of four epilogue warps give every row to one
-// thread: group g takes the tiles t with t % 4 == g, each warp the 32 rows of its
-// TMEM lane quadrant.  A thread reads |x|^2 from the staged tile and its row's 64
+// TMEM accumulators (tile t into t % 8), and six groups of four epilogue warps give
+// every row to one thread: group g takes the tiles t with t % 6 == g, each warp the 32
+// rows of its TMEM lane quadrant.  A thread reads |x|^2 from the staged tile and its row's 64
 // outputs with tcgen05.ld in 16-column chunks, twice (the row maximum sets the fp16
 // scaling before any value is converted; a compact loop keeps the code in the
 // instruction cache), and writes q16, rowinfo and rowub.  W's two bf16 parts sit in shared memory for the whole kernel.  Every
@@ -46,10 +46,10 @@ constexpr int kQtRows = 128;                 // rows per tile (MMA M)
 constexpr int kQtStages = 6;                 // x tile ring
 constexpr int kQtTileB = kQtRows * 128 * 2;  // one x tile: two 128 x 64 boxes (32 KB)
 constexpr int kQtWB = 64 * 128 * 2;          // one W part: two 64 x 64 sub-tiles (16 KB)
-constexpr int kQtGroups = 4;                         // epilogue groups of 4 warps, one tile each in turn
+constexpr int kQtGroups = 6;                         // epilogue groups of 4 warps, one tile each in turn
 constexpr int kQtEpiWarps = 4 * kQtGroups;
 constexpr int kQtThreads = 32 * (2 + kQtEpiWarps);  // warp 0 TMA, warp 1 MMA, then the epilogue warps
-constexpr int kQtAcc = 2 * kQtGroups;        // 64-column TMEM accumulators
+constexpr int kQtAcc = 8;                    // 64-column TMEM accumulators (all 512 columns)
 constexpr uint32_t kQtTmemCols = 64 * kQtAcc;
 constexpr int kQtOffWhi = kQtStages * kQtTileB;
 constexpr int kQtOffWlo = kQtOffWhi + kQtWB;
