@@ -202,6 +202,7 @@ def run_long_context(dev, world, rank, steps: int, warmup: int) -> list:
     alone is 100-400 MB), so no flush is needed between steps."""
     from ossa_b200 import router_topk, topk_attention
     from ossa_b200.bench.long_context import make_inputs
+    from ossa_b200.select import project_router_keys, router_topk_projected
     from ossa_b200.sequence_shard import gather_sequence, local_rows, zigzag_blocks
 
     peaks = _peaks()
@@ -226,8 +227,12 @@ def run_long_context(dev, world, rank, steps: int, warmup: int) -> list:
             vf = gather_sequence(vl, world)
             if evs:
                 evs[1].record(stream)
-            idxs = [router_topk(qb, kf, wq, wk, pb, N, K, causal=True, q_start=st)
-                    for qb, (st, _) in zip(qbs, blocks)]
+            if world == 1:
+                idxs = [router_topk(qbs[0], kf, wq, wk, pb, N, K, causal=True, q_start=0)]
+            else:  # the keys projected once for the rank's two query blocks
+                kp = project_router_keys(kf, wk)
+                idxs = [router_topk_projected(qb, kp, wq, pb, N, K, causal=True, q_start=st)
+                        for qb, (st, _) in zip(qbs, blocks)]
             if evs:
                 evs[2].record(stream)
             outs = [topk_attention(qb, kf, vf, topk_indices=ix, causal=True, q_start=st)

@@ -64,6 +64,76 @@ def router_topk(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Te
     return _router_topk(q, k, wq, wk, pos_bias, seq_len, top_k, causal=causal, q_start=q_start)[0]
 
 
+def project_router_keys(k: torch.Tensor, wk: torch.Tensor) -> torch.Tensor:
+    """Router key projections k' = k Wk^T (the k_proj of ossa/router.py:182), fp32
+    (B, Hkv, Nk, r): every value the canonical fmaf chain router_topk computes
+    internally.  Pass the result to ``router_topk_projected`` to select several query
+    blocks against the same keys without projecting them again."""
+    if k.dim() != 4:
+        raise ValueError(f"k must be (B, Hkv, Nk, D); got {tuple(k.shape)}")
+    B, Hkv, Nk, D = k.shape
+    dev = _lib.require_cuda(k, wk)
+    r = wk.shape[0]
+    if wk.shape != (r, D):
+        raise ValueError(f"projection weights must be ({r}, {D}); got {tuple(wk.shape)}")
+    kc = _as_kernel_input(k, k.dtype if k.dtype in (torch.float32, torch.bfloat16) else torch.float32)
+    wkc = wk.detach().float().contiguous()
+    kp = torch.empty((B, Hkv, Nk, r), dtype=torch.float32, device=dev)
+    if kp.numel() == 0:
+        return kp
+    with torch.cuda.device(dev):
+        st = _lib.lib().ossa_router_project_keys(kc.data_ptr(), _lib.dtype_code(kc), wkc.data_ptr(), B * Hkv * Nk, D,
+                                                 r, kp.data_ptr(), _lib.stream_ptr(dev))
+    _lib.check(st)
+    return kp
+
+
+def router_topk_projected(q: torch.Tensor, kp: torch.Tensor, wq: torch.Tensor, pos_bias: torch.Tensor,
+                          seq_len: int, top_k: int, *, causal: bool = True,
+                          q_start: Optional[int] = None) -> torch.Tensor:
+    """``router_topk`` with the keys given as their projections ``kp`` (from
+    ``project_router_keys``), identical indices.  q: (B, H, Nq, D) query rows at
+    positions q_start .. q_start + Nq - 1 (``q_start`` may be omitted when Nq equals
+    the number of keys); kp: (B, Hkv, Nk, r) fp32."""
+    if q.dim() != 4 or kp.dim() != 4:
+        raise ValueError(f"q must be (B, H, Nq, D) and kp (B, Hkv, Nk, r); got {tuple(q.shape)}, {tuple(kp.shape)}")
+    B, H, Nq, D = q.shape
+    Bk, Hkv, Nk, r = kp.shape
+    if Bk != B or Hkv <= 0 or H % Hkv != 0:
+        raise ValueError(f"q {tuple(q.shape)} and kp {tuple(kp.shape)} disagree on B or the head grouping")
+    if q_start is None and Nq != Nk:
+        raise ValueError("q_start is needed when q holds fewer rows than there are keys")
+    q0 = 0 if q_start is None else int(q_start)
+    if q0 < 0:
+        raise ValueError(f"q_start must be >= 0, got {q0}")
+    if kp.dtype != torch.float32:
+        raise ValueError("kp must be float32 (project_router_keys)")
+    dev = _lib.require_cuda(q, kp, wq, pos_bias)
+    if wq.shape != (r, D):
+        raise ValueError(f"projection weights must be ({r}, {D}); got {tuple(wq.shape)}")
+    if pos_bias.numel() != 2 * seq_len:
+        raise ValueError(f"pos_bias has {pos_bias.numel()} entries, expected 2*seq_len = {2 * seq_len}")
+    if top_k < 0:
+        raise ValueError(f"top_k must be >= 0, got {top_k}")
+    out = torch.empty((B, H, Nq, top_k), dtype=torch.int32, device=dev)
+    if out.numel() == 0:
+        return out
+    qc = _as_kernel_input(q, q.dtype if q.dtype in (torch.float32, torch.bfloat16) else torch.float32)
+    kpc = kp.contiguous()
+    wqc = wq.detach().float().contiguous()
+    pbc = pos_bias.detach().float().contiguous()
+    L = _lib.lib()
+    ws_bytes = L.ossa_router_workspace_size_kp(B, H, Hkv, Nq, Nk, r, int(top_k))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = L.ossa_router_topk_rows_kp(qc.data_ptr(), _lib.dtype_code(qc), wqc.data_ptr(), kpc.data_ptr(),
+                                        pbc.data_ptr(), B, H, Hkv, Nq, Nk, D, r, int(seq_len), int(top_k),
+                                        1 if causal else 0, q0, out.data_ptr(), ws.data_ptr(), ws_bytes,
+                                        _lib.stream_ptr(dev))
+    _lib.check(st)
+    return out
+
+
 def router_topk_with_status(q, k, wq, wk, pos_bias, seq_len: int, top_k: int, *, causal: bool = True):
     """router_topk plus (rows sent to the exact fallback, device status word),
     read back synchronously; a nonzero status means a bounded device wait

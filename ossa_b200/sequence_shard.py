@@ -22,7 +22,7 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-from .select import router_topk
+from .select import project_router_keys, router_topk, router_topk_projected
 from .topk_attention import topk_attention
 
 __all__ = ["zigzag_blocks", "local_rows", "gather_sequence", "sharded_routed_attention"]
@@ -80,6 +80,7 @@ def sharded_routed_attention(q_local: torch.Tensor, k_local: torch.Tensor, v_loc
     package's CUDA kernels (``router_topk``, ``topk_attention``) and take the
     same arguments.
     """
+    own_select = select_fn is None
     select_fn = select_fn or router_topk
     attend_fn = attend_fn or topk_attention
     world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -90,9 +91,14 @@ def sharded_routed_attention(q_local: torch.Tensor, k_local: torch.Tensor, v_loc
     k_full = gather_sequence(k_local, world, group)
     v_full = gather_sequence(v_local, world, group)
     blk = q_local.shape[2] // 2
+    # the keys are projected once for both query blocks (the default selector)
+    kp = project_router_keys(k_full, wk) if own_select else None
     outs = []
     for half, (start, _end) in enumerate(zigzag_blocks(n, world, rank)):
         qb = q_local[:, :, half * blk:(half + 1) * blk].contiguous()
-        idx = select_fn(qb, k_full, wq, wk, pos_bias, seq_len, top_k, causal=causal, q_start=start)
+        if own_select:
+            idx = router_topk_projected(qb, kp, wq, pos_bias, seq_len, top_k, causal=causal, q_start=start)
+        else:
+            idx = select_fn(qb, k_full, wq, wk, pos_bias, seq_len, top_k, causal=causal, q_start=start)
         outs.append(attend_fn(qb, k_full, v_full, topk_indices=idx, causal=causal, q_start=start))
     return torch.cat(outs, dim=2)

@@ -148,3 +148,24 @@ def test_router_key_cache_matches_router_topk(dtype):
         got = cache.topk(qn, K)
         ref = router_topk(qn, k[:, :, :pos + 1].contiguous(), *args, q_start=pos)
         assert torch.equal(got, ref), f"position {pos}"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("K", [64, 128])
+def test_router_topk_projected_keys_match(dtype, K):
+    """Keys projected once (project_router_keys) and two query blocks selected
+    against them (router_topk_projected, what the sequence-sharded path does per
+    rank) give exactly router_topk's rows; so does the whole sequence."""
+    from ossa_b200.select import project_router_keys, router_topk_projected
+
+    B, H, Hkv, N, D, r, L = 2, 12, 2, 1024, 128, 64, 1024
+    q, k, _, wq, wk, pb = _inputs(B, H, Hkv, N, D, r, L, seed=71 + K)
+    q, k = q.to(dtype).to(DEV), k.to(dtype).to(DEV)
+    wq, wk, pb = wq.to(DEV), wk.to(DEV), pb.to(DEV)
+    kp = project_router_keys(k, wk)
+    assert kp.shape == (B, Hkv, N, r) and kp.dtype == torch.float32
+    full = router_topk(q, k, wq, wk, pb, L, K)
+    for q0, nq in ((0, 256), (256, 256), (768, 256)):
+        blk = router_topk_projected(q[:, :, q0:q0 + nq].contiguous(), kp, wq, pb, L, K, q_start=q0)
+        assert torch.equal(blk, full[:, :, q0:q0 + nq]), f"block at {q0}"
+    assert torch.equal(router_topk_projected(q, kp, wq, pb, L, K), full)
