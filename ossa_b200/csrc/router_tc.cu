@@ -9,7 +9,11 @@
 // Pipeline (one CTA = 128 query rows of one (b, h), one CTA per SM):
 //  1. prep kernels turn the canonical fp32 projections q', k' into fp16 copies
 //     scaled by powers of two (q' per row, k' per (b, kv head)) so every value
-//     sits in [2^12, 2^13) at most, plus per row the epilogue multiplier
+//     sits in [2^12, 2^13) at most (for bf16 q at head_dim 128 the query side
+//     comes from the tensor-core operand kernel of router_qtc.cu instead, with
+//     bounds that cover the canonical q', and the canonical q' rows are computed
+//     in this file only for the rows that rescore or fall back), plus per row the
+//     epilogue multiplier
 //     m_i = scale * 2^-(e_q + e_k) and an error bound delta_i with
 //     |approx score - canonical score| <= delta_i, built from the measured fp16
 //     conversion errors dq_i = fp16(q'_i) - q'_i and dk_j (Cauchy-Schwarz):
