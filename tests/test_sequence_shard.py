@@ -71,3 +71,20 @@ def test_sharded_matches_unsharded_two_gpus(tmp_path):
     for rank in range(world):
         res = torch.load(tmp_path / f"rank{rank}.pt")
         assert res["same"], res
+
+
+@pytest.mark.gpu
+def test_sharded_single_process_matches_unsharded():
+    """One process (world 1): its two blocks are the two halves of the sequence,
+    selected against keys projected once (project_router_keys +
+    router_topk_projected, the default selector of the sharded path); the result
+    equals the unsharded CUDA path bit for bit."""
+    from ossa_b200 import router_topk, topk_attention
+    from ossa_b200.sequence_shard import sharded_routed_attention
+
+    B, H, Hkv, N, D, r, L, K = 1, 12, 2, 2048, 128, 64, 2048, 64
+    q, k, v, wq, wk, pb = (t.to("cuda:0") for t in shard_inputs(B, H, Hkv, N, D, r, L, seed=6))
+    q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    out = sharded_routed_attention(q, k, v, wq, wk, pb, L, K)
+    ref = topk_attention(q, k, v, topk_indices=router_topk(q, k, wq, wk, pb, L, K))
+    assert torch.equal(out, ref)
